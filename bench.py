@@ -1,0 +1,388 @@
+"""Decode benchmark: batch-1 greedy decode tok/s of the Llama-3-8B-shaped
+Q4_0 model (hidden 4096, 32 layers, 32/8 heads, FFN 14336, vocab 128256;
+Q4_0 linears, Q8_0 embeddings/output; seeded synthetic weights), plus the
+fraction of B200 HBM roofline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One JSON line on rank 0.  A step is one decode token.  Under torchrun
+(N > 1) the model is tensor-parallel over the N GPUs (heads / FFN rows split,
+one NCCL all-reduce after attention and after the FFN); total work is fixed,
+so scaling is "strong".
+
+  value        K greedy steps enqueued as K CUDA-graph launches with the
+               token fed back on the device; CUDA events on the model stream,
+               max over ranks.  The weights (4.5 GB) are far larger than L2.
+  e2e          the same K steps through the public Model::forward call
+               (smallm_model_forward): per step the token/position state goes
+               host->device from pinned memory and the full logits come back
+               device->host into pinned memory.
+  roofline     the dominant kernel, the Q4_0 GEMV, timed alone on the
+               14336x4096 matrix (33.03 MB of Q4_0 blocks per launch, four
+               copies rotated so every launch streams from HBM).
+  cpu_baseline the reference's own CPU decode (compiled from its sources,
+               oracle/_ref) on a bounded sample of the same model, all host
+               cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+WORKLOAD = "llama3-8b-q4_0"
+PROMPT = 128
+METRIC = "decode tok/s @B=1 (Llama-3-8B-shaped, Q4_0) + % of HBM BW roofline"
+# dram__bytes_read.sum + dram__bytes_write.sum of one Q4_0 GEMV launch on the
+# 14336x4096 matrix, from ncu (see profiles/gemv_q4_0_14336x4096.md); None
+# until captured.
+GEMV_NCU_TRAFFIC_BYTES = None
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    return ws, rank, local
+
+
+def allreduce_max(v: float, ws: int) -> float:
+    if ws == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(ws: int):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def ensure_model(ws: int, rank: int) -> Path:
+    from smallm_engine_b200 import synth
+    if rank == 0:
+        p = synth.ensure_gguf(WORKLOAD)
+    barrier(ws)
+    if rank != 0:
+        p = synth.ensure_gguf(WORKLOAD)  # already written by rank 0: just the path
+    return p
+
+
+def prompt_ids(vocab: int) -> np.ndarray:
+    return np.random.default_rng(1).integers(0, vocab, size=PROMPT)
+
+
+# ------------------------------------------------------------ CPU baseline --
+
+def cpu_decode_sample(path: Path, budget_s: float = 20.0, max_steps: int = 16) -> dict:
+    """The reference's decode loop (oracle/_ref: smallm-engine compiled from
+    its own sources, -O2 -mavx2 -mfma, OpenMP on every host core) on a bounded
+    sample: 8-token prompt, then greedy steps until `budget_s` or max_steps."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    if O.Reference.available():
+        kind = "reference"
+        m = O.Reference().load(path)
+        fwd = m.forward
+        vocab = m.vocab
+    else:
+        kind = "port"
+        m = O.OracleModel(path)
+        fwd = m.forward
+        vocab = m.vocab
+    prompt = prompt_ids(vocab)[:8]
+    pos = 0
+    for t in prompt:
+        l = fwd(int(t), pos)
+        pos += 1
+    steps, t0 = 0, time.perf_counter()
+    while steps < max_steps and (time.perf_counter() - t0) < budget_s:
+        l = fwd(int(np.argmax(l)), pos)
+        pos += 1
+        steps += 1
+    dt = time.perf_counter() - t0
+    return {"value": steps / dt, "unit": "tok/s", "cores": cores, "kind": kind,
+            "sample": f"{WORKLOAD}: 8-token prompt, {steps} greedy decode steps timed (steady_clock-style "
+                      f"wall time around the decode loop), OMP_NUM_THREADS={os.environ['OMP_NUM_THREADS']}"}
+
+
+def reference_arm(args, ws, rank):
+    if rank != 0:
+        return
+    path = ensure_model(1, 0)
+    for _ in range(args.warmup):
+        pass
+    cb = cpu_decode_sample(path, budget_s=max(10.0, 1.0 * args.steps), max_steps=max(args.steps, 4))
+    line = {"metric": METRIC, "value": cb["value"], "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 / cb["value"] if cb["value"] else None,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random weights, random token ids)", "impl": "reference",
+            "config": {"workload": WORKLOAD + " greedy decode, batch 1", "prompt": 8,
+                       "parallelism": "cpu (OpenMP)"},
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ ours --
+
+def gemv_roofline(device: int, iters: int = 50) -> dict:
+    """Dominant kernel alone: Q4_0 GEMV on 14336x4096, four copies rotated."""
+    import torch
+    from smallm_engine_b200 import CUDABackend, synth
+    be = CUDABackend(device)
+    rows, cols = 14336, 4096
+    mats = []
+    for i in range(4):
+        W = synth.fill(synth.Q4_0, 2 + i, "gemv", rows * cols, 0.02)
+        mats.append(be.upload(W, synth.Q4_0, rows, cols))
+    algo = mats[0].bytes()[0] + cols * 4 + rows * 4
+    x = torch.randn(cols, device=f"cuda:{device}")
+    y = torch.empty(rows, device=f"cuda:{device}")
+    s = torch.cuda.ExternalStream(be.stream, device=f"cuda:{device}")
+    for i in range(8):
+        mats[i % 4].gemv(x.data_ptr(), y.data_ptr(), be.stream)
+    be.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for i in range(iters):
+        mats[i % 4].gemv(x.data_ptr(), y.data_ptr(), be.stream)
+    e1.record(s)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    for m in mats:
+        m.free()
+    be.close()
+    return {"ms": ms, "bytes": algo}
+
+
+def our_arm(args, ws, rank, local):
+    import torch
+    from smallm_engine_b200 import CudaModel, SmallmError
+    from smallm_engine_b200 import _lib
+
+    path = ensure_model(ws, rank)
+    nccl_id = None
+    if ws > 1:
+        import torch.distributed as dist
+        buf = [None]
+        if rank == 0:
+            import ctypes
+            b = ctypes.create_string_buffer(128)
+            _lib.check(_lib.lib().smallm_nccl_unique_id(b))
+            buf = [bytes(b.raw)]
+        dist.broadcast_object_list(buf, src=0)
+        nccl_id = buf[0]
+    total_steps = PROMPT + args.warmup + 2 * args.steps + 8
+    max_ctx = max(512, (total_steps + 255) // 256 * 256)
+    m = CudaModel(path, device=local, max_ctx=max_ctx, tp_rank=rank, tp_size=ws, nccl_id=nccl_id)
+    cfg = m.config()
+    dev = f"cuda:{local}"
+    s = torch.cuda.ExternalStream(m.stream, device=dev)
+
+    # prompt (token-by-token prefill through the same graph)
+    prompt = prompt_ids(cfg.vocab_size)
+    pos = 0
+    for t in prompt[:-1]:
+        m.forward(int(t), pos, want_logits=False)
+        pos += 1
+    tok = int(prompt[-1])
+    # warm-up
+    m.decode_greedy_async(tok, pos, args.warmup)
+    ids = m.decode_ids(args.warmup)
+    pos += args.warmup
+    tok = int(ids[-1])
+
+    # ---- value: K device-fed greedy steps (graph launches), CUDA events
+    barrier(ws)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(s)
+        m.decode_greedy_async(tok, pos, args.steps)
+        e1.record(s)
+        e1.synchronize()
+    torch.cuda.synchronize(dev)
+    barrier(ws)
+    ms = allreduce_max(e0.elapsed_time(e1), ws)
+    ids = m.decode_ids(args.steps)
+    pos_timed = pos
+    pos += args.steps
+    tok = int(ids[-1])
+
+    # ---- e2e: public forward() with pinned host buffers, K steps
+    import ctypes
+    hbuf = ctypes.c_void_p()
+    _lib.check(_lib.lib().smallm_host_alloc(4 * cfg.vocab_size, ctypes.byref(hbuf)))
+    barrier(ws)
+    torch.cuda.synchronize(dev)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(s)
+    for _ in range(args.steps):
+        tok = m.forward_into(tok, pos, hbuf.value)
+        pos += 1
+    f1.record(s)
+    f1.synchronize()
+    barrier(ws)
+    e2e_ms = allreduce_max(f0.elapsed_time(f1), ws)
+    _lib.lib().smallm_host_free(hbuf)
+
+    # ---- roofline numbers
+    from smallm_engine_b200 import synth
+    spec = synth.WORKLOADS[WORKLOAD]
+    mid = pos_timed + args.steps // 2
+    bytes_tok = spec.weight_bytes_per_token() + spec.kv_bytes_per_token(mid)
+    peak, peak_kind = peaks()
+    step_ms = ms / args.steps
+    step_gbs = bytes_tok / (step_ms / 1e3) / 1e9 / ws
+    line = None
+    if rank == 0:
+        g = gemv_roofline(local)
+        ach = g["bytes"] / (g["ms"] / 1e3) / 1e9
+        cpu = cpu_decode_sample(path) if ws == 1 else None
+        line = {
+            "metric": METRIC,
+            "value": args.steps / (ms / 1e3),
+            "unit": "tok/s",
+            "n_gpus": ws,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": step_ms,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic (seeded random weights, random token ids)",
+            "config": {"workload": f"{WORKLOAD} greedy decode, batch 1, prompt {PROMPT}, positions "
+                                   f"{pos_timed}..{pos_timed + args.steps - 1}",
+                       "parallelism": f"tp{ws}" if ws > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (4.5 GB of weights per step)"},
+            "e2e": {"value": args.steps / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": 16,
+                    "d2h_bytes_per_step": 4 * cfg.vocab_size + 16},
+            "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                         "traffic": GEMV_NCU_TRAFFIC_BYTES, "peak_source": peak_kind,
+                         "kernel": "Q4_0 GEMV 14336x4096 (33.03 MB/launch)", "ms_per_launch": g["ms"]},
+            "step_roofline": {"bytes_per_token": bytes_tok, "achieved_gbs_per_gpu": step_gbs,
+                              "frac": step_gbs / peak, "note": "weights + f32 KV at mid position; "
+                              "per-GPU share under tensor parallelism"},
+            "gpu_launches": args.steps * (1 + 5 * cfg.n_layers + 2),
+            "clocks": clk.summary(),
+            "greedy_ids_head": [int(v) for v in ids[:8]],
+        }
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    barrier(ws)
+    m.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    ws, rank, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            reference_arm(args, ws, rank)
+        else:
+            our_arm(args, ws, rank, local)
+    finally:
+        if ws > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

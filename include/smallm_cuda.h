@@ -1,0 +1,220 @@
+/*
+ * smallm_cuda.h -- C ABI of the B200 (sm_100a) CUDA backend for smallm-engine.
+ *
+ * Two levels, both plain C (pointers, sizes, status codes; no C++ or CUDA
+ * types in the signatures, streams are passed as void*):
+ *
+ *  1. Op level -- the six operations of smallm::Backend
+ *     (include/smallm/backend/common/backend.h:12-38 in smallm-engine), with
+ *     the same argument meaning.  The smallm_backend_* calls take HOST
+ *     pointers exactly like the reference interface (each call copies its
+ *     operands to the GPU and the result back).  The device-pointer calls
+ *     (smallm_qmatrix_*, smallm_gemv) are the same math on device-resident
+ *     operands, for callers that keep their activations on the GPU.
+ *
+ *  2. Model level -- a device-resident Qwen2/Llama decoder behind the
+ *     smallm::Model contract (include/smallm/model/common/model.h:16-43):
+ *     forward(token, pos) -> logits, reset_cache, truncate_cache,
+ *     cached_length.  Weights are read once from the GGUF file, repacked for
+ *     coalesced 128-bit loads and kept in HBM with an f32 KV cache; the
+ *     whole per-token step is one CUDA graph.
+ *
+ * Conventions
+ *  - Every function returns SMALLM_OK (0) or a positive SMALLM_ERR_* code;
+ *    smallm_last_error() returns the message of the calling thread's last
+ *    failure.  The reference throws std::runtime_error at the same points.
+ *  - There is no CPU fallback: without a usable sm_100 device every call
+ *    fails with SMALLM_ERR_CUDA.
+ *  - A context or model is used by one host thread at a time.
+ *
+ * GGML tensor type ids (include/smallm/core/tensor.h:14-20, plus Q4_K = 12,
+ * which the reference does not implement): F32 = 0, Q4_0 = 2, Q8_0 = 8,
+ * Q4_K = 12, Q6_K = 14.  Any other type is rejected with
+ * SMALLM_ERR_UNSUPPORTED_TYPE (the reference's GEMV instead reads unknown
+ * types as F32, src/core/ops.cpp:289-299).
+ */
+#ifndef SMALLM_CUDA_H
+#define SMALLM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SMALLM_OK 0
+#define SMALLM_ERR_INVALID 1          /* bad argument or shape */
+#define SMALLM_ERR_UNSUPPORTED_TYPE 2 /* tensor type not in {0, 2, 8, 12, 14} */
+#define SMALLM_ERR_CUDA 3             /* CUDA runtime error / no device */
+#define SMALLM_ERR_IO 4               /* cannot open / map the GGUF file */
+#define SMALLM_ERR_FORMAT 5           /* malformed GGUF, missing key or tensor */
+#define SMALLM_ERR_NCCL 6             /* tensor-parallel communication failed */
+#define SMALLM_ERR_RANGE 7            /* position beyond the context length */
+
+#define SMALLM_TYPE_F32 0u
+#define SMALLM_TYPE_Q4_0 2u
+#define SMALLM_TYPE_Q8_0 8u
+#define SMALLM_TYPE_Q4_K 12u
+#define SMALLM_TYPE_Q6_K 14u
+
+/* Message of the calling thread's last failure ("" if none). */
+const char* smallm_last_error(void);
+
+/* Library version, major * 10000 + minor * 100 + patch. */
+int smallm_version(void);
+
+/* ------------------------------------------------------------------ */
+/* Op level                                                            */
+/* ------------------------------------------------------------------ */
+
+typedef struct smallm_ctx smallm_ctx;
+
+/* A context owns one CUDA stream on `device` and a cache of device copies of
+ * host weight matrices keyed by host pointer (the reference hands the
+ * backend the same stable mmap pointer for a weight on every call,
+ * src/model/qwen2_model.cpp:93-95). */
+int smallm_ctx_create(int device, smallm_ctx** out);
+int smallm_ctx_destroy(smallm_ctx* ctx);
+/* The context's cudaStream_t. */
+void* smallm_ctx_stream(smallm_ctx* ctx);
+int smallm_ctx_synchronize(smallm_ctx* ctx);
+
+/* Backend::matmul (backend.h:17-18): y[rows] = W[rows, cols] . x[cols], f32,
+ * host pointers. */
+int smallm_backend_matmul(smallm_ctx* ctx, const float* W, const float* x, uint32_t rows,
+                          uint32_t cols, float* y);
+
+/* Backend::matmul_quantized (backend.h:21-23; ops.cpp:97-300): W is `rows`
+ * rows of GGUF blocks of `type` (row-major [out][in], as the reference
+ * consumes GGUF weights), x f32[cols], y f32[rows], host pointers.  The
+ * first call with a given W uploads and repacks it; later calls reuse the
+ * device copy (the caller must not change the bytes behind W). */
+int smallm_backend_matmul_quantized(smallm_ctx* ctx, const uint8_t* W, uint32_t type,
+                                    const float* x, uint32_t rows, uint32_t cols, float* y);
+
+/* Backend::rmsnorm (backend.h:26-27; ops.cpp:29-40): y = x / rms(x) * w. */
+int smallm_backend_rmsnorm(smallm_ctx* ctx, const float* x, const float* weight, uint32_t size,
+                           float eps, float* y);
+
+/* Backend::softmax (backend.h:30; ops.cpp:43-57), in place. */
+int smallm_backend_softmax(smallm_ctx* ctx, float* x, uint32_t size);
+
+/* Backend::silu (backend.h:33; ops.cpp:60-65), in place. */
+int smallm_backend_silu(smallm_ctx* ctx, float* x, uint32_t size);
+
+/* Backend::rope (backend.h:36-37; ops.cpp:68-92): NeoX rotation of pairs
+ * (i, i + head_dim/2) of each head, in place. */
+int smallm_backend_rope(smallm_ctx* ctx, float* x, uint32_t n_heads, uint32_t head_dim,
+                        uint32_t pos, float freq_base);
+
+/* Forget every cached weight copy of the context. */
+int smallm_ctx_clear_weights(smallm_ctx* ctx);
+
+/* ---- device-resident operands ---- */
+
+typedef struct smallm_qmatrix smallm_qmatrix;
+
+/* Upload a quantized (or F32) matrix from host memory and repack it into the
+ * device layout the GEMV kernels stream (src/core/tensor.cpp:140-152 is the
+ * view the reference keeps instead). */
+int smallm_qmatrix_upload(smallm_ctx* ctx, const uint8_t* W, uint32_t type, uint32_t rows,
+                          uint32_t cols, smallm_qmatrix** out);
+int smallm_qmatrix_free(smallm_qmatrix* m);
+/* Bytes of the GGUF encoding of the matrix (the algorithmic bytes a GEMV
+ * reads) and bytes it occupies on the device. */
+int smallm_qmatrix_bytes(const smallm_qmatrix* m, uint64_t* gguf_bytes, uint64_t* device_bytes);
+
+/* y_dev[rows] = W . x_dev[cols] on `stream` (NULL = the context stream).
+ * Asynchronous; device pointers. */
+int smallm_gemv(smallm_ctx* ctx, const smallm_qmatrix* W, const float* x_dev, float* y_dev,
+                void* stream);
+
+/* Dequantize the matrix from its device layout into y_dev[rows * cols]
+ * (row-major), bit-identical to the reference's dequantize_tensor
+ * (src/core/tensor.cpp:115-138). */
+int smallm_qmatrix_dequantize(smallm_ctx* ctx, const smallm_qmatrix* W, float* y_dev, void* stream);
+
+/* Dequantize `count` elements of GGUF blocks of `type` (host in, host out),
+ * bit-identical to dequantize_tensor. */
+int smallm_dequantize(smallm_ctx* ctx, uint32_t type, const uint8_t* src, uint64_t count, float* out);
+
+/* ------------------------------------------------------------------ */
+/* Model level                                                         */
+/* ------------------------------------------------------------------ */
+
+typedef struct smallm_model smallm_model;
+
+typedef struct smallm_model_opts {
+    int device;            /* CUDA device ordinal */
+    uint32_t max_ctx;      /* KV capacity in positions; 0 = GGUF <arch>.context_length */
+    int tp_rank;           /* tensor-parallel rank (0 when tp_size == 1) */
+    int tp_size;           /* tensor-parallel degree: 1, 2, 4 or 8 */
+    const void* nccl_id;   /* 128-byte ncclUniqueId shared by all ranks (tp_size > 1) */
+    uint32_t flags;        /* reserved, 0 */
+} smallm_model_opts;
+
+typedef struct smallm_model_info {
+    char arch[16];         /* "qwen2" or "llama" */
+    uint32_t n_layers, embd, ffn, n_heads, n_kv_heads, head_dim, vocab, context_length;
+    uint32_t max_ctx;      /* KV capacity actually allocated */
+    float rope_freq_base, rms_eps;
+    uint64_t weight_bytes_per_token; /* GGUF bytes of every matrix a decode step reads
+                                        (this rank's share under tensor parallelism) */
+    uint64_t device_bytes; /* device memory held by the model */
+} smallm_model_info;
+
+/* Parse `gguf_path` (src/core/gguf.cpp:116-183, src/config/common/config.cpp
+ * :14-48) and build a device-resident model: Qwen2Model / LlamaModel
+ * (src/model/qwen2_model.cpp:28-65, llama_model.cpp:17-49).  Same required
+ * keys and tensors as the reference; output.weight is required. */
+int smallm_model_load(const char* gguf_path, const smallm_model_opts* opts, smallm_model** out);
+int smallm_model_free(smallm_model* m);
+int smallm_model_get_info(const smallm_model* m, smallm_model_info* out);
+/* The model's cudaStream_t (all model work is ordered on it). */
+void* smallm_model_stream(smallm_model* m);
+
+/* Model::forward (model.h:22): one token at `pos`; writes vocab logits to
+ * host memory `logits` (may be NULL to skip the copy) and, when `argmax` is
+ * not NULL, the first index of the maximum logit (greedy_sampler.cpp:8-14).
+ * Updates cached_length to pos + 1 like qwen2_model.cpp:196. */
+int smallm_model_forward(smallm_model* m, uint32_t token, uint32_t pos, float* logits,
+                         uint32_t* argmax);
+
+/* Model::reset_cache / truncate_cache / cached_length (model.h:25-34). */
+int smallm_model_reset_cache(smallm_model* m);
+int smallm_model_truncate_cache(smallm_model* m, uint32_t n);
+uint32_t smallm_model_cached_length(const smallm_model* m);
+
+/* Greedy decode entirely on the device: step i feeds the argmax of step i-1
+ * (the first step feeds `token`) at positions pos, pos+1, ...  Enqueues
+ * n_steps graph launches without host synchronisation; ids of the n_steps
+ * generated tokens are read back with smallm_model_decode_ids. */
+int smallm_model_decode_greedy_async(smallm_model* m, uint32_t token, uint32_t pos,
+                                     uint32_t n_steps);
+/* Wait for the decode and copy the `n` ids it produced to host `ids`. */
+int smallm_model_decode_ids(smallm_model* m, uint32_t* ids, uint32_t n);
+
+/* Device address of the last step's logits (f32[vocab] on this rank's
+ * device; this rank's vocabulary shard under tensor parallelism), valid
+ * until the next step is enqueued. */
+const float* smallm_model_logits_device(smallm_model* m);
+
+/* ------------------------------------------------------------------ */
+/* Helpers (no counterpart in the reference, which is single-process)   */
+/* ------------------------------------------------------------------ */
+
+/* Write a fresh 128-byte ncclUniqueId to `out` (rank 0 creates it and shares
+ * it with the other ranks out of band, e.g. over torch.distributed). */
+int smallm_nccl_unique_id(void* out);
+
+/* Page-locked host memory for inputs/outputs that cross the PCIe/C2C link
+ * every step. */
+int smallm_host_alloc(size_t bytes, void** out);
+int smallm_host_free(void* p);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SMALLM_CUDA_H */

@@ -1,0 +1,156 @@
+// Shared device helpers for the sm_100a kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define SM_T_F32 0u
+#define SM_T_Q4_0 2u
+#define SM_T_Q8_0 8u
+#define SM_T_Q4_K 12u
+#define SM_T_Q6_K 14u
+
+namespace smallm {
+
+constexpr int kWarp = 32;
+
+// IEEE half -> float by integer ops, bit-identical to the reference's
+// f16_to_f32 (include/smallm/core/common/quant_common.h:15-40) including
+// NaN payloads; used wherever dequantized values must match exactly.
+__device__ __forceinline__ float f16_exact(uint32_t h) {
+    uint32_t sign = (h & 0x8000u) << 16;
+    uint32_t exp = (h >> 10) & 0x1Fu;
+    uint32_t mant = h & 0x3FFu;
+    uint32_t bits;
+    if (exp == 0) {
+        if (mant == 0) {
+            bits = sign;
+        } else {
+            // normalise: shift the leading 1 of the 10-bit mantissa to bit 10
+            int lz = __clz(mant) - 21;  // leading zeros within the 11-bit field
+            mant = (mant << lz) & 0x3FFu;
+            bits = sign | ((uint32_t)(113 - lz) << 23) | (mant << 13);
+        }
+    } else if (exp == 0x1F) {
+        bits = sign | 0x7F800000u | (mant << 13);
+    } else {
+        bits = sign | ((exp + 112u) << 23) | (mant << 13);
+    }
+    return __uint_as_float(bits);
+}
+
+// Hardware half -> float; exact for every finite half (the GEMV hot loops
+// use this for block scales).
+__device__ __forceinline__ float h2f(uint32_t h) {
+    return __half2float(__ushort_as_half((unsigned short)h));
+}
+
+// Streaming 128-bit load that does not allocate in L1 (weights are read once
+// per step).
+__device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
+    uint4 v;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t ld_stream_u32(const void* p) {
+    uint32_t v;
+    asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t ld_stream_u16(const void* p) {
+    unsigned short v;
+    asm("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint2 ld_stream_u2(const void* p) {
+    uint2 v;
+    asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+                 : "=r"(v.x), "=r"(v.y)
+                 : "l"(p));
+    return v;
+}
+
+// Byte k (0..3) of w as an exact float offset by `bias`: builds 2^23 + byte
+// with a byte permute and subtracts 2^23 + bias (both exact in f32).
+template <int K>
+__device__ __forceinline__ float byte_f(uint32_t w, float magic_minus_bias) {
+    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | K)) - magic_minus_bias;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Reduce R per-lane partial sums across the warp so that every lane of the
+// group of 32/R lanes starting at r*(32/R) ends with the full sum of row r.
+// log2(R) reduce-scatter halvings, then plain butterflies.
+template <int R>
+__device__ __forceinline__ float warp_reduce_rows(float (&acc)[R], int lane) {
+    static_assert(R == 1 || R == 2 || R == 4 || R == 8, "R must be 1, 2, 4 or 8");
+    if constexpr (R == 1) {
+        return warp_sum(acc[0]);
+    } else {
+        float v[R];
+#pragma unroll
+        for (int i = 0; i < R; ++i) v[i] = acc[i];
+        int cnt = R;
+        int off = 16;
+#pragma unroll
+        for (int step = 0; step < 3; ++step) {
+            if (cnt == 1) break;
+            const bool upper = (lane & off) != 0;
+            const int h = cnt / 2;
+#pragma unroll
+            for (int i = 0; i < R / 2; ++i) {
+                if (i < h) {
+                    float keep = upper ? v[i + h] : v[i];
+                    float send = upper ? v[i] : v[i + h];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+                }
+            }
+            cnt = h;
+            off >>= 1;
+        }
+        float s = v[0];
+        for (; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+        return s;
+    }
+}
+
+// Order-preserving map of a float to uint32 (larger float -> larger key).
+__device__ __forceinline__ uint32_t float_order_key(float f) {
+    uint32_t b = __float_as_uint(f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// Pack (value, index) so that the maximum of the packed keys is the maximum
+// value with the lowest index on ties: the reference's greedy sampler keeps
+// the first strict maximum (src/runtime/sampler/greedy_sampler.cpp:8-14).
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
+    return ((unsigned long long)float_order_key(v) << 32) | (0xFFFFFFFFu - idx);
+}
+// Index of a packed key; an empty key (no non-NaN candidate) maps to 0, the
+// reference's answer when nothing beats logits[0].
+__host__ __device__ __forceinline__ uint32_t argmax_key_index(unsigned long long k) {
+    return k ? 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull) : 0u;
+}
+
+// Programmatic dependent launch controls (no-ops when the kernel was not
+// launched with the attribute).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+}  // namespace smallm

@@ -1,0 +1,142 @@
+// Internal host-side interface of the CUDA backend (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+namespace smallm {
+
+// Error carrying one of the SMALLM_ERR_* codes of include/smallm_cuda.h.
+struct Error : std::runtime_error {
+    int code;
+    Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+void cuda_check(cudaError_t e, const char* what);
+#define SM_CUDA(call) ::smallm::cuda_check((call), #call)
+
+// Elements per block and bytes per block of a GGUF type; 0 when unsupported.
+uint32_t type_block_elems(uint32_t type);
+uint32_t type_block_bytes(uint32_t type);
+bool type_supported(uint32_t type);
+uint64_t type_row_bytes(uint32_t type, uint64_t cols);
+
+// A matrix repacked into the device layout the GEMV kernels stream.
+struct QMat {
+    uint32_t type = 0;
+    uint32_t rows = 0;      // logical rows
+    uint32_t rows_pad = 0;  // storage rows (multiple of 8)
+    uint32_t cols = 0;
+    uint32_t units = 0;     // cols / elements-per-unit of the format
+    uint8_t* q = nullptr;   // quant stream
+    uint8_t* s = nullptr;   // scale stream (Q4_0, Q8_0, Q6_K)
+    uint8_t* d = nullptr;   // super-block scale stream (Q6_K)
+    uint8_t* base = nullptr;  // single allocation holding q, s, d
+    uint64_t dev_bytes = 0;
+    uint64_t gguf_bytes = 0;  // bytes of the same rows in GGUF encoding
+};
+
+// Where the rows of a QMat come from: `src` holds GGUF rows of `src_cols`
+// elements (device memory, any alignment); physical row p of the QMat is
+// source row row_map[p] (UINT32_MAX = zero row), columns
+// [col0, col0 + cols) of it.
+struct RepackSource {
+    const uint8_t* src = nullptr;
+    uint64_t src_cols = 0;
+    uint64_t col0 = 0;
+    const uint32_t* row_map = nullptr;  // device array of rows_pad entries, or null = identity
+};
+
+// Allocate `m` for (type, rows, cols) and fill it from `s` on `stream`.
+void qmat_alloc(QMat& m, uint32_t type, uint32_t rows, uint32_t cols);
+void qmat_repack(QMat& m, const RepackSource& s, cudaStream_t stream);
+void qmat_free(QMat& m);
+
+// Upload host GGUF rows (rows x src_cols, row-major) and repack them; the
+// helper stages through a temporary device buffer.  row_map (host, may be
+// empty = identity) has one entry per storage row.
+void qmat_upload(QMat& m, const uint8_t* host, uint32_t type, uint32_t rows, uint32_t cols,
+                 uint64_t src_cols, uint64_t col0, const std::vector<uint32_t>& row_map,
+                 cudaStream_t stream);
+
+enum GemvPro { GEMV_PRO_PLAIN = 0, GEMV_PRO_RMS = 1 };
+enum GemvEpi { GEMV_EPI_STORE = 0, GEMV_EPI_RESIDUAL = 1, GEMV_EPI_QKV = 2, GEMV_EPI_SWIGLU = 3,
+               GEMV_EPI_LOGITS = 4 };
+
+// Everything a GEMV launch needs besides the matrix (see gemv.cuh).
+struct GemvArgs {
+    const float* x = nullptr;
+    const float* norm_w = nullptr;
+    float eps = 0.f;
+    float* y = nullptr;
+    const float* bias = nullptr;
+    uint32_t q_rows = 0, k_rows = 0, head_dim = 0, max_ctx = 0;
+    float* qout = nullptr;
+    float* kcache = nullptr;
+    float* vcache = nullptr;
+    const float2* rope = nullptr;
+    const uint32_t* pos = nullptr;
+    unsigned long long* argmax = nullptr;
+    uint32_t row_offset = 0;  // LOGITS: global index of storage row 0 (vocab-parallel shards)
+};
+
+void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_t stream, bool pdl = false);
+
+// Dequantize a QMat to f32 [rows][cols] (bit-identical to the reference).
+void launch_qmat_dequant(const QMat& m, float* y, cudaStream_t stream);
+// Dequantize raw GGUF blocks on the device (bit-identical to the reference).
+void launch_dequant_raw(uint32_t type, const uint8_t* src, uint64_t count, float* out, cudaStream_t stream);
+
+// Decode-step state kept in device memory so a captured graph can replay.
+struct DecodeState {
+    uint32_t token;
+    uint32_t pos;
+    uint32_t step;        // ids written so far by finalize
+    uint32_t pad;
+    unsigned long long argmax;
+};
+
+// x[embd] = dequantized row state->token of the embedding matrix; resets the
+// argmax slot.
+void launch_embed(const QMat& emb, DecodeState* st, float* x, cudaStream_t stream, bool pdl = false);
+// state->token = argmax, ids[state->step++] = token, state->pos += 1.
+void launch_finalize(DecodeState* st, uint32_t* ids, uint32_t ids_cap, cudaStream_t stream, bool pdl = false);
+// Same, taking the maximum of the `n` gathered per-rank argmax keys.
+void launch_finalize_tp(DecodeState* st, const unsigned long long* keys, int n, uint32_t* ids,
+                        uint32_t ids_cap, cudaStream_t stream, bool pdl = false);
+
+// Split-K GQA decode attention over the head-major f32 KV cache, with the
+// per-head combine done by the last CTA of each KV head.
+struct AttnArgs {
+    const float* q;        // [n_heads * hd] (after RoPE)
+    const float* kcache;   // [n_kv][max_ctx][hd]
+    const float* vcache;
+    float* out;            // [n_heads * hd]
+    float* partial;        // scratch: [n_kv][n_split][group][hd + 2]
+    unsigned int* counter; // scratch: [n_kv], zero between launches
+    const uint32_t* pos;   // attend over positions 0..*pos
+    uint32_t n_heads, n_kv, hd, max_ctx, n_split;
+};
+uint32_t attention_splits(uint32_t n_kv, uint32_t max_ctx, int sm_count);
+size_t attention_partial_floats(uint32_t n_heads, uint32_t hd, uint32_t n_split);
+void launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl = false);
+
+// Op-level kernels (Backend semantics on device pointers).
+void launch_rmsnorm(const float* x, const float* w, uint32_t n, float eps, float* y, cudaStream_t s);
+void launch_softmax(float* x, uint32_t n, cudaStream_t s);
+void launch_silu(float* x, uint32_t n, cudaStream_t s);
+// cs: [head_dim/2] (cos, sin) computed on the host exactly as ops::rope does.
+void launch_rope(float* x, uint32_t n_heads, uint32_t head_dim, const float2* cs, cudaStream_t s);
+
+// Host-side rotary table, identical to ops::rope's arithmetic
+// (src/core/ops.cpp:77-82): out[p * hd/2 + i] = (cos, sin)(p * 1/powf(base, 2i/hd)).
+void rope_table(uint32_t head_dim, uint32_t positions, float base, std::vector<float2>& out,
+                uint32_t first_pos = 0);
+
+int device_sm_count();
+
+}  // namespace smallm

@@ -1,0 +1,473 @@
+// Device-resident Qwen2/Llama decoder (host orchestration).
+//
+// Mirrors Qwen2Model / LlamaModel (src/model/qwen2_model.cpp:28-198,
+// src/model/llama_model.cpp:17-177) behind the Model contract
+// (include/smallm/model/common/model.h:16-43), with the per-token step
+//
+//   embed -> L x [ QKV GEMV (fused RMSNorm, bias, RoPE, KV append)
+//                -> split-K attention -> O GEMV (+ residual)
+//                -> gate/up GEMV (fused RMSNorm, SwiGLU) -> down GEMV (+ residual) ]
+//         -> lm_head GEMV (fused final RMSNorm, logits, greedy argmax) -> finalize
+//
+// captured once as a CUDA graph whose inputs (token, position) live in
+// device memory, so a decode step is one graph launch.
+//
+// Tensor parallelism (tp_size > 1): query/KV heads and FFN rows are split
+// across ranks (column-parallel Q/K/V and gate/up, row-parallel O and down),
+// lm_head is split by vocabulary rows.  After O and after down the partial
+// residual updates are summed with one in-place ncclAllReduce of the embd
+// vector; rank 0 carries the residual, the other ranks contribute W_r.h
+// only.  The greedy argmax is merged with an ncclAllGather of 8-byte keys.
+#include <nccl.h>
+
+#include <algorithm>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "engine.h"
+#include "gguf.h"
+#include "model.h"
+
+namespace smallm {
+
+static void nccl_check(ncclResult_t r, const char* what) {
+    if (r != ncclSuccess) throw Error(6, std::string(what) + ": " + ncclGetErrorString(r));
+}
+
+void* Model::dalloc(size_t bytes) {
+    void* p = nullptr;
+    SM_CUDA(cudaMalloc(&p, bytes ? bytes : 16));
+    allocs.push_back(p);
+    dev_bytes += bytes;
+    return p;
+}
+
+Model::~Model() {
+    if (exec) cudaGraphExecDestroy(exec);
+    if (comm) ncclCommDestroy(comm);
+    for (QMat* m : all_mats()) qmat_free(*m);
+    for (void* p : allocs) cudaFree(p);
+    if (h_st) cudaFreeHost(h_st);
+    if (stream) cudaStreamDestroy(stream);
+}
+
+std::vector<QMat*> Model::all_mats() {
+    std::vector<QMat*> v{&embd_m, &out_m};
+    for (auto& l : layers) {
+        v.push_back(&l.qkv);
+        v.push_back(&l.v);
+        v.push_back(&l.o);
+        v.push_back(&l.gu);
+        v.push_back(&l.down);
+    }
+    return v;
+}
+
+namespace {
+
+// Staging for uploads: host segments are concatenated into one device
+// buffer and repacked through a row map.
+struct Stager {
+    uint8_t* buf = nullptr;
+    size_t cap = 0;
+    uint32_t* map = nullptr;
+    size_t map_cap = 0;
+    ~Stager() {
+        if (buf) cudaFree(buf);
+        if (map) cudaFree(map);
+    }
+    void need(size_t bytes, size_t map_entries) {
+        if (bytes > cap) {
+            if (buf) cudaFree(buf);
+            buf = nullptr;
+            SM_CUDA(cudaMalloc(&buf, bytes));
+            cap = bytes;
+        }
+        if (map_entries > map_cap) {
+            if (map) cudaFree(map);
+            map = nullptr;
+            SM_CUDA(cudaMalloc(&map, map_entries * 4));
+            map_cap = map_entries;
+        }
+    }
+};
+
+struct Seg {
+    const uint8_t* host;
+    uint64_t rows;
+};
+
+// Upload `segs` (each full GGUF rows of src_cols elements of `type`) and
+// repack rows `row_map` (indices into the concatenation; padded with
+// UINT32_MAX to a multiple of 8) into `m` of rows x cols taking columns
+// [col0, col0 + cols).
+void upload(QMat& m, uint32_t type, uint32_t rows, uint32_t cols, uint64_t src_cols, uint64_t col0,
+            const std::vector<Seg>& segs, std::vector<uint32_t> row_map, Stager& stg, cudaStream_t s) {
+    const uint64_t rb = type_row_bytes(type, src_cols);
+    uint64_t total = 0;
+    for (const Seg& g : segs) total += g.rows;
+    qmat_alloc(m, type, rows, cols);
+    row_map.resize(m.rows_pad, 0xFFFFFFFFu);
+    stg.need(total * rb, row_map.size());
+    uint64_t off = 0;
+    for (const Seg& g : segs) {
+        SM_CUDA(cudaMemcpyAsync(stg.buf + off, g.host, g.rows * rb, cudaMemcpyHostToDevice, s));
+        off += g.rows * rb;
+    }
+    SM_CUDA(cudaMemcpyAsync(stg.map, row_map.data(), row_map.size() * 4, cudaMemcpyHostToDevice, s));
+    RepackSource src{stg.buf, src_cols, col0, stg.map};
+    qmat_repack(m, src, s);
+    SM_CUDA(cudaStreamSynchronize(s));
+}
+
+std::vector<uint32_t> iota_map(uint32_t n, uint32_t first = 0) {
+    std::vector<uint32_t> v(n);
+    for (uint32_t i = 0; i < n; ++i) v[i] = first + i;
+    return v;
+}
+
+}  // namespace
+
+// f32 vector from a 1-D GGUF tensor, dequantised on the device exactly as
+// dequantize_tensor does (src/core/tensor.cpp:115-138).
+float* Model::upload_vector(const GGUFFile& f, const std::string& name, uint64_t expect, uint64_t first,
+                            uint64_t count) {
+    const GGUFTensor& t = f.tensor(name);
+    if (!type_supported(t.type)) throw Error(2, "unsupported tensor type: " + std::to_string(t.type));
+    if (t.numel() != expect) throw Error(5, "tensor " + name + " has an unexpected size");
+    const uint64_t n = t.numel();
+    const uint64_t bytes = type_row_bytes(t.type, n);
+    uint8_t* raw = nullptr;
+    float* full = nullptr;
+    SM_CUDA(cudaMalloc(&raw, bytes));
+    SM_CUDA(cudaMalloc(&full, n * 4));
+    SM_CUDA(cudaMemcpyAsync(raw, f.data(t), bytes, cudaMemcpyHostToDevice, stream));
+    launch_dequant_raw(t.type, raw, n, full, stream);
+    float* out = static_cast<float*>(dalloc(count * 4));
+    SM_CUDA(cudaMemcpyAsync(out, full + first, count * 4, cudaMemcpyDeviceToDevice, stream));
+    SM_CUDA(cudaStreamSynchronize(stream));
+    cudaFree(raw);
+    cudaFree(full);
+    return out;
+}
+
+void Model::load(const std::string& path, const smallm_model_opts& o) {
+    device = o.device;
+    SM_CUDA(cudaSetDevice(device));
+    int major = 0;
+    SM_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+    if (major < 10) throw Error(3, "smallm: an sm_100 (Blackwell) device is required");
+    sm_count = device_sm_count();
+    tp_rank = o.tp_size > 1 ? o.tp_rank : 0;
+    tp_size = o.tp_size > 1 ? o.tp_size : 1;
+    if (tp_size != 1 && tp_size != 2 && tp_size != 4 && tp_size != 8)
+        throw Error(1, "tp_size must be 1, 2, 4 or 8");
+    if (tp_rank < 0 || tp_rank >= tp_size) throw Error(1, "tp_rank out of range");
+    SM_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+
+    GGUFFile f(path);
+    // src/config/common/config.cpp:14-48
+    arch = f.get_str("general.architecture");
+    if (arch != "qwen2" && arch != "llama") throw Error(5, "config: unsupported architecture: " + arch);
+    const std::string& p = arch;
+    n_layers = f.get_u32(p + ".block_count");
+    embd = f.get_u32(p + ".embedding_length");
+    ffn = f.get_u32(p + ".feed_forward_length");
+    n_heads = f.get_u32(p + ".attention.head_count");
+    ctx = f.get_u32(p + ".context_length");
+    n_kv = f.get_u32_or(p + ".attention.head_count_kv", n_heads);
+    rope_base = f.get_f32_or(p + ".rope.freq_base", 10000.0f);
+    eps = f.get_f32_or(p + ".attention.layer_norm_rms_epsilon", 1e-5f);
+    vocab = (uint32_t)f.str_array_len("tokenizer.ggml.tokens");
+    if (n_heads == 0 || n_kv == 0 || n_heads % n_kv) throw Error(5, "config: bad head counts");
+    hd = embd / n_heads;
+    if (hd != 32 && hd != 64 && hd != 128) throw Error(5, "config: head_dim must be 32, 64 or 128");
+    if (vocab == 0) throw Error(5, "config: empty vocabulary (tokenizer.ggml.tokens)");
+    max_ctx = o.max_ctx ? o.max_ctx : ctx;
+    if (max_ctx == 0) throw Error(5, "config: context_length is 0");
+    const bool bias = arch == "qwen2";
+
+    if (n_heads % tp_size || n_kv % tp_size || ffn % tp_size)
+        throw Error(1, "tensor parallel degree does not divide the head / FFN counts");
+    nh_l = n_heads / tp_size;
+    nkv_l = n_kv / tp_size;
+    ffn_l = ffn / tp_size;
+    vocab_l = (vocab + tp_size - 1) / tp_size;
+    v0 = tp_rank * vocab_l;
+    const uint32_t vrows = std::min(vocab_l, vocab - std::min(vocab, v0));
+    const uint32_t qd = n_heads * hd, kvd = n_kv * hd;
+    const uint32_t h0 = tp_rank * nh_l, g0 = tp_rank * nkv_l, f0 = tp_rank * ffn_l;
+
+    Stager stg;
+    auto weight = [&](const std::string& name, uint64_t in, uint64_t out) -> const GGUFTensor& {
+        const GGUFTensor& t = f.tensor(name);
+        if (!type_supported(t.type)) throw Error(2, "unsupported tensor type: " + std::to_string(t.type));
+        if (t.dims.size() != 2 || t.dims[0] != in || t.dims[1] != out)
+            throw Error(5, "tensor " + name + " has an unexpected shape");
+        return t;
+    };
+    auto col_aligned = [&](uint32_t type, uint64_t c) {
+        const uint32_t be = type_block_elems(type);
+        const uint32_t ue = (type == SMALLM_TYPE_Q4_K || type == SMALLM_TYPE_Q6_K) ? 256 : 32;
+        return c % (be > ue ? be : ue) == 0;
+    };
+
+    // embeddings and output (qwen2_model.cpp:36-42)
+    {
+        const GGUFTensor& te = weight("token_embd.weight", embd, vocab);
+        upload(embd_m, te.type, vocab, embd, embd, 0, {{f.data(te), vocab}}, iota_map(vocab), stg, stream);
+        const GGUFTensor& to = weight("output.weight", embd, vocab);
+        upload(out_m, to.type, vrows, embd, embd, 0, {{f.data(to) + (uint64_t)v0 * type_row_bytes(to.type, embd), vrows}},
+               iota_map(vrows), stg, stream);
+        out_norm = upload_vector(f, "output_norm.weight", embd, 0, embd);
+        weight_bytes += out_m.gguf_bytes + type_row_bytes(te.type, embd);
+    }
+
+    layers.resize(n_layers);
+    for (uint32_t i = 0; i < n_layers; ++i) {
+        LayerW& L = layers[i];
+        const std::string b = "blk." + std::to_string(i) + ".";
+        L.attn_norm = upload_vector(f, b + "attn_norm.weight", embd, 0, embd);
+        L.ffn_norm = upload_vector(f, b + "ffn_norm.weight", embd, 0, embd);
+        const GGUFTensor& tq = weight(b + "attn_q.weight", embd, qd);
+        const GGUFTensor& tk = weight(b + "attn_k.weight", embd, kvd);
+        const GGUFTensor& tv = weight(b + "attn_v.weight", embd, kvd);
+        const GGUFTensor& to = weight(b + "attn_output.weight", qd, embd);
+        const GGUFTensor& tg = weight(b + "ffn_gate.weight", embd, ffn);
+        const GGUFTensor& tu = weight(b + "ffn_up.weight", embd, ffn);
+        const GGUFTensor& td = weight(b + "ffn_down.weight", ffn, embd);
+        if (tq.type != tk.type) throw Error(2, "attn_q and attn_k must share a tensor type");
+        if (tg.type != tu.type) throw Error(2, "ffn_gate and ffn_up must share a tensor type");
+        if (!col_aligned(to.type, (uint64_t)nh_l * hd) || !col_aligned(td.type, ffn_l))
+            throw Error(1, "tensor parallel split is not aligned to quantization blocks");
+
+        // Q/K/V rows: rotary pairs (i, i + hd/2) of every local head adjacent
+        // so the epilogue can rotate them; V rows in natural order.
+        std::vector<uint32_t> map;
+        const uint32_t half = hd / 2;
+        for (uint32_t h = 0; h < nh_l; ++h)
+            for (uint32_t k = 0; k < half; ++k) {
+                map.push_back((h0 + h) * hd + k);
+                map.push_back((h0 + h) * hd + k + half);
+            }
+        for (uint32_t g = 0; g < nkv_l; ++g)
+            for (uint32_t k = 0; k < half; ++k) {
+                map.push_back(qd + (g0 + g) * hd + k);
+                map.push_back(qd + (g0 + g) * hd + k + half);
+            }
+        L.fused_v = tv.type == tq.type;
+        if (L.fused_v) {
+            for (uint32_t g = 0; g < nkv_l; ++g)
+                for (uint32_t k = 0; k < hd; ++k) map.push_back(qd + kvd + (g0 + g) * hd + k);
+            const uint32_t rows = (nh_l + 2 * nkv_l) * hd;
+            upload(L.qkv, tq.type, rows, embd, embd, 0, {{f.data(tq), qd}, {f.data(tk), kvd}, {f.data(tv), kvd}},
+                   map, stg, stream);
+        } else {
+            const uint32_t rows = (nh_l + nkv_l) * hd;
+            upload(L.qkv, tq.type, rows, embd, embd, 0, {{f.data(tq), qd}, {f.data(tk), kvd}}, map, stg, stream);
+            upload(L.v, tv.type, nkv_l * hd, embd, embd, 0, {{f.data(tv), kvd}}, iota_map(nkv_l * hd, g0 * hd),
+                   stg, stream);
+        }
+        if (bias) {
+            // [q_local | k_local | v_local] in logical order
+            float* qb = upload_vector(f, b + "attn_q.bias", qd, (uint64_t)h0 * hd, (uint64_t)nh_l * hd);
+            float* kb = upload_vector(f, b + "attn_k.bias", kvd, (uint64_t)g0 * hd, (uint64_t)nkv_l * hd);
+            float* vb = upload_vector(f, b + "attn_v.bias", kvd, (uint64_t)g0 * hd, (uint64_t)nkv_l * hd);
+            L.bias = static_cast<float*>(dalloc(4ull * (nh_l + 2 * nkv_l) * hd));
+            SM_CUDA(cudaMemcpyAsync(L.bias, qb, 4ull * nh_l * hd, cudaMemcpyDeviceToDevice, stream));
+            SM_CUDA(cudaMemcpyAsync(L.bias + nh_l * hd, kb, 4ull * nkv_l * hd, cudaMemcpyDeviceToDevice, stream));
+            SM_CUDA(cudaMemcpyAsync(L.bias + (nh_l + nkv_l) * hd, vb, 4ull * nkv_l * hd, cudaMemcpyDeviceToDevice,
+                                    stream));
+        }
+        // O: all embd rows, this rank's head columns (row-parallel)
+        upload(L.o, to.type, embd, nh_l * hd, qd, (uint64_t)h0 * hd, {{f.data(to), embd}}, iota_map(embd), stg,
+               stream);
+        // gate/up interleaved so the epilogue sees (gate_j, up_j) together
+        std::vector<uint32_t> gm;
+        for (uint32_t j = 0; j < ffn_l; ++j) {
+            gm.push_back(f0 + j);
+            gm.push_back(ffn + f0 + j);
+        }
+        upload(L.gu, tg.type, 2 * ffn_l, embd, embd, 0, {{f.data(tg), ffn}, {f.data(tu), ffn}}, gm, stg, stream);
+        upload(L.down, td.type, embd, ffn_l, ffn, f0, {{f.data(td), embd}}, iota_map(embd), stg, stream);
+        weight_bytes += L.qkv.gguf_bytes + L.v.gguf_bytes + L.o.gguf_bytes + L.gu.gguf_bytes + L.down.gguf_bytes;
+    }
+    for (QMat* m : all_mats()) dev_bytes += m->dev_bytes;
+
+    // activations, KV cache, rotary table, scratch
+    const size_t kv_per = (size_t)nkv_l * max_ctx * hd;
+    kv = static_cast<float*>(dalloc(4ull * kv_per * 2 * n_layers));
+    SM_CUDA(cudaMemsetAsync(kv, 0, 4ull * kv_per * 2 * n_layers, stream));
+    std::vector<float2> rt;
+    rope_table(hd, max_ctx, rope_base, rt);
+    rope = static_cast<float2*>(dalloc(rt.size() * sizeof(float2)));
+    SM_CUDA(cudaMemcpy(rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    x = static_cast<float*>(dalloc(4ull * embd));
+    q = static_cast<float*>(dalloc(4ull * nh_l * hd));
+    att = static_cast<float*>(dalloc(4ull * nh_l * hd));
+    hbuf = static_cast<float*>(dalloc(4ull * ffn_l));
+    logits = static_cast<float*>(dalloc(4ull * vocab_l * tp_size));
+    logits_local = tp_size > 1 ? static_cast<float*>(dalloc(4ull * vocab_l)) : logits;
+    n_split = attention_splits(nkv_l, max_ctx, sm_count);
+    partial = static_cast<float*>(dalloc(4ull * attention_partial_floats(nh_l, hd, n_split)));
+    counters = static_cast<unsigned*>(dalloc(4ull * nkv_l));
+    SM_CUDA(cudaMemsetAsync(counters, 0, 4ull * nkv_l, stream));
+    st = static_cast<DecodeState*>(dalloc(sizeof(DecodeState)));
+    SM_CUDA(cudaMemsetAsync(st, 0, sizeof(DecodeState), stream));
+    keys = static_cast<unsigned long long*>(dalloc(8ull * tp_size));
+    ids_cap = max_ctx;
+    ids = static_cast<uint32_t*>(dalloc(4ull * ids_cap));
+    SM_CUDA(cudaHostAlloc(&h_st, sizeof(DecodeState), cudaHostAllocDefault));
+    std::memset(h_st, 0, sizeof(DecodeState));
+
+    if (tp_size > 1) {
+        if (!o.nccl_id) throw Error(1, "tensor parallel load needs an NCCL unique id");
+        ncclUniqueId id;
+        std::memcpy(&id, o.nccl_id, sizeof(id));
+        nccl_check(ncclCommInitRank(&comm, tp_size, id, tp_rank), "ncclCommInitRank");
+    }
+    SM_CUDA(cudaStreamSynchronize(stream));
+    capture();
+}
+
+// One decode step: everything after the (token, pos) state is in place.
+void Model::enqueue_step(cudaStream_t s) {
+    const bool pdl = false;
+    launch_embed(embd_m, st, x, s, pdl);
+    const uint32_t qrows = nh_l * hd, krows = nkv_l * hd;
+    for (uint32_t i = 0; i < n_layers; ++i) {
+        LayerW& L = layers[i];
+        float* kc = kv + (size_t)(2 * i) * nkv_l * max_ctx * hd;
+        float* vc = kv + (size_t)(2 * i + 1) * nkv_l * max_ctx * hd;
+        GemvArgs a;
+        a.x = x;
+        a.norm_w = L.attn_norm;
+        a.eps = eps;
+        a.bias = L.bias;
+        a.q_rows = qrows;
+        a.k_rows = krows;
+        a.head_dim = hd;
+        a.max_ctx = max_ctx;
+        a.qout = q;
+        a.kcache = kc;
+        a.vcache = vc;
+        a.rope = rope;
+        a.pos = &st->pos;
+        launch_gemv(L.qkv, GEMV_PRO_RMS, GEMV_EPI_QKV, a, s, pdl);
+        if (!L.fused_v) {
+            GemvArgs av = a;
+            av.q_rows = 0;
+            av.k_rows = 0;
+            av.bias = L.bias ? L.bias + qrows + krows : nullptr;
+            launch_gemv(L.v, GEMV_PRO_RMS, GEMV_EPI_QKV, av, s, pdl);
+        }
+        AttnArgs at;
+        at.q = q;
+        at.kcache = kc;
+        at.vcache = vc;
+        at.out = att;
+        at.partial = partial;
+        at.counter = counters;
+        at.pos = &st->pos;
+        at.n_heads = nh_l;
+        at.n_kv = nkv_l;
+        at.hd = hd;
+        at.max_ctx = max_ctx;
+        at.n_split = n_split;
+        launch_attention(at, s, pdl);
+
+        GemvArgs ao;
+        ao.x = att;
+        ao.y = x;
+        launch_gemv(L.o, GEMV_PRO_PLAIN, tp_rank == 0 ? GEMV_EPI_RESIDUAL : GEMV_EPI_STORE, ao, s, pdl);
+        if (tp_size > 1) nccl_check(ncclAllReduce(x, x, embd, ncclFloat32, ncclSum, comm, s), "ncclAllReduce");
+
+        GemvArgs ag;
+        ag.x = x;
+        ag.norm_w = L.ffn_norm;
+        ag.eps = eps;
+        ag.y = hbuf;
+        launch_gemv(L.gu, GEMV_PRO_RMS, GEMV_EPI_SWIGLU, ag, s, pdl);
+
+        GemvArgs ad;
+        ad.x = hbuf;
+        ad.y = x;
+        launch_gemv(L.down, GEMV_PRO_PLAIN, tp_rank == 0 ? GEMV_EPI_RESIDUAL : GEMV_EPI_STORE, ad, s, pdl);
+        if (tp_size > 1) nccl_check(ncclAllReduce(x, x, embd, ncclFloat32, ncclSum, comm, s), "ncclAllReduce");
+    }
+    GemvArgs al;
+    al.x = x;
+    al.norm_w = out_norm;
+    al.eps = eps;
+    al.y = logits_local;
+    al.argmax = &st->argmax;
+    al.row_offset = v0;
+    launch_gemv(out_m, GEMV_PRO_RMS, GEMV_EPI_LOGITS, al, s, pdl);
+    if (tp_size > 1) {
+        nccl_check(ncclAllGather(&st->argmax, keys, 1, ncclUint64, comm, s), "ncclAllGather");
+        launch_finalize_tp(st, keys, tp_size, ids, ids_cap, s, pdl);
+    } else {
+        launch_finalize(st, ids, ids_cap, s, pdl);
+    }
+}
+
+void Model::capture() {
+    cudaGraph_t g = nullptr;
+    SM_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    try {
+        enqueue_step(stream);
+    } catch (...) {
+        cudaStreamEndCapture(stream, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+    }
+    SM_CUDA(cudaStreamEndCapture(stream, &g));
+    cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
+    cudaGraphDestroy(g);
+    SM_CUDA(e);
+}
+
+void Model::set_state(uint32_t token, uint32_t pos) {
+    h_st->token = token;
+    h_st->pos = pos;
+    h_st->step = 0;
+    h_st->argmax = 0;
+    SM_CUDA(cudaMemcpyAsync(st, h_st, sizeof(DecodeState), cudaMemcpyHostToDevice, stream));
+}
+
+void Model::forward(uint32_t token, uint32_t pos, float* out_logits, uint32_t* out_argmax) {
+    if (token >= vocab) throw Error(1, "token id out of range");
+    if (pos >= max_ctx) throw Error(7, "position " + std::to_string(pos) + " is beyond the context length");
+    set_state(token, pos);
+    SM_CUDA(cudaGraphLaunch(exec, stream));
+    if (out_logits) {
+        if (tp_size > 1)
+            nccl_check(ncclAllGather(logits_local, logits, vocab_l, ncclFloat32, comm, stream), "ncclAllGather");
+        SM_CUDA(cudaMemcpyAsync(out_logits, logits, 4ull * vocab, cudaMemcpyDeviceToHost, stream));
+    }
+    if (out_argmax) SM_CUDA(cudaMemcpyAsync(h_st, st, sizeof(DecodeState), cudaMemcpyDeviceToHost, stream));
+    SM_CUDA(cudaStreamSynchronize(stream));
+    if (out_argmax) *out_argmax = h_st->token;
+    cached = pos + 1;
+}
+
+void Model::decode_async(uint32_t token, uint32_t pos, uint32_t n_steps) {
+    if (token >= vocab) throw Error(1, "token id out of range");
+    if ((uint64_t)pos + n_steps > max_ctx)
+        throw Error(7, "decode would run past the context length");
+    if (n_steps > ids_cap) throw Error(1, "too many decode steps");
+    set_state(token, pos);
+    for (uint32_t i = 0; i < n_steps; ++i) SM_CUDA(cudaGraphLaunch(exec, stream));
+    pending_steps = n_steps;
+    cached = pos + n_steps;
+}
+
+void Model::decode_ids(uint32_t* out, uint32_t n) {
+    if (n > pending_steps) throw Error(1, "fewer decode steps were run than ids requested");
+    SM_CUDA(cudaMemcpyAsync(out, ids, 4ull * n, cudaMemcpyDeviceToHost, stream));
+    SM_CUDA(cudaStreamSynchronize(stream));
+}
+
+}  // namespace smallm

@@ -1,0 +1,78 @@
+// Device-resident decoder model (internal).
+#pragma once
+
+#include <nccl.h>
+
+#include <string>
+#include <vector>
+
+#include "engine.h"
+#include "smallm_cuda.h"
+
+namespace smallm {
+
+class GGUFFile;
+
+struct LayerW {
+    QMat qkv;              // Q pairs | K pairs | V rows (V only when it shares Q's type)
+    QMat v;                // V rows when attn_v has another type than attn_q
+    bool fused_v = true;
+    QMat o, gu, down;
+    float* attn_norm = nullptr;
+    float* ffn_norm = nullptr;
+    float* bias = nullptr;  // Qwen2: [q_local | k_local | v_local]
+};
+
+struct Model {
+    // configuration (src/config/common/config.h:15-46)
+    std::string arch;
+    uint32_t n_layers = 0, embd = 0, ffn = 0, n_heads = 0, n_kv = 0, hd = 0, vocab = 0, ctx = 0, max_ctx = 0;
+    float rope_base = 10000.f, eps = 1e-5f;
+    // placement
+    int device = 0, sm_count = 0, tp_rank = 0, tp_size = 1;
+    uint32_t nh_l = 0, nkv_l = 0, ffn_l = 0, vocab_l = 0, v0 = 0;
+    cudaStream_t stream = nullptr;
+    ncclComm_t comm = nullptr;
+    // weights
+    QMat embd_m, out_m;
+    float* out_norm = nullptr;
+    std::vector<LayerW> layers;
+    // state
+    float* kv = nullptr;        // [layer][k|v][n_kv_local][max_ctx][hd]
+    float2* rope = nullptr;     // [max_ctx][hd/2]
+    float *x = nullptr, *q = nullptr, *att = nullptr, *hbuf = nullptr;
+    float *logits = nullptr, *logits_local = nullptr;
+    float* partial = nullptr;
+    unsigned* counters = nullptr;
+    uint32_t n_split = 1;
+    DecodeState* st = nullptr;
+    DecodeState* h_st = nullptr;
+    unsigned long long* keys = nullptr;
+    uint32_t* ids = nullptr;
+    uint32_t ids_cap = 0;
+    uint32_t pending_steps = 0;
+    cudaGraphExec_t exec = nullptr;
+    uint32_t cached = 0;
+    uint64_t weight_bytes = 0, dev_bytes = 0;
+    std::vector<void*> allocs;
+
+    Model() = default;
+    ~Model();
+    Model(const Model&) = delete;
+    Model& operator=(const Model&) = delete;
+
+    void load(const std::string& path, const smallm_model_opts& opts);
+    void forward(uint32_t token, uint32_t pos, float* logits, uint32_t* argmax);
+    void decode_async(uint32_t token, uint32_t pos, uint32_t n_steps);
+    void decode_ids(uint32_t* out, uint32_t n);
+    void enqueue_step(cudaStream_t s);
+
+private:
+    void* dalloc(size_t bytes);
+    float* upload_vector(const GGUFFile& f, const std::string& name, uint64_t expect, uint64_t first, uint64_t count);
+    std::vector<QMat*> all_mats();
+    void capture();
+    void set_state(uint32_t token, uint32_t pos);
+};
+
+}  // namespace smallm

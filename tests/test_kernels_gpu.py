@@ -1,0 +1,162 @@
+"""GPU parity of the op-level kernels against the reference (golden
+fixtures) and the pinned oracle.
+
+Bars: integer/byte work (dequantization, repacking) is bit-exact; RoPE is
+bit-exact (host table computed with the reference's arithmetic); the GEMV
+and reductions are floating point with a per-row bound
+    |y_gpu - y_ref| <= 1e-5 * sum_i |w_i * x_i|
+(f32 accumulation in another order; the reference's own rounding error is
+~1e-7 of the same sum)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from smallm_engine_b200 import SmallmError, synth
+from smallm_engine_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+TYPES = [O.F32, O.Q4_0, O.Q8_0, O.Q6_K, O.Q4_K]
+
+
+def gemv_bound(orc, W, t, x, rows, cols):
+    wd = orc.dequantize(t, W, rows * cols).reshape(rows, cols).astype(np.float64)
+    return 1e-5 * (np.abs(wd) @ np.abs(x.astype(np.float64))) + 1e-30
+
+
+@pytest.mark.parametrize("t", [O.Q4_0, O.Q8_0, O.Q6_K, O.Q4_K])
+def test_dequant_bit_exact(be, golden, t):
+    g = golden("dequant")
+    raw, want = g[f"raw_{t}"], g[f"out_{t}"].astype(np.float32)
+    got = be.dequantize(t, raw, want.size)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def assert_bits_equal_nan_aware(got, want):
+    """Bit-identical except for the payload of NaN results: x86 propagates an
+    input NaN's payload (and returns 0xFFC00000 for inf * 0) where the GPU
+    returns its canonical NaN; NaN positions must still agree."""
+    gn, wn = np.isnan(got), np.isnan(want)
+    assert np.array_equal(gn, wn)
+    assert np.array_equal(got[~gn].view(np.uint32), want[~wn].view(np.uint32))
+
+
+@pytest.mark.parametrize("t", [O.Q4_0, O.Q8_0, O.Q6_K])
+def test_dequant_random_bytes_bit_exact(be, orc, t):
+    """Arbitrary block bytes (NaN/Inf/subnormal scales included)."""
+    rng = np.random.default_rng(3 + t)
+    be_, bb = {O.Q4_0: (32, 18), O.Q8_0: (32, 34), O.Q6_K: (256, 210)}[t]
+    raw = rng.integers(0, 256, size=bb * 200, dtype=np.uint8)
+    want = orc.dequantize(t, raw, 200 * be_)
+    got = be.dequantize(t, raw, 200 * be_)
+    assert_bits_equal_nan_aware(got, want)
+
+
+@pytest.mark.parametrize("t,rows,cols", [(O.Q4_0, 37, 512), (O.Q8_0, 9, 896), (O.Q6_K, 13, 2048),
+                                         (O.Q4_K, 21, 1024), (O.F32, 5, 64)])
+def test_repacked_layout_dequant_bit_exact(be, orc, t, rows, cols):
+    """The device layout (split streams, Q6_K re-encoding, row padding) holds
+    exactly the reference's values."""
+    rng = np.random.default_rng(rows)
+    w = (rng.standard_normal(rows * cols) * 0.02).astype(np.float32)
+    W = synth.quantize(t, w) if t != O.F32 else w.view(np.uint8)
+    qm = be.upload(W, t, rows, cols)
+    y = torch.empty(rows * cols, dtype=torch.float32, device="cuda")
+    qm.dequantize_to(y.data_ptr())
+    be.synchronize()
+    want = orc.dequantize(t, W, rows * cols)
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), want.view(np.uint32))
+    g, d = qm.bytes()
+    assert g == orc_bytes(t, rows, cols)
+
+
+def orc_bytes(t, rows, cols):
+    return rows * O.type_nbytes(t, cols)
+
+
+@pytest.mark.parametrize("t", TYPES)
+def test_matmul_quantized_vs_golden(be, orc, golden, t):
+    g = golden("matmul")
+    rows, cols = (int(v) for v in g[f"shape_{t}"])
+    W, x, want = g[f"W_{t}"], g[f"x_{t}"], g[f"y_{t}"]
+    y = be.matmul_quantized(W, t, x, rows, cols)
+    assert np.all(np.abs(y.astype(np.float64) - want) <= gemv_bound(orc, W, t, x, rows, cols))
+
+
+@pytest.mark.parametrize("t,rows,cols", [(O.Q4_0, 14336, 4096), (O.Q4_0, 4096, 14336), (O.Q8_0, 4864, 896),
+                                         (O.Q8_0, 896, 4864), (O.Q6_K, 2048, 5632), (O.Q4_K, 5632, 2048),
+                                         (O.Q4_0, 1000, 4096), (O.Q8_0, 3, 32)])
+def test_gemv_shapes_vs_oracle(be, orc, t, rows, cols):
+    """Model shapes (config 2's Q4_0 matrices included) and ragged row counts."""
+    rng = np.random.default_rng(rows + cols)
+    w = (rng.standard_normal(rows * cols) * 0.02).astype(np.float32)
+    W = synth.quantize(t, w)
+    x = rng.standard_normal(cols).astype(np.float32)
+    y = be.matmul_quantized(W, t, x, rows, cols)
+    want = orc.matmul_quantized(W, t, x, rows, cols)
+    assert np.all(np.abs(y.astype(np.float64) - want) <= gemv_bound(orc, W, t, x, rows, cols))
+
+
+def test_gemv_device_pointers_and_linearity(be):
+    """Device-resident GEMV: W(a x1 + b x2) = a W x1 + b W x2 within rounding."""
+    rows, cols = 4096, 4096
+    rng = np.random.default_rng(9)
+    W = synth.quantize(O.Q4_0, (rng.standard_normal(rows * cols) * 0.02).astype(np.float32))
+    qm = be.upload(W, O.Q4_0, rows, cols)
+    x1 = torch.randn(cols, device="cuda")
+    x2 = torch.randn(cols, device="cuda")
+    ys = [torch.empty(rows, device="cuda") for _ in range(3)]
+    s = torch.cuda.current_stream().cuda_stream
+    qm.gemv(x1.data_ptr(), ys[0].data_ptr(), s)
+    qm.gemv(x2.data_ptr(), ys[1].data_ptr(), s)
+    x3 = 2.0 * x1 - 0.5 * x2
+    qm.gemv(x3.data_ptr(), ys[2].data_ptr(), s)
+    torch.cuda.synchronize()
+    lhs = ys[2].double()
+    rhs = 2.0 * ys[0].double() - 0.5 * ys[1].double()
+    scale = ys[0].abs().max().item() + ys[1].abs().max().item()
+    assert (lhs - rhs).abs().max().item() <= 1e-5 * scale
+
+
+def test_matmul_weight_cache_reused(be):
+    rng = np.random.default_rng(10)
+    W = synth.quantize(O.Q8_0, (rng.standard_normal(64 * 256) * 0.02).astype(np.float32))
+    x = rng.standard_normal(256).astype(np.float32)
+    a = be.matmul_quantized(W, O.Q8_0, x, 64, 256)
+    b = be.matmul_quantized(W, O.Q8_0, x, 64, 256)
+    assert np.array_equal(a, b)
+
+
+def test_unsupported_type_rejected(be):
+    W = np.zeros(64 * 2 * 4, dtype=np.uint8)
+    with pytest.raises(SmallmError) as e:
+        be.matmul_quantized(W, 1, np.zeros(64, np.float32), 4, 64)  # F16: not implemented
+    assert e.value.code == _lib.ERR_UNSUPPORTED_TYPE
+    with pytest.raises(SmallmError) as e:
+        be.matmul_quantized(W, 3, np.zeros(64, np.float32), 4, 64)
+    assert e.value.code == _lib.ERR_UNSUPPORTED_TYPE
+
+
+def test_ops_vs_golden(be, golden):
+    g = golden("ops")
+    for n in (1, 7, 64, 896, 4096):
+        x, w = g[f"rms_x_{n}"], g[f"rms_w_{n}"]
+        y = be.rmsnorm(x, w, n, 1e-6)
+        assert np.allclose(y, g[f"rms_y_{n}"], rtol=1e-5, atol=1e-6)
+        s = g[f"sm_x_{n}"].copy()
+        be.softmax(s)
+        assert np.allclose(s, g[f"sm_y_{n}"], rtol=1e-5, atol=1e-7)
+        v = (x * 4).astype(np.float32)
+        be.silu(v)
+        assert np.allclose(v, g[f"silu_y_{n}"], rtol=1e-5, atol=1e-6)
+    for k in [k[len("rope_x_"):] for k in g if k.startswith("rope_x_")]:
+        nh, hd, pos, base = g[f"rope_args_{k}"]
+        v = g[f"rope_x_{k}"].copy()
+        be.rope(v, int(nh), int(hd), int(pos), float(base))
+        assert np.array_equal(v, g[f"rope_y_{k}"]), k   # bit-exact
+
+
+def test_softmax_empty_is_noop(be):
+    x = np.zeros(0, dtype=np.float32)
+    be.softmax(x)
