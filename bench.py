@@ -153,8 +153,8 @@ def ensure_model(ws: int, rank: int) -> Path:
     return p
 
 
-def prompt_ids(vocab: int) -> np.ndarray:
-    return np.random.default_rng(1).integers(0, vocab, size=PROMPT)
+def prompt_ids(vocab: int, n: int = PROMPT) -> np.ndarray:
+    return np.random.default_rng(1).integers(0, vocab, size=max(n, PROMPT))
 
 
 # ------------------------------------------------------------ CPU baseline --
@@ -260,7 +260,7 @@ def our_arm(args, ws, rank, local):
             buf = [bytes(b.raw)]
         dist.broadcast_object_list(buf, src=0)
         nccl_id = buf[0]
-    total_steps = PROMPT + args.warmup + 2 * args.steps + 8
+    total_steps = args.prompt + args.warmup + 2 * args.steps + 8
     max_ctx = max(512, (total_steps + 255) // 256 * 256)
     m = CudaModel(path, device=local, max_ctx=max_ctx, tp_rank=rank, tp_size=ws, nccl_id=nccl_id)
     cfg = m.config()
@@ -268,7 +268,7 @@ def our_arm(args, ws, rank, local):
     s = torch.cuda.ExternalStream(m.stream, device=dev)
 
     # prompt (token-by-token prefill through the same graph)
-    prompt = prompt_ids(cfg.vocab_size)
+    prompt = prompt_ids(cfg.vocab_size)[:args.prompt]
     pos = 0
     for t in prompt[:-1]:
         m.forward(int(t), pos, want_logits=False)
@@ -326,7 +326,7 @@ def our_arm(args, ws, rank, local):
     if rank == 0:
         g = gemv_roofline(local)
         ach = g["bytes"] / (g["ms"] / 1e3) / 1e9
-        cpu = cpu_decode_sample(path) if ws == 1 else None
+        cpu = cpu_decode_sample(path) if ws == 1 and not args.no_cpu_baseline else None
         line = {
             "metric": METRIC,
             "value": args.steps / (ms / 1e3),
@@ -340,7 +340,7 @@ def our_arm(args, ws, rank, local):
             "vs_baseline": None,
             "dtype": "f32",
             "data": "synthetic (seeded random weights, random token ids)",
-            "config": {"workload": f"{WORKLOAD} greedy decode, batch 1, prompt {PROMPT}, positions "
+            "config": {"workload": f"{WORKLOAD} greedy decode, batch 1, prompt {args.prompt}, positions "
                                    f"{pos_timed}..{pos_timed + args.steps - 1}",
                        "parallelism": f"tp{ws}" if ws > 1 else "single GPU",
                        "l2": "inputs larger than L2 (4.5 GB of weights per step)"},
@@ -369,6 +369,8 @@ def main():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length before the timed steps")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -1,0 +1,215 @@
+// GQA decode attention over the device KV cache (split-K, flash-decoding).
+//
+// qwen2_model.cpp:111-133 (llama_model.cpp:297-317): for each query head h
+// with KV head h / group, scores_t = dot(q_h, k_t) / sqrt(hd) over cached
+// positions t <= pos, softmax, out_h = sum_t p_t v_t.
+//
+// Grid (n_kv, n_split).  CTA (g, s) owns one chunk of positions for the
+// `group` query heads that share KV head g, so every K/V row is read from HBM
+// once per step.  The chunk's K and V rows are contiguous in the head-major
+// cache ([n_kv][max_ctx][hd]), so they arrive in shared memory through two
+// TMA bulk copies completing on one mbarrier; scores, softmax and the V
+// reduction then run from shared memory.  Each CTA writes an unnormalised
+// partial (running max, sum, out); the last CTA of each KV head (atomic
+// ticket, no waiting) merges the partials of the non-empty chunks.
+#include "common.cuh"
+#include "engine.h"
+
+namespace smallm {
+
+constexpr int kAttnThreads = 128;
+constexpr uint32_t kAttnMinChunk = 16;
+constexpr uint32_t kAttnMaxChunk = 64;
+constexpr int kAttnMaxGroup = 8;
+
+uint32_t attention_splits(uint32_t n_kv, uint32_t max_ctx, int sm_count) {
+    uint32_t s = (uint32_t)(2 * sm_count + n_kv - 1) / n_kv;
+    const uint32_t lo = (max_ctx + kAttnMaxChunk - 1) / kAttnMaxChunk;   // chunks never exceed the maximum
+    const uint32_t hi = (max_ctx + kAttnMinChunk - 1) / kAttnMinChunk;   // no split is always empty
+    if (s > hi) s = hi;
+    if (s < lo) s = lo;
+    return s < 1 ? 1 : s;
+}
+
+size_t attention_partial_floats(uint32_t n_heads, uint32_t hd, uint32_t n_split) {
+    return (size_t)n_heads * n_split * (hd + 2);
+}
+
+__host__ __device__ static uint32_t attn_chunk(uint32_t n, uint32_t n_split) {
+    uint32_t c = (n + n_split - 1) / n_split;
+    return c < kAttnMinChunk ? kAttnMinChunk : c;
+}
+
+__host__ __device__ static uint32_t attn_chunk_max(uint32_t max_ctx, uint32_t n_split) {
+    return attn_chunk(max_ctx, n_split);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs a) {
+    constexpr int EPL = HD / 32;               // head-dim elements per lane
+    constexpr int PARTS = kAttnThreads / HD;   // position slices in the V pass
+    extern __shared__ __align__(128) float sm[];
+    const uint32_t G = a.n_heads / a.n_kv;
+    const uint32_t g = blockIdx.x, split = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int nw = kAttnThreads / 32;
+    const uint32_t chmax = attn_chunk_max(a.max_ctx, a.n_split);
+    float* ks = sm;                            // [chmax][HD]
+    float* vs = ks + (size_t)chmax * HD;       // [chmax][HD]
+    float* qs = vs + (size_t)chmax * HD;       // [G][HD]
+    float* sc = qs + G * HD;                   // [G][chmax]
+    float* ml = sc + G * chmax;                // [G][2]
+    float* red = ml + 2 * kAttnMaxGroup;       // [PARTS-1][HD][kAttnMaxGroup]
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ unsigned int is_last;
+
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t n = *a.pos + 1;
+    const uint32_t chunk = attn_chunk(n, a.n_split);
+    const uint32_t t0 = split * chunk;
+    const uint32_t t1 = min(n, t0 + chunk);
+    const uint32_t len = t0 < t1 ? t1 - t0 : 0;
+    float* part = a.partial + ((size_t)g * a.n_split + split) * G * (HD + 2);
+
+    if (len > 0) {
+        if (tid == 0) {
+            mbar_init(&bar, 1);
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
+        __syncthreads();
+        if (tid == 0) {
+            const uint32_t bytes = len * HD * 4;
+            mbar_arrive_expect_tx(&bar, 2 * bytes);
+            bulk_g2s(ks, a.kcache + ((size_t)g * a.max_ctx + t0) * HD, bytes, &bar);
+            bulk_g2s(vs, a.vcache + ((size_t)g * a.max_ctx + t0) * HD, bytes, &bar);
+        }
+        for (uint32_t i = tid; i < G * HD; i += kAttnThreads) qs[i] = a.q[(size_t)g * G * HD + i];
+        __syncthreads();
+        const bool ok = mbar_wait(&bar, 0);
+        if (!ok && tid == 0 && a.err) atomicOr(a.err, 4u);
+        const float scale = 1.0f / sqrtf((float)HD);
+
+        // scores: one warp per position, lanes split the head dimension
+        for (uint32_t t = warp; t < len; t += nw) {
+            float kv[EPL];
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) kv[e] = ok ? ks[t * HD + lane + 32 * e] : 0.f;
+#pragma unroll
+            for (int h = 0; h < kAttnMaxGroup; ++h) {
+                if (h < (int)G) {
+                    float p = 0.f;
+#pragma unroll
+                    for (int e = 0; e < EPL; ++e) p = fmaf(qs[h * HD + lane + 32 * e], kv[e], p);
+                    p = warp_sum(p);
+                    if (lane == 0) sc[h * chmax + t] = p * scale;
+                }
+            }
+        }
+        __syncthreads();
+
+        // softmax numerators and sums per head (ops::softmax, ops.cpp:43-57)
+        for (uint32_t h = warp; h < G; h += nw) {
+            float m = -INFINITY;
+            for (uint32_t i = lane; i < len; i += 32) m = fmaxf(m, sc[h * chmax + i]);
+            m = warp_max(m);
+            float l = 0.f;
+            for (uint32_t i = lane; i < len; i += 32) {
+                const float e = expf(sc[h * chmax + i] - m);
+                sc[h * chmax + i] = e;
+                l += e;
+            }
+            l = warp_sum(l);
+            if (lane == 0) {
+                ml[2 * h] = m;
+                ml[2 * h + 1] = l;
+            }
+        }
+        __syncthreads();
+
+        // o[h][d] = sum_t p[h][t] v[t][d]: thread -> (d, slice of positions)
+        const int d = tid % HD, pi = tid / HD;
+        float acc[kAttnMaxGroup];
+#pragma unroll
+        for (int h = 0; h < kAttnMaxGroup; ++h) acc[h] = 0.f;
+        for (uint32_t i = pi; i < len; i += PARTS) {
+            const float v = ok ? vs[i * HD + d] : 0.f;
+#pragma unroll
+            for (int h = 0; h < kAttnMaxGroup; ++h)
+                if (h < (int)G) acc[h] = fmaf(sc[h * chmax + i], v, acc[h]);
+        }
+        if constexpr (PARTS > 1) {
+            if (pi > 0)
+                for (int h = 0; h < kAttnMaxGroup; ++h) red[((pi - 1) * HD + d) * kAttnMaxGroup + h] = acc[h];
+            __syncthreads();
+        }
+        if (pi == 0) {
+            for (uint32_t h = 0; h < G; ++h) {
+                float o = acc[h];
+#pragma unroll
+                for (int k = 1; k < PARTS; ++k) o += red[((k - 1) * HD + d) * kAttnMaxGroup + h];
+                part[h * (HD + 2) + d] = o;
+                if (d == 0) {
+                    part[h * (HD + 2) + HD] = ml[2 * h];
+                    part[h * (HD + 2) + HD + 1] = ml[2 * h + 1];
+                }
+            }
+        }
+    }
+
+    // last CTA of this KV head merges the partials of the non-empty chunks
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) is_last = (atomicAdd(&a.counter[g], 1u) == a.n_split - 1) ? 1u : 0u;
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    const float* base = a.partial + (size_t)g * a.n_split * G * (HD + 2);
+    const uint32_t nact = min(a.n_split, (n + chunk - 1) / chunk);
+    for (uint32_t o = tid; o < G * HD; o += kAttnThreads) {
+        const uint32_t h = o / HD, dd = o % HD;
+        float M = -INFINITY;
+        for (uint32_t s = 0; s < nact; ++s) M = fmaxf(M, __ldcg(base + (s * G + h) * (HD + 2) + HD));
+        float L = 0.f, O = 0.f;
+        for (uint32_t s = 0; s < nact; ++s) {
+            const float* r = base + (s * G + h) * (HD + 2);
+            const float w = expf(__ldcg(r + HD) - M);
+            L = fmaf(w, __ldcg(r + HD + 1), L);
+            O = fmaf(w, __ldcg(r + dd), O);
+        }
+        a.out[((size_t)g * G + h) * HD + dd] = O / L;
+    }
+    if (tid == 0) a.counter[g] = 0u;
+}
+
+size_t attention_smem(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t max_ctx, uint32_t n_split) {
+    const uint32_t G = n_heads / n_kv;
+    const uint32_t chmax = attn_chunk_max(max_ctx, n_split);
+    return sizeof(float) * (2 * (size_t)chmax * hd + (size_t)G * hd + (size_t)G * chmax + 2 * kAttnMaxGroup +
+                            (size_t)(kAttnThreads - hd) * kAttnMaxGroup);
+}
+
+void launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {
+    const uint32_t G = a.n_heads / a.n_kv;
+    if (G > (uint32_t)kAttnMaxGroup || a.n_heads % a.n_kv)
+        throw Error(1, "attention: unsupported head grouping");
+    const size_t smem = attention_smem(a.n_heads, a.n_kv, a.hd, a.max_ctx, a.n_split);
+    if (smem > 200 * 1024) throw Error(1, "attention: chunk does not fit in shared memory");
+    AttnArgs aa = a;
+    void* args[] = {&aa};
+    const void* fn;
+    if (a.hd == 32) fn = (const void*)attention_kernel<32>;
+    else if (a.hd == 64) fn = (const void*)attention_kernel<64>;
+    else if (a.hd == 128) fn = (const void*)attention_kernel<128>;
+    else throw Error(1, "attention: head_dim must be 32, 64 or 128");
+    static bool attr_set = false;
+    if (!attr_set) {
+        SM_CUDA(cudaFuncSetAttribute(attention_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        SM_CUDA(cudaFuncSetAttribute(attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        SM_CUDA(cudaFuncSetAttribute(attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        attr_set = true;
+    }
+    launch_kernel_ex(fn, dim3(a.n_kv, a.n_split), dim3(kAttnThreads), smem, stream, pdl, args);
+}
+
+}  // namespace smallm

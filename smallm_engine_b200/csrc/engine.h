@@ -25,17 +25,22 @@ uint32_t type_block_bytes(uint32_t type);
 bool type_supported(uint32_t type);
 uint64_t type_row_bytes(uint32_t type, uint64_t cols);
 
-// A matrix repacked into the device layout the GEMV kernels stream.
+// A matrix repacked into the device layout the GEMV kernels stream: every
+// storage row is one contiguous record of row_stride bytes (a multiple of
+// 16), so any run of consecutive rows is one contiguous range:
+//   F32   [cols][f32]
+//   Q4_0  [units][16 B nibbles] [units][f16 d]          (+ pad)   unit = 32 elements
+//   Q8_0  [units][32 B int8]    [units][f16 d]          (+ pad)   unit = 32
+//   Q4_K  [nsb][144 B GGUF super-block]                           unit = 64
+//   Q6_K  [units][48 B codes]   [units][4 x i8 scales] [nsb][f16 d] (+ pad)  unit = 64
 struct QMat {
     uint32_t type = 0;
-    uint32_t rows = 0;      // logical rows
-    uint32_t rows_pad = 0;  // storage rows (multiple of 8)
+    uint32_t rows = 0;        // logical rows
+    uint32_t rows_pad = 0;    // storage rows (multiple of 32; the extra rows are zero)
     uint32_t cols = 0;
-    uint32_t units = 0;     // cols / elements-per-unit of the format
-    uint8_t* q = nullptr;   // quant stream
-    uint8_t* s = nullptr;   // scale stream (Q4_0, Q8_0, Q6_K)
-    uint8_t* d = nullptr;   // super-block scale stream (Q6_K)
-    uint8_t* base = nullptr;  // single allocation holding q, s, d
+    uint32_t units = 0;       // cols / elements-per-unit of the format
+    uint32_t row_stride = 0;  // bytes per storage row
+    uint8_t* base = nullptr;  // rows_pad * row_stride bytes
     uint64_t dev_bytes = 0;
     uint64_t gguf_bytes = 0;  // bytes of the same rows in GGUF encoding
 };
@@ -86,6 +91,17 @@ struct GemvArgs {
 
 void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_t stream, bool pdl = false);
 
+// Pipeline shape the GEMV uses for a matrix: rows per tile, stages of the
+// shared-memory ring, bytes of staged x, total dynamic shared memory.
+struct GemvPlan {
+    uint32_t rt = 0, stages = 0, nwarps = 0, kring = 0;
+    size_t xbytes = 0, smem = 0;
+};
+GemvPlan gemv_plan(const QMat& m);
+
+// Error bits raised by GEMV kernels whose bounded waits gave up (0 = none).
+unsigned int gemv_error_flags(bool clear);
+
 // Dequantize a QMat to f32 [rows][cols] (bit-identical to the reference).
 void launch_qmat_dequant(const QMat& m, float* y, cudaStream_t stream);
 // Dequantize raw GGUF blocks on the device (bit-identical to the reference).
@@ -120,10 +136,19 @@ struct AttnArgs {
     unsigned int* counter; // scratch: [n_kv], zero between launches
     const uint32_t* pos;   // attend over positions 0..*pos
     uint32_t n_heads, n_kv, hd, max_ctx, n_split;
+    unsigned int* err = nullptr;  // raised if a bounded wait gives up
 };
 uint32_t attention_splits(uint32_t n_kv, uint32_t max_ctx, int sm_count);
 size_t attention_partial_floats(uint32_t n_heads, uint32_t hd, uint32_t n_split);
+size_t attention_smem(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t max_ctx, uint32_t n_split);
 void launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl = false);
+
+// cudaLaunchKernelExC with optional programmatic dependent launch.
+void launch_kernel_ex(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                      void** args);
+// Device address of the current device's kernel error word (see
+// gemv_error_flags).
+unsigned int* device_error_flag();
 
 // Op-level kernels (Backend semantics on device pointers).
 void launch_rmsnorm(const float* x, const float* w, uint32_t n, float eps, float* y, cudaStream_t s);

@@ -1,21 +1,36 @@
-// Batch-1 quantized GEMV for sm_100a: y = W . x with W in a repacked GGUF
-// block layout streamed once from HBM.
+// Batch-1 quantized GEMV for sm_100a: y = W . x, W in a repacked GGUF block
+// layout streamed once from HBM, CUDA cores only.
 //
-// Design (bandwidth-bound, CUDA cores, no tensor cores):
-//  * x (f32, K elements) is staged once per CTA in shared memory, optionally
-//    RMS-normalised on the way in (fused ops::rmsnorm, src/core/ops.cpp:29-40).
-//    The staging is XOR-swizzled per 16-byte granule so that the 32 lanes of
-//    a warp, which read 32 different K-units at once, hit distinct banks.
-//  * Persistent CTAs; each warp owns a tile of R consecutive (physical) rows
-//    and its lanes stride the K dimension in "units" (one Q4_0/Q8_0 block of
-//    32, or a quarter Q4_K/Q6_K super-block of 64 elements).  Every lane
-//    issues 128-bit streaming loads, so a warp reads whole 512-byte segments.
-//  * Dequantisation uses no int->float conversion instructions: a byte
-//    permute builds 2^23 + q as an f32 bit pattern and one FADD removes the
-//    offset exactly (byte_f in common.cuh).
-//  * The R partial sums are combined with a reduce-scatter butterfly and
-//    handed to a fused epilogue: plain store, residual add, Q/K/V bias + RoPE +
-//    KV-cache append, SwiGLU, or logits + greedy argmax.
+// Memory side -- a TMA bulk-copy pipeline.  The device layout stores every
+// row as one contiguous, 16-byte padded record (quants, then scales), so a
+// tile of RT consecutive rows is ONE contiguous range.  One elected lane of a
+// producer warp streams tiles into an S-stage shared-memory ring with
+// cp.async.bulk (completion through mbarrier transaction counts).
+//
+// Compute side -- row-owner warps.  A tile is 4 rows and belongs to one
+// consumer warp for the whole K: its lanes stride the K-units, then one warp
+// butterfly yields the 4 row sums and the same warp runs the epilogue.  Each
+// of the W working warps has a private ring of k stages: warp w takes tiles
+// w, w+W, w+2W, ... and its j-th tile lands in stage w*k + j%k, so every
+// mbarrier wait is on the next phase of a stage only that warp consumes
+// (parity waits are only unambiguous that way) and the warp alone releases
+// it.  No CTA-wide barrier sits inside the tile loop.  Every wait is bounded:
+// on timeout the kernel raises an error flag and skips the remaining math.
+//
+// Math side -- integer dot products.  In the prologue each CTA turns x (f32;
+// times the RMSNorm weight when the norm is fused, ops::rmsnorm,
+// src/core/ops.cpp:29-40) into block fixed point: per 32-element block,
+// X_i = rint(x_i * 2^(22-e)) with 2^e > max|x_i|, split into three balanced
+// signed bytes X = D2*2^16 + D1*2^8 + D0.  A block's integer weight codes q
+// meet x through IDP4A: sum_i q_i X_i = 2^16 S2 + 2^8 S1 + S0 with
+// S_d = sum_i q_i D_d,i, exact in 32-bit integers, and one float scale per
+// block (weight scale * 2^(e-22)).  The representation error of x is below
+// 2^-22 of the block maximum, the same order as the f32 rounding of the
+// reference's FMA chain.  The norm's 1/rms is a scalar and is applied to the
+// row results in the epilogue.
+//
+// Epilogues (fused): plain store, residual add, Q/K/V bias + RoPE + KV-cache
+// append, SwiGLU, logits + greedy argmax.
 #pragma once
 
 #include "common.cuh"
@@ -25,24 +40,33 @@ namespace smallm {
 enum { PRO_PLAIN = 0, PRO_RMS = 1 };
 enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4 };
 
+constexpr int kGemvConsumerWarps = 16;
+constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;  // + one producer warp
+constexpr int kXRecBytes = 112;                              // per 32-element block of x
+constexpr int kMaxRT = 32;                                   // storage rows pad to this
+
 struct GemvParams {
-    // repacked matrix (see repack kernels for the layouts)
-    const uint8_t* q;
-    const uint8_t* s;
-    const uint8_t* d;
+    // repacked matrix: rows_pad records of row_stride bytes
+    const uint8_t* w;
+    uint32_t row_stride;
     uint32_t rows;      // logical rows; writes are masked to these
-    uint32_t rows_pad;  // storage rows, a multiple of 8
+    uint32_t rows_pad;  // storage rows (multiple of kMaxRT)
     uint32_t cols;
     uint32_t units;     // cols / Fmt::UE
+    uint32_t rt;        // rows per tile (4: one consumer warp per tile)
+    uint32_t stages;    // pipeline depth = nwarps * kring
+    uint32_t nwarps;    // consumer warps that take tiles (<= kGemvConsumerWarps)
+    uint32_t kring;     // stages in each warp's private ring
+    uint32_t xbytes;    // bytes of the staged x region
     // input vector and fused RMSNorm
     const float* x;
     const float* norm_w;
     float eps;
     // outputs
-    float* y;           // STORE / RESIDUAL / SWIGLU / LOGITS destination
-    const float* bias;  // optional per logical row bias (QKV)
-    // QKV epilogue: physical rows [0, q_rows) are query pairs, [q_rows,
-    // q_rows + k_rows) key pairs, the rest value rows (natural order).
+    float* y;
+    const float* bias;
+    // QKV epilogue: storage rows [0, q_rows) are query rotary pairs, [q_rows,
+    // q_rows + k_rows) key pairs, the rest value rows in natural order.
     uint32_t q_rows, k_rows;
     uint32_t head_dim, max_ctx;
     float* qout;
@@ -52,87 +76,169 @@ struct GemvParams {
     const uint32_t* pos;
     unsigned long long* argmax;
     uint32_t row_offset;  // LOGITS: global vocabulary index of storage row 0
+    unsigned int* err;    // set non-zero when a bounded wait gives up
 };
+
+// ------------------------------------------------------- x in fixed point --
+
+// Shared-memory record of one 32-element block of x.
+struct XRec {
+    uint32_t d0[8], d1[8], d2[8];  // balanced signed digits, 4 elements per word
+    int32_t sx_lo, sx_hi;          // sum of X over elements 0-15 / 16-31
+    float xs;                      // 2^(e-22): x_i ~= X_i * xs
+    float xsum;                    // sum of the f32 x_i
+};
+static_assert(sizeof(XRec) == kXRecBytes, "XRec layout");
+
+// Exact int -> float for |v| < 2^22 (IADD + FADD, no conversion unit).
+__device__ __forceinline__ float i2f_small(int v) {
+    return __int_as_float(0x4B400000 + v) - 12582912.0f;
+}
+
+// Build the record of one 32-element block cooperatively: the 8 aligned lanes
+// of a group each hold one float4 (elements 4j..4j+3, j = lane & 7).  All 32
+// lanes must call it (shuffles); lanes with act == false hold zeros and write
+// nothing.
+__device__ __forceinline__ void build_xrec_lane(float4 q, int lane, bool act, uint8_t* rec) {
+    const int j = lane & 7;
+    float m = fmaxf(fmaxf(fabsf(q.x), fabsf(q.y)), fmaxf(fabsf(q.z), fabsf(q.w)));
+    float s = (q.x + q.y) + (q.z + q.w);
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        s += __shfl_xor_sync(0xffffffffu, s, o);
+    }
+    const bool finite = m <= 3.4028235e38f;  // false for inf and NaN
+    if (!finite || m < 1e-30f) m = 0.f;      // tiny blocks contribute below f32 resolution
+    int e = 0;
+    frexpf(m, &e);  // m = f * 2^e, f in [0.5, 1): 2^e > m
+    const float up = m > 0.f ? ldexpf(1.0f, 22 - e) : 0.f;
+    const float v[4] = {q.x, q.y, q.z, q.w};
+    uint32_t p0 = 0, p1 = 0, p2 = 0;
+    int sx = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int X = __float2int_rn(v[k] * up);  // exact scaling by a power of two, |X| <= 2^22
+        sx += X;
+        const int a0 = (int)(int8_t)(X & 0xFF);
+        const int X1 = (X - a0) >> 8;
+        const int a1 = (int)(int8_t)(X1 & 0xFF);
+        const int a2 = (X1 - a1) >> 8;
+        p0 |= (uint32_t)(a0 & 0xFF) << (8 * k);
+        p1 |= (uint32_t)(a1 & 0xFF) << (8 * k);
+        p2 |= (uint32_t)(a2 & 0xFF) << (8 * k);
+    }
+    sx += __shfl_xor_sync(0xffffffffu, sx, 1);
+    sx += __shfl_xor_sync(0xffffffffu, sx, 2);  // lanes 0-3: elements 0-15, lanes 4-7: 16-31
+    const int sx_other = __shfl_xor_sync(0xffffffffu, sx, 4);
+    if (act) {
+        uint32_t* w = reinterpret_cast<uint32_t*>(rec);
+        w[j] = p0;
+        w[8 + j] = p1;
+        w[16 + j] = p2;
+        if (j == 0) {
+            const float nan = __int_as_float(0x7FC00000);  // propagate like the reference's f32 math
+            w[24] = (uint32_t)sx;
+            w[25] = (uint32_t)sx_other;
+            reinterpret_cast<float*>(w)[26] = !finite ? nan : (m > 0.f ? ldexpf(1.0f, e - 22) : 0.f);
+            reinterpret_cast<float*>(w)[27] = !finite ? nan : s;
+        }
+    }
+}
+
+__device__ __forceinline__ void load_xrec(const uint8_t* base, uint32_t blk, XRec& r) {
+    const uint4* p = reinterpret_cast<const uint4*>(base + (size_t)blk * kXRecBytes);
+#pragma unroll
+    for (int i = 0; i < 7; ++i) reinterpret_cast<uint4*>(&r)[i] = p[i];
+}
+
+// sum_i q_i x_i of one block = xs * (2^16 S2 + 2^8 S1 + S0); the S are exact
+// and below 2^22 in magnitude for every format here.
+__device__ __forceinline__ float combine(int s0, int s1, int s2) {
+    return fmaf(i2f_small(s2), 65536.0f, fmaf(i2f_small(s1), 256.0f, i2f_small(s0)));
+}
 
 // ---------------------------------------------------------------- formats --
+// Device row records (kernels.cu: qmat_alloc / repack):
+//  Q4_0  [units][16 B nibbles] [units][f16 d]          unit = one 32-block
+//  Q8_0  [units][32 B int8]    [units][f16 d]          unit = one 32-block
+//  Q4_K  [nsb][144 B GGUF super-block]                 unit = quarter super-block (64)
+//  Q6_K  [units][48 B codes]   [units][4 x i8 scale] [nsb][f16 d]   unit = 64
+//  F32   [cols][f32]                                   unit = 32 values
 
-// Q4_0: q stream [rows][units][16 B], s stream [rows][units] f16.
-// Element i of a block is the low nibble of byte i, element i+16 the high
-// nibble (src/core/tensor.cpp:57-63); value (q - 8) * d.
+// Q4_0: element i of a block is the low nibble of byte i, element i+16 the
+// high nibble (src/core/tensor.cpp:57-63); value (q - 8) * d.
 struct FmtQ4_0 {
-    static constexpr int UE = 32, SUBS = 1, GS = 3;
-    static constexpr bool XSUM = false;
+    static constexpr int UE = 32, SUBS = 1;
+    static constexpr bool F32X = false;
     struct Raw { uint4 q; uint32_t s; };
-    __device__ __forceinline__ static void load(const GemvParams& p, uint32_t row, uint32_t u, Raw& r) {
-        size_t i = (size_t)row * p.units + u;
-        r.q = ld_stream_u4(p.q + i * 16);
-        r.s = ld_stream_u16(p.s + i * 2);
+    __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t units, Raw& r) {
+        r.q = *reinterpret_cast<const uint4*>(row + (size_t)u * 16);
+        r.s = *reinterpret_cast<const uint16_t*>(row + (size_t)units * 16 + (size_t)u * 2);
     }
-    __device__ __forceinline__ static float dot(const Raw& r, int, const float (&x)[32], const float*, uint32_t) {
-        const float M = 8388616.0f;  // 2^23 + 8
+    __device__ __forceinline__ static float dot(const Raw& r, int, const XRec& x, uint32_t) {
         const uint32_t w[4] = {r.q.x, r.q.y, r.q.z, r.q.w};
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        int s0 = 0, s1 = 0, s2 = 0;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            uint32_t lo = w[j] & 0x0F0F0F0Fu, hi = (w[j] >> 4) & 0x0F0F0F0Fu;
-            a0 = fmaf(byte_f<0>(lo, M), x[4 * j + 0], a0);
-            a1 = fmaf(byte_f<1>(lo, M), x[4 * j + 1], a1);
-            a2 = fmaf(byte_f<2>(lo, M), x[4 * j + 2], a2);
-            a3 = fmaf(byte_f<3>(lo, M), x[4 * j + 3], a3);
-            a0 = fmaf(byte_f<0>(hi, M), x[16 + 4 * j + 0], a0);
-            a1 = fmaf(byte_f<1>(hi, M), x[16 + 4 * j + 1], a1);
-            a2 = fmaf(byte_f<2>(hi, M), x[16 + 4 * j + 2], a2);
-            a3 = fmaf(byte_f<3>(hi, M), x[16 + 4 * j + 3], a3);
+            const int lo = (int)(w[j] & 0x0F0F0F0Fu), hi = (int)((w[j] >> 4) & 0x0F0F0F0Fu);
+            s0 = __dp4a(lo, (int)x.d0[j], s0);
+            s1 = __dp4a(lo, (int)x.d1[j], s1);
+            s2 = __dp4a(lo, (int)x.d2[j], s2);
+            s0 = __dp4a(hi, (int)x.d0[4 + j], s0);
+            s1 = __dp4a(hi, (int)x.d1[4 + j], s1);
+            s2 = __dp4a(hi, (int)x.d2[4 + j], s2);
         }
-        return ((a0 + a1) + (a2 + a3)) * h2f(r.s);
+        // sum (q - 8) X = 2^16 S2 + 2^8 S1 + S0 - 8 sum X
+        const float v = fmaf(-8.0f, (float)(x.sx_lo + x.sx_hi), combine(s0, s1, s2));
+        return v * (h2f(r.s) * x.xs);
     }
 };
 
-// Q8_0: q stream [rows][units][32 B] (int8), s stream [rows][units] f16.
+// Q8_0: int8 codes; value q * d.
 struct FmtQ8_0 {
-    static constexpr int UE = 32, SUBS = 1, GS = 3;
-    static constexpr bool XSUM = false;
+    static constexpr int UE = 32, SUBS = 1;
+    static constexpr bool F32X = false;
     struct Raw { uint4 a, b; uint32_t s; };
-    __device__ __forceinline__ static void load(const GemvParams& p, uint32_t row, uint32_t u, Raw& r) {
-        size_t i = (size_t)row * p.units + u;
-        r.a = ld_stream_u4(p.q + i * 32);
-        r.b = ld_stream_u4(p.q + i * 32 + 16);
-        r.s = ld_stream_u16(p.s + i * 2);
+    __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t units, Raw& r) {
+        const uint4* q = reinterpret_cast<const uint4*>(row + (size_t)u * 32);
+        // lanes with bit 2 of u set read the upper half first, so the 8 lanes
+        // of each quarter-warp touch distinct banks in both loads
+        const uint32_t f = (u >> 2) & 1u;
+        const uint4 first = q[f], second = q[f ^ 1u];
+        r.a = f ? second : first;
+        r.b = f ? first : second;
+        r.s = *reinterpret_cast<const uint16_t*>(row + (size_t)units * 32 + (size_t)u * 2);
     }
-    __device__ __forceinline__ static float dot(const Raw& r, int, const float (&x)[32], const float*, uint32_t) {
-        const float M = 8388736.0f;  // 2^23 + 128 (bytes are biased by 128 first)
+    __device__ __forceinline__ static float dot(const Raw& r, int, const XRec& x, uint32_t) {
         const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        int s0 = 0, s1 = 0, s2 = 0;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            uint32_t u = w[j] ^ 0x80808080u;
-            a0 = fmaf(byte_f<0>(u, M), x[4 * j + 0], a0);
-            a1 = fmaf(byte_f<1>(u, M), x[4 * j + 1], a1);
-            a2 = fmaf(byte_f<2>(u, M), x[4 * j + 2], a2);
-            a3 = fmaf(byte_f<3>(u, M), x[4 * j + 3], a3);
+            s0 = __dp4a((int)w[j], (int)x.d0[j], s0);
+            s1 = __dp4a((int)w[j], (int)x.d1[j], s1);
+            s2 = __dp4a((int)w[j], (int)x.d2[j], s2);
         }
-        return ((a0 + a1) + (a2 + a3)) * h2f(r.s);
+        return combine(s0, s1, s2) * (h2f(r.s) * x.xs);
     }
 };
 
-// Q4_K: GGUF super-blocks kept as they are, [rows][nsb][144 B] (144 = 9 x 16,
-// so every super-block is 16-byte aligned): f16 d, f16 dmin, 12 bytes of
-// 6-bit scales/mins, 128 bytes of nibbles.  A unit is a quarter super-block:
-// sub-blocks 2k (low nibbles of qs[32k..32k+32)) and 2k+1 (high nibbles).
-// Value of an element: (d*sc)*q - dmin*m (gguf-py Q4_K.dequantize_blocks).
+// Q4_K: GGUF super-blocks {f16 d, f16 dmin, 12 B packed 6-bit scales/mins,
+// 128 B nibbles}; a unit is a quarter super-block: sub-block 2k = low
+// nibbles of qs[32k..32k+32), sub-block 2k+1 = high nibbles.
+// Value: (d*sc)*q - dmin*m (gguf-py Q4_K.dequantize_blocks).
 struct FmtQ4K {
-    static constexpr int UE = 64, SUBS = 2, GS = 4;
-    static constexpr bool XSUM = true;
+    static constexpr int UE = 64, SUBS = 2;
+    static constexpr bool F32X = false;
     struct Raw { uint4 h, a, b; };
-    __device__ __forceinline__ static void load(const GemvParams& p, uint32_t row, uint32_t u, Raw& r) {
-        const uint8_t* sb = p.q + ((size_t)row * (p.units >> 2) + (u >> 2)) * 144;
-        r.h = ld_stream_u4(sb);
-        r.a = ld_stream_u4(sb + 16 + (u & 3) * 32);
-        r.b = ld_stream_u4(sb + 32 + (u & 3) * 32);
+    __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t, Raw& r) {
+        const uint8_t* sb = row + (size_t)(u >> 2) * 144;
+        r.h = *reinterpret_cast<const uint4*>(sb);
+        r.a = *reinterpret_cast<const uint4*>(sb + 16 + (u & 3) * 32);
+        r.b = *reinterpret_cast<const uint4*>(sb + 32 + (u & 3) * 32);
     }
-    // 6-bit scale and min of sub-block j from the 12 packed bytes.
     __device__ __forceinline__ static void scale_min(const uint4& h, int j, int& sc, int& m) {
-        const uint32_t s0 = h.y, s1 = h.z, s2 = h.w;  // scales bytes 0-3, 4-7, 8-11
+        const uint32_t s0 = h.y, s1 = h.z, s2 = h.w;  // scale bytes 0-3, 4-7, 8-11
         auto byte = [](uint32_t w, int k) { return (int)((w >> (8 * k)) & 0xFFu); };
         if (j < 4) {
             sc = byte(s0, j) & 63;
@@ -142,52 +248,45 @@ struct FmtQ4K {
             m = (byte(s2, j - 4) >> 4) | ((byte(s1, j - 4) >> 6) << 4);
         }
     }
-    __device__ __forceinline__ static float dot(const Raw& r, int sub, const float (&x)[32], const float* xsum,
-                                                uint32_t u) {
-        const float M = 8388608.0f;  // 2^23
+    __device__ __forceinline__ static float dot(const Raw& r, int sub, const XRec& x, uint32_t u) {
         const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        int s0 = 0, s1 = 0, s2 = 0;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            uint32_t n = sub ? ((w[j] >> 4) & 0x0F0F0F0Fu) : (w[j] & 0x0F0F0F0Fu);
-            a0 = fmaf(byte_f<0>(n, M), x[4 * j + 0], a0);
-            a1 = fmaf(byte_f<1>(n, M), x[4 * j + 1], a1);
-            a2 = fmaf(byte_f<2>(n, M), x[4 * j + 2], a2);
-            a3 = fmaf(byte_f<3>(n, M), x[4 * j + 3], a3);
+            const int n = (int)(sub ? ((w[j] >> 4) & 0x0F0F0F0Fu) : (w[j] & 0x0F0F0F0Fu));
+            s0 = __dp4a(n, (int)x.d0[j], s0);
+            s1 = __dp4a(n, (int)x.d1[j], s1);
+            s2 = __dp4a(n, (int)x.d2[j], s2);
         }
         int sc, m;
-        scale_min(r.h, 2 * (u & 3) + sub, sc, m);
+        scale_min(r.h, 2 * (int)(u & 3) + sub, sc, m);
         const float d = h2f(r.h.x & 0xFFFFu), dmin = h2f(r.h.x >> 16);
         const float d1 = d * (float)sc, m1 = dmin * (float)m;
-        return fmaf(d1, (a0 + a1) + (a2 + a3), -m1 * xsum[2 * u + sub]);
+        return fmaf(d1 * x.xs, combine(s0, s1, s2), -m1 * x.xsum);
     }
 };
 
-// Q6_K re-encoded per 64-element unit (lossless re-arrangement of the 6-bit
-// codes done by the repack kernel): q stream [rows][units][48 B] = 32 bytes
-// of nibbles (byte k: element k low, element 32+k high) + 16 bytes of 2-bit
+// Q6_K re-encoded per 64-element unit by the repack kernel: 32 bytes of
+// nibbles (byte k: element k low, element 32+k high) and 16 bytes of 2-bit
 // high parts (byte k: elements k, 16+k, 32+k, 48+k in bits 0-1, 2-3, 4-5,
-// 6-7); s stream [rows][units][4] int8 scales (one per 16 elements, element
-// e of a super-block uses scale e/16); d stream [rows][nsb] f16.
-// Value: (d*sc)*(q - 32) (src/core/tensor.cpp:97-106).
+// 6-7); 4 int8 scales per unit (element e of a super-block uses scale e/16);
+// f16 d per super-block.  Value: (d*sc)*(q - 32) (src/core/tensor.cpp:97-106).
 struct FmtQ6K {
-    static constexpr int UE = 64, SUBS = 2, GS = 4;
-    static constexpr bool XSUM = false;
+    static constexpr int UE = 64, SUBS = 2;
+    static constexpr bool F32X = false;
     struct Raw { uint4 n0, n1, hb; uint32_t sc; uint32_t d; };
-    __device__ __forceinline__ static void load(const GemvParams& p, uint32_t row, uint32_t u, Raw& r) {
-        size_t i = (size_t)row * p.units + u;
-        const uint8_t* qb = p.q + i * 48;
-        r.n0 = ld_stream_u4(qb);
-        r.n1 = ld_stream_u4(qb + 16);
-        r.hb = ld_stream_u4(qb + 32);
-        r.sc = ld_stream_u32(p.s + i * 4);
-        r.d = ld_stream_u16(p.d + ((size_t)row * (p.units >> 2) + (u >> 2)) * 2);
+    __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t units, Raw& r) {
+        const uint8_t* qb = row + (size_t)u * 48;
+        r.n0 = *reinterpret_cast<const uint4*>(qb);
+        r.n1 = *reinterpret_cast<const uint4*>(qb + 16);
+        r.hb = *reinterpret_cast<const uint4*>(qb + 32);
+        r.sc = *reinterpret_cast<const uint32_t*>(row + (size_t)units * 48 + (size_t)u * 4);
+        r.d = *reinterpret_cast<const uint16_t*>(row + (size_t)units * 52 + (size_t)(u >> 2) * 2);
     }
-    __device__ __forceinline__ static float dot(const Raw& r, int sub, const float (&x)[32], const float*, uint32_t) {
-        const float M = 8388640.0f;  // 2^23 + 32
+    __device__ __forceinline__ static float dot(const Raw& r, int sub, const XRec& x, uint32_t) {
         const uint32_t n[8] = {r.n0.x, r.n0.y, r.n0.z, r.n0.w, r.n1.x, r.n1.y, r.n1.z, r.n1.w};
         const uint32_t h[4] = {r.hb.x, r.hb.y, r.hb.z, r.hb.w};
-        float g0 = 0.f, g1 = 0.f, g2 = 0.f, g3 = 0.f;  // g0,g1: first 16 elements; g2,g3: last 16
+        int a0 = 0, a1 = 0, a2 = 0, b0 = 0, b1 = 0, b2 = 0;  // first / second 16 elements
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             uint32_t q;
@@ -196,170 +295,222 @@ struct FmtQ6K {
             else
                 q = ((n[j] >> 4) & 0x0F0F0F0Fu) | ((j < 4 ? h[j] : (h[j - 4] >> 2)) & 0x30303030u);
             if (j < 4) {
-                g0 = fmaf(byte_f<0>(q, M), x[4 * j + 0], g0);
-                g1 = fmaf(byte_f<1>(q, M), x[4 * j + 1], g1);
-                g0 = fmaf(byte_f<2>(q, M), x[4 * j + 2], g0);
-                g1 = fmaf(byte_f<3>(q, M), x[4 * j + 3], g1);
+                a0 = __dp4a((int)q, (int)x.d0[j], a0);
+                a1 = __dp4a((int)q, (int)x.d1[j], a1);
+                a2 = __dp4a((int)q, (int)x.d2[j], a2);
             } else {
-                g2 = fmaf(byte_f<0>(q, M), x[4 * j + 0], g2);
-                g3 = fmaf(byte_f<1>(q, M), x[4 * j + 1], g3);
-                g2 = fmaf(byte_f<2>(q, M), x[4 * j + 2], g2);
-                g3 = fmaf(byte_f<3>(q, M), x[4 * j + 3], g3);
+                b0 = __dp4a((int)q, (int)x.d0[j], b0);
+                b1 = __dp4a((int)q, (int)x.d1[j], b1);
+                b2 = __dp4a((int)q, (int)x.d2[j], b2);
             }
         }
-        const float d = h2f(r.d);
-        const float sa = d * (float)(int8_t)((r.sc >> (16 * sub)) & 0xFFu);
-        const float sb = d * (float)(int8_t)((r.sc >> (16 * sub + 8)) & 0xFFu);
-        return fmaf(sb, g2 + g3, sa * (g0 + g1));
+        // codes are q + 32: subtract 32 * sum X per 16-element group
+        const float va = fmaf(-32.0f, (float)x.sx_lo, combine(a0, a1, a2));
+        const float vb = fmaf(-32.0f, (float)x.sx_hi, combine(b0, b1, b2));
+        const float sa = (float)(int8_t)((r.sc >> (16 * sub)) & 0xFFu);
+        const float sbv = (float)(int8_t)((r.sc >> (16 * sub + 8)) & 0xFFu);
+        return (h2f(r.d) * x.xs) * fmaf(sbv, vb, sa * va);
     }
 };
 
-// F32 (the reference's catch-all branch, ops.cpp:289-299): q stream
-// [rows][cols] f32.
+// F32 (the reference's catch-all branch, ops.cpp:289-299): plain f32 FMAs
+// against an f32 copy of x.
 struct FmtF32 {
-    static constexpr int UE = 32, SUBS = 1, GS = 3;
-    static constexpr bool XSUM = false;
-    struct Raw { uint4 v[8]; };
-    __device__ __forceinline__ static void load(const GemvParams& p, uint32_t row, uint32_t u, Raw& r) {
-        const uint8_t* b = p.q + ((size_t)row * p.cols + (size_t)u * 32) * 4;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) r.v[i] = ld_stream_u4(b + 16 * i);
-    }
-    __device__ __forceinline__ static float dot(const Raw& r, int, const float (&x)[32], const float*, uint32_t) {
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            a0 = fmaf(__uint_as_float(r.v[i].x), x[4 * i + 0], a0);
-            a1 = fmaf(__uint_as_float(r.v[i].y), x[4 * i + 1], a1);
-            a2 = fmaf(__uint_as_float(r.v[i].z), x[4 * i + 2], a2);
-            a3 = fmaf(__uint_as_float(r.v[i].w), x[4 * i + 3], a3);
-        }
-        return (a0 + a1) + (a2 + a3);
-    }
+    static constexpr int UE = 32, SUBS = 1;
+    static constexpr bool F32X = true;
 };
 
-// Swizzled granule index of float4 granule g of the staged x vector: the low
-// 3 bits are XORed with the index of the K-unit the granule belongs to.
-template <class Fmt>
-__device__ __forceinline__ int xswz(int g) {
-    return g ^ ((g >> Fmt::GS) & 7);
+// Named barrier over the consumer warps only (the producer never joins).
+__device__ __forceinline__ void consumers_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kGemvConsumerWarps * 32) : "memory");
 }
 
-__device__ __forceinline__ float block_sum(float v, float* red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    v = warp_sum(v);
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float t = 0.f;
-    for (int i = 0; i < nw; ++i) t += red[i];
-    return t;
-}
+// ------------------------------------------------------------------ kernel --
 
-constexpr int kGemvThreads = 512;
-
-template <class Fmt, int PRO, int EPI, int R>
+template <class Fmt, int PRO, int EPI>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams p) {
-    extern __shared__ float4 smem4[];
-    float4* xs = smem4;
-    float* xsum = reinterpret_cast<float*>(smem4 + p.cols / 4);
-    __shared__ float red[32];
-    __shared__ unsigned long long best_sh[32];
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t* xreg = smem;                                   // x records (or f32 x)
+    uint8_t* stage0 = smem + p.xbytes;                      // S stages
+    const uint32_t sbytes = p.rt * p.row_stride;            // bytes per stage
+    uint64_t* full = reinterpret_cast<uint64_t*>(stage0 + (size_t)p.stages * sbytes);
+    uint64_t* empty = full + p.stages;
+    float* red = reinterpret_cast<float*>(empty + p.stages);            // [kGemvConsumerWarps]
+    unsigned long long* best_sh = reinterpret_cast<unsigned long long*>(red + kGemvConsumerWarps);
 
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
-    const int G = p.cols / 4;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t ntiles = p.rows_pad / p.rt;
+    const uint32_t W = p.nwarps, K = p.kring;
 
-    pdl_wait();
-
-    // ---- stage x (fused RMSNorm: y = x * (1/sqrt(mean(x^2) + eps)) * w)
-    const float4* x4 = reinterpret_cast<const float4*>(p.x);
-    float ss = 0.f;
-    for (int g = tid; g < G; g += blockDim.x) {
-        float4 v = x4[g];
-        if constexpr (PRO == PRO_RMS) ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-        xs[xswz<Fmt>(g)] = v;
-    }
-    if constexpr (PRO == PRO_RMS) {
-        ss = block_sum(ss, red);
-        const float inv = 1.0f / sqrtf(ss / (float)p.cols + p.eps);
-        const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
-        for (int g = tid; g < G; g += blockDim.x) {
-            float4 v = xs[xswz<Fmt>(g)];
-            const float4 w = w4[g];
-            v.x = (v.x * inv) * w.x;
-            v.y = (v.y * inv) * w.y;
-            v.z = (v.z * inv) * w.z;
-            v.w = (v.w * inv) * w.w;
-            xs[xswz<Fmt>(g)] = v;
+    if (tid == 0) {
+        for (uint32_t s = 0; s < p.stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
         }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    if constexpr (Fmt::XSUM) {
-        for (int b = tid; b < (int)(p.cols / 32); b += blockDim.x) {
-            float t = 0.f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                float4 v = xs[xswz<Fmt>(b * 8 + j)];
-                t += (v.x + v.y) + (v.z + v.w);
+    // let the next kernel of the step launch now: it only reads what this one
+    // writes after its own griddepcontrol.wait, and its producer warp can
+    // start streaming weights while this kernel drains
+    pdl_launch_dependents();
+
+    if (warp == kGemvConsumerWarps) {
+        // ---------------- producer: weights do not depend on the previous kernel
+        if (lane == 0) {
+            uint32_t i = 0;
+            for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+                // tile i goes to warp i % W as its j-th tile, stage w*K + j%K
+                const uint32_t j = i / W;
+                const uint32_t s = (i % W) * K + j % K;
+                if (j >= K && !mbar_wait(&empty[s], ((j / K) - 1) & 1)) {
+                    atomicOr(p.err, 1u);  // consumers then time out once and skip their work
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[s], sbytes);
+                bulk_g2s(stage0 + (size_t)s * sbytes, p.w + (size_t)t * sbytes, sbytes, &full[s]);
             }
-            xsum[b] = t;
         }
-        __syncthreads();
+        return;
+    }
+
+    // ---------------- consumers: stage x (after the producer of x finished)
+    const int ctid = tid;  // 0 .. 32 * kGemvConsumerWarps - 1
+    // RMSNorm is linear in x given its scalar: the records hold x * w and the
+    // epilogue multiplies each row result by 1/rms, so x is read only once.
+    // 8 consecutive lanes own the 8 float4 granules of one 32-element block;
+    // loads are issued in batches of kB granules per thread before any of them
+    // is used, and the norm weights (constant) are fetched before the wait.
+    constexpr int kB = 4;
+    constexpr uint32_t kStride = kGemvConsumerWarps * 32;
+    const float4* x4 = reinterpret_cast<const float4*>(p.x);
+    const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
+    const uint32_t ngr = p.cols / 4;  // a multiple of 8: whole blocks are in or out
+    float4 wpre[kB];
+    if constexpr (PRO == PRO_RMS) {
+#pragma unroll
+        for (int k = 0; k < kB; ++k) {
+            const uint32_t g = ctid + k * kStride;
+            wpre[k] = g < ngr ? w4[g] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+    pdl_wait();
+    float ss = 0.f;
+    for (uint32_t g0 = 0; g0 < ngr; g0 += kB * kStride) {
+        float4 xq[kB];
+#pragma unroll
+        for (int k = 0; k < kB; ++k) {
+            const uint32_t g = g0 + ctid + k * kStride;
+            xq[k] = g < ngr ? x4[g] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < kB; ++k) {
+            const uint32_t g = g0 + ctid + k * kStride;
+            const bool act = g < ngr;
+            float4 q = xq[k];
+            if constexpr (PRO == PRO_RMS) {
+                ss += q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w;
+                const float4 w = g0 == 0 ? wpre[k] : (act ? w4[g] : make_float4(0.f, 0.f, 0.f, 0.f));
+                q.x *= w.x;
+                q.y *= w.y;
+                q.z *= w.z;
+                q.w *= w.w;
+            }
+            if constexpr (Fmt::F32X) {
+                if (act) reinterpret_cast<float4*>(xreg)[g] = q;
+            } else {
+                // uniform across the warp: all lanes reach the shuffles inside
+                build_xrec_lane(q, lane, act, xreg + (size_t)(g >> 3) * kXRecBytes);
+            }
+        }
+    }
+    float inv = 1.0f;
+    if constexpr (PRO == PRO_RMS) {
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+    }
+    consumers_sync();
+    if constexpr (PRO == PRO_RMS) {
+        float t = 0.f;
+#pragma unroll
+        for (int k = 0; k < kGemvConsumerWarps; ++k) t += red[k];
+        inv = 1.0f / sqrtf(t / (float)p.cols + p.eps);
     }
 
     unsigned long long best = 0ull;
-    const uint32_t ntiles = p.rows_pad / R;
-    for (uint32_t t = blockIdx.x * nwarps + warp; t < ntiles; t += gridDim.x * nwarps) {
-        const uint32_t row0 = t * R;
-        float acc[R];
-#pragma unroll
-        for (int r = 0; r < R; ++r) acc[r] = 0.f;
-
-        // two K-units per lane per iteration: all their loads are issued
-        // before any of them is consumed
-        for (uint32_t u0 = lane; u0 < p.units; u0 += 64) {
-            const bool two = u0 + 32 < p.units;
-            typename Fmt::Raw raw[2][R];
-#pragma unroll
-            for (int r = 0; r < R; ++r) Fmt::load(p, row0 + r, u0, raw[0][r]);
-            if (two) {
-#pragma unroll
-                for (int r = 0; r < R; ++r) Fmt::load(p, row0 + r, u0 + 32, raw[1][r]);
-            }
-#pragma unroll
-            for (int k = 0; k < 2; ++k) {
-                if (k == 1 && !two) break;
-                const uint32_t u = u0 + 32 * k;
-#pragma unroll
-                for (int sub = 0; sub < Fmt::SUBS; ++sub) {
-                    float x[32];
-                    const int g0 = (int)(u * Fmt::SUBS + sub) * 8;
+    // A warp whose bounded wait gave up marks itself dead: it skips the math
+    // but still releases its stages.
+    bool dead = false;
+    const uint32_t first = (uint32_t)warp < W ? blockIdx.x + warp * gridDim.x : ntiles;  // idle warps skip
+    uint32_t j = 0;
+    for (uint32_t t = first; t < ntiles; t += W * gridDim.x, ++j) {
+        const uint32_t s = warp * K + j % K;
+        if (!dead && !mbar_wait(&full[s], (j / K) & 1)) {
+            dead = true;
+            if (lane == 0) atomicOr(p.err, 2u);
+        }
+        const uint8_t* rows4 = stage0 + (size_t)s * sbytes;
+        constexpr uint32_t sub4 = 0;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        if (!dead) {
+            if constexpr (Fmt::F32X) {
+                for (uint32_t u = lane; u < p.units; u += 32) {
+                    float xv[32];
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
-                        const float4 v = xs[xswz<Fmt>(g0 + j)];
-                        x[4 * j + 0] = v.x;
-                        x[4 * j + 1] = v.y;
-                        x[4 * j + 2] = v.z;
-                        x[4 * j + 3] = v.w;
+                        const float4 q = reinterpret_cast<const float4*>(xreg)[u * 8 + j];
+                        xv[4 * j] = q.x;
+                        xv[4 * j + 1] = q.y;
+                        xv[4 * j + 2] = q.z;
+                        xv[4 * j + 3] = q.w;
                     }
 #pragma unroll
-                    for (int r = 0; r < R; ++r) acc[r] += Fmt::dot(raw[k][r], sub, x, xsum, u);
+                    for (int r = 0; r < 4; ++r) {
+                        const float4* wr = reinterpret_cast<const float4*>(rows4 + (size_t)r * p.row_stride) + u * 8;
+                        float a = 0.f;
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const float4 q = wr[j];
+                            a = fmaf(q.x, xv[4 * j], a);
+                            a = fmaf(q.y, xv[4 * j + 1], a);
+                            a = fmaf(q.z, xv[4 * j + 2], a);
+                            a = fmaf(q.w, xv[4 * j + 3], a);
+                        }
+                        acc[r] += a;
+                    }
+                }
+            } else {
+                for (uint32_t u = lane; u < p.units; u += 32) {
+                    typename Fmt::Raw raw[4];
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) Fmt::load(rows4 + (size_t)r * p.row_stride, u, p.units, raw[r]);
+#pragma unroll
+                    for (int sb = 0; sb < Fmt::SUBS; ++sb) {
+                        XRec xr;
+                        load_xrec(xreg, u * Fmt::SUBS + sb, xr);
+#pragma unroll
+                        for (int r = 0; r < 4; ++r) acc[r] += Fmt::dot(raw[r], sb, xr, u);
+                    }
                 }
             }
         }
+        // this warp no longer reads the stage
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
 
-        const float v = warp_reduce_rows<R>(acc, lane);
-        constexpr int LPR = 32 / R;  // lanes holding each row's total
-        const int rl = lane / LPR;   // row of this lane within the tile
-        const uint32_t row = row0 + rl;
-        const bool leader = (lane % LPR) == 0;
+        // lanes 8r..8r+7 hold the total of row r (of this warp's 4)
+        float v = warp_reduce_rows<4>(acc, lane) * inv;  // 1/rms of the fused RMSNorm (1 if plain)
+        const float v_next = __shfl_down_sync(0xffffffffu, v, 8);  // partner row of a pair
+        const uint32_t rl = (uint32_t)lane >> 3;
+        const uint32_t row = t * p.rt + sub4 + rl;
+        if ((lane & 7) != 0 || dead) continue;
 
         if constexpr (EPI == EPI_STORE) {
-            if (leader && row < p.rows) p.y[row] = v;
+            if (row < p.rows) p.y[row] = v;
         } else if constexpr (EPI == EPI_RESIDUAL) {
-            if (leader && row < p.rows) p.y[row] += v;  // x += W.h (ops::axpy, qwen2_model.cpp:178,184)
+            if (row < p.rows) p.y[row] += v;  // x += W.h (ops::axpy, qwen2_model.cpp:178,184)
         } else if constexpr (EPI == EPI_LOGITS) {
-            if (leader && row < p.rows) {
+            if (row < p.rows) {
                 p.y[row] = v;
                 if (v == v) {  // a NaN never wins (greedy_sampler.cpp:11 compares with >)
                     const unsigned long long k = argmax_key(v, p.row_offset + row);
@@ -367,70 +518,64 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
                 }
             }
         } else if constexpr (EPI == EPI_SWIGLU) {
-            // physical rows 2j / 2j+1 hold gate_j / up_j: h_j = silu(gate_j) * up_j
-            // (ops::silu then ops::mul, qwen2_model.cpp:154-155)
-            const float up = __shfl_down_sync(0xffffffffu, v, LPR);
-            if (leader && (rl & 1) == 0 && row + 1 < p.rows) {
+            // storage rows 2j / 2j+1 hold gate_j / up_j (ops::silu then ops::mul,
+            // qwen2_model.cpp:154-155)
+            if ((rl & 1) == 0 && row + 1 < p.rows) {
                 const float g = v / (1.0f + expf(-v));
-                p.y[row >> 1] = g * up;
+                p.y[row >> 1] = g * v_next;
             }
         } else if constexpr (EPI == EPI_QKV) {
-            const float v1 = __shfl_down_sync(0xffffffffu, v, LPR);
             const uint32_t hd = p.head_dim, half = hd >> 1;
             const uint32_t pos = *p.pos;
-            if (leader && row < p.rows) {
-                if (row < p.q_rows + p.k_rows) {
-                    if ((rl & 1) == 0) {
-                        // a rotary pair (i, i + hd/2) of one head
-                        const bool isq = row < p.q_rows;
-                        const uint32_t pr = (isq ? row : row - p.q_rows) >> 1;  // pair index
-                        const uint32_t head = pr / half, i = pr % half;
-                        const uint32_t la = head * hd + i, lb = la + half;      // logical index in q or k
-                        float x0 = v, x1 = v1;
-                        if (p.bias) {
-                            const uint32_t bo = isq ? 0u : p.q_rows;
-                            x0 += p.bias[bo + la];
-                            x1 += p.bias[bo + lb];
-                        }
-                        // ops::rope (ops.cpp:84-89) with the reference build's fused rounding
-                        const float2 cs = p.rope[(size_t)pos * half + i];
-                        const float o0 = fmaf(x0, cs.x, -__fmul_rn(x1, cs.y));
-                        const float o1 = fmaf(x0, cs.y, __fmul_rn(x1, cs.x));
-                        if (isq) {
-                            p.qout[la] = o0;
-                            p.qout[lb] = o1;
-                        } else {
-                            float* kr = p.kcache + ((size_t)head * p.max_ctx + pos) * hd;
-                            kr[i] = o0;
-                            kr[i + half] = o1;
-                        }
+            if (row < p.q_rows + p.k_rows) {
+                if ((rl & 1) == 0 && row + 1 < p.rows) {
+                    const bool isq = row < p.q_rows;
+                    const uint32_t pr = (isq ? row : row - p.q_rows) >> 1;  // rotary pair index
+                    const uint32_t head = pr / half, ii = pr % half;
+                    const uint32_t la = head * hd + ii, lb = la + half;
+                    float x0 = v, x1 = v_next;
+                    if (p.bias) {
+                        const uint32_t bo = isq ? 0u : p.q_rows;
+                        x0 += p.bias[bo + la];
+                        x1 += p.bias[bo + lb];
                     }
-                } else {
-                    const uint32_t lv = row - p.q_rows - p.k_rows;
-                    float val = v;
-                    if (p.bias) val += p.bias[p.q_rows + p.k_rows + lv];
-                    const uint32_t head = lv / hd, dd = lv % hd;
-                    p.vcache[((size_t)head * p.max_ctx + pos) * hd + dd] = val;
+                    // ops::rope (ops.cpp:84-89) with the reference build's fused rounding
+                    const float2 cs = p.rope[(size_t)pos * half + ii];
+                    const float o0 = fmaf(x0, cs.x, -__fmul_rn(x1, cs.y));
+                    const float o1 = fmaf(x0, cs.y, __fmul_rn(x1, cs.x));
+                    if (isq) {
+                        p.qout[la] = o0;
+                        p.qout[lb] = o1;
+                    } else {
+                        float* kr = p.kcache + ((size_t)head * p.max_ctx + pos) * hd;
+                        kr[ii] = o0;
+                        kr[ii + half] = o1;
+                    }
                 }
+            } else if (row < p.rows) {
+                const uint32_t lv = row - p.q_rows - p.k_rows;
+                float vv = v;
+                if (p.bias) vv += p.bias[p.q_rows + p.k_rows + lv];
+                const uint32_t head = lv / hd, dd = lv % hd;
+                p.vcache[((size_t)head * p.max_ctx + pos) * hd + dd] = vv;
             }
         }
     }
 
     if constexpr (EPI == EPI_LOGITS) {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
+        for (int o = 8; o < 32; o <<= 1) {
             const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
             best = other > best ? other : best;
         }
         if (lane == 0) best_sh[warp] = best;
-        __syncthreads();
-        if (tid == 0) {
+        consumers_sync();
+        if (ctid == 0) {
             unsigned long long b = 0ull;
-            for (int i = 0; i < nwarps; ++i) b = best_sh[i] > b ? best_sh[i] : b;
+            for (int k = 0; k < kGemvConsumerWarps; ++k) b = best_sh[k] > b ? best_sh[k] : b;
             if (b) atomicMax(p.argmax, b);
         }
     }
-    pdl_launch_dependents();
 }
 
 }  // namespace smallm

@@ -334,7 +334,7 @@ void Model::load(const std::string& path, const smallm_model_opts& o) {
 
 // One decode step: everything after the (token, pos) state is in place.
 void Model::enqueue_step(cudaStream_t s) {
-    const bool pdl = false;
+    const bool pdl = true;  // programmatic dependent launch between the step's kernels
     launch_embed(embd_m, st, x, s, pdl);
     const uint32_t qrows = nh_l * hd, krows = nkv_l * hd;
     for (uint32_t i = 0; i < n_layers; ++i) {
@@ -376,6 +376,7 @@ void Model::enqueue_step(cudaStream_t s) {
         at.hd = hd;
         at.max_ctx = max_ctx;
         at.n_split = n_split;
+        at.err = device_error_flag();
         launch_attention(at, s, pdl);
 
         GemvArgs ao;
