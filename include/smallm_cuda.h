@@ -200,6 +200,17 @@ int smallm_model_decode_ids(smallm_model* m, uint32_t* ids, uint32_t n);
  * until the next step is enqueued. */
 const float* smallm_model_logits_device(smallm_model* m);
 
+/* Tracing (the reference only times the decode loop with steady_clock,
+ * src/runtime/generator.cpp:57-68): run one step like smallm_model_forward
+ * (no logits copy) through a copy of the step graph whose kernels stamp the
+ * GPU global timer.  Writes up to `cap` records of 4 uint64 each to `out`:
+ * start of the kernel's first CTA, first CTA past its wait on the previous
+ * kernel, end of its last CTA (ns, relative to the first record's start),
+ * and a kind code (1 embed, 2 QKV, 3 V, 4 attention, 5 O, 6 gate/up,
+ * 7 down, 8 lm_head, 9 finalize).  *n receives the number of kernels. */
+int smallm_model_trace_step(smallm_model* m, uint32_t token, uint32_t pos, uint64_t* out, uint32_t cap,
+                            uint32_t* n);
+
 /* ------------------------------------------------------------------ */
 /* Helpers (no counterpart in the reference, which is single-process)   */
 /* ------------------------------------------------------------------ */

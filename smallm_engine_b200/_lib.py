@@ -78,6 +78,7 @@ SIGNATURES = {
     "smallm_model_decode_greedy_async": (_I, [_P, _U32, _U32, _U32]),
     "smallm_model_decode_ids": (_I, [_P, _P, _U32]),
     "smallm_model_logits_device": (_P, [_P]),
+    "smallm_model_trace_step": (_I, [_P, _U32, _U32, _P, _U32, ctypes.POINTER(_U32)]),
     "smallm_nccl_unique_id": (_I, [_P]),
     "smallm_host_alloc": (_I, [ctypes.c_size_t, ctypes.POINTER(_P)]),
     "smallm_host_free": (_I, [_P]),

@@ -423,4 +423,22 @@ int smallm_model_decode_ids(smallm_model* m, uint32_t* ids, uint32_t n) {
 
 const float* smallm_model_logits_device(smallm_model* m) { return m ? m->m.logits_local : nullptr; }
 
+int smallm_model_trace_step(smallm_model* m, uint32_t token, uint32_t pos, uint64_t* out, uint32_t cap,
+                            uint32_t* n) {
+    return guard([&] {
+        need(m && n && (out || !cap), "NULL argument");
+        set_dev(m->m.device);
+        std::vector<smallm::TraceSlot> t;
+        m->m.trace_step(token, pos, t);
+        *n = (uint32_t)t.size();
+        const uint64_t t0 = t.empty() ? 0 : t[0].t_start;
+        for (uint32_t i = 0; i < t.size() && i < cap; ++i) {
+            out[4 * i] = t[i].t_start - t0;
+            out[4 * i + 1] = t[i].t_ready - t0;
+            out[4 * i + 2] = t[i].t_end - t0;
+            out[4 * i + 3] = t[i].kind;
+        }
+    });
+}
+
 }  // extern "C"

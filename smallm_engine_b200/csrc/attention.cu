@@ -63,8 +63,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
     __shared__ __align__(8) uint64_t bar;
     __shared__ unsigned int is_last;
 
+    if (tid == 0) trace_mark(a.trace, 0);
     pdl_launch_dependents();
     pdl_wait();
+    if (tid == 0) trace_mark(a.trace, 1);
     const uint32_t n = *a.pos + 1;
     const uint32_t chunk = attn_chunk(n, a.n_split);
     const uint32_t t0 = split * chunk;
@@ -162,31 +164,54 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
     __syncthreads();
     if (tid == 0) is_last = (atomicAdd(&a.counter[g], 1u) == a.n_split - 1) ? 1u : 0u;
     __syncthreads();
-    if (!is_last) return;
+    if (!is_last) {
+        if (tid == 0) trace_mark(a.trace, 2);
+        return;
+    }
     __threadfence();
     const float* base = a.partial + (size_t)g * a.n_split * G * (HD + 2);
     const uint32_t nact = min(a.n_split, (n + chunk - 1) / chunk);
+    // (max, sum) of every active chunk and head in one parallel load; the
+    // per-chunk weights exp(m_s - M) / L then come from shared memory, and
+    // the partial outputs are summed with loads independent of the sum.
+    float* wts = sm;  // [nact][G] weights (the K/V staging is no longer needed)
+    for (uint32_t i = tid; i < nact * G; i += kAttnThreads) {
+        const float* r = base + (size_t)i * (HD + 2);
+        wts[i] = __ldcg(r + HD);
+        wts[nact * G + i] = __ldcg(r + HD + 1);
+    }
+    __syncthreads();
+    if (tid < (int)G) {
+        float M = -INFINITY;
+        for (uint32_t s = 0; s < nact; ++s) M = fmaxf(M, wts[s * G + tid]);
+        float L = 0.f;
+        for (uint32_t s = 0; s < nact; ++s) {
+            const float w = expf(wts[s * G + tid] - M);
+            wts[s * G + tid] = w;
+            L = fmaf(w, wts[nact * G + s * G + tid], L);
+        }
+        for (uint32_t s = 0; s < nact; ++s) wts[s * G + tid] /= L;
+    }
+    __syncthreads();
     for (uint32_t o = tid; o < G * HD; o += kAttnThreads) {
         const uint32_t h = o / HD, dd = o % HD;
-        float M = -INFINITY;
-        for (uint32_t s = 0; s < nact; ++s) M = fmaxf(M, __ldcg(base + (s * G + h) * (HD + 2) + HD));
-        float L = 0.f, O = 0.f;
-        for (uint32_t s = 0; s < nact; ++s) {
-            const float* r = base + (s * G + h) * (HD + 2);
-            const float w = expf(__ldcg(r + HD) - M);
-            L = fmaf(w, __ldcg(r + HD + 1), L);
-            O = fmaf(w, __ldcg(r + dd), O);
-        }
-        a.out[((size_t)g * G + h) * HD + dd] = O / L;
+        float O = 0.f;
+#pragma unroll 8
+        for (uint32_t s = 0; s < nact; ++s) O = fmaf(wts[s * G + h], __ldcg(base + (s * G + h) * (HD + 2) + dd), O);
+        a.out[((size_t)g * G + h) * HD + dd] = O;
     }
     if (tid == 0) a.counter[g] = 0u;
+    __syncthreads();
+    if (tid == 0) trace_mark(a.trace, 2);
 }
 
 size_t attention_smem(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t max_ctx, uint32_t n_split) {
     const uint32_t G = n_heads / n_kv;
     const uint32_t chmax = attn_chunk_max(max_ctx, n_split);
-    return sizeof(float) * (2 * (size_t)chmax * hd + (size_t)G * hd + (size_t)G * chmax + 2 * kAttnMaxGroup +
-                            (size_t)(kAttnThreads - hd) * kAttnMaxGroup);
+    const size_t main = 2 * (size_t)chmax * hd + (size_t)G * hd + (size_t)G * chmax + 2 * kAttnMaxGroup +
+                        (size_t)(kAttnThreads - hd) * kAttnMaxGroup;
+    const size_t combine = 2 * (size_t)n_split * G;  // the merging CTA's (max, sum) staging
+    return sizeof(float) * (main > combine ? main : combine);
 }
 
 void launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {

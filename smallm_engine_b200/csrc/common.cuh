@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "trace.h"
+
 #define SM_T_F32 0u
 #define SM_T_Q4_0 2u
 #define SM_T_Q8_0 8u
@@ -163,6 +165,21 @@ __host__ __device__ __forceinline__ uint32_t argmax_key_index(unsigned long long
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ------------------------------------------------------- kernel tracing --
+// Kernels of the production graph get a null slot and skip all of it.
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void trace_mark(TraceSlot* s, int which) {
+    if (!s) return;
+    const unsigned long long t = global_ns();
+    if (which == 0) atomicMin(&s->t_start, t);
+    else if (which == 1) atomicMin(&s->t_ready, t);
+    else atomicMax(&s->t_end, t);
 }
 
 // ------------------------------------------- mbarriers and bulk copies --

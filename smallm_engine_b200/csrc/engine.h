@@ -8,6 +8,8 @@
 #include <string>
 #include <vector>
 
+#include "trace.h"
+
 namespace smallm {
 
 // Error carrying one of the SMALLM_ERR_* codes of include/smallm_cuda.h.
@@ -87,6 +89,7 @@ struct GemvArgs {
     const uint32_t* pos = nullptr;
     unsigned long long* argmax = nullptr;
     uint32_t row_offset = 0;  // LOGITS: global index of storage row 0 (vocab-parallel shards)
+    TraceSlot* trace = nullptr;  // traced steps only
 };
 
 void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_t stream, bool pdl = false);
@@ -94,7 +97,7 @@ void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_
 // Pipeline shape the GEMV uses for a matrix: rows per tile, stages of the
 // shared-memory ring, bytes of staged x, total dynamic shared memory.
 struct GemvPlan {
-    uint32_t rt = 0, stages = 0, nwarps = 0, kring = 0;
+    uint32_t rt = 0, stages = 0, ngroups = 0, gsize = 0, kring = 0;
     size_t xbytes = 0, smem = 0;
 };
 GemvPlan gemv_plan(const QMat& m);
@@ -118,9 +121,11 @@ struct DecodeState {
 
 // x[embd] = dequantized row state->token of the embedding matrix; resets the
 // argmax slot.
-void launch_embed(const QMat& emb, DecodeState* st, float* x, cudaStream_t stream, bool pdl = false);
+void launch_embed(const QMat& emb, DecodeState* st, float* x, cudaStream_t stream, bool pdl = false,
+                  TraceSlot* trace = nullptr);
 // state->token = argmax, ids[state->step++] = token, state->pos += 1.
-void launch_finalize(DecodeState* st, uint32_t* ids, uint32_t ids_cap, cudaStream_t stream, bool pdl = false);
+void launch_finalize(DecodeState* st, uint32_t* ids, uint32_t ids_cap, cudaStream_t stream, bool pdl = false,
+                     TraceSlot* trace = nullptr);
 // Same, taking the maximum of the `n` gathered per-rank argmax keys.
 void launch_finalize_tp(DecodeState* st, const unsigned long long* keys, int n, uint32_t* ids,
                         uint32_t ids_cap, cudaStream_t stream, bool pdl = false);
@@ -137,6 +142,7 @@ struct AttnArgs {
     const uint32_t* pos;   // attend over positions 0..*pos
     uint32_t n_heads, n_kv, hd, max_ctx, n_split;
     unsigned int* err = nullptr;  // raised if a bounded wait gives up
+    TraceSlot* trace = nullptr;   // traced steps only
 };
 uint32_t attention_splits(uint32_t n_kv, uint32_t max_ctx, int sm_count);
 size_t attention_partial_floats(uint32_t n_heads, uint32_t hd, uint32_t n_split);

@@ -7,27 +7,31 @@
 // producer warp streams tiles into an S-stage shared-memory ring with
 // cp.async.bulk (completion through mbarrier transaction counts).
 //
-// Compute side -- row-owner warps.  A tile is 4 rows and belongs to one
-// consumer warp for the whole K: its lanes stride the K-units, then one warp
-// butterfly yields the 4 row sums and the same warp runs the epilogue.  Each
-// of the W working warps has a private ring of k stages: warp w takes tiles
-// w, w+W, w+2W, ... and its j-th tile lands in stage w*k + j%k, so every
-// mbarrier wait is on the next phase of a stage only that warp consumes
-// (parity waits are only unambiguous that way) and the warp alone releases
-// it.  No CTA-wide barrier sits inside the tile loop.  Every wait is bounded:
-// on timeout the kernel raises an error flag and skips the remaining math.
+// Compute side -- warp groups with private rings.  A tile is 4 rows.  The 16
+// consumer warps form NG groups of G warps; group g owns a ring of k stages
+// and takes tiles g, g+NG, g+2NG, ..., its j-th tile landing in stage
+// g*k + j%k, so every mbarrier wait is on the next phase of a stage only
+// that group uses (parity waits are only unambiguous that way).  Producer
+// lane g serves ring g, so a slow group never stalls another's loads.  The G
+// warps of a group split the tile's K-units; each reduces its 4 partial row
+// sums with one butterfly, and with G > 1 the partials meet in shared memory
+// behind a per-stage "done" mbarrier, after which the group leader runs the
+// epilogue and releases the stage.  No CTA-wide barrier sits inside the tile
+// loop.  Every wait is bounded: on timeout the kernel raises an error flag
+// and skips the remaining math.
 //
 // Math side -- integer dot products.  In the prologue each CTA turns x (f32;
 // times the RMSNorm weight when the norm is fused, ops::rmsnorm,
 // src/core/ops.cpp:29-40) into block fixed point: per 32-element block,
-// X_i = rint(x_i * 2^(22-e)) with 2^e > max|x_i|, split into three balanced
+// X_i = rint(x_i * 2^(21-e)) with 2^e > max|x_i|, split into three balanced
 // signed bytes X = D2*2^16 + D1*2^8 + D0.  A block's integer weight codes q
-// meet x through IDP4A: sum_i q_i X_i = 2^16 S2 + 2^8 S1 + S0 with
-// S_d = sum_i q_i D_d,i, exact in 32-bit integers, and one float scale per
-// block (weight scale * 2^(e-22)).  The representation error of x is below
-// 2^-22 of the block maximum, the same order as the f32 rounding of the
-// reference's FMA chain.  The norm's 1/rms is a scalar and is applied to the
-// row results in the epilogue.
+// meet x through IDP4A: S_d = sum_i q_i D_d,i per digit, and for the 4-bit
+// formats sum_i q_i X_i = (S2*2^8 + S1)*2^8 + S0 is exact in int32 (|q| <= 15
+// and |X| <= 2^21 over 32 elements stay below 2^31), so the block needs one
+// int->float conversion and one float scale (weight scale * 2^(e-21)).  The
+// representation error of x is below 2^-21 of the block maximum, the order
+// of the f32 rounding of the reference's FMA chain.  The norm's 1/rms is a
+// scalar and is applied to the row results in the epilogue.
 //
 // Epilogues (fused): plain store, residual add, Q/K/V bias + RoPE + KV-cache
 // append, SwiGLU, logits + greedy argmax.
@@ -53,10 +57,11 @@ struct GemvParams {
     uint32_t rows_pad;  // storage rows (multiple of kMaxRT)
     uint32_t cols;
     uint32_t units;     // cols / Fmt::UE
-    uint32_t rt;        // rows per tile (4: one consumer warp per tile)
-    uint32_t stages;    // pipeline depth = nwarps * kring
-    uint32_t nwarps;    // consumer warps that take tiles (<= kGemvConsumerWarps)
-    uint32_t kring;     // stages in each warp's private ring
+    uint32_t rt;        // rows per tile (4)
+    uint32_t stages;    // pipeline depth = ngroups * kring
+    uint32_t ngroups;   // warp groups; each owns a private ring of kring stages
+    uint32_t gsize;     // warps per group; they split each tile's K-units
+    uint32_t kring;     // stages per ring
     uint32_t xbytes;    // bytes of the staged x region
     // input vector and fused RMSNorm
     const float* x;
@@ -77,6 +82,7 @@ struct GemvParams {
     unsigned long long* argmax;
     uint32_t row_offset;  // LOGITS: global vocabulary index of storage row 0
     unsigned int* err;    // set non-zero when a bounded wait gives up
+    TraceSlot* trace;     // null outside traced steps
 };
 
 // ------------------------------------------------------- x in fixed point --
@@ -85,9 +91,10 @@ struct GemvParams {
 struct XRec {
     uint32_t d0[8], d1[8], d2[8];  // balanced signed digits, 4 elements per word
     int32_t sx_lo, sx_hi;          // sum of X over elements 0-15 / 16-31
-    float xs;                      // 2^(e-22): x_i ~= X_i * xs
+    float xs;                      // 2^(e-21): x_i ~= X_i * xs
     float xsum;                    // sum of the f32 x_i
 };
+constexpr int kXBits = 21;         // |X| <= 2^21
 static_assert(sizeof(XRec) == kXRecBytes, "XRec layout");
 
 // Exact int -> float for |v| < 2^22 (IADD + FADD, no conversion unit).
@@ -112,13 +119,13 @@ __device__ __forceinline__ void build_xrec_lane(float4 q, int lane, bool act, ui
     if (!finite || m < 1e-30f) m = 0.f;      // tiny blocks contribute below f32 resolution
     int e = 0;
     frexpf(m, &e);  // m = f * 2^e, f in [0.5, 1): 2^e > m
-    const float up = m > 0.f ? ldexpf(1.0f, 22 - e) : 0.f;
+    const float up = m > 0.f ? ldexpf(1.0f, kXBits - e) : 0.f;
     const float v[4] = {q.x, q.y, q.z, q.w};
     uint32_t p0 = 0, p1 = 0, p2 = 0;
     int sx = 0;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        const int X = __float2int_rn(v[k] * up);  // exact scaling by a power of two, |X| <= 2^22
+        const int X = __float2int_rn(v[k] * up);  // exact scaling by a power of two, |X| <= 2^21
         sx += X;
         const int a0 = (int)(int8_t)(X & 0xFF);
         const int X1 = (X - a0) >> 8;
@@ -140,7 +147,7 @@ __device__ __forceinline__ void build_xrec_lane(float4 q, int lane, bool act, ui
             const float nan = __int_as_float(0x7FC00000);  // propagate like the reference's f32 math
             w[24] = (uint32_t)sx;
             w[25] = (uint32_t)sx_other;
-            reinterpret_cast<float*>(w)[26] = !finite ? nan : (m > 0.f ? ldexpf(1.0f, e - 22) : 0.f);
+            reinterpret_cast<float*>(w)[26] = !finite ? nan : (m > 0.f ? ldexpf(1.0f, e - kXBits) : 0.f);
             reinterpret_cast<float*>(w)[27] = !finite ? nan : s;
         }
     }
@@ -152,10 +159,14 @@ __device__ __forceinline__ void load_xrec(const uint8_t* base, uint32_t blk, XRe
     for (int i = 0; i < 7; ++i) reinterpret_cast<uint4*>(&r)[i] = p[i];
 }
 
-// sum_i q_i x_i of one block = xs * (2^16 S2 + 2^8 S1 + S0); the S are exact
-// and below 2^22 in magnitude for every format here.
+// sum_i q_i x_i of one block = xs * (2^16 S2 + 2^8 S1 + S0).  combine() works
+// in float (each S exact and below 2^22 for every format); horner() in int32,
+// for codes small enough that the full sum cannot overflow (4-bit formats).
 __device__ __forceinline__ float combine(int s0, int s1, int s2) {
     return fmaf(i2f_small(s2), 65536.0f, fmaf(i2f_small(s1), 256.0f, i2f_small(s0)));
+}
+__device__ __forceinline__ int horner(int s0, int s1, int s2) {
+    return (s2 * 256 + s1) * 256 + s0;
 }
 
 // ---------------------------------------------------------------- formats --
@@ -189,9 +200,9 @@ struct FmtQ4_0 {
             s1 = __dp4a(hi, (int)x.d1[4 + j], s1);
             s2 = __dp4a(hi, (int)x.d2[4 + j], s2);
         }
-        // sum (q - 8) X = 2^16 S2 + 2^8 S1 + S0 - 8 sum X
-        const float v = fmaf(-8.0f, (float)(x.sx_lo + x.sx_hi), combine(s0, s1, s2));
-        return v * (h2f(r.s) * x.xs);
+        // sum (q - 8) X = (S2*2^8 + S1)*2^8 + S0 - 8 sum X, exact in int32
+        const int v = horner(s0, s1, s2) - 8 * (x.sx_lo + x.sx_hi);
+        return (float)v * (h2f(r.s) * x.xs);
     }
 };
 
@@ -262,7 +273,7 @@ struct FmtQ4K {
         scale_min(r.h, 2 * (int)(u & 3) + sub, sc, m);
         const float d = h2f(r.h.x & 0xFFFFu), dmin = h2f(r.h.x >> 16);
         const float d1 = d * (float)sc, m1 = dmin * (float)m;
-        return fmaf(d1 * x.xs, combine(s0, s1, s2), -m1 * x.xsum);
+        return fmaf(d1 * x.xs, (float)horner(s0, s1, s2), -m1 * x.xsum);
     }
 };
 
@@ -335,17 +346,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     const uint32_t sbytes = p.rt * p.row_stride;            // bytes per stage
     uint64_t* full = reinterpret_cast<uint64_t*>(stage0 + (size_t)p.stages * sbytes);
     uint64_t* empty = full + p.stages;
-    float* red = reinterpret_cast<float*>(empty + p.stages);            // [kGemvConsumerWarps]
+    uint64_t* done = empty + p.stages;
+    float* red = reinterpret_cast<float*>(done + p.stages);             // [kGemvConsumerWarps]
     unsigned long long* best_sh = reinterpret_cast<unsigned long long*>(red + kGemvConsumerWarps);
+    float* part = reinterpret_cast<float*>(best_sh + kGemvConsumerWarps);  // [stages][gsize][4]
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t ntiles = p.rows_pad / p.rt;
-    const uint32_t W = p.nwarps, K = p.kring;
+    const uint32_t NG = p.ngroups, G = p.gsize, K = p.kring;
 
+    if (tid == 0) trace_mark(p.trace, 0);
     if (tid == 0) {
         for (uint32_t s = 0; s < p.stages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
+            mbar_init(&done[s], G);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -357,12 +372,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
 
     if (warp == kGemvConsumerWarps) {
         // ---------------- producer: weights do not depend on the previous kernel
-        if (lane == 0) {
-            uint32_t i = 0;
-            for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
-                // tile i goes to warp i % W as its j-th tile, stage w*K + j%K
-                const uint32_t j = i / W;
-                const uint32_t s = (i % W) * K + j % K;
+        // lane g feeds ring g: the group's j-th tile (CTA tile g + j*NG) goes
+        // to stage g*K + j%K once the group has released that stage
+        if ((uint32_t)lane < NG) {
+            const uint32_t g = lane;
+            uint32_t j = 0;
+            for (uint32_t t = blockIdx.x + g * gridDim.x; t < ntiles; t += NG * gridDim.x, ++j) {
+                const uint32_t s = g * K + j % K;
                 if (j >= K && !mbar_wait(&empty[s], ((j / K) - 1) & 1)) {
                     atomicOr(p.err, 1u);  // consumers then time out once and skip their work
                     break;
@@ -395,6 +411,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         }
     }
     pdl_wait();
+    if (ctid == 0) trace_mark(p.trace, 1);
     float ss = 0.f;
     for (uint32_t g0 = 0; g0 < ngr; g0 += kB * kStride) {
         float4 xq[kB];
@@ -441,11 +458,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     // A warp whose bounded wait gave up marks itself dead: it skips the math
     // but still releases its stages.
     bool dead = false;
-    const uint32_t first = (uint32_t)warp < W ? blockIdx.x + warp * gridDim.x : ntiles;  // idle warps skip
+    const uint32_t grp = (uint32_t)warp / G, gpart = (uint32_t)warp % G;
+    const bool working = grp < NG;  // warps beyond NG * G idle
+    const uint32_t ua = (uint32_t)(((uint64_t)p.units * gpart) / G);       // this warp's K-units
+    const uint32_t ub = (uint32_t)(((uint64_t)p.units * (gpart + 1)) / G);
+    const uint32_t first = working ? blockIdx.x + grp * gridDim.x : ntiles;
     uint32_t j = 0;
-    for (uint32_t t = first; t < ntiles; t += W * gridDim.x, ++j) {
-        const uint32_t s = warp * K + j % K;
-        if (!dead && !mbar_wait(&full[s], (j / K) & 1)) {
+    for (uint32_t t = first; t < ntiles; t += NG * gridDim.x, ++j) {
+        const uint32_t s = grp * K + j % K;
+        const uint32_t ph = (j / K) & 1;
+        if (!dead && !mbar_wait(&full[s], ph)) {
             dead = true;
             if (lane == 0) atomicOr(p.err, 2u);
         }
@@ -454,7 +476,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         if (!dead) {
             if constexpr (Fmt::F32X) {
-                for (uint32_t u = lane; u < p.units; u += 32) {
+                for (uint32_t u = ua + lane; u < ub; u += 32) {
                     float xv[32];
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
@@ -480,7 +502,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
                     }
                 }
             } else {
-                for (uint32_t u = lane; u < p.units; u += 32) {
+                for (uint32_t u = ua + lane; u < ub; u += 32) {
                     typename Fmt::Raw raw[4];
 #pragma unroll
                     for (int r = 0; r < 4; ++r) Fmt::load(rows4 + (size_t)r * p.row_stride, u, p.units, raw[r]);
@@ -494,12 +516,27 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
                 }
             }
         }
-        // this warp no longer reads the stage
+        // lanes 8r..8r+7 hold this warp's partial of row r (of the tile's 4)
+        float v = warp_reduce_rows<4>(acc, lane);
+        if (G > 1) {
+            // partials of the group's warps meet in shared memory; the leader
+            // (gpart 0) waits for all of them, sums and runs the epilogue
+            float* ps = part + (size_t)s * G * 4;
+            if ((lane & 7) == 0) ps[gpart * 4 + (lane >> 3)] = v;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&done[s]);  // also: this warp no longer reads the stage
+            if (gpart != 0) continue;
+            if (!dead && !mbar_wait(&done[s], ph)) {
+                dead = true;
+                if (lane == 0) atomicOr(p.err, 4u);
+            }
+            v = 0.f;
+            for (uint32_t k = 0; k < G; ++k) v += ps[k * 4 + (lane >> 3)];
+        }
+        // every reader of the stage is done: release it to the producer
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
-
-        // lanes 8r..8r+7 hold the total of row r (of this warp's 4)
-        float v = warp_reduce_rows<4>(acc, lane) * inv;  // 1/rms of the fused RMSNorm (1 if plain)
+        v *= inv;  // 1/rms of the fused RMSNorm (1 if plain)
         const float v_next = __shfl_down_sync(0xffffffffu, v, 8);  // partner row of a pair
         const uint32_t rl = (uint32_t)lane >> 3;
         const uint32_t row = t * p.rt + sub4 + rl;
@@ -575,6 +612,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
             for (int k = 0; k < kGemvConsumerWarps; ++k) b = best_sh[k] > b ? best_sh[k] : b;
             if (b) atomicMax(p.argmax, b);
         }
+    }
+    if (p.trace) {
+        consumers_sync();
+        if (ctid == 0) trace_mark(p.trace, 2);
     }
 }
 

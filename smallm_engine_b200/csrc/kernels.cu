@@ -398,36 +398,41 @@ void launch_kernel_ex(const void* fn, dim3 grid, dim3 block, size_t smem, cudaSt
 // ------------------------------------------------------------- embedding --
 
 // One thread per 32-element group of the token's row.
-__global__ void embed_kernel(const QMat m, DecodeState* st, float* x) {
+__global__ void embed_kernel(const QMat m, DecodeState* st, float* x, TraceSlot* trace) {
+    if (threadIdx.x == 0) trace_mark(trace, 0);
     pdl_launch_dependents();
     pdl_wait();
+    if (threadIdx.x == 0) trace_mark(trace, 1);
     uint32_t tok = st->token;
     if (tok >= m.rows) tok = 0;  // the host validates ids; never read outside the table
     const uint32_t g = blockIdx.x * blockDim.x + threadIdx.x;
     if (g < m.cols / 32) dequant_group(m, tok, g, x + (size_t)g * 32);
     if (g == 0) st->argmax = 0ull;
+    if (threadIdx.x == 0) trace_mark(trace, 2);
 }
 
-void launch_embed(const QMat& emb, DecodeState* st, float* x, cudaStream_t stream, bool pdl) {
+void launch_embed(const QMat& emb, DecodeState* st, float* x, cudaStream_t stream, bool pdl, TraceSlot* trace) {
     QMat m = emb;
-    void* args[] = {&m, &st, &x};
+    void* args[] = {&m, &st, &x, &trace};
     const uint32_t groups = m.cols / 32;
     launch_kernel_ex((const void*)embed_kernel, dim3((groups + 31) / 32), dim3(32), 0, stream, pdl, args);
 }
 
-__global__ void finalize_kernel(DecodeState* st, uint32_t* ids, uint32_t cap) {
+__global__ void finalize_kernel(DecodeState* st, uint32_t* ids, uint32_t cap, TraceSlot* trace) {
+    trace_mark(trace, 0);
     pdl_launch_dependents();
     pdl_wait();
+    trace_mark(trace, 1);
     const uint32_t tok = argmax_key_index(st->argmax);
     st->token = tok;
     if (ids && st->step < cap) ids[st->step] = tok;
     st->step += 1;
     st->pos += 1;
-    pdl_launch_dependents();
+    trace_mark(trace, 2);
 }
 
-void launch_finalize(DecodeState* st, uint32_t* ids, uint32_t cap, cudaStream_t stream, bool pdl) {
-    void* args[] = {&st, &ids, &cap};
+void launch_finalize(DecodeState* st, uint32_t* ids, uint32_t cap, cudaStream_t stream, bool pdl, TraceSlot* trace) {
+    void* args[] = {&st, &ids, &cap, &trace};
     launch_kernel_ex((const void*)finalize_kernel, dim3(1), dim3(1), 0, stream, pdl, args);
 }
 
@@ -582,20 +587,29 @@ constexpr uint32_t kMaxStages = 32;
 GemvPlan gemv_plan(const QMat& m) {
     GemvPlan pl;
     pl.xbytes = m.type == SM_T_F32 ? (size_t)m.cols * 4 : (size_t)(m.cols / 32) * kXRecBytes;
-    const size_t misc = kGemvConsumerWarps * 4 + kGemvConsumerWarps * 8 + 16 * kMaxStages + 128;
+    // per stage: the tile, three mbarriers, the group's partial sums
+    const size_t misc = kGemvConsumerWarps * 4 + kGemvConsumerWarps * 8 + 128;
     const uint32_t rt = 4;
     const size_t sb = (size_t)rt * m.row_stride;
-    if (pl.xbytes + misc + sb > kSmemLimit)
+    const size_t per_stage = sb + 24 + kGemvConsumerWarps * 4 * 4;
+    if (pl.xbytes + misc + per_stage > kSmemLimit)
         throw Error(1, "gemv: rows of " + std::to_string(m.cols) + " columns do not fit the shared-memory pipeline");
-    uint32_t st = (uint32_t)((kSmemLimit - pl.xbytes - misc) / sb);
-    if (st > kMaxStages) st = kMaxStages;
-    // W working warps with private rings of k stages each
-    pl.nwarps = st < (uint32_t)kGemvConsumerWarps ? st : (uint32_t)kGemvConsumerWarps;
-    pl.kring = st / pl.nwarps;
-    st = pl.nwarps * pl.kring;
+    uint32_t smax = (uint32_t)((kSmemLimit - pl.xbytes - misc) / per_stage);
+    if (smax > kMaxStages) smax = kMaxStages;
+    // NG groups of G warps, each group with a private ring of k >= 2 stages
+    // where shared memory allows; the G warps of a group split K, with at
+    // least one 32-unit sweep per warp.
+    uint32_t ng = 1;
+    while (ng * 2 <= (uint32_t)kGemvConsumerWarps && ng * 2 * 2 <= smax) ng *= 2;
+    uint32_t g = kGemvConsumerWarps / ng;
+    while (g > 1 && m.units / g < 32) g /= 2;
+    pl.ngroups = ng;
+    pl.gsize = g;
+    pl.kring = smax / ng;
     pl.rt = rt;
-    pl.stages = st;
-    pl.smem = pl.xbytes + st * sb + 16 * st + kGemvConsumerWarps * 4 + kGemvConsumerWarps * 8;
+    pl.stages = ng * pl.kring;
+    pl.smem = pl.xbytes + (size_t)pl.stages * sb + 24 * (size_t)pl.stages + kGemvConsumerWarps * 4 +
+              kGemvConsumerWarps * 8 + (size_t)pl.stages * g * 4 * 4;
     return pl;
 }
 
@@ -640,7 +654,8 @@ void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_
     p.units = m.units;
     p.rt = pl.rt;
     p.stages = pl.stages;
-    p.nwarps = pl.nwarps;
+    p.ngroups = pl.ngroups;
+    p.gsize = pl.gsize;
     p.kring = pl.kring;
     p.xbytes = (uint32_t)pl.xbytes;
     p.x = a.x;
@@ -660,6 +675,7 @@ void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_
     p.argmax = a.argmax;
     p.row_offset = a.row_offset;
     p.err = err;
+    p.trace = a.trace;
     void* args[] = {&p};
     launch_kernel_ex(fn, dim3(grid), dim3(kGemvThreads), pl.smem, stream, pdl, args);
 }

@@ -46,6 +46,7 @@ void* Model::dalloc(size_t bytes) {
 
 Model::~Model() {
     if (exec) cudaGraphExecDestroy(exec);
+    if (trace_exec) cudaGraphExecDestroy(trace_exec);
     if (comm) ncclCommDestroy(comm);
     for (QMat* m : all_mats()) qmat_free(*m);
     for (void* p : allocs) cudaFree(p);
@@ -329,13 +330,27 @@ void Model::load(const std::string& path, const smallm_model_opts& o) {
         nccl_check(ncclCommInitRank(&comm, tp_size, id, tp_rank), "ncclCommInitRank");
     }
     SM_CUDA(cudaStreamSynchronize(stream));
-    capture();
+    capture(&exec, nullptr);
 }
 
 // One decode step: everything after the (token, pos) state is in place.
-void Model::enqueue_step(cudaStream_t s) {
+// Kind codes of the kernels of a traced step (smallm_model_trace_step).
+enum TraceKind { TK_EMBED = 1, TK_QKV = 2, TK_V = 3, TK_ATTN = 4, TK_O = 5, TK_GATE_UP = 6, TK_DOWN = 7,
+                 TK_LM_HEAD = 8, TK_FINALIZE = 9 };
+
+// One decode step: everything after the (token, pos) state is in place.
+// With `trace`, kernel k of the step stamps slot trace[k] and its kind is
+// recorded in trace_kinds.
+void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
     const bool pdl = true;  // programmatic dependent launch between the step's kernels
-    launch_embed(embd_m, st, x, s, pdl);
+    uint32_t nslot = 0;
+    if (trace) trace_kinds.clear();
+    auto slot = [&](uint32_t kind) -> TraceSlot* {
+        if (!trace) return nullptr;
+        trace_kinds.push_back(kind);
+        return trace + nslot++;
+    };
+    launch_embed(embd_m, st, x, s, pdl, slot(TK_EMBED));
     const uint32_t qrows = nh_l * hd, krows = nkv_l * hd;
     for (uint32_t i = 0; i < n_layers; ++i) {
         LayerW& L = layers[i];
@@ -355,12 +370,14 @@ void Model::enqueue_step(cudaStream_t s) {
         a.vcache = vc;
         a.rope = rope;
         a.pos = &st->pos;
+        a.trace = slot(TK_QKV);
         launch_gemv(L.qkv, GEMV_PRO_RMS, GEMV_EPI_QKV, a, s, pdl);
         if (!L.fused_v) {
             GemvArgs av = a;
             av.q_rows = 0;
             av.k_rows = 0;
             av.bias = L.bias ? L.bias + qrows + krows : nullptr;
+            av.trace = slot(TK_V);
             launch_gemv(L.v, GEMV_PRO_RMS, GEMV_EPI_QKV, av, s, pdl);
         }
         AttnArgs at;
@@ -377,11 +394,13 @@ void Model::enqueue_step(cudaStream_t s) {
         at.max_ctx = max_ctx;
         at.n_split = n_split;
         at.err = device_error_flag();
+        at.trace = slot(TK_ATTN);
         launch_attention(at, s, pdl);
 
         GemvArgs ao;
         ao.x = att;
         ao.y = x;
+        ao.trace = slot(TK_O);
         launch_gemv(L.o, GEMV_PRO_PLAIN, tp_rank == 0 ? GEMV_EPI_RESIDUAL : GEMV_EPI_STORE, ao, s, pdl);
         if (tp_size > 1) nccl_check(ncclAllReduce(x, x, embd, ncclFloat32, ncclSum, comm, s), "ncclAllReduce");
 
@@ -390,11 +409,13 @@ void Model::enqueue_step(cudaStream_t s) {
         ag.norm_w = L.ffn_norm;
         ag.eps = eps;
         ag.y = hbuf;
+        ag.trace = slot(TK_GATE_UP);
         launch_gemv(L.gu, GEMV_PRO_RMS, GEMV_EPI_SWIGLU, ag, s, pdl);
 
         GemvArgs ad;
         ad.x = hbuf;
         ad.y = x;
+        ad.trace = slot(TK_DOWN);
         launch_gemv(L.down, GEMV_PRO_PLAIN, tp_rank == 0 ? GEMV_EPI_RESIDUAL : GEMV_EPI_STORE, ad, s, pdl);
         if (tp_size > 1) nccl_check(ncclAllReduce(x, x, embd, ncclFloat32, ncclSum, comm, s), "ncclAllReduce");
     }
@@ -405,29 +426,51 @@ void Model::enqueue_step(cudaStream_t s) {
     al.y = logits_local;
     al.argmax = &st->argmax;
     al.row_offset = v0;
+    al.trace = slot(TK_LM_HEAD);
     launch_gemv(out_m, GEMV_PRO_RMS, GEMV_EPI_LOGITS, al, s, pdl);
     if (tp_size > 1) {
         nccl_check(ncclAllGather(&st->argmax, keys, 1, ncclUint64, comm, s), "ncclAllGather");
         launch_finalize_tp(st, keys, tp_size, ids, ids_cap, s, pdl);
     } else {
-        launch_finalize(st, ids, ids_cap, s, pdl);
+        launch_finalize(st, ids, ids_cap, s, pdl, slot(TK_FINALIZE));
     }
 }
 
-void Model::capture() {
+void Model::capture(cudaGraphExec_t* out, TraceSlot* trace) {
     cudaGraph_t g = nullptr;
     SM_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
     try {
-        enqueue_step(stream);
+        enqueue_step(stream, trace);
     } catch (...) {
         cudaStreamEndCapture(stream, &g);
         if (g) cudaGraphDestroy(g);
         throw;
     }
     SM_CUDA(cudaStreamEndCapture(stream, &g));
-    cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
+    cudaError_t e = cudaGraphInstantiate(out, g, 0);
     cudaGraphDestroy(g);
     SM_CUDA(e);
+}
+
+// Run one step through a copy of the graph whose kernels stamp trace slots.
+void Model::trace_step(uint32_t token, uint32_t pos, std::vector<TraceSlot>& out) {
+    if (token >= vocab) throw Error(1, "token id out of range");
+    if (pos >= max_ctx) throw Error(7, "position " + std::to_string(pos) + " is beyond the context length");
+    const uint32_t nmax = 8 + 6 * n_layers;
+    if (!trace_dev) {
+        trace_dev = static_cast<TraceSlot*>(dalloc(sizeof(TraceSlot) * nmax));
+        capture(&trace_exec, trace_dev);
+    }
+    const uint32_t n = (uint32_t)trace_kinds.size();
+    std::vector<TraceSlot> init(n);
+    for (uint32_t k = 0; k < n; ++k) init[k] = TraceSlot{~0ull, ~0ull, 0ull, trace_kinds[k]};
+    SM_CUDA(cudaMemcpyAsync(trace_dev, init.data(), sizeof(TraceSlot) * n, cudaMemcpyHostToDevice, stream));
+    set_state(token, pos);
+    SM_CUDA(cudaGraphLaunch(trace_exec, stream));
+    out.resize(n);
+    SM_CUDA(cudaMemcpyAsync(out.data(), trace_dev, sizeof(TraceSlot) * n, cudaMemcpyDeviceToHost, stream));
+    SM_CUDA(cudaStreamSynchronize(stream));
+    cached = pos + 1;
 }
 
 void Model::set_state(uint32_t token, uint32_t pos) {

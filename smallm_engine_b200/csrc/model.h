@@ -52,6 +52,9 @@ struct Model {
     uint32_t ids_cap = 0;
     uint32_t pending_steps = 0;
     cudaGraphExec_t exec = nullptr;
+    cudaGraphExec_t trace_exec = nullptr;  // copy of the step that stamps trace slots
+    TraceSlot* trace_dev = nullptr;
+    std::vector<uint32_t> trace_kinds;
     uint32_t cached = 0;
     uint64_t weight_bytes = 0, dev_bytes = 0;
     std::vector<void*> allocs;
@@ -65,13 +68,14 @@ struct Model {
     void forward(uint32_t token, uint32_t pos, float* logits, uint32_t* argmax);
     void decode_async(uint32_t token, uint32_t pos, uint32_t n_steps);
     void decode_ids(uint32_t* out, uint32_t n);
-    void enqueue_step(cudaStream_t s);
+    void enqueue_step(cudaStream_t s, TraceSlot* trace = nullptr);
+    void trace_step(uint32_t token, uint32_t pos, std::vector<TraceSlot>& out);
 
 private:
     void* dalloc(size_t bytes);
     float* upload_vector(const GGUFFile& f, const std::string& name, uint64_t expect, uint64_t first, uint64_t count);
     std::vector<QMat*> all_mats();
-    void capture();
+    void capture(cudaGraphExec_t* out, TraceSlot* trace);
     void set_state(uint32_t token, uint32_t pos);
 };
 

@@ -104,6 +104,19 @@ class CudaModel:
     def logits_device_ptr(self) -> int:
         return lib().smallm_model_logits_device(self.h) or 0
 
+    TRACE_KINDS = {1: "embed", 2: "qkv", 3: "v", 4: "attention", 5: "o", 6: "gate_up", 7: "down",
+                   8: "lm_head", 9: "finalize"}
+
+    def trace_step(self, token: int, pos: int) -> list[dict]:
+        """One step with GPU timestamps per kernel (ns from the step start)."""
+        cap = 16 + 6 * self._config.n_layers
+        buf = np.zeros(4 * cap, dtype=np.uint64)
+        n = ctypes.c_uint32()
+        check(lib().smallm_model_trace_step(self.h, int(token), int(pos), buf.ctypes.data, cap, ctypes.byref(n)))
+        r = buf[:4 * min(n.value, cap)].reshape(-1, 4)
+        return [{"kind": self.TRACE_KINDS.get(int(k), str(int(k))), "start": int(s), "ready": int(rd),
+                 "end": int(e)} for s, rd, e, k in r]
+
     def close(self):
         if getattr(self, "h", None):
             lib().smallm_model_free(self.h)
