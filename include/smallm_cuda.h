@@ -139,6 +139,38 @@ int smallm_qmatrix_dequantize(smallm_ctx* ctx, const smallm_qmatrix* W, float* y
  * bit-identical to dequantize_tensor. */
 int smallm_dequantize(smallm_ctx* ctx, uint32_t type, const uint8_t* src, uint64_t count, float* out);
 
+/* Decode attention that allocates nothing.  No counterpart in the reference
+ * (there, attention is a loop inside each model's forward,
+ * src/model/qwen2/qwen2_model.cpp:111-133).
+ *
+ * out_dev[n_heads * head_dim] = softmax(q . K^T / sqrt(head_dim)) . V over
+ * positions 0..pos, query head h reading KV head h / (n_heads / n_kv_heads):
+ * the split-K kernel a loaded model runs, on caller-owned device buffers
+ * q_dev[n_heads * head_dim] and kcache_dev / vcache_dev laid out
+ * [n_kv_heads][max_ctx][head_dim] (f32).  Asynchronous on `stream` (NULL =
+ * the context stream).
+ *
+ * For callers that cannot let the library allocate device memory (a serving
+ * engine whose memory all belongs to its own KV pool; a loop that cannot absorb
+ * the device synchronisation cudaMalloc / cudaFree may cause): the kernel's
+ * scratch (split-K partials, per-KV-head tickets, the position word) is one
+ * static 4 MiB + 1.25 KiB array inside the library, not a buffer.
+ *   - The first call on each device does one-time set-up on that device (looks
+ *     up the array's address and zeroes the tickets on `stream`); make it
+ *     before any stream capture begins.
+ *   - Calls on one device share the array: calls whose kernels overlap in time
+ *     (different streams or threads) race and must be ordered by the caller.
+ *   - Limits: n_kv_heads <= 256; n_heads / n_kv_heads <= 8 and a whole
+ *     number; head_dim 32, 64 or 128; pos < max_ctx; and the partials,
+ *     4 * n_heads * (head_dim + 2) bytes per split, fit in 4 MiB (about
+ *     max_ctx 16128 at 32 heads of 128).  Beyond them the call returns
+ *     SMALLM_ERR_RANGE (or SMALLM_ERR_INVALID for an unsupported shape) and
+ *     launches nothing. */
+int smallm_attention_noalloc(smallm_ctx* ctx, const float* q_dev, const float* kcache_dev,
+                             const float* vcache_dev, uint32_t n_heads, uint32_t n_kv_heads,
+                             uint32_t head_dim, uint32_t max_ctx, uint32_t pos, float* out_dev,
+                             void* stream);
+
 /* ------------------------------------------------------------------ */
 /* Model level                                                         */
 /* ------------------------------------------------------------------ */

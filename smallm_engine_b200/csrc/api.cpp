@@ -282,6 +282,17 @@ int smallm_gemv(smallm_ctx* ctx, const smallm_qmatrix* W, const float* x_dev, fl
     });
 }
 
+int smallm_attention_noalloc(smallm_ctx* ctx, const float* q_dev, const float* kcache_dev,
+                             const float* vcache_dev, uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
+                             uint32_t max_ctx, uint32_t pos, float* out_dev, void* stream) {
+    return guard([&] {
+        need(ctx && q_dev && kcache_dev && vcache_dev && out_dev, "NULL argument");
+        set_dev(ctx->device);
+        smallm::launch_attention_static(q_dev, kcache_dev, vcache_dev, n_heads, n_kv_heads, head_dim, max_ctx,
+                                        pos, out_dev, stream ? (cudaStream_t)stream : ctx->stream);
+    });
+}
+
 int smallm_qmatrix_dequantize(smallm_ctx* ctx, const smallm_qmatrix* W, float* y_dev, void* stream) {
     return guard([&] {
         need(ctx && W && y_dev, "NULL argument");

@@ -12,8 +12,11 @@
 // reduction then run from shared memory.  Each CTA writes an unnormalised
 // partial (running max, sum, out); the last CTA of each KV head (atomic
 // ticket, no waiting) merges the partials of the non-empty chunks.
+#include <mutex>
+
 #include "common.cuh"
 #include "engine.h"
+#include "smallm_cuda.h"
 
 namespace smallm {
 
@@ -235,6 +238,94 @@ void launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {
         attr_set = true;
     }
     launch_kernel_ex(fn, dim3(a.n_kv, a.n_split), dim3(kAttnThreads), smem, stream, pdl, args);
+}
+
+// ---------------------------------------------------------------------------
+// The same attention kernel with library-owned static scratch.
+//
+// A loaded model allocates its attention scratch once, at load.  A caller that
+// keeps its own q / K / V on the device and wants only this kernel may be
+// unable to let the library allocate at all: a serving engine that has handed
+// the GPU's memory to its own KV-block pool has none left for cudaMalloc to
+// find, and cudaMalloc / cudaFree can synchronise the device, which a
+// latency-bound decode loop cannot absorb.  For those callers the split-K
+// partials, the per-KV-head tickets and the position word live in this one
+// fixed array of the module, so a call allocates nothing.
+//
+// Layout: [0, kAttnStaticPartialBytes) partials, then kAttnStaticMaxKv
+// tickets (u32, must be zero before a launch; the merging CTA of each KV head
+// puts its ticket back to zero), then the position word.  Tickets start at zero
+// because the first call on a device clears them on its stream before its
+// launch.  Every call on a device shares this array, so calls whose kernels
+// overlap in time (other streams, other threads) race on it; callers must order
+// them.
+constexpr size_t kAttnStaticPartialBytes = 4u << 20;  // 4 MiB
+constexpr uint32_t kAttnStaticMaxKv = 256;
+constexpr size_t kAttnStaticTicketOff = kAttnStaticPartialBytes;
+constexpr size_t kAttnStaticPosOff = kAttnStaticTicketOff + 4 * kAttnStaticMaxKv;
+constexpr size_t kAttnStaticBytes = kAttnStaticPosOff + 256;
+static __device__ __align__(256) unsigned char g_attn_scratch[kAttnStaticBytes];
+
+constexpr int kAttnStaticMaxDevices = 64;
+static std::mutex g_attn_static_mu;
+static unsigned char* g_attn_static_base[kAttnStaticMaxDevices];
+
+// Device address of g_attn_scratch on the current device; the first call for a
+// device looks it up (once, with that device current) and zeroes the tickets on
+// `stream`, ahead of that call's launch.
+static unsigned char* attention_static_scratch(cudaStream_t stream) {
+    int dev = 0;
+    SM_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kAttnStaticMaxDevices) throw Error(SMALLM_ERR_RANGE, "attention (static scratch): device ordinal too large");
+    std::lock_guard<std::mutex> lock(g_attn_static_mu);
+    if (!g_attn_static_base[dev]) {
+        void* p = nullptr;
+        const cudaError_t rc = cudaGetSymbolAddress(&p, g_attn_scratch);
+        if (rc != cudaSuccess || !p)
+            throw Error(SMALLM_ERR_CUDA, std::string("attention (static scratch): cudaGetSymbolAddress failed: ") +
+                                             cudaGetErrorString(rc));
+        unsigned char* base = static_cast<unsigned char*>(p);
+        SM_CUDA(cudaMemsetAsync(base + kAttnStaticTicketOff, 0, 4 * kAttnStaticMaxKv, stream));
+        g_attn_static_base[dev] = base;
+    }
+    return g_attn_static_base[dev];
+}
+
+void launch_attention_static(const float* q, const float* kcache, const float* vcache, uint32_t n_heads,
+                             uint32_t n_kv, uint32_t hd, uint32_t max_ctx, uint32_t pos, float* out,
+                             cudaStream_t stream) {
+    if (!n_heads || !n_kv || n_heads % n_kv || n_heads / n_kv > (uint32_t)kAttnMaxGroup)
+        throw Error(SMALLM_ERR_INVALID, "attention: n_heads must be a multiple of n_kv_heads, at most 8 per KV head");
+    if (hd != 32 && hd != 64 && hd != 128) throw Error(SMALLM_ERR_INVALID, "attention: head_dim must be 32, 64 or 128");
+    if (pos >= max_ctx) throw Error(SMALLM_ERR_RANGE, "attention: pos must be below max_ctx");
+    if (n_kv > kAttnStaticMaxKv)
+        throw Error(SMALLM_ERR_RANGE, "attention (static scratch): more than 256 KV heads");
+    const uint32_t n_split = attention_splits(n_kv, max_ctx, device_sm_count());
+    const size_t need = 4 * attention_partial_floats(n_heads, hd, n_split);
+    if (need > kAttnStaticPartialBytes)
+        throw Error(SMALLM_ERR_RANGE, "attention (static scratch): this shape needs " + std::to_string(need) +
+                                          " bytes of partials for max_ctx " + std::to_string(max_ctx) +
+                                          "; the static scratch holds 4194304 (lower max_ctx or n_heads)");
+    if (attention_smem(n_heads, n_kv, hd, max_ctx, n_split) > 200 * 1024)
+        throw Error(SMALLM_ERR_INVALID, "attention: chunk does not fit in shared memory");
+    unsigned char* base = attention_static_scratch(stream);
+    uint32_t* pos_dev = reinterpret_cast<uint32_t*>(base + kAttnStaticPosOff);
+    SM_CUDA(cudaMemcpyAsync(pos_dev, &pos, sizeof(pos), cudaMemcpyHostToDevice, stream));
+    AttnArgs a;
+    a.q = q;
+    a.kcache = kcache;
+    a.vcache = vcache;
+    a.out = out;
+    a.partial = reinterpret_cast<float*>(base);
+    a.counter = reinterpret_cast<unsigned int*>(base + kAttnStaticTicketOff);
+    a.pos = pos_dev;
+    a.n_heads = n_heads;
+    a.n_kv = n_kv;
+    a.hd = hd;
+    a.max_ctx = max_ctx;
+    a.n_split = n_split;
+    a.err = device_error_flag();
+    launch_attention(a, stream, false);
 }
 
 }  // namespace smallm

@@ -148,6 +148,11 @@ uint32_t attention_splits(uint32_t n_kv, uint32_t max_ctx, int sm_count);
 size_t attention_partial_floats(uint32_t n_heads, uint32_t hd, uint32_t n_split);
 size_t attention_smem(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t max_ctx, uint32_t n_split);
 void launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl = false);
+// The same kernel with its scratch in a static array of attention.cu (no
+// allocation; calls that overlap in time race on it).
+void launch_attention_static(const float* q, const float* kcache, const float* vcache, uint32_t n_heads,
+                             uint32_t n_kv, uint32_t hd, uint32_t max_ctx, uint32_t pos, float* out,
+                             cudaStream_t stream);
 
 // cudaLaunchKernelExC with optional programmatic dependent launch.
 void launch_kernel_ex(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
