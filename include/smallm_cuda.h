@@ -81,7 +81,7 @@ void* smallm_ctx_stream(smallm_ctx* ctx);
 int smallm_ctx_synchronize(smallm_ctx* ctx);
 
 /* Backend::matmul (backend.h:17-18): y[rows] = W[rows, cols] . x[cols], f32,
- * host pointers. */
+ * host pointers, any cols (cols == 0 gives zeros; rows == 0 does nothing). */
 int smallm_backend_matmul(smallm_ctx* ctx, const float* W, const float* x, uint32_t rows,
                           uint32_t cols, float* y);
 
@@ -89,7 +89,12 @@ int smallm_backend_matmul(smallm_ctx* ctx, const float* W, const float* x, uint3
  * rows of GGUF blocks of `type` (row-major [out][in], as the reference
  * consumes GGUF weights), x f32[cols], y f32[rows], host pointers.  The
  * first call with a given W uploads and repacks it; later calls reuse the
- * device copy (the caller must not change the bytes behind W). */
+ * device copy (the caller must not change the bytes behind W).  As in the
+ * reference, a quantized row holds only whole blocks (cols / 32, or cols / 256
+ * for the K types), so columns past the last whole block are ignored and a
+ * row with no whole block gives 0.  Unlike the reference, whose fallback reads
+ * any type other than Q8_0 / Q4_0 / Q6_K as F32 (ops.cpp:283-293), Q4_K is
+ * computed as Q4_K and unknown types return SMALLM_ERR_UNSUPPORTED_TYPE. */
 int smallm_backend_matmul_quantized(smallm_ctx* ctx, const uint8_t* W, uint32_t type,
                                     const float* x, uint32_t rows, uint32_t cols, float* y);
 

@@ -268,11 +268,13 @@ static float row_f32(const float* wr, const float* x, uint32_t cols) {
 }
 
 /* y[rows] = W[rows, cols] . x[cols]; returns -1 for types other than
- * F32/Q4_0/Q8_0/Q4_K/Q6_K (the reference would silently read them as F32). */
+ * F32/Q4_0/Q8_0/Q4_K/Q6_K (the reference would silently read them as F32).
+ * Quantized rows hold cols / 32 (cols / 256) whole blocks (ops.cpp:101,186),
+ * so trailing columns are ignored and a row without a whole block gives 0. */
 int orc_matmul_quantized(const uint8_t* W, uint32_t type, const float* x,
                          uint32_t rows, uint32_t cols, float* y) {
+    if (type != T_F32 && type != T_Q4_0 && type != T_Q8_0 && type != T_Q4_K && type != T_Q6_K) return -1;
     uint64_t rb = orc_row_bytes(type, cols);
-    if (rb == 0 || type == T_F16) return -1;
     long r;
 #pragma omp parallel for schedule(static)
     for (r = 0; r < (long)rows; ++r) {

@@ -137,20 +137,45 @@ int smallm_ctx_clear_weights(smallm_ctx* ctx) {
     });
 }
 
+// Columns a Backend matmul row actually covers, as the reference computes it
+// (src/core/ops.cpp:97-101, 184-187): quantized rows hold whole blocks only
+// (cols / 32 blocks, cols / 256 super-blocks), so the tail of x is ignored;
+// F32 rows (ops.cpp:15-26, 283-293) use every column.
+static uint32_t matmul_cols(uint32_t type, uint32_t cols) {
+    if (type == SMALLM_TYPE_F32) return cols;
+    const uint32_t be = smallm::type_block_elems(type);
+    return cols / be * be;
+}
+
+// Device copy of host matrix W (keyed by its address and shape).  F32 rows
+// whose length is not a multiple of 32 are padded with zero columns to whole
+// 32-element records; the padding multiplies zero-filled x entries.
 static const smallm::QMat& cached_matrix(smallm_ctx* ctx, const uint8_t* W, uint32_t type, uint32_t rows,
                                          uint32_t cols) {
     auto key = std::make_tuple((const void*)W, type, rows, cols);
     auto it = ctx->cache.find(key);
     if (it != ctx->cache.end()) return it->second;
     smallm::QMat m;
-    smallm::qmat_upload(m, W, type, rows, cols, cols, 0, {}, ctx->stream);
+    if (type == SMALLM_TYPE_F32 && cols % 32) {
+        const uint32_t cp = (cols + 31) / 32 * 32;
+        std::vector<float> pad((size_t)rows * cp, 0.f);
+        for (uint32_t r = 0; r < rows; ++r)
+            std::memcpy(pad.data() + (size_t)r * cp, W + (size_t)r * cols * 4, (size_t)cols * 4);
+        smallm::qmat_upload(m, reinterpret_cast<const uint8_t*>(pad.data()), type, rows, cp, cp, 0, {},
+                            ctx->stream);
+    } else {
+        smallm::qmat_upload(m, W, type, rows, cols, cols, 0, {}, ctx->stream);
+    }
     return ctx->cache.emplace(key, m).first->second;
 }
 
-static void gemv_host(smallm_ctx* ctx, const smallm::QMat& m, const float* x, float* y) {
+// y = m . x with host x (x_cols valid entries; the rest of m's columns read
+// zeros) and host y.
+static void gemv_host(smallm_ctx* ctx, const smallm::QMat& m, const float* x, uint32_t x_cols, float* y) {
     float* dx = static_cast<float*>(ctx->a.get(4ull * m.cols));
     float* dy = static_cast<float*>(ctx->b.get(4ull * m.rows));
-    SM_CUDA(cudaMemcpyAsync(dx, x, 4ull * m.cols, cudaMemcpyHostToDevice, ctx->stream));
+    SM_CUDA(cudaMemcpyAsync(dx, x, 4ull * x_cols, cudaMemcpyHostToDevice, ctx->stream));
+    if (x_cols < m.cols) SM_CUDA(cudaMemsetAsync(dx + x_cols, 0, 4ull * (m.cols - x_cols), ctx->stream));
     smallm::GemvArgs a;
     a.x = dx;
     a.y = dy;
@@ -168,11 +193,18 @@ int smallm_backend_matmul(smallm_ctx* ctx, const float* W, const float* x, uint3
 int smallm_backend_matmul_quantized(smallm_ctx* ctx, const uint8_t* W, uint32_t type, const float* x,
                                     uint32_t rows, uint32_t cols, float* y) {
     return guard([&] {
-        need(ctx && W && x && y, "NULL argument");
+        need(ctx != nullptr, "NULL argument");
         if (!smallm::type_supported(type))
             throw Error(SMALLM_ERR_UNSUPPORTED_TYPE, "unsupported tensor type: " + std::to_string(type));
+        if (!rows) return;  // the reference's row loop runs zero times
+        const uint32_t c = matmul_cols(type, cols);
+        need(y && (c == 0 || (W && x)), "NULL argument");
+        if (!c) {  // no whole block: every accumulator stays 0
+            std::memset(y, 0, 4ull * rows);
+            return;
+        }
         set_dev(ctx->device);
-        gemv_host(ctx, cached_matrix(ctx, W, type, rows, cols), x, y);
+        gemv_host(ctx, cached_matrix(ctx, W, type, rows, c), x, c, y);
     });
 }
 

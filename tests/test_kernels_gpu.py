@@ -98,6 +98,34 @@ def test_gemv_shapes_vs_oracle(be, orc, t, rows, cols):
     assert np.all(np.abs(y.astype(np.float64) - want) <= gemv_bound(orc, W, t, x, rows, cols))
 
 
+@pytest.mark.parametrize("t,rows,cols", [(O.Q8_0, 5, 40), (O.Q4_0, 6, 70), (O.Q6_K, 3, 300), (O.Q8_0, 4, 20),
+                                         (O.Q4_0, 2, 0), (O.F32, 3, 0), (O.F32, 4, 1), (O.F32, 7, 45),
+                                         (O.F32, 33, 301)])
+def test_backend_matmul_partial_blocks_vs_oracle(be, orc, t, rows, cols):
+    """Backend::matmul takes any column count; matmul_quantized covers whole
+    blocks only (the tail of x is ignored, no whole block gives 0)."""
+    from test_oracle import partial_case
+    W, x = partial_case(t, rows, cols)
+    want = orc.matmul_quantized(W, t, x, rows, cols)
+    if t == O.F32:
+        y = be.matmul(W.view(np.float32) if cols else np.zeros(1, np.float32), x, rows, cols)
+    else:
+        y = be.matmul_quantized(W, t, x, rows, cols)
+    ce = cols if t == O.F32 else cols // (256 if t == O.Q6_K else 32) * (256 if t == O.Q6_K else 32)
+    if ce == 0:
+        assert np.array_equal(y, np.zeros(rows, np.float32)) and np.array_equal(want, y)
+        return
+    wd = orc.dequantize(t, W, rows * ce).reshape(rows, ce).astype(np.float64)
+    bound = 1e-5 * (np.abs(wd) @ np.abs(x[:ce].astype(np.float64))) + 1e-30
+    assert np.all(np.abs(y.astype(np.float64) - want) <= bound)
+
+
+def test_backend_matmul_zero_rows(be):
+    y = np.full(3, 7.0, np.float32)
+    _lib.check(_lib.lib().smallm_backend_matmul(be.h, None, None, 0, 64, y.ctypes.data))
+    assert np.all(y == 7.0)
+
+
 def test_gemv_device_pointers_and_linearity(be):
     """Device-resident GEMV: W(a x1 + b x2) = a W x1 + b W x2 within rounding."""
     rows, cols = 4096, 4096

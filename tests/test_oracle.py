@@ -104,6 +104,28 @@ def test_matmul_random_vs_reference(orc, ref, t, rows, cols):
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
+# rows of whole blocks only: trailing columns ignored, no whole block -> 0
+PARTIAL_SHAPES = [(O.Q8_0, 5, 40), (O.Q4_0, 6, 70), (O.Q6_K, 3, 300), (O.Q8_0, 4, 20), (O.Q4_0, 2, 0),
+                  (O.F32, 3, 0), (O.F32, 4, 1), (O.F32, 7, 45)]
+
+
+def partial_case(t, rows, cols, seed=43):
+    rng = np.random.default_rng(seed)
+    ce = cols if t == O.F32 else cols // (256 if t == O.Q6_K else 32) * (256 if t == O.Q6_K else 32)
+    w = (rng.standard_normal(rows * ce) * 0.02).astype(np.float32)
+    W = (synth.quantize(t, w) if t != O.F32 else w.view(np.uint8)) if ce else np.zeros(1, np.uint8)
+    x = rng.standard_normal(max(cols, 1)).astype(np.float32)
+    return W, x
+
+
+@pytest.mark.parametrize("t,rows,cols", PARTIAL_SHAPES)
+def test_matmul_partial_blocks_vs_reference(orc, ref, t, rows, cols):
+    W, x = partial_case(t, rows, cols)
+    a = orc.matmul_quantized(W, t, x, rows, cols)
+    b = ref.matmul_quantized(W, t, x, rows, cols)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
 def test_model_llama_kq_restatement_runs(orc, gguf_dir):
     """Q4_K/Q6_K model: the reference cannot run it (no Q4_K); the
     restatement must at least be self-consistent across cache truncation."""
