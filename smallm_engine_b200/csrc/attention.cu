@@ -12,6 +12,8 @@
 // reduction then run from shared memory.  Each CTA writes an unnormalised
 // partial (running max, sum, out); the last CTA of each KV head (atomic
 // ticket, no waiting) merges the partials of the non-empty chunks.
+#include <cooperative_groups.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -19,6 +21,8 @@
 #include "smallm_cuda.h"
 
 namespace smallm {
+
+namespace cg = cooperative_groups;
 
 constexpr int kAttnThreads = 128;
 constexpr uint32_t kAttnMinChunk = 16;
@@ -238,6 +242,279 @@ void launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {
         attr_set = true;
     }
     launch_kernel_ex(fn, dim3(a.n_kv, a.n_split), dim3(kAttnThreads), smem, stream, pdl, args);
+}
+
+// ---------------------------------------------------------------------------
+// Cluster attention: the decode step's attention.
+//
+// One thread-block cluster of C CTAs per KV head; CTA c of the cluster owns
+// the c-th of C equal contiguous ranges of positions 0..pos.  It stages its
+// range 32 positions at a time (K and V rows: two bulk copies on one
+// mbarrier), scores the `group` query heads of the KV head against them, and
+// keeps a running (max, sum, unnormalised output) per head across its chunks
+// (online softmax).  The C partials then meet through distributed shared
+// memory: after a cluster barrier each CTA merges a 1/C slice of the outputs
+// from every peer's shared memory, and a second barrier keeps every CTA's
+// shared memory alive until its peers have read it.  No global scratch, no
+// atomics, one launch.
+constexpr int kCAttnThreads = 128;
+constexpr uint32_t kCAttnChunk = 32;
+constexpr uint32_t kCAttnMaxCluster = 16;
+
+__host__ __device__ constexpr size_t cattn_smem_floats(uint32_t G, uint32_t hd) {
+    return 2 * (size_t)kCAttnChunk * hd            // ks, vs
+           + (size_t)G * hd                        // qs
+           + (size_t)G * kCAttnChunk               // sc
+           + 3 * kAttnMaxGroup                     // corr, pm, pl
+           + (size_t)(kCAttnThreads - hd) * kAttnMaxGroup  // V-pass slice partials
+           + (size_t)G * hd                        // po
+           + (size_t)kAttnMaxGroup * kCAttnMaxCluster;     // merge weights
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const AttnArgs a) {
+    constexpr int PARTS = kCAttnThreads / HD;  // position slices in the V pass
+    constexpr int DL = HD / 8;                 // head-dim elements per lane in the score pass
+    constexpr int DV = DL / 4;                 // ... as float4
+    extern __shared__ __align__(128) float sm[];
+    __shared__ __align__(8) uint64_t bar;
+    cg::cluster_group cluster = cg::this_cluster();
+    const uint32_t C = cluster.num_blocks();
+    const uint32_t rank = cluster.block_rank();
+    const uint32_t G = a.n_heads / a.n_kv;
+    const uint32_t g = blockIdx.x / C;  // KV head of this cluster
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int nw = kCAttnThreads / 32;
+    float* ks = sm;
+    float* vs = ks + kCAttnChunk * HD;
+    float* qs = vs + kCAttnChunk * HD;
+    float* sc = qs + G * HD;
+    float* corr = sc + G * kCAttnChunk;
+    float* pm = corr + kAttnMaxGroup;
+    float* pl = pm + kAttnMaxGroup;
+    float* red = pl + kAttnMaxGroup;
+    float* po = red + (kCAttnThreads - HD) * kAttnMaxGroup;
+    float* wts = po + G * HD;
+
+    if (tid == 0) {
+        trace_mark(a.trace, 0);
+        mbar_init(&bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+    if (tid == 0) trace_mark(a.trace, 1);
+    const uint32_t n = *a.pos + 1;
+    const uint32_t per = (n + C - 1) / C;
+    const uint32_t t_begin = min(n, rank * per), t_end = min(n, t_begin + per);
+    for (uint32_t i = tid; i < G * HD; i += kCAttnThreads) qs[i] = a.q[(size_t)g * G * HD + i];
+    if (tid < kAttnMaxGroup) {
+        pm[tid] = -INFINITY;
+        pl[tid] = 0.f;
+    }
+    const float scale = 1.0f / sqrtf((float)HD);
+    const int d = tid % HD, part = tid / HD;
+    float acc[kAttnMaxGroup];
+#pragma unroll
+    for (int h = 0; h < kAttnMaxGroup; ++h) acc[h] = 0.f;
+    bool ok = true;
+    uint32_t phase = 0;
+    for (uint32_t c0 = t_begin; c0 < t_end; c0 += kCAttnChunk, phase ^= 1u) {
+        const uint32_t len = min(kCAttnChunk, t_end - c0);
+        __syncthreads();  // the previous chunk's K/V/scores are no longer read (and q is staged)
+        if (tid == 0) {
+            const uint32_t bytes = len * HD * 4;
+            mbar_arrive_expect_tx(&bar, 2 * bytes);
+            bulk_g2s(ks, a.kcache + ((size_t)g * a.max_ctx + c0) * HD, bytes, &bar);
+            bulk_g2s(vs, a.vcache + ((size_t)g * a.max_ctx + c0) * HD, bytes, &bar);
+        }
+        if (!mbar_wait(&bar, phase)) {
+            ok = false;
+            if (tid == 0 && a.err) atomicOr(a.err, 4u);
+        }
+        // scores: 8 lanes per position, lane k of the 8 holds elements
+        // 4k + 32j .. +3 (conflict-free float4 rows), 16 positions per pass.
+        // The pass loop is uniform across the CTA (all lanes reach the
+        // shuffles); groups past the chunk's end compute on zeros.
+        const int l8 = tid & 7, grp = tid >> 3;
+        for (uint32_t tb = 0; tb < len; tb += kCAttnThreads / 8) {
+            const uint32_t t = tb + grp;
+            const bool act = ok && t < len;
+            float4 kv[DV];
+#pragma unroll
+            for (int j = 0; j < DV; ++j)
+                kv[j] = act ? reinterpret_cast<const float4*>(ks + t * HD)[l8 + 8 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+            // heads unrolled so their dot products and shuffles interleave
+            float s[kAttnMaxGroup];
+#pragma unroll
+            for (int h = 0; h < kAttnMaxGroup; ++h) {
+                s[h] = 0.f;
+                if (h < (int)G) {
+#pragma unroll
+                    for (int j = 0; j < DV; ++j) {
+                        const float4 q4 = reinterpret_cast<const float4*>(qs + h * HD)[l8 + 8 * j];
+                        s[h] = fmaf(q4.x, kv[j].x, s[h]);
+                        s[h] = fmaf(q4.y, kv[j].y, s[h]);
+                        s[h] = fmaf(q4.z, kv[j].z, s[h]);
+                        s[h] = fmaf(q4.w, kv[j].w, s[h]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int o = 4; o >= 1; o >>= 1) {
+#pragma unroll
+                for (int h = 0; h < kAttnMaxGroup; ++h)
+                    if (h < (int)G) s[h] += __shfl_xor_sync(0xffffffffu, s[h], o);
+            }
+            if (l8 == 0 && t < len) {
+#pragma unroll
+                for (int h = 0; h < kAttnMaxGroup; ++h)
+                    if (h < (int)G) sc[h * kCAttnChunk + t] = s[h] * scale;
+            }
+        }
+        __syncthreads();
+        // online softmax (ops::softmax, ops.cpp:43-57, across chunks)
+        for (uint32_t h = warp; h < G; h += nw) {
+            const float s = (uint32_t)lane < len ? sc[h * kCAttnChunk + lane] : -INFINITY;
+            const float m_old = pm[h];
+            const float m_new = fmaxf(m_old, warp_max(s));
+            const float e = (uint32_t)lane < len ? expf(s - m_new) : 0.f;
+            const float l = warp_sum(e);
+            if ((uint32_t)lane < len) sc[h * kCAttnChunk + lane] = e;
+            if (lane == 0) {
+                const float cf = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
+                corr[h] = cf;
+                pl[h] = fmaf(pl[h], cf, l);
+                pm[h] = m_new;
+            }
+        }
+        __syncthreads();
+        // o[h][d] = o[h][d] * corr[h] + sum_t p[h][t] v[t][d]
+#pragma unroll
+        for (int h = 0; h < kAttnMaxGroup; ++h)
+            if (h < (int)G) acc[h] *= corr[h];
+        for (uint32_t t = part; t < len; t += PARTS) {
+            const float v = ok ? vs[t * HD + d] : 0.f;
+#pragma unroll
+            for (int h = 0; h < kAttnMaxGroup; ++h)
+                if (h < (int)G) acc[h] = fmaf(sc[h * kCAttnChunk + t], v, acc[h]);
+        }
+    }
+    if constexpr (PARTS > 1) {
+        __syncthreads();
+        if (part > 0) {
+#pragma unroll
+            for (int h = 0; h < kAttnMaxGroup; ++h) red[((part - 1) * HD + d) * kAttnMaxGroup + h] = acc[h];
+        }
+        __syncthreads();
+    }
+    if (part == 0) {
+#pragma unroll
+        for (int h = 0; h < kAttnMaxGroup; ++h) {
+            if (h < (int)G) {
+                float o = acc[h];
+#pragma unroll
+                for (int k = 1; k < PARTS; ++k) o += red[((k - 1) * HD + d) * kAttnMaxGroup + h];
+                po[h * HD + d] = o;
+            }
+        }
+    }
+    cluster.sync();  // every CTA's (pm, pl, po) is final and visible to the cluster
+
+    // Remote loads are issued together (unrolled over the largest cluster),
+    // so each merge step waits for one distributed-shared-memory round trip.
+    if (tid < (int)G) {
+        const uint32_t h = tid;
+        float mc[kCAttnMaxCluster], lc[kCAttnMaxCluster];
+#pragma unroll
+        for (uint32_t c = 0; c < kCAttnMaxCluster; ++c) {
+            mc[c] = c < C ? *cluster.map_shared_rank(pm + h, c) : -INFINITY;
+            lc[c] = c < C ? *cluster.map_shared_rank(pl + h, c) : 0.f;
+        }
+        float M = -INFINITY;
+#pragma unroll
+        for (uint32_t c = 0; c < kCAttnMaxCluster; ++c) M = fmaxf(M, mc[c]);
+        float L = 0.f;
+#pragma unroll
+        for (uint32_t c = 0; c < kCAttnMaxCluster; ++c) {
+            mc[c] = mc[c] == -INFINITY ? 0.f : expf(mc[c] - M);
+            L = fmaf(mc[c], lc[c], L);
+        }
+#pragma unroll
+        for (uint32_t c = 0; c < kCAttnMaxCluster; ++c) wts[h * kCAttnMaxCluster + c] = mc[c] / L;
+    }
+    __syncthreads();
+    for (uint32_t o = rank * kCAttnThreads + tid; o < G * HD; o += C * kCAttnThreads) {
+        const uint32_t h = o / HD;
+        float pc[kCAttnMaxCluster];
+#pragma unroll
+        for (uint32_t c = 0; c < kCAttnMaxCluster; ++c) pc[c] = c < C ? *cluster.map_shared_rank(po + o, c) : 0.f;
+        float O = 0.f;
+#pragma unroll
+        for (uint32_t c = 0; c < kCAttnMaxCluster; ++c) O = fmaf(wts[h * kCAttnMaxCluster + c], pc[c], O);
+        a.out[(size_t)g * G * HD + o] = O;
+    }
+    cluster.sync();  // peers may still be reading this CTA's shared memory
+    if (tid == 0) trace_mark(a.trace, 2);
+}
+
+static const void* cattn_fn(uint32_t hd) {
+    if (hd == 32) return (const void*)attention_cluster_kernel<32>;
+    if (hd == 64) return (const void*)attention_cluster_kernel<64>;
+    if (hd == 128) return (const void*)attention_cluster_kernel<128>;
+    throw Error(SMALLM_ERR_INVALID, "attention: head_dim must be 32, 64 or 128");
+}
+
+uint32_t attention_cluster_size(uint32_t n_heads, uint32_t n_kv, uint32_t hd) {
+    const void* fn = cattn_fn(hd);
+    const size_t smem = 4 * cattn_smem_floats(n_heads / n_kv, hd);
+    SM_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    SM_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    for (uint32_t C = kCAttnMaxCluster; C > 1; C /= 2) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(n_kv * C);
+        cfg.blockDim = dim3(kCAttnThreads);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = C;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int nclusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&nclusters, fn, &cfg) == cudaSuccess && nclusters > 0) return C;
+        (void)cudaGetLastError();
+    }
+    return 1;
+}
+
+void launch_attention_cluster(const AttnArgs& a, uint32_t C, cudaStream_t stream, bool pdl) {
+    const uint32_t G = a.n_heads / a.n_kv;
+    if (G > (uint32_t)kAttnMaxGroup || a.n_heads % a.n_kv)
+        throw Error(SMALLM_ERR_INVALID, "attention: unsupported head grouping");
+    if (C < 1 || C > kCAttnMaxCluster) throw Error(SMALLM_ERR_INVALID, "attention: bad cluster size");
+    const void* fn = cattn_fn(a.hd);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.n_kv * C);
+    cfg.blockDim = dim3(kCAttnThreads);
+    cfg.dynamicSmemBytes = 4 * cattn_smem_floats(G, a.hd);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = C;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.numAttrs = 1;
+    if (pdl) {
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.numAttrs = 2;
+    }
+    cfg.attrs = attr;
+    AttnArgs aa = a;
+    void* args[] = {&aa};
+    SM_CUDA(cudaLaunchKernelExC(&cfg, fn, args));
 }
 
 // ---------------------------------------------------------------------------

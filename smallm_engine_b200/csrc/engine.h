@@ -148,7 +148,13 @@ uint32_t attention_splits(uint32_t n_kv, uint32_t max_ctx, int sm_count);
 size_t attention_partial_floats(uint32_t n_heads, uint32_t hd, uint32_t n_split);
 size_t attention_smem(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t max_ctx, uint32_t n_split);
 void launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl = false);
-// The same kernel with its scratch in a static array of attention.cu (no
+// Cluster attention (the decode step's): one cluster of C CTAs per KV head,
+// partials merged through distributed shared memory.  attention_cluster_size
+// picks the largest C <= 16 the device can schedule (and sets the kernel's
+// attributes on the current device).
+uint32_t attention_cluster_size(uint32_t n_heads, uint32_t n_kv, uint32_t hd);
+void launch_attention_cluster(const AttnArgs& a, uint32_t C, cudaStream_t stream, bool pdl);
+// The split-K kernel with its scratch in a static array of attention.cu (no
 // allocation; calls that overlap in time race on it).
 void launch_attention_static(const float* q, const float* kcache, const float* vcache, uint32_t n_heads,
                              uint32_t n_kv, uint32_t hd, uint32_t max_ctx, uint32_t pos, float* out,

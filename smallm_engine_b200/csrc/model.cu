@@ -311,10 +311,7 @@ void Model::load(const std::string& path, const smallm_model_opts& o) {
     hbuf = static_cast<float*>(dalloc(4ull * ffn_l));
     logits = static_cast<float*>(dalloc(4ull * vocab_l * tp_size));
     logits_local = tp_size > 1 ? static_cast<float*>(dalloc(4ull * vocab_l)) : logits;
-    n_split = attention_splits(nkv_l, max_ctx, sm_count);
-    partial = static_cast<float*>(dalloc(4ull * attention_partial_floats(nh_l, hd, n_split)));
-    counters = static_cast<unsigned*>(dalloc(4ull * nkv_l));
-    SM_CUDA(cudaMemsetAsync(counters, 0, 4ull * nkv_l, stream));
+    attn_cluster = attention_cluster_size(nh_l, nkv_l, hd);
     st = static_cast<DecodeState*>(dalloc(sizeof(DecodeState)));
     SM_CUDA(cudaMemsetAsync(st, 0, sizeof(DecodeState), stream));
     keys = static_cast<unsigned long long*>(dalloc(8ull * tp_size));
@@ -385,17 +382,14 @@ void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
         at.kcache = kc;
         at.vcache = vc;
         at.out = att;
-        at.partial = partial;
-        at.counter = counters;
         at.pos = &st->pos;
         at.n_heads = nh_l;
         at.n_kv = nkv_l;
         at.hd = hd;
         at.max_ctx = max_ctx;
-        at.n_split = n_split;
         at.err = device_error_flag();
         at.trace = slot(TK_ATTN);
-        launch_attention(at, s, pdl);
+        launch_attention_cluster(at, attn_cluster, s, pdl);
 
         GemvArgs ao;
         ao.x = att;

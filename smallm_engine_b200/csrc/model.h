@@ -42,9 +42,7 @@ struct Model {
     float2* rope = nullptr;     // [max_ctx][hd/2]
     float *x = nullptr, *q = nullptr, *att = nullptr, *hbuf = nullptr;
     float *logits = nullptr, *logits_local = nullptr;
-    float* partial = nullptr;
-    unsigned* counters = nullptr;
-    uint32_t n_split = 1;
+    uint32_t attn_cluster = 1;  // CTAs per KV head in the cluster attention
     DecodeState* st = nullptr;
     DecodeState* h_st = nullptr;
     unsigned long long* keys = nullptr;
