@@ -45,9 +45,9 @@ WORKLOAD = "llama3-8b-q4_0"
 PROMPT = 128
 METRIC = "decode tok/s @B=1 (Llama-3-8B-shaped, Q4_0) + % of HBM BW roofline"
 # dram__bytes_read.sum + dram__bytes_write.sum of one Q4_0 GEMV launch on the
-# 14336x4096 matrix, from ncu (see profiles/gemv_q4_0_14336x4096.md); None
-# until captured.
-GEMV_NCU_TRAFFIC_BYTES = None
+# 14336x4096 matrix, from one ncu capture of gemv_kernel<FmtQ4_0, 0, 0>:
+# 33.078528 MB read, 0 written (the algorithmic bytes are 33.10 MB).
+GEMV_NCU_TRAFFIC_BYTES = 33078528
 
 
 def peaks() -> tuple[float, str]:
@@ -214,7 +214,10 @@ def reference_arm(args, ws, rank):
 # ------------------------------------------------------------------ ours --
 
 def gemv_roofline(device: int, iters: int = 50) -> dict:
-    """Dominant kernel alone: Q4_0 GEMV on 14336x4096, four copies rotated."""
+    """Dominant kernel alone: Q4_0 GEMV on 14336x4096, four copies rotated
+    (132 MB > L2), `iters` launches replayed from a CUDA graph on the
+    launching stream and timed with CUDA events there (device time per
+    launch, no host launch cost)."""
     import torch
     from smallm_engine_b200 import CUDABackend, synth
     be = CUDABackend(device)
@@ -230,13 +233,20 @@ def gemv_roofline(device: int, iters: int = 50) -> dict:
     for i in range(8):
         mats[i % 4].gemv(x.data_ptr(), y.data_ptr(), be.stream)
     be.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(iters):
+            mats[i % 4].gemv(x.data_ptr(), y.data_ptr(), be.stream)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(s)
-    for i in range(iters):
-        mats[i % 4].gemv(x.data_ptr(), y.data_ptr(), be.stream)
-    e1.record(s)
+    with torch.cuda.stream(s):  # replay on the stream the events are recorded on
+        g.replay()
+        s.synchronize()
+        e0.record(s)
+        g.replay()
+        e1.record(s)
     e1.synchronize()
     ms = e0.elapsed_time(e1) / iters
+    del g
     for m in mats:
         m.free()
     be.close()

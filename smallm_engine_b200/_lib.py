@@ -11,7 +11,8 @@ import os
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
-LIB_PATH = PKG / "lib" / "libsmallm_cuda.so"
+# SMALLM_CUDA_LIB points at another build of the same library (e.g. a variant)
+LIB_PATH = Path(os.environ.get("SMALLM_CUDA_LIB", PKG / "lib" / "libsmallm_cuda.so"))
 HEADER = PKG.parent / "include" / "smallm_cuda.h"
 
 OK = 0

@@ -336,6 +336,69 @@ __device__ __forceinline__ void consumers_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kGemvConsumerWarps * 32) : "memory");
 }
 
+// Fused epilogue of one finished row (v = the row's W.x after 1/rms).  The
+// pair epilogues (RoPE, SwiGLU) run on the even row of a pair and read the
+// odd row's value from v_next; `best` collects the LOGITS argmax key.
+template <int EPI>
+__device__ __forceinline__ void gemv_epilogue_row(const GemvParams& p, uint32_t row, float v, float v_next,
+                                                  unsigned long long& best) {
+    if constexpr (EPI == EPI_STORE) {
+        if (row < p.rows) p.y[row] = v;
+    } else if constexpr (EPI == EPI_RESIDUAL) {
+        if (row < p.rows) p.y[row] += v;  // x += W.h (ops::axpy, qwen2_model.cpp:178,184)
+    } else if constexpr (EPI == EPI_LOGITS) {
+        if (row < p.rows) {
+            p.y[row] = v;
+            if (v == v) {  // a NaN never wins (greedy_sampler.cpp:11 compares with >)
+                const unsigned long long k = argmax_key(v, p.row_offset + row);
+                best = k > best ? k : best;
+            }
+        }
+    } else if constexpr (EPI == EPI_SWIGLU) {
+        // storage rows 2j / 2j+1 hold gate_j / up_j (ops::silu then ops::mul,
+        // qwen2_model.cpp:154-155)
+        if ((row & 1) == 0 && row + 1 < p.rows) {
+            const float g = v / (1.0f + expf(-v));
+            p.y[row >> 1] = g * v_next;
+        }
+    } else if constexpr (EPI == EPI_QKV) {
+        const uint32_t hd = p.head_dim, half = hd >> 1;
+        const uint32_t pos = *p.pos;
+        if (row < p.q_rows + p.k_rows) {
+            if ((row & 1) == 0 && row + 1 < p.rows) {
+                const bool isq = row < p.q_rows;
+                const uint32_t pr = (isq ? row : row - p.q_rows) >> 1;  // rotary pair index
+                const uint32_t head = pr / half, ii = pr % half;
+                const uint32_t la = head * hd + ii, lb = la + half;
+                float x0 = v, x1 = v_next;
+                if (p.bias) {
+                    const uint32_t bo = isq ? 0u : p.q_rows;
+                    x0 += p.bias[bo + la];
+                    x1 += p.bias[bo + lb];
+                }
+                // ops::rope (ops.cpp:84-89) with the reference build's fused rounding
+                const float2 cs = p.rope[(size_t)pos * half + ii];
+                const float o0 = fmaf(x0, cs.x, -__fmul_rn(x1, cs.y));
+                const float o1 = fmaf(x0, cs.y, __fmul_rn(x1, cs.x));
+                if (isq) {
+                    p.qout[la] = o0;
+                    p.qout[lb] = o1;
+                } else {
+                    float* kr = p.kcache + ((size_t)head * p.max_ctx + pos) * hd;
+                    kr[ii] = o0;
+                    kr[ii + half] = o1;
+                }
+            }
+        } else if (row < p.rows) {
+            const uint32_t lv = row - p.q_rows - p.k_rows;
+            float vv = v;
+            if (p.bias) vv += p.bias[p.q_rows + p.k_rows + lv];
+            const uint32_t head = lv / hd, dd = lv % hd;
+            p.vcache[((size_t)head * p.max_ctx + pos) * hd + dd] = vv;
+        }
+    }
+}
+
 // ------------------------------------------------------------------ kernel --
 
 template <class Fmt, int PRO, int EPI>
@@ -542,61 +605,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         const uint32_t row = t * p.rt + sub4 + rl;
         if ((lane & 7) != 0 || dead) continue;
 
-        if constexpr (EPI == EPI_STORE) {
-            if (row < p.rows) p.y[row] = v;
-        } else if constexpr (EPI == EPI_RESIDUAL) {
-            if (row < p.rows) p.y[row] += v;  // x += W.h (ops::axpy, qwen2_model.cpp:178,184)
-        } else if constexpr (EPI == EPI_LOGITS) {
-            if (row < p.rows) {
-                p.y[row] = v;
-                if (v == v) {  // a NaN never wins (greedy_sampler.cpp:11 compares with >)
-                    const unsigned long long k = argmax_key(v, p.row_offset + row);
-                    best = k > best ? k : best;
-                }
-            }
-        } else if constexpr (EPI == EPI_SWIGLU) {
-            // storage rows 2j / 2j+1 hold gate_j / up_j (ops::silu then ops::mul,
-            // qwen2_model.cpp:154-155)
-            if ((rl & 1) == 0 && row + 1 < p.rows) {
-                const float g = v / (1.0f + expf(-v));
-                p.y[row >> 1] = g * v_next;
-            }
-        } else if constexpr (EPI == EPI_QKV) {
-            const uint32_t hd = p.head_dim, half = hd >> 1;
-            const uint32_t pos = *p.pos;
-            if (row < p.q_rows + p.k_rows) {
-                if ((rl & 1) == 0 && row + 1 < p.rows) {
-                    const bool isq = row < p.q_rows;
-                    const uint32_t pr = (isq ? row : row - p.q_rows) >> 1;  // rotary pair index
-                    const uint32_t head = pr / half, ii = pr % half;
-                    const uint32_t la = head * hd + ii, lb = la + half;
-                    float x0 = v, x1 = v_next;
-                    if (p.bias) {
-                        const uint32_t bo = isq ? 0u : p.q_rows;
-                        x0 += p.bias[bo + la];
-                        x1 += p.bias[bo + lb];
-                    }
-                    // ops::rope (ops.cpp:84-89) with the reference build's fused rounding
-                    const float2 cs = p.rope[(size_t)pos * half + ii];
-                    const float o0 = fmaf(x0, cs.x, -__fmul_rn(x1, cs.y));
-                    const float o1 = fmaf(x0, cs.y, __fmul_rn(x1, cs.x));
-                    if (isq) {
-                        p.qout[la] = o0;
-                        p.qout[lb] = o1;
-                    } else {
-                        float* kr = p.kcache + ((size_t)head * p.max_ctx + pos) * hd;
-                        kr[ii] = o0;
-                        kr[ii + half] = o1;
-                    }
-                }
-            } else if (row < p.rows) {
-                const uint32_t lv = row - p.q_rows - p.k_rows;
-                float vv = v;
-                if (p.bias) vv += p.bias[p.q_rows + p.k_rows + lv];
-                const uint32_t head = lv / hd, dd = lv % hd;
-                p.vcache[((size_t)head * p.max_ctx + pos) * hd + dd] = vv;
-            }
-        }
+        gemv_epilogue_row<EPI>(p, row, v, v_next, best);
     }
 
     if constexpr (EPI == EPI_LOGITS) {

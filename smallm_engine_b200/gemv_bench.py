@@ -4,8 +4,10 @@
 
 Uploads `--copies` independent seeded matrices (enough that together they
 exceed the 126 MB L2, so every launch streams from HBM), launches the GEMV
-`--iters` times round-robin on the context stream and times the launches
-with CUDA events on that stream.  Prints one JSON line: ms per launch and
+`--iters` times round-robin on the context stream, once from the host and
+once replayed from a CUDA graph, and times both with CUDA events on that
+stream (the graph figure is the device time; the host-launched one also
+pays the Python launch cost).  Prints one JSON line: ms per launch and
 the achieved bandwidth counted in ALGORITHMIC bytes (the GGUF bytes of the
 matrix plus x and y), the same count as the reference's memory traffic.
 """
@@ -40,18 +42,34 @@ def run(type_: str, rows: int, cols: int, iters: int = 50, copies: int = 0, devi
         mats[i % copies].gemv(x.data_ptr(), y.data_ptr(), be.stream)
     be.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # host-launched: includes the Python/ctypes cost of each launch
     e0.record(s)
     for i in range(iters):
         mats[i % copies].gemv(x.data_ptr(), y.data_ptr(), be.stream)
     e1.record(s)
     e1.synchronize()
+    ms_stream = e0.elapsed_time(e1) / iters
+    # the same launches captured in a CUDA graph: device time only
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(iters):
+            mats[i % copies].gemv(x.data_ptr(), y.data_ptr(), be.stream)
+    with torch.cuda.stream(s):  # replay on the stream the events are recorded on
+        g.replay()
+        s.synchronize()
+        e0.record(s)
+        g.replay()
+        e1.record(s)
+    e1.synchronize()
     ms = e0.elapsed_time(e1) / iters
+    del g
     algo = per + 4 * (rows + cols)
     for m in mats:
         m.free()
     be.close()
     return {"type": type_, "rows": rows, "cols": cols, "iters": iters, "copies": copies,
-            "ms_per_launch": ms, "algorithmic_bytes": algo, "gbs": algo / (ms / 1e3) / 1e9}
+            "ms_per_launch": ms, "ms_per_launch_stream": ms_stream, "algorithmic_bytes": algo,
+            "gbs": algo / (ms / 1e3) / 1e9}
 
 
 def main(argv=None):

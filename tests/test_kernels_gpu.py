@@ -53,8 +53,8 @@ def test_dequant_random_bytes_bit_exact(be, orc, t):
     assert_bits_equal_nan_aware(got, want)
 
 
-@pytest.mark.parametrize("t,rows,cols", [(O.Q4_0, 37, 512), (O.Q8_0, 9, 896), (O.Q6_K, 13, 2048),
-                                         (O.Q4_K, 21, 1024), (O.F32, 5, 64)])
+@pytest.mark.parametrize("t,rows,cols", [(O.Q4_0, 37, 512), (O.Q4_0, 21, 96), (O.Q8_0, 9, 896),
+                                         (O.Q6_K, 13, 2048), (O.Q4_K, 21, 1024), (O.F32, 5, 64)])
 def test_repacked_layout_dequant_bit_exact(be, orc, t, rows, cols):
     """The device layout (split streams, Q6_K re-encoding, row padding) holds
     exactly the reference's values."""
@@ -86,7 +86,8 @@ def test_matmul_quantized_vs_golden(be, orc, golden, t):
 
 @pytest.mark.parametrize("t,rows,cols", [(O.Q4_0, 14336, 4096), (O.Q4_0, 4096, 14336), (O.Q8_0, 4864, 896),
                                          (O.Q8_0, 896, 4864), (O.Q6_K, 2048, 5632), (O.Q4_K, 5632, 2048),
-                                         (O.Q4_0, 1000, 4096), (O.Q8_0, 3, 32)])
+                                         (O.Q4_0, 1000, 4096), (O.Q8_0, 3, 32), (O.Q4_0, 3, 32),
+                                         (O.Q4_0, 33, 96), (O.Q4_0, 100, 4128), (O.Q4_0, 6144, 4096)])
 def test_gemv_shapes_vs_oracle(be, orc, t, rows, cols):
     """Model shapes (config 2's Q4_0 matrices included) and ragged row counts."""
     rng = np.random.default_rng(rows + cols)
@@ -145,6 +146,12 @@ def test_gemv_device_pointers_and_linearity(be):
     rhs = 2.0 * ys[0].double() - 0.5 * ys[1].double()
     scale = ys[0].abs().max().item() + ys[1].abs().max().item()
     assert (lhs - rhs).abs().max().item() <= 1e-5 * scale
+    # split tiles are summed in a fixed order and their tickets reset: a
+    # repeated launch gives the same bits
+    again = torch.empty(rows, device="cuda")
+    qm.gemv(x1.data_ptr(), again.data_ptr(), s)
+    torch.cuda.synchronize()
+    assert torch.equal(again, ys[0])
 
 
 def test_matmul_weight_cache_reused(be):
