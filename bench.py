@@ -128,13 +128,8 @@ def dist_setup():
 
 
 def allreduce_max(v: float, ws: int) -> float:
-    if ws == 1:
-        return v
-    import torch
-    import torch.distributed as dist
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    from smallm_engine_b200.tp import max_over_ranks
+    return max_over_ranks(v, ws, device="cuda")
 
 
 def barrier(ws: int):
@@ -259,17 +254,8 @@ def our_arm(args, ws, rank, local):
     from smallm_engine_b200 import _lib
 
     path = ensure_model(ws, rank)
-    nccl_id = None
-    if ws > 1:
-        import torch.distributed as dist
-        buf = [None]
-        if rank == 0:
-            import ctypes
-            b = ctypes.create_string_buffer(128)
-            _lib.check(_lib.lib().smallm_nccl_unique_id(b))
-            buf = [bytes(b.raw)]
-        dist.broadcast_object_list(buf, src=0)
-        nccl_id = buf[0]
+    from smallm_engine_b200.tp import share_nccl_id
+    nccl_id = share_nccl_id(rank, ws)
     total_steps = args.prompt + args.warmup + 2 * args.steps + 8
     max_ctx = max(512, (total_steps + 255) // 256 * 256)
     m = CudaModel(path, device=local, max_ctx=max_ctx, tp_rank=rank, tp_size=ws, nccl_id=nccl_id)
