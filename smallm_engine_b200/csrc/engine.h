@@ -70,9 +70,10 @@ void qmat_upload(QMat& m, const uint8_t* host, uint32_t type, uint32_t rows, uin
                  uint64_t src_cols, uint64_t col0, const std::vector<uint32_t>& row_map,
                  cudaStream_t stream);
 
-enum GemvPro { GEMV_PRO_PLAIN = 0, GEMV_PRO_RMS = 1 };
+enum GemvPro { GEMV_PRO_PLAIN = 0, GEMV_PRO_RMS = 1, GEMV_PRO_RMS_SUM = 2 };
 enum GemvEpi { GEMV_EPI_STORE = 0, GEMV_EPI_RESIDUAL = 1, GEMV_EPI_QKV = 2, GEMV_EPI_SWIGLU = 3,
-               GEMV_EPI_LOGITS = 4 };
+               GEMV_EPI_LOGITS = 4, GEMV_EPI_PEER = 5 };
+constexpr int kMaxTPRanks = 8;
 
 // Everything a GEMV launch needs besides the matrix (see gemv.cuh).
 struct GemvArgs {
@@ -90,6 +91,16 @@ struct GemvArgs {
     unsigned long long* argmax = nullptr;
     uint32_t row_offset = 0;  // LOGITS: global index of storage row 0 (vocab-parallel shards)
     TraceSlot* trace = nullptr;  // traced steps only
+    // tensor-parallel residual through peer memory (gemv.cuh, GemvParams)
+    const float* x_res = nullptr;
+    float* x_out = nullptr;
+    const float* rx = nullptr;
+    const unsigned int* rx_flag = nullptr;
+    float* peer_out[kMaxTPRanks] = {};
+    unsigned int* peer_flag[kMaxTPRanks] = {};
+    unsigned int* done_ctr = nullptr;
+    const unsigned int* epoch = nullptr;
+    uint32_t tp = 1;
 };
 
 void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_t stream, bool pdl = false);
@@ -127,8 +138,9 @@ void launch_embed(const QMat& emb, DecodeState* st, float* x, cudaStream_t strea
 void launch_finalize(DecodeState* st, uint32_t* ids, uint32_t ids_cap, cudaStream_t stream, bool pdl = false,
                      TraceSlot* trace = nullptr);
 // Same, taking the maximum of the `n` gathered per-rank argmax keys.
+// Also counts the step in *epoch (the tensor-parallel flags carry it).
 void launch_finalize_tp(DecodeState* st, const unsigned long long* keys, int n, uint32_t* ids,
-                        uint32_t ids_cap, cudaStream_t stream, bool pdl = false);
+                        uint32_t ids_cap, unsigned int* epoch, cudaStream_t stream, bool pdl = false);
 
 // Split-K GQA decode attention over the head-major f32 KV cache, with the
 // per-head combine done by the last CTA of each KV head.

@@ -41,8 +41,9 @@
 
 namespace smallm {
 
-enum { PRO_PLAIN = 0, PRO_RMS = 1 };
-enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4 };
+enum { PRO_PLAIN = 0, PRO_RMS = 1, PRO_RMS_SUM = 2 };
+enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4, EPI_PEER = 5 };
+constexpr int kMaxTP = 8;
 
 constexpr int kGemvConsumerWarps = 16;
 constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;  // + one producer warp
@@ -83,6 +84,22 @@ struct GemvParams {
     uint32_t row_offset;  // LOGITS: global vocabulary index of storage row 0
     unsigned int* err;    // set non-zero when a bounded wait gives up
     TraceSlot* trace;     // null outside traced steps
+    // Tensor-parallel residual, all-reduced through peer memory instead of a
+    // separate collective.  EPI_PEER (row-parallel O / down): each finished
+    // row's partial goes straight into every rank's receive buffer, and the
+    // kernel's last CTA raises this rank's arrival flag at every rank.
+    // PRO_RMS_SUM (the next GEMV): waits for all ranks' flags, takes
+    // x = x_res + sum over ranks of the partials (rank order: identical bits on
+    // every rank), CTA 0 stores it to x_out, then the RMSNorm prologue runs.
+    const float* x_res;             // PRO_RMS_SUM: residual before the add
+    float* x_out;                   // PRO_RMS_SUM: residual after the add
+    const float* rx;                // PRO_RMS_SUM: [tp][cols] received partials
+    const unsigned int* rx_flag;    // PRO_RMS_SUM: [tp] arrival flags (epoch + 1 when ready)
+    float* peer_out[kMaxTP];        // EPI_PEER: rank q's receive slot for this rank's partial
+    unsigned int* peer_flag[kMaxTP];// EPI_PEER: this rank's arrival flag at rank q
+    unsigned int* done_ctr;         // EPI_PEER: finished CTAs, zero between launches
+    const unsigned int* epoch;      // steps completed so far (same on every rank)
+    uint32_t tp;
 };
 
 // ------------------------------------------------------- x in fixed point --
@@ -344,6 +361,9 @@ __device__ __forceinline__ void gemv_epilogue_row(const GemvParams& p, uint32_t 
                                                   unsigned long long& best) {
     if constexpr (EPI == EPI_STORE) {
         if (row < p.rows) p.y[row] = v;
+    } else if constexpr (EPI == EPI_PEER) {
+        if (row < p.rows)
+            for (uint32_t r = 0; r < p.tp; ++r) p.peer_out[r][row] = v;  // NVLink stores to peers
     } else if constexpr (EPI == EPI_RESIDUAL) {
         if (row < p.rows) p.y[row] += v;  // x += W.h (ops::axpy, qwen2_model.cpp:178,184)
     } else if constexpr (EPI == EPI_LOGITS) {
@@ -465,8 +485,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     const float4* x4 = reinterpret_cast<const float4*>(p.x);
     const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
     const uint32_t ngr = p.cols / 4;  // a multiple of 8: whole blocks are in or out
+    constexpr bool kRms = PRO != PRO_PLAIN;
     float4 wpre[kB];
-    if constexpr (PRO == PRO_RMS) {
+    if constexpr (kRms) {
 #pragma unroll
         for (int k = 0; k < kB; ++k) {
             const uint32_t g = ctid + k * kStride;
@@ -475,20 +496,56 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     }
     pdl_wait();
     if (ctid == 0) trace_mark(p.trace, 1);
+    if constexpr (PRO == PRO_RMS_SUM) {
+        // every rank's partial of the previous row-parallel GEMV must have
+        // arrived (bounded wait; on timeout the error flag is raised and the
+        // step's result is not valid)
+        if (ctid == 0) {
+            const unsigned int want = __ldcg(p.epoch) + 1u;
+            const long long t0 = clock64();
+            for (uint32_t r = 0; r < p.tp; ++r) {
+                while (ld_acquire_sys(p.rx_flag + r) != want) {
+                    if (clock64() - t0 > (1ll << 31)) {
+                        atomicOr(p.err, 8u);
+                        break;
+                    }
+                    __nanosleep(32);
+                }
+            }
+        }
+        consumers_sync();
+    }
+    const float4* xr4 = reinterpret_cast<const float4*>(p.rx);
     float ss = 0.f;
     for (uint32_t g0 = 0; g0 < ngr; g0 += kB * kStride) {
         float4 xq[kB];
 #pragma unroll
         for (int k = 0; k < kB; ++k) {
             const uint32_t g = g0 + ctid + k * kStride;
-            xq[k] = g < ngr ? x4[g] : make_float4(0.f, 0.f, 0.f, 0.f);
+            if constexpr (PRO == PRO_RMS_SUM) {
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (g < ngr) {
+                    v = reinterpret_cast<const float4*>(p.x_res)[g];
+                    for (uint32_t r = 0; r < p.tp; ++r) {  // rank order: the same sum on every rank
+                        const float4 d = __ldcg(xr4 + (size_t)r * ngr + g);
+                        v.x += d.x;
+                        v.y += d.y;
+                        v.z += d.z;
+                        v.w += d.w;
+                    }
+                    if (blockIdx.x == 0) reinterpret_cast<float4*>(p.x_out)[g] = v;
+                }
+                xq[k] = v;
+            } else {
+                xq[k] = g < ngr ? x4[g] : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
         }
 #pragma unroll
         for (int k = 0; k < kB; ++k) {
             const uint32_t g = g0 + ctid + k * kStride;
             const bool act = g < ngr;
             float4 q = xq[k];
-            if constexpr (PRO == PRO_RMS) {
+            if constexpr (kRms) {
                 ss += q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w;
                 const float4 w = g0 == 0 ? wpre[k] : (act ? w4[g] : make_float4(0.f, 0.f, 0.f, 0.f));
                 q.x *= w.x;
@@ -505,12 +562,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         }
     }
     float inv = 1.0f;
-    if constexpr (PRO == PRO_RMS) {
+    if constexpr (kRms) {
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
     }
     consumers_sync();
-    if constexpr (PRO == PRO_RMS) {
+    if constexpr (kRms) {
         float t = 0.f;
 #pragma unroll
         for (int k = 0; k < kGemvConsumerWarps; ++k) t += red[k];
@@ -620,6 +677,18 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
             unsigned long long b = 0ull;
             for (int k = 0; k < kGemvConsumerWarps; ++k) b = best_sh[k] > b ? best_sh[k] : b;
             if (b) atomicMax(p.argmax, b);
+        }
+    }
+    if constexpr (EPI == EPI_PEER) {
+        // every row partial of this CTA is stored (at the peers too); the last
+        // CTA to finish raises this rank's flag at every rank
+        __threadfence_system();
+        consumers_sync();
+        if (ctid == 0 && atomicAdd(p.done_ctr, 1u) == gridDim.x - 1) {
+            *p.done_ctr = 0u;
+            __threadfence_system();
+            const unsigned int e = __ldcg(p.epoch) + 1u;
+            for (uint32_t r = 0; r < p.tp; ++r) st_release_sys(p.peer_flag[r], e);
         }
     }
     if (p.trace) {

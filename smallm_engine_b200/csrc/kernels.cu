@@ -437,8 +437,9 @@ void launch_finalize(DecodeState* st, uint32_t* ids, uint32_t cap, cudaStream_t 
 }
 
 __global__ void finalize_tp_kernel(DecodeState* st, const unsigned long long* keys, int n, uint32_t* ids,
-                                   uint32_t cap) {
+                                   uint32_t cap, unsigned int* epoch) {
     pdl_wait();
+    if (epoch) *epoch += 1u;
     unsigned long long b = 0ull;
     for (int i = 0; i < n; ++i) b = keys[i] > b ? keys[i] : b;
     st->argmax = b;
@@ -451,8 +452,8 @@ __global__ void finalize_tp_kernel(DecodeState* st, const unsigned long long* ke
 }
 
 void launch_finalize_tp(DecodeState* st, const unsigned long long* keys, int n, uint32_t* ids, uint32_t cap,
-                        cudaStream_t stream, bool pdl) {
-    void* args[] = {&st, &keys, &n, &ids, &cap};
+                        unsigned int* epoch, cudaStream_t stream, bool pdl) {
+    void* args[] = {&st, &keys, &n, &ids, &cap, &epoch};
     launch_kernel_ex((const void*)finalize_tp_kernel, dim3(1), dim3(1), 0, stream, pdl, args);
 }
 
@@ -564,6 +565,11 @@ static const void* pick(int pro, int epi) {
     if (pro == PRO_RMS && epi == EPI_QKV) return (const void*)gemv_kernel<Fmt, PRO_RMS, EPI_QKV>;
     if (pro == PRO_RMS && epi == EPI_SWIGLU) return (const void*)gemv_kernel<Fmt, PRO_RMS, EPI_SWIGLU>;
     if (pro == PRO_RMS && epi == EPI_LOGITS) return (const void*)gemv_kernel<Fmt, PRO_RMS, EPI_LOGITS>;
+    // tensor parallel: row-parallel partials to peers, and the GEMVs that sum them
+    if (pro == PRO_PLAIN && epi == EPI_PEER) return (const void*)gemv_kernel<Fmt, PRO_PLAIN, EPI_PEER>;
+    if (pro == PRO_RMS_SUM && epi == EPI_QKV) return (const void*)gemv_kernel<Fmt, PRO_RMS_SUM, EPI_QKV>;
+    if (pro == PRO_RMS_SUM && epi == EPI_SWIGLU) return (const void*)gemv_kernel<Fmt, PRO_RMS_SUM, EPI_SWIGLU>;
+    if (pro == PRO_RMS_SUM && epi == EPI_LOGITS) return (const void*)gemv_kernel<Fmt, PRO_RMS_SUM, EPI_LOGITS>;
     throw Error(1, "gemv: unsupported prologue/epilogue combination");
 }
 
@@ -677,6 +683,21 @@ void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_
     p.row_offset = a.row_offset;
     p.err = err;
     p.trace = a.trace;
+    p.x_res = a.x_res;
+    p.x_out = a.x_out;
+    p.rx = a.rx;
+    p.rx_flag = a.rx_flag;
+    for (int r = 0; r < kMaxTPRanks; ++r) {
+        p.peer_out[r] = a.peer_out[r];
+        p.peer_flag[r] = a.peer_flag[r];
+    }
+    p.done_ctr = a.done_ctr;
+    p.epoch = a.epoch;
+    p.tp = a.tp;
+    if ((pro == GEMV_PRO_RMS_SUM || epi == GEMV_EPI_PEER) &&
+        (a.tp < 1 || a.tp > (uint32_t)kMaxTPRanks || !a.epoch || (epi == GEMV_EPI_PEER && !a.done_ctr) ||
+         (pro == GEMV_PRO_RMS_SUM && (!a.x_res || !a.x_out || !a.rx || !a.rx_flag))))
+        throw Error(1, "gemv: incomplete tensor-parallel arguments");
     void* args[] = {&p};
     launch_kernel_ex(fn, dim3(grid), dim3(kGemvThreads), pl.smem, stream, pdl, args);
 }

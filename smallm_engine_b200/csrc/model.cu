@@ -14,10 +14,14 @@
 //
 // Tensor parallelism (tp_size > 1): query/KV heads and FFN rows are split
 // across ranks (column-parallel Q/K/V and gate/up, row-parallel O and down),
-// lm_head is split by vocabulary rows.  After O and after down the partial
-// residual updates are summed with one in-place ncclAllReduce of the embd
-// vector; rank 0 carries the residual, the other ranks contribute W_r.h
-// only.  The greedy argmax is merged with an ncclAllGather of 8-byte keys.
+// lm_head is split by vocabulary rows.  The residual all-reduce after O and
+// after down is fused into the GEMVs over peer memory: the row-parallel GEMV
+// stores each finished row of its partial W_r.h into every rank's receive
+// buffer (CUDA IPC mappings, NVLink stores) and its last CTA raises this
+// rank's flag there; the next GEMV waits for every rank's flag and adds the
+// partials to the residual in rank order in its prologue (no collective
+// launch between them).  The greedy argmax is merged with an ncclAllGather of
+// 8-byte keys.
 #include <nccl.h>
 
 #include <algorithm>
@@ -45,6 +49,9 @@ void* Model::dalloc(size_t bytes) {
 }
 
 Model::~Model() {
+    if (stream) cudaStreamSynchronize(stream);
+    for (int r = 0; r < tp_size && r < kMaxTPRanks; ++r)
+        if (peer_xchg[r] && peer_xchg[r] != xchg) cudaIpcCloseMemHandle(peer_xchg[r]);
     if (exec) cudaGraphExecDestroy(exec);
     if (trace_exec) cudaGraphExecDestroy(trace_exec);
     if (comm) ncclCommDestroy(comm);
@@ -325,6 +332,41 @@ void Model::load(const std::string& path, const smallm_model_opts& o) {
         ncclUniqueId id;
         std::memcpy(&id, o.nccl_id, sizeof(id));
         nccl_check(ncclCommInitRank(&comm, tp_size, id, tp_rank), "ncclCommInitRank");
+        // residual exchange buffers, mapped into every peer (CUDA IPC; the
+        // 64-byte handles travel over the communicator)
+        const uint32_t ops = 2 * n_layers;
+        xchg_rx_bytes = 4ull * ops * tp_size * embd;
+        const size_t xbytes = xchg_rx_bytes + 4ull * ops * tp_size;
+        xchg = static_cast<uint8_t*>(dalloc(xbytes));
+        SM_CUDA(cudaMemset(xchg, 0, xbytes));
+        cudaIpcMemHandle_t mine;
+        SM_CUDA(cudaIpcGetMemHandle(&mine, xchg));
+        uint8_t* hbuf_dev = static_cast<uint8_t*>(dalloc(sizeof(mine) * (tp_size + 1)));
+        SM_CUDA(cudaMemcpy(hbuf_dev, &mine, sizeof(mine), cudaMemcpyHostToDevice));
+        nccl_check(ncclAllGather(hbuf_dev, hbuf_dev + sizeof(mine), sizeof(mine), ncclUint8, comm, stream),
+                   "ncclAllGather");
+        std::vector<cudaIpcMemHandle_t> handles(tp_size);
+        SM_CUDA(cudaMemcpyAsync(handles.data(), hbuf_dev + sizeof(mine), sizeof(mine) * tp_size,
+                                cudaMemcpyDeviceToHost, stream));
+        SM_CUDA(cudaStreamSynchronize(stream));
+        for (int r = 0; r < tp_size; ++r) {
+            if (r == tp_rank) {
+                peer_xchg[r] = xchg;
+                continue;
+            }
+            void* pm = nullptr;
+            SM_CUDA(cudaIpcOpenMemHandle(&pm, handles[r], cudaIpcMemLazyEnablePeerAccess));
+            peer_xchg[r] = static_cast<uint8_t*>(pm);
+        }
+        done = static_cast<unsigned int*>(dalloc(4ull * ops));
+        SM_CUDA(cudaMemset(done, 0, 4ull * ops));
+        epoch = static_cast<unsigned int*>(dalloc(4));
+        SM_CUDA(cudaMemset(epoch, 0, 4));
+        xbuf[0] = x;
+        xbuf[1] = static_cast<float*>(dalloc(4ull * embd));
+        // every rank's buffers are zeroed and mapped before any step writes into them
+        nccl_check(ncclAllGather(hbuf_dev, hbuf_dev + sizeof(mine), sizeof(mine), ncclUint8, comm, stream),
+                   "ncclAllGather");
     }
     SM_CUDA(cudaStreamSynchronize(stream));
     capture(&exec, nullptr);
@@ -349,12 +391,39 @@ void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
     };
     launch_embed(embd_m, st, x, s, pdl, slot(TK_EMBED));
     const uint32_t qrows = nh_l * hd, krows = nkv_l * hd;
+    const bool tpx = tp_size > 1;
+    // op k's receive slot for sender r in rank base's buffers, and its flag
+    auto rx_at = [&](uint8_t* base, uint32_t op, int r) {
+        return reinterpret_cast<float*>(base) + ((size_t)op * tp_size + r) * embd;
+    };
+    auto flag_at = [&](uint8_t* base, uint32_t op, int r) {
+        return reinterpret_cast<unsigned int*>(base + xchg_rx_bytes) + (size_t)op * tp_size + r;
+    };
+    auto send = [&](GemvArgs& a, uint32_t op) {  // this rank's partial of op -> every rank
+        a.tp = tp_size;
+        a.epoch = epoch;
+        a.done_ctr = done + op;
+        for (int r = 0; r < tp_size; ++r) {
+            a.peer_out[r] = rx_at(peer_xchg[r], op, tp_rank);
+            a.peer_flag[r] = flag_at(peer_xchg[r], op, tp_rank);
+        }
+    };
+    auto gather = [&](GemvArgs& a, uint32_t op) {  // residual after op = before + all partials
+        a.tp = tp_size;
+        a.epoch = epoch;
+        a.x_res = xbuf[op % 2];
+        a.x_out = xbuf[(op + 1) % 2];
+        a.x = a.x_res;
+        a.rx = rx_at(xchg, op, 0);
+        a.rx_flag = flag_at(xchg, op, 0);
+    };
     for (uint32_t i = 0; i < n_layers; ++i) {
         LayerW& L = layers[i];
         float* kc = kv + (size_t)(2 * i) * nkv_l * max_ctx * hd;
         float* vc = kv + (size_t)(2 * i + 1) * nkv_l * max_ctx * hd;
+        const bool sum_in = tpx && i > 0;  // QKV completes the previous layer's down all-reduce
         GemvArgs a;
-        a.x = x;
+        a.x = tpx ? xbuf[0] : x;
         a.norm_w = L.attn_norm;
         a.eps = eps;
         a.bias = L.bias;
@@ -368,13 +437,15 @@ void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
         a.rope = rope;
         a.pos = &st->pos;
         a.trace = slot(TK_QKV);
-        launch_gemv(L.qkv, GEMV_PRO_RMS, GEMV_EPI_QKV, a, s, pdl);
+        if (sum_in) gather(a, 2 * i - 1);
+        launch_gemv(L.qkv, sum_in ? GEMV_PRO_RMS_SUM : GEMV_PRO_RMS, GEMV_EPI_QKV, a, s, pdl);
         if (!L.fused_v) {
             GemvArgs av = a;
             av.q_rows = 0;
             av.k_rows = 0;
             av.bias = L.bias ? L.bias + qrows + krows : nullptr;
             av.trace = slot(TK_V);
+            if (sum_in) av.x = xbuf[(2 * i) % 2];  // the residual the QKV GEMV just completed
             launch_gemv(L.v, GEMV_PRO_RMS, GEMV_EPI_QKV, av, s, pdl);
         }
         AttnArgs at;
@@ -395,8 +466,8 @@ void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
         ao.x = att;
         ao.y = x;
         ao.trace = slot(TK_O);
-        launch_gemv(L.o, GEMV_PRO_PLAIN, tp_rank == 0 ? GEMV_EPI_RESIDUAL : GEMV_EPI_STORE, ao, s, pdl);
-        if (tp_size > 1) nccl_check(ncclAllReduce(x, x, embd, ncclFloat32, ncclSum, comm, s), "ncclAllReduce");
+        if (tpx) send(ao, 2 * i);
+        launch_gemv(L.o, GEMV_PRO_PLAIN, tpx ? GEMV_EPI_PEER : GEMV_EPI_RESIDUAL, ao, s, pdl);
 
         GemvArgs ag;
         ag.x = x;
@@ -404,14 +475,15 @@ void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
         ag.eps = eps;
         ag.y = hbuf;
         ag.trace = slot(TK_GATE_UP);
-        launch_gemv(L.gu, GEMV_PRO_RMS, GEMV_EPI_SWIGLU, ag, s, pdl);
+        if (tpx) gather(ag, 2 * i);
+        launch_gemv(L.gu, tpx ? GEMV_PRO_RMS_SUM : GEMV_PRO_RMS, GEMV_EPI_SWIGLU, ag, s, pdl);
 
         GemvArgs ad;
         ad.x = hbuf;
         ad.y = x;
         ad.trace = slot(TK_DOWN);
-        launch_gemv(L.down, GEMV_PRO_PLAIN, tp_rank == 0 ? GEMV_EPI_RESIDUAL : GEMV_EPI_STORE, ad, s, pdl);
-        if (tp_size > 1) nccl_check(ncclAllReduce(x, x, embd, ncclFloat32, ncclSum, comm, s), "ncclAllReduce");
+        if (tpx) send(ad, 2 * i + 1);
+        launch_gemv(L.down, GEMV_PRO_PLAIN, tpx ? GEMV_EPI_PEER : GEMV_EPI_RESIDUAL, ad, s, pdl);
     }
     GemvArgs al;
     al.x = x;
@@ -421,10 +493,11 @@ void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
     al.argmax = &st->argmax;
     al.row_offset = v0;
     al.trace = slot(TK_LM_HEAD);
-    launch_gemv(out_m, GEMV_PRO_RMS, GEMV_EPI_LOGITS, al, s, pdl);
-    if (tp_size > 1) {
+    if (tpx) gather(al, 2 * n_layers - 1);
+    launch_gemv(out_m, tpx ? GEMV_PRO_RMS_SUM : GEMV_PRO_RMS, GEMV_EPI_LOGITS, al, s, pdl);
+    if (tpx) {
         nccl_check(ncclAllGather(&st->argmax, keys, 1, ncclUint64, comm, s), "ncclAllGather");
-        launch_finalize_tp(st, keys, tp_size, ids, ids_cap, s, pdl);
+        launch_finalize_tp(st, keys, tp_size, ids, ids_cap, epoch, s, pdl);
     } else {
         launch_finalize(st, ids, ids_cap, s, pdl, slot(TK_FINALIZE));
     }

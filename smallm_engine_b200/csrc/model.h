@@ -43,6 +43,17 @@ struct Model {
     float *x = nullptr, *q = nullptr, *att = nullptr, *hbuf = nullptr;
     float *logits = nullptr, *logits_local = nullptr;
     uint32_t attn_cluster = 1;  // CTAs per KV head in the cluster attention
+    // Tensor parallelism (tp_size > 1): the residual is all-reduced through
+    // peer memory by the GEMVs themselves (gemv.cuh EPI_PEER / PRO_RMS_SUM).
+    // xchg (this rank's, mapped into every peer) holds the receive buffers
+    // [op][sender][embd] f32 then the flags [op][sender]; op 2i is layer i's
+    // O projection, op 2i+1 its down projection.
+    float* xbuf[2] = {nullptr, nullptr};  // residual before / after each add (op k reads xbuf[k % 2])
+    uint8_t* xchg = nullptr;
+    size_t xchg_rx_bytes = 0;
+    uint8_t* peer_xchg[kMaxTPRanks] = {};  // every rank's xchg as mapped here (own at tp_rank)
+    unsigned int* done = nullptr;          // [op] finished-CTA counters
+    unsigned int* epoch = nullptr;         // steps run, identical on every rank
     DecodeState* st = nullptr;
     DecodeState* h_st = nullptr;
     unsigned long long* keys = nullptr;
