@@ -302,6 +302,21 @@ __global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const 
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     pdl_launch_dependents();
+    if (tid == 0) {
+        // The cached K/V rows of this CTA's range do not depend on the QKV
+        // kernel still running: warm L2 with them before the dependency wait.
+        // A prefetch cannot change results (the new row's write goes through
+        // L2 as well), so the position read here need not be final.
+        const uint32_t n0 = min(*(volatile const uint32_t*)a.pos + 1, a.max_ctx);
+        const uint32_t per0 = (n0 + C - 1) / C;
+        const uint32_t b0 = min(n0, rank * per0), e0 = min(n0, b0 + per0);
+        if (e0 > b0) {
+            const uint32_t bytes = (e0 - b0) * HD * 4;
+            const size_t off = ((size_t)g * a.max_ctx + b0) * HD;
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.kcache + off), "r"(bytes) : "memory");
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.vcache + off), "r"(bytes) : "memory");
+        }
+    }
     pdl_wait();
     if (tid == 0) trace_mark(a.trace, 1);
     const uint32_t n = *a.pos + 1;
