@@ -146,11 +146,12 @@ int smallm_dequantize(smallm_ctx* ctx, uint32_t type, const uint8_t* src, uint64
 
 /* Decode attention that allocates nothing.  No counterpart in the reference
  * (there, attention is a loop inside each model's forward,
- * src/model/qwen2/qwen2_model.cpp:111-133).
+ * src/model/qwen2_model.cpp:111-133).
  *
  * out_dev[n_heads * head_dim] = softmax(q . K^T / sqrt(head_dim)) . V over
  * positions 0..pos, query head h reading KV head h / (n_heads / n_kv_heads):
- * the split-K kernel a loaded model runs, on caller-owned device buffers
+ * a split-K decode-attention kernel (partials merged by the last CTA of each
+ * KV head; a loaded model runs a cluster variant), on caller-owned device buffers
  * q_dev[n_heads * head_dim] and kcache_dev / vcache_dev laid out
  * [n_kv_heads][max_ctx][head_dim] (f32).  Asynchronous on `stream` (NULL =
  * the context stream).
@@ -175,6 +176,20 @@ int smallm_attention_noalloc(smallm_ctx* ctx, const float* q_dev, const float* k
                              const float* vcache_dev, uint32_t n_heads, uint32_t n_kv_heads,
                              uint32_t head_dim, uint32_t max_ctx, uint32_t pos, float* out_dev,
                              void* stream);
+
+/* Samplers (src/runtime/sampler/*.cpp): one token from `n` HOST logits.
+ * kind 0 = GreedySampler (first maximum), 1 = TemperatureSampler(temperature),
+ * 2 = TopKSampler(k, temperature), 3 = TopPSampler(p, temperature).  `u` is
+ * the uniform the reference sampler would draw for this call
+ * (std::uniform_real_distribution<float>(0, 1) on its std::mt19937; ignored
+ * for greedy), so the caller owns the random stream.  k must be >= 1 for
+ * top-k (the reference's k = 0 reads out of bounds). */
+#define SMALLM_SAMPLE_GREEDY 0u
+#define SMALLM_SAMPLE_TEMPERATURE 1u
+#define SMALLM_SAMPLE_TOP_K 2u
+#define SMALLM_SAMPLE_TOP_P 3u
+int smallm_sample(smallm_ctx* ctx, const float* logits, uint32_t n, uint32_t kind, uint32_t k, float p,
+                  float temperature, float u, uint32_t* token);
 
 /* ------------------------------------------------------------------ */
 /* Model level                                                         */
@@ -231,6 +246,11 @@ int smallm_model_decode_greedy_async(smallm_model* m, uint32_t token, uint32_t p
                                      uint32_t n_steps);
 /* Wait for the decode and copy the `n` ids it produced to host `ids`. */
 int smallm_model_decode_ids(smallm_model* m, uint32_t* ids, uint32_t n);
+
+/* The same samplers on the last step's logits, on the device (no logits
+ * copy); under tensor parallelism the vocabulary shards are gathered first. */
+int smallm_model_sample(smallm_model* m, uint32_t kind, uint32_t k, float p, float temperature, float u,
+                        uint32_t* token);
 
 /* Device address of the last step's logits (f32[vocab] on this rank's
  * device; this rank's vocabulary shard under tensor parallelism), valid

@@ -9,7 +9,9 @@ Public surface (mirrors the reference's interfaces):
 """
 from ._lib import SmallmError  # noqa: F401
 from .backend import CUDABackend, QMatrix  # noqa: F401
-from .model import CudaModel, GenerationStats, Generator, GreedySampler, MT19937  # noqa: F401
+from .model import (CudaModel, GenerationStats, Generator, GreedySampler, MT19937,  # noqa: F401
+                    TemperatureSampler, TopKSampler, TopPSampler)
 
 __all__ = ["SmallmError", "CUDABackend", "QMatrix", "CudaModel", "Generator", "GenerationStats",
+           "TemperatureSampler", "TopKSampler", "TopPSampler",
            "GreedySampler", "MT19937"]

@@ -325,6 +325,37 @@ int smallm_attention_noalloc(smallm_ctx* ctx, const float* q_dev, const float* k
     });
 }
 
+static void check_sampler(uint32_t kind, uint32_t k, float temperature) {
+    need(kind <= SMALLM_SAMPLE_TOP_P, "unknown sampler kind");
+    need(kind != SMALLM_SAMPLE_TOP_K || k >= 1, "top-k needs k >= 1");
+    need(kind == SMALLM_SAMPLE_GREEDY || temperature > 0.f, "temperature must be positive");
+}
+
+int smallm_sample(smallm_ctx* ctx, const float* logits, uint32_t n, uint32_t kind, uint32_t k, float p,
+                  float temperature, float u, uint32_t* token) {
+    return guard([&] {
+        need(ctx && logits && token && n > 0, "NULL argument or empty logits");
+        check_sampler(kind, k, temperature);
+        set_dev(ctx->device);
+        float* dl = static_cast<float*>(ctx->a.get(4ull * n));
+        uint32_t* scratch = static_cast<uint32_t*>(ctx->b.get(16ull * n + 16));
+        SM_CUDA(cudaMemcpyAsync(dl, logits, 4ull * n, cudaMemcpyHostToDevice, ctx->stream));
+        smallm::launch_sample(dl, n, kind, k, p, temperature, u, scratch, scratch + 4ull * n, ctx->stream);
+        SM_CUDA(cudaMemcpyAsync(token, scratch + 4ull * n, 4, cudaMemcpyDeviceToHost, ctx->stream));
+        SM_CUDA(cudaStreamSynchronize(ctx->stream));
+    });
+}
+
+int smallm_model_sample(smallm_model* m, uint32_t kind, uint32_t k, float p, float temperature, float u,
+                        uint32_t* token) {
+    return guard([&] {
+        need(m && token, "NULL argument");
+        check_sampler(kind, k, temperature);
+        set_dev(m->m.device);
+        *token = m->m.sample(kind, k, p, temperature, u);
+    });
+}
+
 int smallm_qmatrix_dequantize(smallm_ctx* ctx, const smallm_qmatrix* W, float* y_dev, void* stream) {
     return guard([&] {
         need(ctx && W && y_dev, "NULL argument");

@@ -179,6 +179,12 @@ void launch_kernel_ex(const void* fn, dim3 grid, dim3 block, size_t smem, cudaSt
 // gemv_error_flags).
 unsigned int* device_error_flag();
 
+// One sample from n logits on the device (sampler.cu): kind 0 greedy, 1
+// temperature, 2 top-k, 3 top-p; r is the host's uniform draw; scratch holds
+// 4 * n u32; the token is written to *out (device).
+void launch_sample(const float* logits, uint32_t n, uint32_t kind, uint32_t k, float p, float temp, float r,
+                   uint32_t* scratch, uint32_t* out, cudaStream_t stream);
+
 // Op-level kernels (Backend semantics on device pointers).
 void launch_rmsnorm(const float* x, const float* w, uint32_t n, float eps, float* y, cudaStream_t s);
 void launch_softmax(float* x, uint32_t n, cudaStream_t s);

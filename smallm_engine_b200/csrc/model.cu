@@ -575,6 +575,18 @@ void Model::decode_async(uint32_t token, uint32_t pos, uint32_t n_steps) {
     cached = pos + n_steps;
 }
 
+uint32_t Model::sample(uint32_t kind, uint32_t k, float p, float temperature, float u) {
+    if (!samp_scratch) samp_scratch = static_cast<uint32_t*>(dalloc(16ull * vocab + 16));
+    if (tp_size > 1)
+        nccl_check(ncclAllGather(logits_local, logits, vocab_l, ncclFloat32, comm, stream), "ncclAllGather");
+    launch_sample(logits, vocab, kind, k, p, temperature, u, samp_scratch, samp_scratch + 4ull * vocab, stream);
+    SM_CUDA(cudaMemcpyAsync(h_st, samp_scratch + 4ull * vocab, 4, cudaMemcpyDeviceToHost, stream));
+    SM_CUDA(cudaStreamSynchronize(stream));
+    uint32_t tok;
+    std::memcpy(&tok, h_st, 4);
+    return tok;
+}
+
 void Model::decode_ids(uint32_t* out, uint32_t n) {
     if (n > pending_steps) throw Error(1, "fewer decode steps were run than ids requested");
     SM_CUDA(cudaMemcpyAsync(out, ids, 4ull * n, cudaMemcpyDeviceToHost, stream));

@@ -77,6 +77,9 @@ struct Model {
     void forward(uint32_t token, uint32_t pos, float* logits, uint32_t* argmax);
     void decode_async(uint32_t token, uint32_t pos, uint32_t n_steps);
     void decode_ids(uint32_t* out, uint32_t n);
+    // One sample (sampler.cu) from the last step's logits.
+    uint32_t sample(uint32_t kind, uint32_t k, float p, float temperature, float u);
+    uint32_t* samp_scratch = nullptr;  // 4 * vocab + 4 u32
     void enqueue_step(cudaStream_t s, TraceSlot* trace = nullptr);
     void trace_step(uint32_t token, uint32_t pos, std::vector<TraceSlot>& out);
 

@@ -148,11 +148,84 @@ class MT19937:
         return float(r)
 
 
-class GreedySampler:
-    """src/runtime/sampler/greedy_sampler.cpp:8-14 (first index of the max)."""
+class _DeviceSampler:
+    """A reference sampler (src/runtime/sampler/*.cpp) whose arithmetic runs on
+    the GPU (csrc/sampler.cu) and whose random stream is the reference's: one
+    std::uniform_real_distribution<float>(0, 1) draw from its std::mt19937 per
+    sample, made here on the host."""
+    KIND = 0
+    DRAWS = True
+
+    def __init__(self, k: int = 0, p: float = 0.0, temperature: float = 1.0, seed: int = 0, device: int = 0):
+        self.k, self.p, self.temperature = int(k), float(p), float(temperature)
+        self.rng = MT19937(seed)
+        self.device = device
+        self._ctx = None
+
+    def _u(self) -> float:
+        return self.rng.uniform01() if self.DRAWS else 0.0
 
     def sample(self, logits: np.ndarray) -> int:
-        return int(np.argmax(logits))
+        """Sampler::sample(const std::vector<float>& logits) on host logits."""
+        if self._ctx is None:
+            h = ctypes.c_void_p()
+            check(lib().smallm_ctx_create(self.device, ctypes.byref(h)))
+            self._ctx = h
+        logits = np.ascontiguousarray(logits, dtype=np.float32)
+        tok = ctypes.c_uint32()
+        check(lib().smallm_sample(self._ctx, logits.ctypes.data, logits.size, self.KIND, self.k, self.p,
+                                  self.temperature, self._u(), ctypes.byref(tok)))
+        return int(tok.value)
+
+    def sample_model(self, model: "CudaModel") -> int:
+        """The same on the model's last logits, which stay on the device."""
+        tok = ctypes.c_uint32()
+        check(lib().smallm_model_sample(model.h, self.KIND, self.k, self.p, self.temperature, self._u(),
+                                        ctypes.byref(tok)))
+        return int(tok.value)
+
+    def __del__(self):
+        if getattr(self, "_ctx", None):
+            try:
+                lib().smallm_ctx_destroy(self._ctx)
+            except Exception:
+                pass
+            self._ctx = None
+
+
+class GreedySampler(_DeviceSampler):
+    """src/runtime/sampler/greedy_sampler.cpp:8-14: the first index of the
+    maximum, no random draw."""
+    KIND, DRAWS = 0, False
+
+    def __init__(self, device: int = 0):
+        super().__init__(device=device)
+
+
+class TemperatureSampler(_DeviceSampler):
+    """src/runtime/sampler/temperature_sampler.cpp: softmax(logits / T), then
+    the first index whose cumulative probability reaches the draw."""
+    KIND = 1
+
+    def __init__(self, temperature: float, seed: int, device: int = 0):
+        super().__init__(temperature=temperature, seed=seed, device=device)
+
+
+class TopKSampler(_DeviceSampler):
+    """src/runtime/sampler/top_k_sampler.cpp: the k largest logits only."""
+    KIND = 2
+
+    def __init__(self, k: int, temperature: float, seed: int, device: int = 0):
+        super().__init__(k=k, temperature=temperature, seed=seed, device=device)
+
+
+class TopPSampler(_DeviceSampler):
+    """src/runtime/sampler/top_p_sampler.cpp: the smallest prefix of the sorted
+    distribution whose mass reaches p, the draw scaled by that mass."""
+    KIND = 3
+
+    def __init__(self, p: float, temperature: float, seed: int, device: int = 0):
+        super().__init__(p=p, temperature=temperature, seed=seed, device=device)
 
 
 def _seq_sum(a: np.ndarray) -> float:
@@ -204,10 +277,12 @@ class Generator:
         self.stats.reused_tokens = shared
         self.model.truncate_cache(shared)
         pos = shared
+        # samplers that run on the device read the model's logits in place
+        on_device = hasattr(self.sampler, "sample_model")
         t0 = time.perf_counter()
         logits = None
         for i in range(shared, len(tokens)):
-            logits = self.model.forward(tokens[i], pos)
+            logits = self.model.forward(tokens[i], pos, want_logits=not on_device)
             pos += 1
             self.stats.prefill_tokens += 1
         self.stats.prefill_ms = (time.perf_counter() - t0) * 1e3
@@ -215,12 +290,12 @@ class Generator:
         generated = list(tokens)
         t0 = time.perf_counter()
         for _ in range(max_new_tokens):
-            nxt = self.sampler.sample(logits)
+            nxt = self.sampler.sample_model(self.model) if on_device else self.sampler.sample(logits)
             if self.eos >= 0 and nxt == self.eos:
                 break
             out.append(nxt)
             generated.append(nxt)
-            logits = self.model.forward(nxt, pos)
+            logits = self.model.forward(nxt, pos, want_logits=not on_device)
             pos += 1
             self.stats.generated_tokens += 1
         self.stats.decode_ms = (time.perf_counter() - t0) * 1e3
