@@ -11,7 +11,10 @@
 // TMA bulk copies completing on one mbarrier; scores, softmax and the V
 // reduction then run from shared memory.  Each CTA writes an unnormalised
 // partial (running max, sum, out); the last CTA of each KV head (atomic
-// ticket, no waiting) merges the partials of the non-empty chunks.
+// ticket, no waiting) merges the partials of the non-empty chunks.  This
+// split-K kernel serves smallm_attention_noalloc; the decode step runs the
+// cluster variant further down, which merges through distributed shared
+// memory instead of global scratch.
 #include <cooperative_groups.h>
 
 #include <mutex>
@@ -485,7 +488,10 @@ uint32_t attention_cluster_size(uint32_t n_heads, uint32_t n_kv, uint32_t hd) {
     const size_t smem = 4 * cattn_smem_floats(n_heads / n_kv, hd);
     SM_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     SM_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    for (uint32_t C = kCAttnMaxCluster; C > 1; C /= 2) {
+#ifndef SMALLM_ATTN_CLUSTER
+#define SMALLM_ATTN_CLUSTER 16u  // largest cluster tried (a power of two <= kCAttnMaxCluster)
+#endif
+    for (uint32_t C = SMALLM_ATTN_CLUSTER; C > 1; C /= 2) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(n_kv * C);
         cfg.blockDim = dim3(kCAttnThreads);
