@@ -247,6 +247,19 @@ int smallm_model_decode_greedy_async(smallm_model* m, uint32_t token, uint32_t p
 /* Wait for the decode and copy the `n` ids it produced to host `ids`. */
 int smallm_model_decode_ids(smallm_model* m, uint32_t* ids, uint32_t n);
 
+/* Batched prefill: tokens[0..n) at positions start_pos .. start_pos + n - 1
+ * in one pass per layer (GEMMs over the n tokens; the reference calls
+ * Model::forward once per prompt token, src/runtime/generator.cpp:47-51).
+ * Fills the KV cache like n forward calls and returns the last token's
+ * logits (host `logits`, may be NULL) and greedy id (`argmax`, may be NULL);
+ * cached_length becomes start_pos + n.  Single GPU (tp_size 1).  The first
+ * call keeps an f32 copy of the layer weights on the device (4 bytes per
+ * weight).  flags: SMALLM_PREFILL_TF32 runs the GEMMs on TF32 tensor cores
+ * (10-bit mantissa inputs); without it they are exact f32. */
+#define SMALLM_PREFILL_TF32 1u
+int smallm_model_prefill(smallm_model* m, const uint32_t* tokens, uint32_t n, uint32_t start_pos, float* logits,
+                         uint32_t* argmax, uint32_t flags);
+
 /* The same samplers on the last step's logits, on the device (no logits
  * copy); under tensor parallelism the vocabulary shards are gathered first. */
 int smallm_model_sample(smallm_model* m, uint32_t kind, uint32_t k, float p, float temperature, float u,

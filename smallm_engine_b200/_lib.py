@@ -73,6 +73,7 @@ SIGNATURES = {
                            ctypes.POINTER(_U32)]),
     "smallm_model_sample": (_I, [_P, _U32, _U32, ctypes.c_float, ctypes.c_float, ctypes.c_float,
                                  ctypes.POINTER(_U32)]),
+    "smallm_model_prefill": (_I, [_P, _P, _U32, _U32, _P, ctypes.POINTER(_U32), _U32]),
     "smallm_model_load": (_I, [ctypes.c_char_p, ctypes.POINTER(ModelOpts), ctypes.POINTER(_P)]),
     "smallm_model_free": (_I, [_P]),
     "smallm_model_get_info": (_I, [_P, ctypes.POINTER(ModelInfo)]),

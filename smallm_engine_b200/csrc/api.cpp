@@ -346,6 +346,15 @@ int smallm_sample(smallm_ctx* ctx, const float* logits, uint32_t n, uint32_t kin
     });
 }
 
+int smallm_model_prefill(smallm_model* m, const uint32_t* tokens, uint32_t n, uint32_t start_pos, float* logits,
+                         uint32_t* argmax, uint32_t flags) {
+    return guard([&] {
+        need(m && (tokens || n == 0), "NULL argument");
+        set_dev(m->m.device);
+        m->m.prefill(tokens, n, start_pos, logits, argmax, flags);
+    });
+}
+
 int smallm_model_sample(smallm_model* m, uint32_t kind, uint32_t k, float p, float temperature, float u,
                         uint32_t* token) {
     return guard([&] {

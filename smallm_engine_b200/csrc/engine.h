@@ -179,6 +179,19 @@ void launch_kernel_ex(const void* fn, dim3 grid, dim3 block, size_t smem, cudaSt
 // gemv_error_flags).
 unsigned int* device_error_flag();
 
+// Batched prefill (prefill.cu and the embedding in kernels.cu): rows are
+// tokens, T of them at positions pos0 .. pos0 + T - 1.
+void launch_embed_rows(const QMat& emb, const uint32_t* tokens, uint32_t T, float* X, cudaStream_t stream);
+void launch_rmsnorm_rows(const float* X, const float* w, uint32_t n, uint32_t T, float eps, float* Y,
+                         cudaStream_t s);
+void launch_qkv_post(const float* Y, uint32_t rows, uint32_t T, uint32_t q_rows, uint32_t k_rows, uint32_t hd,
+                     const float* bias, const float2* rope, uint32_t pos0, uint32_t max_ctx, float* Q, float* kc,
+                     float* vc, cudaStream_t s);
+void launch_attention_prefill(const float* Q, const float* kc, const float* vc, uint32_t n_heads, uint32_t n_kv,
+                              uint32_t hd, uint32_t max_ctx, uint32_t pos0, uint32_t T, float* out, cudaStream_t s);
+void launch_swiglu_rows(const float* Y, uint32_t ffn, uint32_t T, float* H, cudaStream_t s);
+void launch_add_rows(float* X, const float* Y, uint64_t n, cudaStream_t s);
+
 // One sample from n logits on the device (sampler.cu): kind 0 greedy, 1
 // temperature, 2 top-k, 3 top-p; r is the host's uniform draw; scratch holds
 // 4 * n u32; the token is written to *out (device).

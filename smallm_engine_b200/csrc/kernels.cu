@@ -418,6 +418,22 @@ void launch_embed(const QMat& emb, DecodeState* st, float* x, cudaStream_t strea
     launch_kernel_ex((const void*)embed_kernel, dim3((groups + 31) / 32), dim3(32), 0, stream, pdl, args);
 }
 
+// Prefill: X[t] = dequantized row tokens[t] for t < T (one thread per
+// 32-element group).  Ids were validated on the host.
+__global__ void embed_rows_kernel(const QMat m, const uint32_t* tokens, uint32_t T, float* X) {
+    const uint32_t groups = m.cols / 32;
+    const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (uint64_t)T * groups) return;
+    const uint32_t t = (uint32_t)(idx / groups), g = (uint32_t)(idx % groups);
+    dequant_group(m, tokens[t], g, X + (size_t)t * m.cols + (size_t)g * 32);
+}
+
+void launch_embed_rows(const QMat& emb, const uint32_t* tokens, uint32_t T, float* X, cudaStream_t stream) {
+    const uint64_t n = (uint64_t)T * (emb.cols / 32);
+    embed_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(emb, tokens, T, X);
+    SM_CUDA(cudaGetLastError());
+}
+
 __global__ void finalize_kernel(DecodeState* st, uint32_t* ids, uint32_t cap, TraceSlot* trace) {
     trace_mark(trace, 0);
     pdl_launch_dependents();

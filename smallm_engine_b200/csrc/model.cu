@@ -50,6 +50,8 @@ void* Model::dalloc(size_t bytes) {
 
 Model::~Model() {
     if (stream) cudaStreamSynchronize(stream);
+    if (cublas) cublasDestroy(cublas);
+    for (void* p : pre_allocs) cudaFree(p);
     for (int r = 0; r < tp_size && r < kMaxTPRanks; ++r)
         if (peer_xchg[r] && peer_xchg[r] != xchg) cudaIpcCloseMemHandle(peer_xchg[r]);
     if (exec) cudaGraphExecDestroy(exec);
@@ -573,6 +575,119 @@ void Model::decode_async(uint32_t token, uint32_t pos, uint32_t n_steps) {
     for (uint32_t i = 0; i < n_steps; ++i) SM_CUDA(cudaGraphLaunch(exec, stream));
     pending_steps = n_steps;
     cached = pos + n_steps;
+}
+
+// ------------------------------------------------------------ prefill --
+
+static void cublas_check(cublasStatus_t r, const char* what) {
+    if (r != CUBLAS_STATUS_SUCCESS) throw Error(3, std::string(what) + ": cuBLAS status " + std::to_string((int)r));
+}
+
+// Y[T][rows] = X[T][cols] . W[rows][cols]^T (all row-major f32).  A plain
+// library GEMM: exact f32 (pedantic) or TF32 tensor cores.
+void Model::gemm(const float* W, uint32_t rows, uint32_t cols, const float* X, uint32_t T, float* Y, bool tf32) {
+    const float one = 1.0f, zero = 0.0f;
+    cublas_check(cublasGemmEx(cublas, CUBLAS_OP_T, CUBLAS_OP_N, (int)rows, (int)T, (int)cols, &one, W, CUDA_R_32F,
+                              (int)cols, X, CUDA_R_32F, (int)cols, &zero, Y, CUDA_R_32F, (int)rows,
+                              tf32 ? CUBLAS_COMPUTE_32F_FAST_TF32 : CUBLAS_COMPUTE_32F_PEDANTIC, CUBLAS_GEMM_DEFAULT),
+                 "cublasGemmEx");
+}
+
+// The prompt tokens[0..T) at positions pos0 .. pos0 + T - 1 in one pass per
+// layer: every linear layer is a GEMM over the T tokens (the reference runs
+// Model::forward once per token, generator.cpp:47-51); the KV cache receives
+// all T positions and the last token's logits go through the decode lm_head
+// (fused final RMSNorm, logits, argmax).
+void Model::prefill(const uint32_t* tokens, uint32_t T, uint32_t pos0, float* out_logits, uint32_t* out_argmax,
+                    uint32_t flags) {
+    if (tp_size > 1) throw Error(1, "prefill runs on a single GPU (tp_size 1)");
+    if (T == 0) throw Error(1, "prefill needs at least one token");
+    for (uint32_t t = 0; t < T; ++t)
+        if (tokens[t] >= vocab) throw Error(1, "token id out of range");
+    if ((uint64_t)pos0 + T > max_ctx) throw Error(7, "prefill would run past the context length");
+    const bool tf32 = (flags & SMALLM_PREFILL_TF32) != 0;
+    if (!cublas) {
+        cublas_check(cublasCreate(&cublas), "cublasCreate");
+        cublas_check(cublasSetStream(cublas, stream), "cublasSetStream");
+    }
+    auto palloc = [&](size_t bytes) {
+        void* p = nullptr;
+        SM_CUDA(cudaMalloc(&p, bytes));
+        pre_allocs.push_back(p);
+        return static_cast<float*>(p);
+    };
+    if (layers_f32.empty()) {
+        layers_f32.resize(n_layers);
+        auto deq = [&](const QMat& q) -> float* {
+            if (!q.base) return nullptr;
+            float* w = palloc(4ull * q.rows * q.cols);
+            launch_qmat_dequant(q, w, stream);
+            return w;
+        };
+        for (uint32_t i = 0; i < n_layers; ++i) {
+            LayerW& L = layers[i];
+            LayerF32& F = layers_f32[i];
+            F.qkv = deq(L.qkv);
+            F.v = L.fused_v ? nullptr : deq(L.v);
+            F.o = deq(L.o);
+            F.gu = deq(L.gu);
+            F.down = deq(L.down);
+        }
+    }
+    const uint32_t qrows = nh_l * hd, krows = nkv_l * hd;
+    if (T > pre_cap) {
+        for (float** b : {&pre_x, &pre_xn, &pre_y, &pre_q, &pre_a, &pre_h}) *b = nullptr;
+        const uint32_t wide = std::max({layers[0].qkv.rows, layers[0].gu.rows, embd});
+        pre_x = palloc(4ull * T * embd);
+        pre_xn = palloc(4ull * T * embd);
+        pre_y = palloc(4ull * T * wide);
+        pre_q = palloc(4ull * T * qrows);
+        pre_a = palloc(4ull * T * qrows);
+        pre_h = palloc(4ull * T * ffn_l);
+        pre_tok = reinterpret_cast<uint32_t*>(palloc(4ull * T));
+        pre_cap = T;
+    }
+    SM_CUDA(cudaMemcpyAsync(pre_tok, tokens, 4ull * T, cudaMemcpyHostToDevice, stream));
+    launch_embed_rows(embd_m, pre_tok, T, pre_x, stream);
+    for (uint32_t i = 0; i < n_layers; ++i) {
+        LayerW& L = layers[i];
+        LayerF32& F = layers_f32[i];
+        float* kc = kv + (size_t)(2 * i) * nkv_l * max_ctx * hd;
+        float* vc = kv + (size_t)(2 * i + 1) * nkv_l * max_ctx * hd;
+        launch_rmsnorm_rows(pre_x, L.attn_norm, embd, T, eps, pre_xn, stream);
+        gemm(F.qkv, L.qkv.rows, embd, pre_xn, T, pre_y, tf32);
+        launch_qkv_post(pre_y, L.qkv.rows, T, qrows, krows, hd, L.bias, rope, pos0, max_ctx, pre_q, kc, vc, stream);
+        if (!L.fused_v) {
+            gemm(F.v, L.v.rows, embd, pre_xn, T, pre_y, tf32);
+            launch_qkv_post(pre_y, L.v.rows, T, 0, 0, hd, L.bias ? L.bias + qrows + krows : nullptr, rope, pos0,
+                            max_ctx, pre_q, kc, vc, stream);
+        }
+        launch_attention_prefill(pre_q, kc, vc, nh_l, nkv_l, hd, max_ctx, pos0, T, pre_a, stream);
+        gemm(F.o, embd, qrows, pre_a, T, pre_y, tf32);
+        launch_add_rows(pre_x, pre_y, (uint64_t)T * embd, stream);
+        launch_rmsnorm_rows(pre_x, L.ffn_norm, embd, T, eps, pre_xn, stream);
+        gemm(F.gu, L.gu.rows, embd, pre_xn, T, pre_y, tf32);
+        launch_swiglu_rows(pre_y, ffn_l, T, pre_h, stream);
+        gemm(F.down, embd, ffn_l, pre_h, T, pre_y, tf32);
+        launch_add_rows(pre_x, pre_y, (uint64_t)T * embd, stream);
+    }
+    SM_CUDA(cudaMemsetAsync(&st->argmax, 0, sizeof(unsigned long long), stream));
+    GemvArgs al;
+    al.x = pre_x + (size_t)(T - 1) * embd;
+    al.norm_w = out_norm;
+    al.eps = eps;
+    al.y = logits_local;
+    al.argmax = &st->argmax;
+    al.row_offset = v0;
+    launch_gemv(out_m, GEMV_PRO_RMS, GEMV_EPI_LOGITS, al, stream);
+    if (out_logits) SM_CUDA(cudaMemcpyAsync(out_logits, logits, 4ull * vocab, cudaMemcpyDeviceToHost, stream));
+    SM_CUDA(cudaMemcpyAsync(h_st, st, sizeof(DecodeState), cudaMemcpyDeviceToHost, stream));
+    SM_CUDA(cudaStreamSynchronize(stream));
+    if (out_argmax) {  // packed key (common.cuh argmax_key): low word = ~index
+        const unsigned long long k = h_st->argmax;
+        *out_argmax = k ? 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull) : 0u;
+    }
+    cached = pos0 + T;
 }
 
 uint32_t Model::sample(uint32_t kind, uint32_t k, float p, float temperature, float u) {

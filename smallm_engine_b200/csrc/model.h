@@ -1,6 +1,7 @@
 // Device-resident decoder model (internal).
 #pragma once
 
+#include <cublas_v2.h>
 #include <nccl.h>
 
 #include <string>
@@ -80,6 +81,21 @@ struct Model {
     // One sample (sampler.cu) from the last step's logits.
     uint32_t sample(uint32_t kind, uint32_t k, float p, float temperature, float u);
     uint32_t* samp_scratch = nullptr;  // 4 * vocab + 4 u32
+    // Batched prefill: f32 copies of the layer matrices in storage row order
+    // (made at the first prefill), GEMMs over the T tokens.
+    void prefill(const uint32_t* tokens, uint32_t T, uint32_t pos0, float* out_logits, uint32_t* out_argmax,
+                 uint32_t flags);
+    struct LayerF32 {
+        float *qkv = nullptr, *v = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
+    };
+    std::vector<LayerF32> layers_f32;
+    cublasHandle_t cublas = nullptr;
+    uint32_t pre_cap = 0;  // tokens the prefill buffers hold
+    float *pre_x = nullptr, *pre_xn = nullptr, *pre_y = nullptr, *pre_q = nullptr, *pre_a = nullptr,
+          *pre_h = nullptr;
+    uint32_t* pre_tok = nullptr;
+    std::vector<void*> pre_allocs;
+    void gemm(const float* W, uint32_t rows, uint32_t cols, const float* X, uint32_t T, float* Y, bool tf32);
     void enqueue_step(cudaStream_t s, TraceSlot* trace = nullptr);
     void trace_step(uint32_t token, uint32_t pos, std::vector<TraceSlot>& out);
 

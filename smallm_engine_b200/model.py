@@ -43,6 +43,7 @@ class CudaModel:
     def __init__(self, path, device: int = 0, max_ctx: int = 0, tp_rank: int = 0, tp_size: int = 1,
                  nccl_id: bytes | None = None):
         opts = ModelOpts(device, max_ctx, tp_rank, tp_size, None, 0)
+        self.tp_size = tp_size
         self._id = None
         if nccl_id is not None:
             self._id = ctypes.create_string_buffer(bytes(nccl_id), 128)
@@ -100,6 +101,18 @@ class CudaModel:
     def decode_greedy(self, token: int, pos: int, n_steps: int) -> np.ndarray:
         self.decode_greedy_async(token, pos, n_steps)
         return self.decode_ids(n_steps)
+
+    def prefill(self, tokens, start_pos: int, want_logits: bool = True, tf32: bool = False):
+        """Batched prefill (smallm_model_prefill): tokens at positions
+        start_pos.. in one pass per layer.  Returns (last logits or None,
+        greedy id of the last token)."""
+        toks = np.ascontiguousarray(tokens, dtype=np.uint32)
+        out = np.empty(self._config.vocab_size, dtype=np.float32) if want_logits else None
+        am = ctypes.c_uint32()
+        check(lib().smallm_model_prefill(self.h, toks.ctypes.data, toks.size, int(start_pos),
+                                         out.ctypes.data if want_logits else None, ctypes.byref(am),
+                                         1 if tf32 else 0))
+        return out, int(am.value)
 
     def logits_device_ptr(self) -> int:
         return lib().smallm_model_logits_device(self.h) or 0
@@ -257,8 +270,11 @@ class Generator:
     this backend): prefix reuse against the previous call, one forward per
     new prompt token, then sample / forward until max_new or EOS."""
 
-    def __init__(self, model: CudaModel, sampler, eos_id: int = -1):
+    def __init__(self, model: CudaModel, sampler, eos_id: int = -1, batched_prefill: bool = True):
         self.model, self.sampler, self.eos = model, sampler, eos_id
+        # the prompt in one pass per layer (smallm_model_prefill) instead of
+        # one forward per token; single GPU only
+        self.batched_prefill = batched_prefill and model.config().n_layers > 0
         self.cached_tokens: list[int] = []
         self.stats = GenerationStats()
 
@@ -281,10 +297,15 @@ class Generator:
         on_device = hasattr(self.sampler, "sample_model")
         t0 = time.perf_counter()
         logits = None
-        for i in range(shared, len(tokens)):
-            logits = self.model.forward(tokens[i], pos, want_logits=not on_device)
-            pos += 1
-            self.stats.prefill_tokens += 1
+        if self.batched_prefill and getattr(self.model, "tp_size", 1) == 1:
+            logits, _ = self.model.prefill(tokens[shared:], pos, want_logits=not on_device)
+            self.stats.prefill_tokens += len(tokens) - shared
+            pos = len(tokens)
+        else:
+            for i in range(shared, len(tokens)):
+                logits = self.model.forward(tokens[i], pos, want_logits=not on_device)
+                pos += 1
+                self.stats.prefill_tokens += 1
         self.stats.prefill_ms = (time.perf_counter() - t0) * 1e3
         out: list[int] = []
         generated = list(tokens)
