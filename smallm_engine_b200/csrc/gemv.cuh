@@ -23,15 +23,19 @@
 // Math side -- integer dot products.  In the prologue each CTA turns x (f32;
 // times the RMSNorm weight when the norm is fused, ops::rmsnorm,
 // src/core/ops.cpp:29-40) into block fixed point: per 32-element block,
-// X_i = rint(x_i * 2^(21-e)) with 2^e > max|x_i|, split into three balanced
-// signed bytes X = D2*2^16 + D1*2^8 + D0.  A block's integer weight codes q
-// meet x through IDP4A: S_d = sum_i q_i D_d,i per digit, and for the 4-bit
-// formats sum_i q_i X_i = (S2*2^8 + S1)*2^8 + S0 is exact in int32 (|q| <= 15
-// and |X| <= 2^21 over 32 elements stay below 2^31), so the block needs one
-// int->float conversion and one float scale (weight scale * 2^(e-21)).  The
-// representation error of x is below 2^-21 of the block maximum, the order
-// of the f32 rounding of the reference's FMA chain.  The norm's 1/rms is a
-// scalar and is applied to the row results in the epilogue.
+// X_i = rint(x_i * 2^(B-e)) with 2^e > max|x_i|, split into signed bytes
+// ("digits").  A block's integer weight codes q meet x through IDP4A, one
+// sum S_d = sum_i q_i D_d,i per digit, so the block needs one int->float
+// conversion and one float scale (weight scale * 2^(e-B)).
+//  - 8-bit and 6-bit codes: B = 21, three balanced digits
+//    X = D2*2^16 + D1*2^8 + D0; x is held to 2^-21 of the block maximum, the
+//    order of the f32 rounding of the reference's FMA chain.
+//  - 4-bit codes: B = 15, two digits X = D1*2^8 + D0 (D0 unsigned), x held to
+//    2^-15 of the block maximum.  High nibbles are masked in place (16 q, no
+//    shift) and their sums joined with the low ones as 16 S_lo + S_hi16, so a
+//    32-weight block costs 8 masks and 16 IDP4A; 16 sum q X stays below 2^28.
+// The norm's 1/rms is a scalar and is applied to the row results in the
+// epilogue.
 //
 // Epilogues (fused): plain store, residual add, Q/K/V bias + RoPE + KV-cache
 // append, SwiGLU, logits + greedy argmax.
@@ -47,7 +51,6 @@ constexpr int kMaxTP = 8;
 
 constexpr int kGemvConsumerWarps = 16;
 constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;  // + one producer warp
-constexpr int kXRecBytes = 112;                              // per 32-element block of x
 constexpr int kMaxRT = 32;                                   // storage rows pad to this
 
 struct GemvParams {
@@ -104,15 +107,19 @@ struct GemvParams {
 
 // ------------------------------------------------------- x in fixed point --
 
-// Shared-memory record of one 32-element block of x.
+// Shared-memory record of one 32-element block of x with ND digits.
+template <int ND>
 struct XRec {
-    uint32_t d0[8], d1[8], d2[8];  // balanced signed digits, 4 elements per word
+    uint32_t d[ND][8];             // digits, 4 elements per word (d[0] least significant)
     int32_t sx_lo, sx_hi;          // sum of X over elements 0-15 / 16-31
-    float xs;                      // 2^(e-21): x_i ~= X_i * xs
+    float xs;                      // x_i ~= X_i * 2^(e-B); 4-bit codes fold in 1/16 (see dot)
     float xsum;                    // sum of the f32 x_i
 };
-constexpr int kXBits = 21;         // |X| <= 2^21
-static_assert(sizeof(XRec) == kXRecBytes, "XRec layout");
+template <int ND>
+__host__ __device__ constexpr int xrec_bytes() { return ND * 32 + 16; }
+template <int ND>
+__host__ __device__ constexpr int xrec_bits() { return ND == 3 ? 21 : 15; }
+static_assert(sizeof(XRec<3>) == xrec_bytes<3>() && sizeof(XRec<2>) == xrec_bytes<2>(), "XRec layout");
 
 // Exact int -> float for |v| < 2^22 (IADD + FADD, no conversion unit).
 __device__ __forceinline__ float i2f_small(int v) {
@@ -123,7 +130,9 @@ __device__ __forceinline__ float i2f_small(int v) {
 // of a group each hold one float4 (elements 4j..4j+3, j = lane & 7).  All 32
 // lanes must call it (shuffles); lanes with act == false hold zeros and write
 // nothing.
+template <int ND>
 __device__ __forceinline__ void build_xrec_lane(float4 q, int lane, bool act, uint8_t* rec) {
+    constexpr int B = xrec_bits<ND>();
     const int j = lane & 7;
     float m = fmaxf(fmaxf(fabsf(q.x), fabsf(q.y)), fmaxf(fabsf(q.z), fabsf(q.w)));
     float s = (q.x + q.y) + (q.z + q.w);
@@ -136,54 +145,70 @@ __device__ __forceinline__ void build_xrec_lane(float4 q, int lane, bool act, ui
     if (!finite || m < 1e-30f) m = 0.f;      // tiny blocks contribute below f32 resolution
     int e = 0;
     frexpf(m, &e);  // m = f * 2^e, f in [0.5, 1): 2^e > m
-    const float up = m > 0.f ? ldexpf(1.0f, kXBits - e) : 0.f;
+    const float up = m > 0.f ? ldexpf(1.0f, B - e) : 0.f;
     const float v[4] = {q.x, q.y, q.z, q.w};
-    uint32_t p0 = 0, p1 = 0, p2 = 0;
+    uint32_t p[ND] = {};
     int sx = 0;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        const int X = __float2int_rn(v[k] * up);  // exact scaling by a power of two, |X| <= 2^21
+        int X = __float2int_rn(v[k] * up);  // exact scaling by a power of two, |X| <= 2^B
+        if constexpr (ND == 2) {
+            X = min(X, 32767);  // x * up < 2^15 may round up to 2^15
+            p[0] |= (uint32_t)(X & 0xFF) << (8 * k);         // unsigned low digit
+            p[1] |= (uint32_t)((X >> 8) & 0xFF) << (8 * k);  // signed high digit
+        } else {
+            const int a0 = (int)(int8_t)(X & 0xFF);
+            const int X1 = (X - a0) >> 8;
+            const int a1 = (int)(int8_t)(X1 & 0xFF);
+            const int a2 = (X1 - a1) >> 8;
+            p[0] |= (uint32_t)(a0 & 0xFF) << (8 * k);
+            p[1] |= (uint32_t)(a1 & 0xFF) << (8 * k);
+            p[2] |= (uint32_t)(a2 & 0xFF) << (8 * k);
+        }
         sx += X;
-        const int a0 = (int)(int8_t)(X & 0xFF);
-        const int X1 = (X - a0) >> 8;
-        const int a1 = (int)(int8_t)(X1 & 0xFF);
-        const int a2 = (X1 - a1) >> 8;
-        p0 |= (uint32_t)(a0 & 0xFF) << (8 * k);
-        p1 |= (uint32_t)(a1 & 0xFF) << (8 * k);
-        p2 |= (uint32_t)(a2 & 0xFF) << (8 * k);
     }
     sx += __shfl_xor_sync(0xffffffffu, sx, 1);
     sx += __shfl_xor_sync(0xffffffffu, sx, 2);  // lanes 0-3: elements 0-15, lanes 4-7: 16-31
     const int sx_other = __shfl_xor_sync(0xffffffffu, sx, 4);
     if (act) {
         uint32_t* w = reinterpret_cast<uint32_t*>(rec);
-        w[j] = p0;
-        w[8 + j] = p1;
-        w[16 + j] = p2;
+#pragma unroll
+        for (int d = 0; d < ND; ++d) w[8 * d + j] = p[d];
         if (j == 0) {
             const float nan = __int_as_float(0x7FC00000);  // propagate like the reference's f32 math
-            w[24] = (uint32_t)sx;
-            w[25] = (uint32_t)sx_other;
-            reinterpret_cast<float*>(w)[26] = !finite ? nan : (m > 0.f ? ldexpf(1.0f, e - kXBits) : 0.f);
-            reinterpret_cast<float*>(w)[27] = !finite ? nan : s;
+            // 4-bit codes produce 16 sum q X (high nibbles stay in place)
+            const int scale_e = e - B - (ND == 2 ? 4 : 0);
+            w[8 * ND] = (uint32_t)sx;
+            w[8 * ND + 1] = (uint32_t)sx_other;
+            reinterpret_cast<float*>(w)[8 * ND + 2] = !finite ? nan : (m > 0.f ? ldexpf(1.0f, scale_e) : 0.f);
+            reinterpret_cast<float*>(w)[8 * ND + 3] = !finite ? nan : s;
         }
     }
 }
 
-__device__ __forceinline__ void load_xrec(const uint8_t* base, uint32_t blk, XRec& r) {
-    const uint4* p = reinterpret_cast<const uint4*>(base + (size_t)blk * kXRecBytes);
+template <int ND>
+__device__ __forceinline__ void load_xrec(const uint8_t* base, uint32_t blk, XRec<ND>& r) {
+    const uint4* p = reinterpret_cast<const uint4*>(base + (size_t)blk * xrec_bytes<ND>());
 #pragma unroll
-    for (int i = 0; i < 7; ++i) reinterpret_cast<uint4*>(&r)[i] = p[i];
+    for (int i = 0; i < xrec_bytes<ND>() / 16; ++i) reinterpret_cast<uint4*>(&r)[i] = p[i];
 }
 
-// sum_i q_i x_i of one block = xs * (2^16 S2 + 2^8 S1 + S0).  combine() works
-// in float (each S exact and below 2^22 for every format); horner() in int32,
-// for codes small enough that the full sum cannot overflow (4-bit formats).
+// IDP4A with an unsigned first operand: unsigned x unsigned / unsigned x signed bytes.
+__device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Three-digit records: sum_i q_i x_i of one block = xs * (2^16 S2 + 2^8 S1 +
+// S0), joined in float by combine() (each S exact and below 2^22).
 __device__ __forceinline__ float combine(int s0, int s1, int s2) {
     return fmaf(i2f_small(s2), 65536.0f, fmaf(i2f_small(s1), 256.0f, i2f_small(s0)));
-}
-__device__ __forceinline__ int horner(int s0, int s1, int s2) {
-    return (s2 * 256 + s1) * 256 + s0;
 }
 
 // ---------------------------------------------------------------- formats --
@@ -197,35 +222,33 @@ __device__ __forceinline__ int horner(int s0, int s1, int s2) {
 // Q4_0: element i of a block is the low nibble of byte i, element i+16 the
 // high nibble (src/core/tensor.cpp:57-63); value (q - 8) * d.
 struct FmtQ4_0 {
-    static constexpr int UE = 32, SUBS = 1;
+    static constexpr int UE = 32, SUBS = 1, ND = 2;
     static constexpr bool F32X = false;
     struct Raw { uint4 q; uint32_t s; };
     __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t units, Raw& r) {
         r.q = *reinterpret_cast<const uint4*>(row + (size_t)u * 16);
         r.s = *reinterpret_cast<const uint16_t*>(row + (size_t)units * 16 + (size_t)u * 2);
     }
-    __device__ __forceinline__ static float dot(const Raw& r, int, const XRec& x, uint32_t) {
+    __device__ __forceinline__ static float dot(const Raw& r, int, const XRec<ND>& x, uint32_t) {
         const uint32_t w[4] = {r.q.x, r.q.y, r.q.z, r.q.w};
-        int s0 = 0, s1 = 0, s2 = 0;
+        int l0 = 0, l1 = 0, h0 = 0, h1 = 0;  // low nibbles (q) / high nibbles in place (16 q)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const int lo = (int)(w[j] & 0x0F0F0F0Fu), hi = (int)((w[j] >> 4) & 0x0F0F0F0Fu);
-            s0 = __dp4a(lo, (int)x.d0[j], s0);
-            s1 = __dp4a(lo, (int)x.d1[j], s1);
-            s2 = __dp4a(lo, (int)x.d2[j], s2);
-            s0 = __dp4a(hi, (int)x.d0[4 + j], s0);
-            s1 = __dp4a(hi, (int)x.d1[4 + j], s1);
-            s2 = __dp4a(hi, (int)x.d2[4 + j], s2);
+            const uint32_t lo = w[j] & 0x0F0F0F0Fu, hi = w[j] & 0xF0F0F0F0u;
+            l0 = dp4a_uu(lo, x.d[0][j], l0);
+            l1 = dp4a_us(lo, x.d[1][j], l1);
+            h0 = dp4a_uu(hi, x.d[0][4 + j], h0);
+            h1 = dp4a_us(hi, x.d[1][4 + j], h1);
         }
-        // sum (q - 8) X = (S2*2^8 + S1)*2^8 + S0 - 8 sum X, exact in int32
-        const int v = horner(s0, s1, s2) - 8 * (x.sx_lo + x.sx_hi);
+        // 16 sum (q - 8) X = (16 L1 + H1) 2^8 + 16 L0 + H0 - 128 sum X, exact in int32
+        const int v = ((l1 * 16 + h1) * 256 + (l0 * 16 + h0)) - 128 * (x.sx_lo + x.sx_hi);
         return (float)v * (h2f(r.s) * x.xs);
     }
 };
 
 // Q8_0: int8 codes; value q * d.
 struct FmtQ8_0 {
-    static constexpr int UE = 32, SUBS = 1;
+    static constexpr int UE = 32, SUBS = 1, ND = 3;
     static constexpr bool F32X = false;
     struct Raw { uint4 a, b; uint32_t s; };
     __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t units, Raw& r) {
@@ -238,14 +261,14 @@ struct FmtQ8_0 {
         r.b = f ? first : second;
         r.s = *reinterpret_cast<const uint16_t*>(row + (size_t)units * 32 + (size_t)u * 2);
     }
-    __device__ __forceinline__ static float dot(const Raw& r, int, const XRec& x, uint32_t) {
+    __device__ __forceinline__ static float dot(const Raw& r, int, const XRec<ND>& x, uint32_t) {
         const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
         int s0 = 0, s1 = 0, s2 = 0;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            s0 = __dp4a((int)w[j], (int)x.d0[j], s0);
-            s1 = __dp4a((int)w[j], (int)x.d1[j], s1);
-            s2 = __dp4a((int)w[j], (int)x.d2[j], s2);
+            s0 = __dp4a((int)w[j], (int)x.d[0][j], s0);
+            s1 = __dp4a((int)w[j], (int)x.d[1][j], s1);
+            s2 = __dp4a((int)w[j], (int)x.d[2][j], s2);
         }
         return combine(s0, s1, s2) * (h2f(r.s) * x.xs);
     }
@@ -256,7 +279,7 @@ struct FmtQ8_0 {
 // nibbles of qs[32k..32k+32), sub-block 2k+1 = high nibbles.
 // Value: (d*sc)*q - dmin*m (gguf-py Q4_K.dequantize_blocks).
 struct FmtQ4K {
-    static constexpr int UE = 64, SUBS = 2;
+    static constexpr int UE = 64, SUBS = 2, ND = 2;
     static constexpr bool F32X = false;
     struct Raw { uint4 h, a, b; };
     __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t, Raw& r) {
@@ -276,21 +299,23 @@ struct FmtQ4K {
             m = (byte(s2, j - 4) >> 4) | ((byte(s1, j - 4) >> 6) << 4);
         }
     }
-    __device__ __forceinline__ static float dot(const Raw& r, int sub, const XRec& x, uint32_t u) {
+    __device__ __forceinline__ static float dot(const Raw& r, int sub, const XRec<ND>& x, uint32_t u) {
         const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
-        int s0 = 0, s1 = 0, s2 = 0;
+        // sub-block 1's high nibbles stay in place: its sums are 16 sum q X
+        const uint32_t mask = sub ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+        int s0 = 0, s1 = 0;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int n = (int)(sub ? ((w[j] >> 4) & 0x0F0F0F0Fu) : (w[j] & 0x0F0F0F0Fu));
-            s0 = __dp4a(n, (int)x.d0[j], s0);
-            s1 = __dp4a(n, (int)x.d1[j], s1);
-            s2 = __dp4a(n, (int)x.d2[j], s2);
+            const uint32_t n = w[j] & mask;
+            s0 = dp4a_uu(n, x.d[0][j], s0);
+            s1 = dp4a_us(n, x.d[1][j], s1);
         }
         int sc, m;
         scale_min(r.h, 2 * (int)(u & 3) + sub, sc, m);
         const float d = h2f(r.h.x & 0xFFFFu), dmin = h2f(r.h.x >> 16);
         const float d1 = d * (float)sc, m1 = dmin * (float)m;
-        return fmaf(d1 * x.xs, (float)horner(s0, s1, s2), -m1 * x.xsum);
+        const float xs = sub ? x.xs : x.xs * 16.0f;  // x.xs carries 1/16 for in-place high nibbles
+        return fmaf(d1 * xs, (float)(s1 * 256 + s0), -m1 * x.xsum);
     }
 };
 
@@ -300,7 +325,7 @@ struct FmtQ4K {
 // 6-7); 4 int8 scales per unit (element e of a super-block uses scale e/16);
 // f16 d per super-block.  Value: (d*sc)*(q - 32) (src/core/tensor.cpp:97-106).
 struct FmtQ6K {
-    static constexpr int UE = 64, SUBS = 2;
+    static constexpr int UE = 64, SUBS = 2, ND = 3;
     static constexpr bool F32X = false;
     struct Raw { uint4 n0, n1, hb; uint32_t sc; uint32_t d; };
     __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t units, Raw& r) {
@@ -311,7 +336,7 @@ struct FmtQ6K {
         r.sc = *reinterpret_cast<const uint32_t*>(row + (size_t)units * 48 + (size_t)u * 4);
         r.d = *reinterpret_cast<const uint16_t*>(row + (size_t)units * 52 + (size_t)(u >> 2) * 2);
     }
-    __device__ __forceinline__ static float dot(const Raw& r, int sub, const XRec& x, uint32_t) {
+    __device__ __forceinline__ static float dot(const Raw& r, int sub, const XRec<ND>& x, uint32_t) {
         const uint32_t n[8] = {r.n0.x, r.n0.y, r.n0.z, r.n0.w, r.n1.x, r.n1.y, r.n1.z, r.n1.w};
         const uint32_t h[4] = {r.hb.x, r.hb.y, r.hb.z, r.hb.w};
         int a0 = 0, a1 = 0, a2 = 0, b0 = 0, b1 = 0, b2 = 0;  // first / second 16 elements
@@ -323,13 +348,13 @@ struct FmtQ6K {
             else
                 q = ((n[j] >> 4) & 0x0F0F0F0Fu) | ((j < 4 ? h[j] : (h[j - 4] >> 2)) & 0x30303030u);
             if (j < 4) {
-                a0 = __dp4a((int)q, (int)x.d0[j], a0);
-                a1 = __dp4a((int)q, (int)x.d1[j], a1);
-                a2 = __dp4a((int)q, (int)x.d2[j], a2);
+                a0 = __dp4a((int)q, (int)x.d[0][j], a0);
+                a1 = __dp4a((int)q, (int)x.d[1][j], a1);
+                a2 = __dp4a((int)q, (int)x.d[2][j], a2);
             } else {
-                b0 = __dp4a((int)q, (int)x.d0[j], b0);
-                b1 = __dp4a((int)q, (int)x.d1[j], b1);
-                b2 = __dp4a((int)q, (int)x.d2[j], b2);
+                b0 = __dp4a((int)q, (int)x.d[0][j], b0);
+                b1 = __dp4a((int)q, (int)x.d[1][j], b1);
+                b2 = __dp4a((int)q, (int)x.d[2][j], b2);
             }
         }
         // codes are q + 32: subtract 32 * sum X per 16-element group
@@ -344,7 +369,7 @@ struct FmtQ6K {
 // F32 (the reference's catch-all branch, ops.cpp:289-299): plain f32 FMAs
 // against an f32 copy of x.
 struct FmtF32 {
-    static constexpr int UE = 32, SUBS = 1;
+    static constexpr int UE = 32, SUBS = 1, ND = 3;
     static constexpr bool F32X = true;
 };
 
@@ -557,7 +582,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
                 if (act) reinterpret_cast<float4*>(xreg)[g] = q;
             } else {
                 // uniform across the warp: all lanes reach the shuffles inside
-                build_xrec_lane(q, lane, act, xreg + (size_t)(g >> 3) * kXRecBytes);
+                build_xrec_lane<Fmt::ND>(q, lane, act, xreg + (size_t)(g >> 3) * xrec_bytes<Fmt::ND>());
             }
         }
     }
@@ -628,8 +653,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
                     for (int r = 0; r < 4; ++r) Fmt::load(rows4 + (size_t)r * p.row_stride, u, p.units, raw[r]);
 #pragma unroll
                     for (int sb = 0; sb < Fmt::SUBS; ++sb) {
-                        XRec xr;
-                        load_xrec(xreg, u * Fmt::SUBS + sb, xr);
+                        XRec<Fmt::ND> xr;
+                        load_xrec<Fmt::ND>(xreg, u * Fmt::SUBS + sb, xr);
 #pragma unroll
                         for (int r = 0; r < 4; ++r) acc[r] += Fmt::dot(raw[r], sb, xr, u);
                     }

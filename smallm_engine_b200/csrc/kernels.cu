@@ -608,7 +608,10 @@ constexpr uint32_t kMaxStages = 32;
 // is ~23 tiles (~210 KB) in flight per SM.
 GemvPlan gemv_plan(const QMat& m) {
     GemvPlan pl;
-    pl.xbytes = m.type == SM_T_F32 ? (size_t)m.cols * 4 : (size_t)(m.cols / 32) * kXRecBytes;
+    // x records: two digits for the 4-bit codes, three for the others
+    const bool four_bit = m.type == SM_T_Q4_0 || m.type == SM_T_Q4_K;
+    const size_t xrec = four_bit ? xrec_bytes<2>() : xrec_bytes<3>();
+    pl.xbytes = m.type == SM_T_F32 ? (size_t)m.cols * 4 : (size_t)(m.cols / 32) * xrec;
     // per stage: the tile, three mbarriers, the group's partial sums
     const size_t misc = kGemvConsumerWarps * 4 + kGemvConsumerWarps * 8 + 128;
     const uint32_t rt = 4;
