@@ -255,22 +255,35 @@ void launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {
 // range 32 positions at a time (K and V rows: two bulk copies on one
 // mbarrier), scores the `group` query heads of the KV head against them, and
 // keeps a running (max, sum, unnormalised output) per head across its chunks
-// (online softmax).  The C partials then meet through distributed shared
-// memory: after a cluster barrier each CTA merges a 1/C slice of the outputs
-// from every peer's shared memory, and a second barrier keeps every CTA's
-// shared memory alive until its peers have read it.  No global scratch, no
-// atomics, one launch.
+// (online softmax).
+//
+// Before the dependency wait.  The position is fixed for the whole step (only
+// the step's last kernel advances it) and rows below it were written by
+// earlier steps, so the first chunk's rows other than the new one are copied
+// into shared memory while the QKV kernel still runs; the QKV kernel leaves
+// room on each SM for this kernel's CTAs.  After the wait only q and the new
+// row are read (the position is re-read, and a mismatch reloads the chunk).
+//
+// Merge.  Each CTA pushes its partial into its peers' shared memory: the
+// (max, sum) of every head to every CTA, and each output element to the CTA
+// that merges it (CTA j merges a 1/C slice), then arrives on each peer's
+// merge mbarrier.  A CTA waits only for its own C arrivals, merges its slice
+// and writes it.  A split cluster barrier publishes the mbarrier
+// initialisation (arrive at the start, wait before the first push) and keeps
+// every CTA alive until all of its peers' pushes are done (arrive after the
+// pushes, wait at the end).  No global scratch, no atomics, one launch.
 constexpr int kCAttnThreads = 128;
 constexpr uint32_t kCAttnChunk = 32;
 constexpr uint32_t kCAttnMaxCluster = 16;
 
 __host__ __device__ constexpr size_t cattn_smem_floats(uint32_t G, uint32_t hd) {
-    return 2 * (size_t)kCAttnChunk * hd            // ks, vs
-           + (size_t)G * hd                        // qs
-           + (size_t)G * kCAttnChunk               // sc
-           + 3 * kAttnMaxGroup                     // corr, pm, pl
+    return 2 * (size_t)kCAttnChunk * hd                    // ks, vs
+           + (size_t)G * hd                                // qs
+           + (size_t)G * kCAttnChunk                       // sc
+           + 3 * kAttnMaxGroup                             // corr, pm, pl
            + (size_t)(kCAttnThreads - hd) * kAttnMaxGroup  // V-pass slice partials
-           + (size_t)G * hd                        // po
+           + (size_t)G * hd + kCAttnMaxCluster             // received output slices: C x ceil(G hd / C)
+           + 2 * (size_t)kCAttnMaxCluster * kAttnMaxGroup  // received (max, sum) per CTA and head
            + (size_t)kAttnMaxGroup * kCAttnMaxCluster;     // merge weights
 }
 
@@ -280,7 +293,8 @@ __global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const 
     constexpr int DL = HD / 8;                 // head-dim elements per lane in the score pass
     constexpr int DV = DL / 4;                 // ... as float4
     extern __shared__ __align__(128) float sm[];
-    __shared__ __align__(8) uint64_t bar;
+    __shared__ __align__(8) uint64_t bar, bar_pre, mrg;
+    __shared__ uint32_t pre_n, pre_rows;
     cg::cluster_group cluster = cg::this_cluster();
     const uint32_t C = cluster.num_blocks();
     const uint32_t rank = cluster.block_rank();
@@ -288,6 +302,7 @@ __global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const 
     const uint32_t g = blockIdx.x / C;  // KV head of this cluster
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int nw = kCAttnThreads / 32;
+    const uint32_t S = (G * HD + C - 1) / C;  // outputs merged per CTA
     float* ks = sm;
     float* vs = ks + kCAttnChunk * HD;
     float* qs = vs + kCAttnChunk * HD;
@@ -296,29 +311,43 @@ __global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const 
     float* pm = corr + kAttnMaxGroup;
     float* pl = pm + kAttnMaxGroup;
     float* red = pl + kAttnMaxGroup;
-    float* po = red + (kCAttnThreads - HD) * kAttnMaxGroup;
-    float* wts = po + G * HD;
+    float* rpo = red + (kCAttnThreads - HD) * kAttnMaxGroup;  // [C][S]
+    float* rm = rpo + G * HD + kCAttnMaxCluster;               // [C][G]
+    float* rl = rm + kCAttnMaxCluster * kAttnMaxGroup;         // [C][G]
+    float* wts = rl + kCAttnMaxCluster * kAttnMaxGroup;        // [G][kCAttnMaxCluster]
 
     if (tid == 0) {
         trace_mark(a.trace, 0);
         mbar_init(&bar, 1);
+        mbar_init(&bar_pre, 1);
+        mbar_init(&mrg, C);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    cluster_arrive_relaxed();  // matched by the cluster_wait before the first push
     pdl_launch_dependents();
     if (tid == 0) {
-        // The cached K/V rows of this CTA's range do not depend on the QKV
-        // kernel still running: warm L2 with them before the dependency wait.
-        // A prefetch cannot change results (the new row's write goes through
-        // L2 as well), so the position read here need not be final.
         const uint32_t n0 = min(*(volatile const uint32_t*)a.pos + 1, a.max_ctx);
         const uint32_t per0 = (n0 + C - 1) / C;
         const uint32_t b0 = min(n0, rank * per0), e0 = min(n0, b0 + per0);
-        if (e0 > b0) {
-            const uint32_t bytes = (e0 - b0) * HD * 4;
+        // rows below the position are final; the new row comes after the wait
+        const uint32_t fin = min(min(e0, b0 + kCAttnChunk), n0 - 1);
+        const uint32_t rows = fin > b0 ? fin - b0 : 0u;
+        if (rows) {
+            const uint32_t bytes = rows * HD * 4;
             const size_t off = ((size_t)g * a.max_ctx + b0) * HD;
+            mbar_arrive_expect_tx(&bar_pre, 2 * bytes);
+            bulk_g2s(ks, a.kcache + off, bytes, &bar_pre);
+            bulk_g2s(vs, a.vcache + off, bytes, &bar_pre);
+        }
+        // warm L2 with the rest of the range (longer contexts)
+        if (e0 > b0 + kCAttnChunk) {
+            const uint32_t bytes = (e0 - b0 - kCAttnChunk) * HD * 4;
+            const size_t off = ((size_t)g * a.max_ctx + b0 + kCAttnChunk) * HD;
             asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.kcache + off), "r"(bytes) : "memory");
             asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.vcache + off), "r"(bytes) : "memory");
         }
+        pre_n = n0;
+        pre_rows = rows;
     }
     pdl_wait();
     if (tid == 0) trace_mark(a.trace, 1);
@@ -330,25 +359,40 @@ __global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const 
         pm[tid] = -INFINITY;
         pl[tid] = 0.f;
     }
+    bool ok = true;
+    __syncthreads();  // pre_n / pre_rows
+    uint32_t have = 0;  // rows of the first chunk already in shared memory
+    if (pre_rows) {
+        // the copy issued before the wait lands before anything else is
+        // staged over it (even when the position changed and it is dropped)
+        if (!mbar_wait(&bar_pre, 0)) {
+            ok = false;
+            if (tid == 0 && a.err) atomicOr(a.err, 4u);
+        }
+        if (pre_n == n) have = pre_rows;
+    }
     const float scale = 1.0f / sqrtf((float)HD);
     const int d = tid % HD, part = tid / HD;
     float acc[kAttnMaxGroup];
 #pragma unroll
     for (int h = 0; h < kAttnMaxGroup; ++h) acc[h] = 0.f;
-    bool ok = true;
     uint32_t phase = 0;
-    for (uint32_t c0 = t_begin; c0 < t_end; c0 += kCAttnChunk, phase ^= 1u) {
+    for (uint32_t c0 = t_begin; c0 < t_end; c0 += kCAttnChunk, have = 0) {
         const uint32_t len = min(kCAttnChunk, t_end - c0);
         __syncthreads();  // the previous chunk's K/V/scores are no longer read (and q is staged)
-        if (tid == 0) {
-            const uint32_t bytes = len * HD * 4;
-            mbar_arrive_expect_tx(&bar, 2 * bytes);
-            bulk_g2s(ks, a.kcache + ((size_t)g * a.max_ctx + c0) * HD, bytes, &bar);
-            bulk_g2s(vs, a.vcache + ((size_t)g * a.max_ctx + c0) * HD, bytes, &bar);
-        }
-        if (!mbar_wait(&bar, phase)) {
-            ok = false;
-            if (tid == 0 && a.err) atomicOr(a.err, 4u);
+        if (have < len) {
+            if (tid == 0) {
+                const uint32_t bytes = (len - have) * HD * 4;
+                const size_t off = ((size_t)g * a.max_ctx + c0 + have) * HD;
+                mbar_arrive_expect_tx(&bar, 2 * bytes);
+                bulk_g2s(ks + have * HD, a.kcache + off, bytes, &bar);
+                bulk_g2s(vs + have * HD, a.vcache + off, bytes, &bar);
+            }
+            if (!mbar_wait(&bar, phase)) {
+                ok = false;
+                if (tid == 0 && a.err) atomicOr(a.err, 4u);
+            }
+            phase ^= 1u;
         }
         // scores: 8 lanes per position, lane k of the 8 holds elements
         // 4k + 32j .. +3 (conflict-free float4 rows), 16 positions per pass.
@@ -425,54 +469,60 @@ __global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const 
             for (int h = 0; h < kAttnMaxGroup; ++h) red[((part - 1) * HD + d) * kAttnMaxGroup + h] = acc[h];
         }
         __syncthreads();
+        if (part == 0) {
+#pragma unroll
+            for (int h = 0; h < kAttnMaxGroup; ++h)
+#pragma unroll
+                for (int k = 1; k < PARTS; ++k) acc[h] += red[((k - 1) * HD + d) * kAttnMaxGroup + h];
+        }
     }
+    __syncthreads();  // pm / pl final
+    cluster_wait();   // every peer's merge barrier is initialised
+    // push this CTA's partial: output h*HD + d to the CTA merging it, row `rank`
     if (part == 0) {
 #pragma unroll
         for (int h = 0; h < kAttnMaxGroup; ++h) {
             if (h < (int)G) {
-                float o = acc[h];
-#pragma unroll
-                for (int k = 1; k < PARTS; ++k) o += red[((k - 1) * HD + d) * kAttnMaxGroup + h];
-                po[h * HD + d] = o;
+                const uint32_t o = (uint32_t)h * HD + d, j = o / S;
+                *cluster.map_shared_rank(rpo + rank * S + (o - j * S), j) = acc[h];
             }
         }
     }
-    cluster.sync();  // every CTA's (pm, pl, po) is final and visible to the cluster
-
-    // Remote loads are issued together (unrolled over the largest cluster),
-    // so each merge step waits for one distributed-shared-memory round trip.
-    if (tid < (int)G) {
-        const uint32_t h = tid;
-        float mc[kCAttnMaxCluster], lc[kCAttnMaxCluster];
-#pragma unroll
-        for (uint32_t c = 0; c < kCAttnMaxCluster; ++c) {
-            mc[c] = c < C ? *cluster.map_shared_rank(pm + h, c) : -INFINITY;
-            lc[c] = c < C ? *cluster.map_shared_rank(pl + h, c) : 0.f;
-        }
-        float M = -INFINITY;
-#pragma unroll
-        for (uint32_t c = 0; c < kCAttnMaxCluster; ++c) M = fmaxf(M, mc[c]);
-        float L = 0.f;
-#pragma unroll
-        for (uint32_t c = 0; c < kCAttnMaxCluster; ++c) {
-            mc[c] = mc[c] == -INFINITY ? 0.f : expf(mc[c] - M);
-            L = fmaf(mc[c], lc[c], L);
-        }
-#pragma unroll
-        for (uint32_t c = 0; c < kCAttnMaxCluster; ++c) wts[h * kCAttnMaxCluster + c] = mc[c] / L;
+    for (uint32_t i = tid; i < C * G; i += kCAttnThreads) {
+        const uint32_t j = i / G, h = i % G;
+        *cluster.map_shared_rank(rm + rank * G + h, j) = pm[h];
+        *cluster.map_shared_rank(rl + rank * G + h, j) = pl[h];
     }
     __syncthreads();
-    for (uint32_t o = rank * kCAttnThreads + tid; o < G * HD; o += C * kCAttnThreads) {
-        const uint32_t h = o / HD;
-        float pc[kCAttnMaxCluster];
-#pragma unroll
-        for (uint32_t c = 0; c < kCAttnMaxCluster; ++c) pc[c] = c < C ? *cluster.map_shared_rank(po + o, c) : 0.f;
+    if ((uint32_t)tid < C) {
+        asm volatile("fence.acq_rel.cluster;" ::: "memory");
+        mbar_arrive_remote(&mrg, tid);
+    }
+    cluster_arrive_release();  // matched at the end: peers stay alive until every push has landed
+    // merge this CTA's slice once all C partials are here
+    if (!mbar_wait_cluster(&mrg, 0)) {
+        ok = false;
+        if (tid == 0 && a.err) atomicOr(a.err, 4u);
+    }
+    // weights of the C partials per head: warp h, lane c
+    for (uint32_t h = warp; h < G; h += nw) {
+        const float mc = (uint32_t)lane < C ? rm[lane * G + h] : -INFINITY;
+        const float lc = (uint32_t)lane < C ? rl[lane * G + h] : 0.f;
+        const float M = warp_max(mc);
+        const float e = mc == -INFINITY ? 0.f : expf(mc - M);
+        const float L = warp_sum(e * lc);
+        if ((uint32_t)lane < C) wts[h * kCAttnMaxCluster + lane] = e / L;
+    }
+    __syncthreads();
+    for (uint32_t ol = tid; ol < S; ol += kCAttnThreads) {
+        const uint32_t o = rank * S + ol;
+        if (o >= G * HD) break;
+        const float* w = wts + (o / HD) * kCAttnMaxCluster;
         float O = 0.f;
-#pragma unroll
-        for (uint32_t c = 0; c < kCAttnMaxCluster; ++c) O = fmaf(wts[h * kCAttnMaxCluster + c], pc[c], O);
+        for (uint32_t c = 0; c < C; ++c) O = fmaf(w[c], rpo[c * S + ol], O);
         a.out[(size_t)g * G * HD + o] = O;
     }
-    cluster.sync();  // peers may still be reading this CTA's shared memory
+    cluster_wait();
     if (tid == 0) trace_mark(a.trace, 2);
 }
 

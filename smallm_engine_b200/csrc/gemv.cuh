@@ -143,20 +143,37 @@ __device__ __forceinline__ void build_xrec_lane(float4 q, int lane, bool act, ui
     }
     const bool finite = m <= 3.4028235e38f;  // false for inf and NaN
     if (!finite || m < 1e-30f) m = 0.f;      // tiny blocks contribute below f32 resolution
-    int e = 0;
-    frexpf(m, &e);  // m = f * 2^e, f in [0.5, 1): 2^e > m
-    const float up = m > 0.f ? ldexpf(1.0f, B - e) : 0.f;
+    // m = f * 2^e with f in [0.5, 1) (m is 0 or normal): e = biased exponent - 126,
+    // so 2^e > m; 2^(B-e) and the record's scale are built from their exponent
+    // bits (both stay in the normal range for 1e-30 <= m <= FLT_MAX)
+    const int e = (int)((__float_as_uint(m) >> 23) & 0xFFu) - 126;
+    const float up = m > 0.f ? __uint_as_float((uint32_t)(B - e + 127) << 23) : 0.f;
+    // X = rint(x * 2^(B-e)): x * 2^(B-e) is exact and |X| <= 2^B < 2^22, so
+    // one FMA with 1.5 * 2^23 rounds it (ties to even) into the low mantissa
+    // bits: bits = 0x4B400000 + X, and the low bytes of bits are those of X
+    constexpr float kMagic = 12582912.0f;
+    constexpr uint32_t kMagicBits = 0x4B400000u;
     const float v[4] = {q.x, q.y, q.z, q.w};
-    uint32_t p[ND] = {};
-    int sx = 0;
+    uint32_t bits[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        int X = __float2int_rn(v[k] * up);  // exact scaling by a power of two, |X| <= 2^B
-        if constexpr (ND == 2) {
-            X = min(X, 32767);  // x * up < 2^15 may round up to 2^15
-            p[0] |= (uint32_t)(X & 0xFF) << (8 * k);         // unsigned low digit
-            p[1] |= (uint32_t)((X >> 8) & 0xFF) << (8 * k);  // signed high digit
-        } else {
+        float r = fmaf(v[k], up, kMagic);
+        if constexpr (ND == 2) r = fminf(r, kMagic + 32767.0f);  // x * up < 2^15 may round up to 2^15
+        bits[k] = __float_as_uint(r);
+    }
+    uint32_t p[ND];
+    if constexpr (ND == 2) {
+        // unsigned low digit = byte 0 of X, signed high digit = byte 1
+        const uint32_t t01 = __byte_perm(bits[0], bits[1], 0x5140);  // X0.b0 X1.b0 X0.b1 X1.b1
+        const uint32_t t23 = __byte_perm(bits[2], bits[3], 0x5140);
+        p[0] = __byte_perm(t01, t23, 0x5410);
+        p[1] = __byte_perm(t01, t23, 0x7632);
+    } else {
+#pragma unroll
+        for (int d = 0; d < ND; ++d) p[d] = 0u;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {  // balanced digits: X = D2 2^16 + D1 2^8 + D0
+            const int X = (int)(bits[k] - kMagicBits);
             const int a0 = (int)(int8_t)(X & 0xFF);
             const int X1 = (X - a0) >> 8;
             const int a1 = (int)(int8_t)(X1 & 0xFF);
@@ -165,8 +182,8 @@ __device__ __forceinline__ void build_xrec_lane(float4 q, int lane, bool act, ui
             p[1] |= (uint32_t)(a1 & 0xFF) << (8 * k);
             p[2] |= (uint32_t)(a2 & 0xFF) << (8 * k);
         }
-        sx += X;
     }
+    int sx = (int)((bits[0] + bits[1]) + (bits[2] + bits[3]) - 4u * kMagicBits);
     sx += __shfl_xor_sync(0xffffffffu, sx, 1);
     sx += __shfl_xor_sync(0xffffffffu, sx, 2);  // lanes 0-3: elements 0-15, lanes 4-7: 16-31
     const int sx_other = __shfl_xor_sync(0xffffffffu, sx, 4);
@@ -180,7 +197,8 @@ __device__ __forceinline__ void build_xrec_lane(float4 q, int lane, bool act, ui
             const int scale_e = e - B - (ND == 2 ? 4 : 0);
             w[8 * ND] = (uint32_t)sx;
             w[8 * ND + 1] = (uint32_t)sx_other;
-            reinterpret_cast<float*>(w)[8 * ND + 2] = !finite ? nan : (m > 0.f ? ldexpf(1.0f, scale_e) : 0.f);
+            const float scale = __uint_as_float((uint32_t)(scale_e + 127) << 23);
+            reinterpret_cast<float*>(w)[8 * ND + 2] = !finite ? nan : (m > 0.f ? scale : 0.f);
             reinterpret_cast<float*>(w)[8 * ND + 3] = !finite ? nan : s;
         }
     }
@@ -568,6 +586,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
 #pragma unroll
         for (int k = 0; k < kB; ++k) {
             const uint32_t g = g0 + ctid + k * kStride;
+            // a warp whose first granule lies past the end has no block here
+            // (warp-uniform, so the shuffles inside stay whole-warp)
+            if (g0 + (uint32_t)warp * 32 + k * kStride >= ngr) continue;
             const bool act = g < ngr;
             float4 q = xq[k];
             if constexpr (kRms) {
