@@ -67,6 +67,7 @@ struct GemvParams {
     uint32_t gsize;     // warps per group; they split each tile's K-units
     uint32_t kring;     // stages per ring
     uint32_t xbytes;    // bytes of the staged x region
+    uint32_t hold;      // the producer's j-th tile per ring waits for x to be staged (~0u: never)
     // input vector and fused RMSNorm
     const float* x;
     const float* norm_w;
@@ -473,7 +474,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     uint64_t* full = reinterpret_cast<uint64_t*>(stage0 + (size_t)p.stages * sbytes);
     uint64_t* empty = full + p.stages;
     uint64_t* done = empty + p.stages;
-    float* red = reinterpret_cast<float*>(done + p.stages);             // [kGemvConsumerWarps]
+    uint64_t* xready = done + p.stages;                                 // x records staged
+    float* red = reinterpret_cast<float*>(xready + 1);                  // [kGemvConsumerWarps]
     unsigned long long* best_sh = reinterpret_cast<unsigned long long*>(red + kGemvConsumerWarps);
     float* part = reinterpret_cast<float*>(best_sh + kGemvConsumerWarps);  // [stages][gsize][4]
 
@@ -488,6 +490,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
             mbar_init(&empty[s], 1);
             mbar_init(&done[s], G);
         }
+        mbar_init(xready, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -499,12 +502,20 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     if (warp == kGemvConsumerWarps) {
         // ---------------- producer: weights do not depend on the previous kernel
         // lane g feeds ring g: the group's j-th tile (CTA tile g + j*NG) goes
-        // to stage g*K + j%K once the group has released that stage
+        // to stage g*K + j%K once the group has released that stage.  When
+        // the ring cannot hold all of the CTA's tiles anyway, only the first
+        // tile per ring is fetched before the consumers have staged x (tile
+        // p.hold onwards waits): a full ring's burst would queue the x loads
+        // behind it.
         if ((uint32_t)lane < NG) {
             const uint32_t g = lane;
             uint32_t j = 0;
             for (uint32_t t = blockIdx.x + g * gridDim.x; t < ntiles; t += NG * gridDim.x, ++j) {
                 const uint32_t s = g * K + j % K;
+                if (j == p.hold && !mbar_wait(xready, 0)) {
+                    atomicOr(p.err, 1u);
+                    break;
+                }
                 if (j >= K && !mbar_wait(&empty[s], ((j / K) - 1) & 1)) {
                     atomicOr(p.err, 1u);  // consumers then time out once and skip their work
                     break;
@@ -522,8 +533,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     // epilogue multiplies each row result by 1/rms, so x is read only once.
     // 8 consecutive lanes own the 8 float4 granules of one 32-element block;
     // loads are issued in batches of kB granules per thread before any of them
-    // is used, and the norm weights (constant) are fetched before the wait.
-    constexpr int kB = 4;
+    // is used (one batch covers 8192 columns with the norm, 16384 without),
+    // and the norm weights (constant) are fetched before the wait.
+    constexpr int kB = PRO == PRO_PLAIN ? 8 : 4;
     constexpr uint32_t kStride = kGemvConsumerWarps * 32;
     const float4* x4 = reinterpret_cast<const float4*>(p.x);
     const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
@@ -613,6 +625,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         if (lane == 0) red[warp] = ss;
     }
     consumers_sync();
+    if (ctid == 0) mbar_arrive(xready);  // the producer may fill the rest of the rings
     if constexpr (kRms) {
         float t = 0.f;
 #pragma unroll
