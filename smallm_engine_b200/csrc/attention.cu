@@ -320,7 +320,11 @@ __global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const 
         trace_mark(a.trace, 0);
         mbar_init(&bar, 1);
         mbar_init(&bar_pre, 1);
-        mbar_init(&mrg, C);
+        mbar_init(&mrg, 1);
+        // the merge barrier completes when every peer's pushed bytes are in:
+        // (its slice of outputs + its (max, sum) per head) from each of the C CTAs
+        const uint32_t lo = min(G * HD, rank * S), slice = min(S, G * HD - lo);
+        mbar_arrive_expect_tx(&mrg, C * (slice + 2 * G) * 4);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     cluster_arrive_relaxed();  // matched by the cluster_wait before the first push
@@ -354,7 +358,10 @@ __global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const 
     const uint32_t n = *a.pos + 1;
     const uint32_t per = (n + C - 1) / C;
     const uint32_t t_begin = min(n, rank * per), t_end = min(n, t_begin + per);
-    for (uint32_t i = tid; i < G * HD; i += kCAttnThreads) qs[i] = a.q[(size_t)g * G * HD + i];
+    {
+        const float4* q4 = reinterpret_cast<const float4*>(a.q + (size_t)g * G * HD);
+        for (uint32_t i = tid; i < G * HD / 4; i += kCAttnThreads) reinterpret_cast<float4*>(qs)[i] = q4[i];
+    }
     if (tid < kAttnMaxGroup) {
         pm[tid] = -INFINITY;
         pl[tid] = 0.f;
@@ -478,29 +485,26 @@ __global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const 
     }
     __syncthreads();  // pm / pl final
     cluster_wait();   // every peer's merge barrier is initialised
-    // push this CTA's partial: output h*HD + d to the CTA merging it, row `rank`
+    // push this CTA's partial with asynchronous remote stores that count
+    // their bytes on the receiver's merge barrier: output h*HD + d to the CTA
+    // merging it (row `rank` of its slice table), (max, sum) to every CTA
     if (part == 0) {
 #pragma unroll
         for (int h = 0; h < kAttnMaxGroup; ++h) {
             if (h < (int)G) {
                 const uint32_t o = (uint32_t)h * HD + d, j = o / S;
-                *cluster.map_shared_rank(rpo + rank * S + (o - j * S), j) = acc[h];
+                st_async_remote(rpo + rank * S + (o - j * S), j, acc[h], &mrg);
             }
         }
     }
     for (uint32_t i = tid; i < C * G; i += kCAttnThreads) {
         const uint32_t j = i / G, h = i % G;
-        *cluster.map_shared_rank(rm + rank * G + h, j) = pm[h];
-        *cluster.map_shared_rank(rl + rank * G + h, j) = pl[h];
-    }
-    __syncthreads();
-    if ((uint32_t)tid < C) {
-        asm volatile("fence.acq_rel.cluster;" ::: "memory");
-        mbar_arrive_remote(&mrg, tid);
+        st_async_remote(rm + rank * G + h, j, pm[h], &mrg);
+        st_async_remote(rl + rank * G + h, j, pl[h], &mrg);
     }
     cluster_arrive_release();  // matched at the end: peers stay alive until every push has landed
     // merge this CTA's slice once all C partials are here
-    if (!mbar_wait_cluster(&mrg, 0)) {
+    if (!mbar_wait(&mrg, 0)) {
         ok = false;
         if (tid == 0 && a.err) atomicOr(a.err, 4u);
     }

@@ -236,30 +236,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
         if (clock64() - t0 > (1ll << 31)) return false;
     }
 }
-// The same wait with cluster-scope acquire: the phase was completed by
-// arrivals of other CTAs of the cluster (mbar_arrive_remote), and their
-// distributed-shared-memory stores before those arrivals are visible after it.
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
-    const uint32_t a = smem_u32(bar);
-    const long long t0 = clock64();
-    for (;;) {
-        uint32_t ok;
-        asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n"
-            " selp.u32 %0, 1, 0, p;\n}"
-            : "=r"(ok)
-            : "r"(a), "r"(parity), "r"(1000000u)
-            : "memory");
-        if (ok) return true;
-        if (clock64() - t0 > (1ll << 31)) return false;
-    }
-}
-// Arrive (release, cluster scope) on the barrier at the same shared-memory
-// offset in CTA `rank` of this cluster.
-__device__ __forceinline__ void mbar_arrive_remote(uint64_t* bar, uint32_t rank) {
-    uint32_t remote;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(bar)), "r"(rank));
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+// Asynchronous store of one float into CTA `rank`'s shared memory at the
+// offset of `p` in this CTA, completing 4 bytes on that CTA's barrier at the
+// offset of `bar` (the receiver expects the bytes with mbar_arrive_expect_tx
+// and sees the data once the phase completes).
+__device__ __forceinline__ void st_async_remote(float* p, uint32_t rank, float v, uint64_t* bar) {
+    uint32_t ra, rb;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(p)), "r"(rank));
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rb) : "r"(smem_u32(bar)), "r"(rank));
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(ra),
+                 "r"(__float_as_uint(v)), "r"(rb)
+                 : "memory");
 }
 // Split cluster barrier (every thread of every CTA of the cluster executes
 // both, arrive first).

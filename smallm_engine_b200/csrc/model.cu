@@ -60,6 +60,7 @@ Model::~Model() {
     for (QMat* m : all_mats()) qmat_free(*m);
     for (void* p : allocs) cudaFree(p);
     if (h_st) cudaFreeHost(h_st);
+    if (h_err) cudaFreeHost(h_err);
     if (stream) cudaStreamDestroy(stream);
 }
 
@@ -328,6 +329,8 @@ void Model::load(const std::string& path, const smallm_model_opts& o) {
     ids = static_cast<uint32_t*>(dalloc(4ull * ids_cap));
     SM_CUDA(cudaHostAlloc(&h_st, sizeof(DecodeState), cudaHostAllocDefault));
     std::memset(h_st, 0, sizeof(DecodeState));
+    SM_CUDA(cudaHostAlloc(&h_err, 4, cudaHostAllocDefault));
+    *h_err = 0;
 
     if (tp_size > 1) {
         if (!o.nccl_id) throw Error(1, "tensor parallel load needs an NCCL unique id");
@@ -538,7 +541,9 @@ void Model::trace_step(uint32_t token, uint32_t pos, std::vector<TraceSlot>& out
     SM_CUDA(cudaGraphLaunch(trace_exec, stream));
     out.resize(n);
     SM_CUDA(cudaMemcpyAsync(out.data(), trace_dev, sizeof(TraceSlot) * n, cudaMemcpyDeviceToHost, stream));
+    SM_CUDA(cudaMemcpyAsync(h_err, device_error_flag(), 4, cudaMemcpyDeviceToHost, stream));
     SM_CUDA(cudaStreamSynchronize(stream));
+    check_step_errors();
     cached = pos + 1;
 }
 
@@ -561,9 +566,20 @@ void Model::forward(uint32_t token, uint32_t pos, float* out_logits, uint32_t* o
         SM_CUDA(cudaMemcpyAsync(out_logits, logits, 4ull * vocab, cudaMemcpyDeviceToHost, stream));
     }
     if (out_argmax) SM_CUDA(cudaMemcpyAsync(h_st, st, sizeof(DecodeState), cudaMemcpyDeviceToHost, stream));
+    SM_CUDA(cudaMemcpyAsync(h_err, device_error_flag(), 4, cudaMemcpyDeviceToHost, stream));
     SM_CUDA(cudaStreamSynchronize(stream));
+    check_step_errors();
     if (out_argmax) *out_argmax = h_st->token;
     cached = pos + 1;
+}
+
+void Model::check_step_errors() {
+    const unsigned int e = *h_err;
+    if (!e) return;
+    *h_err = 0;
+    gemv_error_flags(true);
+    throw Error(SMALLM_ERR_CUDA, "a bounded device wait gave up during the step (flags " + std::to_string(e) +
+                                     "); its results are invalid");
 }
 
 void Model::decode_async(uint32_t token, uint32_t pos, uint32_t n_steps) {
@@ -705,7 +721,9 @@ uint32_t Model::sample(uint32_t kind, uint32_t k, float p, float temperature, fl
 void Model::decode_ids(uint32_t* out, uint32_t n) {
     if (n > pending_steps) throw Error(1, "fewer decode steps were run than ids requested");
     SM_CUDA(cudaMemcpyAsync(out, ids, 4ull * n, cudaMemcpyDeviceToHost, stream));
+    SM_CUDA(cudaMemcpyAsync(h_err, device_error_flag(), 4, cudaMemcpyDeviceToHost, stream));
     SM_CUDA(cudaStreamSynchronize(stream));
+    check_step_errors();
 }
 
 }  // namespace smallm

@@ -57,6 +57,7 @@ struct Model {
     unsigned int* epoch = nullptr;         // steps run, identical on every rank
     DecodeState* st = nullptr;
     DecodeState* h_st = nullptr;
+    unsigned int* h_err = nullptr;  // pinned copy of the device error word after a step
     unsigned long long* keys = nullptr;
     uint32_t* ids = nullptr;
     uint32_t ids_cap = 0;
@@ -105,6 +106,9 @@ private:
     std::vector<QMat*> all_mats();
     void capture(cudaGraphExec_t* out, TraceSlot* trace);
     void set_state(uint32_t token, uint32_t pos);
+    // After a synchronised step: raise if a bounded device wait gave up (the
+    // step's results are then invalid).
+    void check_step_errors();
 };
 
 }  // namespace smallm
