@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const 
     constexpr int DV = DL / 4;                 // ... as float4
     extern __shared__ __align__(128) float sm[];
     __shared__ __align__(8) uint64_t bar, bar_pre, mrg;
-    __shared__ uint32_t pre_n, pre_rows;
+    __shared__ uint32_t pre_n, pre_rows, post_n, early;
     cg::cluster_group cluster = cg::this_cluster();
     const uint32_t C = cluster.num_blocks();
     const uint32_t rank = cluster.block_rank();
@@ -354,10 +354,28 @@ __global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const 
         pre_rows = rows;
     }
     pdl_wait();
-    if (tid == 0) trace_mark(a.trace, 1);
-    const uint32_t n = *a.pos + 1;
-    const uint32_t per = (n + C - 1) / C;
-    const uint32_t t_begin = min(n, rank * per), t_end = min(n, t_begin + per);
+    if (tid == 0) {
+        trace_mark(a.trace, 1);
+        // the rest of the first chunk (from the row the QKV kernel has just
+        // written) is copied right away, overlapping the q load
+        const uint32_t n1 = *a.pos + 1;
+        uint32_t e = 0;
+        if (n1 == pre_n) {
+            const uint32_t per1 = (n1 + C - 1) / C;
+            const uint32_t b1 = min(n1, rank * per1), e1 = min(n1, b1 + per1);
+            const uint32_t len1 = min(kCAttnChunk, e1 - b1);
+            if (pre_rows < len1) {
+                const uint32_t bytes = (len1 - pre_rows) * HD * 4;
+                const size_t off = ((size_t)g * a.max_ctx + b1 + pre_rows) * HD;
+                mbar_arrive_expect_tx(&bar, 2 * bytes);
+                bulk_g2s(ks + pre_rows * HD, a.kcache + off, bytes, &bar);
+                bulk_g2s(vs + pre_rows * HD, a.vcache + off, bytes, &bar);
+                e = 1;
+            }
+        }
+        post_n = n1;
+        early = e;
+    }
     {
         const float4* q4 = reinterpret_cast<const float4*>(a.q + (size_t)g * G * HD);
         for (uint32_t i = tid; i < G * HD / 4; i += kCAttnThreads) reinterpret_cast<float4*>(qs)[i] = q4[i];
@@ -367,8 +385,12 @@ __global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const 
         pl[tid] = 0.f;
     }
     bool ok = true;
-    __syncthreads();  // pre_n / pre_rows
-    uint32_t have = 0;  // rows of the first chunk already in shared memory
+    __syncthreads();  // pre_n / pre_rows / post_n / early
+    const uint32_t n = post_n;
+    const uint32_t per = (n + C - 1) / C;
+    const uint32_t t_begin = min(n, rank * per), t_end = min(n, t_begin + per);
+    uint32_t have = 0;  // rows of the first chunk already in shared memory (or on their way: issued)
+    uint32_t issued = early;
     if (pre_rows) {
         // the copy issued before the wait lands before anything else is
         // staged over it (even when the position changed and it is dropped)
@@ -384,11 +406,11 @@ __global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const 
 #pragma unroll
     for (int h = 0; h < kAttnMaxGroup; ++h) acc[h] = 0.f;
     uint32_t phase = 0;
-    for (uint32_t c0 = t_begin; c0 < t_end; c0 += kCAttnChunk, have = 0) {
+    for (uint32_t c0 = t_begin; c0 < t_end; c0 += kCAttnChunk, have = 0, issued = 0) {
         const uint32_t len = min(kCAttnChunk, t_end - c0);
         __syncthreads();  // the previous chunk's K/V/scores are no longer read (and q is staged)
         if (have < len) {
-            if (tid == 0) {
+            if (tid == 0 && !issued) {
                 const uint32_t bytes = (len - have) * HD * 4;
                 const size_t off = ((size_t)g * a.max_ctx + c0 + have) * HD;
                 mbar_arrive_expect_tx(&bar, 2 * bytes);
