@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const 
     constexpr int DV = DL / 4;                 // ... as float4
     extern __shared__ __align__(128) float sm[];
     __shared__ __align__(8) uint64_t bar, bar_pre, mrg;
-    __shared__ uint32_t pre_n, pre_rows, post_n, early;
+    __shared__ uint32_t pre_n, pre_rows, early;
     cg::cluster_group cluster = cg::this_cluster();
     const uint32_t C = cluster.num_blocks();
     const uint32_t rank = cluster.block_rank();
@@ -358,22 +358,19 @@ __global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const 
         trace_mark(a.trace, 1);
         // the rest of the first chunk (from the row the QKV kernel has just
         // written) is copied right away, overlapping the q load
-        const uint32_t n1 = *a.pos + 1;
+        const uint32_t n1 = pre_n;
+        const uint32_t per1 = (n1 + C - 1) / C;
+        const uint32_t b1 = min(n1, rank * per1), e1 = min(n1, b1 + per1);
+        const uint32_t len1 = min(kCAttnChunk, e1 - b1);
         uint32_t e = 0;
-        if (n1 == pre_n) {
-            const uint32_t per1 = (n1 + C - 1) / C;
-            const uint32_t b1 = min(n1, rank * per1), e1 = min(n1, b1 + per1);
-            const uint32_t len1 = min(kCAttnChunk, e1 - b1);
-            if (pre_rows < len1) {
-                const uint32_t bytes = (len1 - pre_rows) * HD * 4;
-                const size_t off = ((size_t)g * a.max_ctx + b1 + pre_rows) * HD;
-                mbar_arrive_expect_tx(&bar, 2 * bytes);
-                bulk_g2s(ks + pre_rows * HD, a.kcache + off, bytes, &bar);
-                bulk_g2s(vs + pre_rows * HD, a.vcache + off, bytes, &bar);
-                e = 1;
-            }
+        if (pre_rows < len1) {
+            const uint32_t bytes = (len1 - pre_rows) * HD * 4;
+            const size_t off = ((size_t)g * a.max_ctx + b1 + pre_rows) * HD;
+            mbar_arrive_expect_tx(&bar, 2 * bytes);
+            bulk_g2s(ks + pre_rows * HD, a.kcache + off, bytes, &bar);
+            bulk_g2s(vs + pre_rows * HD, a.vcache + off, bytes, &bar);
+            e = 1;
         }
-        post_n = n1;
         early = e;
     }
     {
@@ -385,20 +382,20 @@ __global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const 
         pl[tid] = 0.f;
     }
     bool ok = true;
-    __syncthreads();  // pre_n / pre_rows / post_n / early
-    const uint32_t n = post_n;
+    __syncthreads();  // pre_n / pre_rows / early
+    // The position read before the wait is the step's: only the step's last
+    // kernel advances it (checked once more at the end).
+    const uint32_t n = pre_n;
     const uint32_t per = (n + C - 1) / C;
     const uint32_t t_begin = min(n, rank * per), t_end = min(n, t_begin + per);
     uint32_t have = 0;  // rows of the first chunk already in shared memory (or on their way: issued)
     uint32_t issued = early;
     if (pre_rows) {
-        // the copy issued before the wait lands before anything else is
-        // staged over it (even when the position changed and it is dropped)
         if (!mbar_wait(&bar_pre, 0)) {
             ok = false;
             if (tid == 0 && a.err) atomicOr(a.err, 4u);
         }
-        if (pre_n == n) have = pre_rows;
+        have = pre_rows;
     }
     const float scale = 1.0f / sqrtf((float)HD);
     const int d = tid % HD, part = tid / HD;
@@ -549,6 +546,8 @@ __global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const 
         a.out[(size_t)g * G * HD + o] = O;
     }
     cluster_wait();
+    if (tid == 0 && a.err && min(*(volatile const uint32_t*)a.pos + 1, a.max_ctx) != pre_n)
+        atomicOr(a.err, 32u);  // the position moved during the step: results invalid
     if (tid == 0) trace_mark(a.trace, 2);
 }
 
