@@ -551,6 +551,10 @@ __global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const 
     if (tid == 0) trace_mark(a.trace, 2);
 }
 
+size_t attention_cluster_smem(uint32_t n_heads, uint32_t n_kv, uint32_t hd) {
+    return 4 * cattn_smem_floats(n_heads / n_kv, hd);
+}
+
 static const void* cattn_fn(uint32_t hd) {
     if (hd == 32) return (const void*)attention_cluster_kernel<32>;
     if (hd == 64) return (const void*)attention_cluster_kernel<64>;

@@ -101,6 +101,11 @@ struct GemvArgs {
     unsigned int* done_ctr = nullptr;
     const unsigned int* epoch = nullptr;
     uint32_t tp = 1;
+    // Shared memory the launch may use (0: the 227 KB limit).  The decode
+    // step caps the QKV and O GEMVs so the attention kernel's CTAs fit next
+    // to theirs (it stages cached K/V while the QKV GEMV runs, and the O
+    // GEMV prefetches weights while attention runs).
+    size_t smem_cap = 0;
 };
 
 void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_t stream, bool pdl = false);
@@ -108,10 +113,10 @@ void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_
 // Pipeline shape the GEMV uses for a matrix: rows per tile, stages of the
 // shared-memory ring, bytes of staged x, total dynamic shared memory.
 struct GemvPlan {
-    uint32_t rt = 0, stages = 0, ngroups = 0, gsize = 0, kring = 0;
+    uint32_t rt = 0, stages = 0, ngroups = 0, gsize = 0, kring = 0, warps = 0;
     size_t xbytes = 0, smem = 0;
 };
-GemvPlan gemv_plan(const QMat& m);
+GemvPlan gemv_plan(const QMat& m, size_t smem_cap = 0);
 
 // Error bits raised by GEMV kernels whose bounded waits gave up (0 = none).
 unsigned int gemv_error_flags(bool clear);
@@ -165,6 +170,8 @@ void launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl = false);
 // picks the largest C <= 16 the device can schedule (and sets the kernel's
 // attributes on the current device).
 uint32_t attention_cluster_size(uint32_t n_heads, uint32_t n_kv, uint32_t hd);
+// Dynamic shared memory of one cluster-attention CTA.
+size_t attention_cluster_smem(uint32_t n_heads, uint32_t n_kv, uint32_t hd);
 void launch_attention_cluster(const AttnArgs& a, uint32_t C, cudaStream_t stream, bool pdl);
 // The split-K kernel with its scratch in a static array of attention.cu (no
 // allocation; calls that overlap in time race on it).

@@ -7,8 +7,8 @@
 // producer warp streams tiles into an S-stage shared-memory ring with
 // cp.async.bulk (completion through mbarrier transaction counts).
 //
-// Compute side -- warp groups with private rings.  A tile is 4 rows.  The 16
-// consumer warps form NG groups of G warps; group g owns a ring of k stages
+// Compute side -- warp groups with private rings.  A tile is 4 rows.  The W
+// consumer warps (Fmt::WARPS) form NG groups of G warps; group g owns a ring of k stages
 // and takes tiles g, g+NG, g+2NG, ..., its j-th tile landing in stage
 // g*k + j%k, so every mbarrier wait is on the next phase of a stage only
 // that group uses (parity waits are only unambiguous that way).  Producer
@@ -49,8 +49,12 @@ enum { PRO_PLAIN = 0, PRO_RMS = 1, PRO_RMS_SUM = 2 };
 enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4, EPI_PEER = 5 };
 constexpr int kMaxTP = 8;
 
-constexpr int kGemvConsumerWarps = 16;
-constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;  // + one producer warp
+// Consumer warps per CTA (one producer warp more): 22 for Q4_0, which fits
+// 72 registers per thread and still leaves room on the SM for the decode
+// attention's CTAs next to a QKV GEMV's (more warps hide the shared-memory
+// latency of the dot loop and share the x staging); 16 for the formats whose
+// dot needs more registers.
+constexpr int kGemvMaxWarps = 22;
 constexpr int kMaxRT = 32;                                   // storage rows pad to this
 
 struct GemvParams {
@@ -241,7 +245,7 @@ __device__ __forceinline__ float combine(int s0, int s1, int s2) {
 // Q4_0: element i of a block is the low nibble of byte i, element i+16 the
 // high nibble (src/core/tensor.cpp:57-63); value (q - 8) * d.
 struct FmtQ4_0 {
-    static constexpr int UE = 32, SUBS = 1, ND = 2;
+    static constexpr int UE = 32, SUBS = 1, ND = 2, WARPS = 22;
     static constexpr bool F32X = false;
     struct Raw { uint4 q; uint32_t s; };
     __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t units, Raw& r) {
@@ -267,7 +271,7 @@ struct FmtQ4_0 {
 
 // Q8_0: int8 codes; value q * d.
 struct FmtQ8_0 {
-    static constexpr int UE = 32, SUBS = 1, ND = 3;
+    static constexpr int UE = 32, SUBS = 1, ND = 3, WARPS = 16;
     static constexpr bool F32X = false;
     struct Raw { uint4 a, b; uint32_t s; };
     __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t units, Raw& r) {
@@ -298,7 +302,7 @@ struct FmtQ8_0 {
 // nibbles of qs[32k..32k+32), sub-block 2k+1 = high nibbles.
 // Value: (d*sc)*q - dmin*m (gguf-py Q4_K.dequantize_blocks).
 struct FmtQ4K {
-    static constexpr int UE = 64, SUBS = 2, ND = 2;
+    static constexpr int UE = 64, SUBS = 2, ND = 2, WARPS = 16;
     static constexpr bool F32X = false;
     struct Raw { uint4 h, a, b; };
     __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t, Raw& r) {
@@ -344,7 +348,7 @@ struct FmtQ4K {
 // 6-7); 4 int8 scales per unit (element e of a super-block uses scale e/16);
 // f16 d per super-block.  Value: (d*sc)*(q - 32) (src/core/tensor.cpp:97-106).
 struct FmtQ6K {
-    static constexpr int UE = 64, SUBS = 2, ND = 3;
+    static constexpr int UE = 64, SUBS = 2, ND = 3, WARPS = 16;
     static constexpr bool F32X = false;
     struct Raw { uint4 n0, n1, hb; uint32_t sc; uint32_t d; };
     __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t units, Raw& r) {
@@ -388,13 +392,14 @@ struct FmtQ6K {
 // F32 (the reference's catch-all branch, ops.cpp:289-299): plain f32 FMAs
 // against an f32 copy of x.
 struct FmtF32 {
-    static constexpr int UE = 32, SUBS = 1, ND = 3;
+    static constexpr int UE = 32, SUBS = 1, ND = 3, WARPS = 16;
     static constexpr bool F32X = true;
 };
 
 // Named barrier over the consumer warps only (the producer never joins).
+template <int W>
 __device__ __forceinline__ void consumers_sync() {
-    asm volatile("bar.sync 1, %0;" ::"n"(kGemvConsumerWarps * 32) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(W * 32) : "memory");
 }
 
 // Fused epilogue of one finished row (v = the row's W.x after 1/rms).  The
@@ -466,7 +471,8 @@ __device__ __forceinline__ void gemv_epilogue_row(const GemvParams& p, uint32_t 
 // ------------------------------------------------------------------ kernel --
 
 template <class Fmt, int PRO, int EPI>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__((Fmt::WARPS + 1) * 32, 1) gemv_kernel(const GemvParams p) {
+    constexpr int W = Fmt::WARPS;  // consumer warps; warp W is the producer
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* xreg = smem;                                   // x records (or f32 x)
     uint8_t* stage0 = smem + p.xbytes;                      // S stages
@@ -475,9 +481,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     uint64_t* empty = full + p.stages;
     uint64_t* done = empty + p.stages;
     uint64_t* xready = done + p.stages;                                 // x records staged
-    float* red = reinterpret_cast<float*>(xready + 1);                  // [kGemvConsumerWarps]
-    unsigned long long* best_sh = reinterpret_cast<unsigned long long*>(red + kGemvConsumerWarps);
-    float* part = reinterpret_cast<float*>(best_sh + kGemvConsumerWarps);  // [stages][gsize][4]
+    float* red = reinterpret_cast<float*>(xready + 1);                  // [kGemvMaxWarps]
+    unsigned long long* best_sh = reinterpret_cast<unsigned long long*>(red + kGemvMaxWarps);
+    float* part = reinterpret_cast<float*>(best_sh + kGemvMaxWarps);   // [stages][gsize][4]
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t ntiles = p.rows_pad / p.rt;
@@ -499,7 +505,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     // start streaming weights while this kernel drains
     pdl_launch_dependents();
 
-    if (warp == kGemvConsumerWarps) {
+    if (warp == W) {
         // ---------------- producer: weights do not depend on the previous kernel
         // lane g feeds ring g: the group's j-th tile (CTA tile g + j*NG) goes
         // to stage g*K + j%K once the group has released that stage.  When
@@ -528,7 +534,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     }
 
     // ---------------- consumers: stage x (after the producer of x finished)
-    const int ctid = tid;  // 0 .. 32 * kGemvConsumerWarps - 1
+    const int ctid = tid;  // 0 .. 32 * W - 1
     // RMSNorm is linear in x given its scalar: the records hold x * w and the
     // epilogue multiplies each row result by 1/rms, so x is read only once.
     // 8 consecutive lanes own the 8 float4 granules of one 32-element block;
@@ -536,7 +542,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     // is used (one batch covers 8192 columns with the norm, 16384 without),
     // and the norm weights (constant) are fetched before the wait.
     constexpr int kB = PRO == PRO_PLAIN ? 8 : 4;
-    constexpr uint32_t kStride = kGemvConsumerWarps * 32;
+    constexpr uint32_t kStride = W * 32;
     const float4* x4 = reinterpret_cast<const float4*>(p.x);
     const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
     const uint32_t ngr = p.cols / 4;  // a multiple of 8: whole blocks are in or out
@@ -568,7 +574,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
                 }
             }
         }
-        consumers_sync();
+        consumers_sync<W>();
     }
     const float4* xr4 = reinterpret_cast<const float4*>(p.rx);
     float ss = 0.f;
@@ -624,12 +630,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
     }
-    consumers_sync();
+    consumers_sync<W>();
     if (ctid == 0) mbar_arrive(xready);  // the producer may fill the rest of the rings
     if constexpr (kRms) {
         float t = 0.f;
 #pragma unroll
-        for (int k = 0; k < kGemvConsumerWarps; ++k) t += red[k];
+        for (int k = 0; k < W; ++k) t += red[k];
         inv = 1.0f / sqrtf(t / (float)p.cols + p.eps);
     }
 
@@ -731,10 +737,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
             best = other > best ? other : best;
         }
         if (lane == 0) best_sh[warp] = best;
-        consumers_sync();
+        consumers_sync<W>();
         if (ctid == 0) {
             unsigned long long b = 0ull;
-            for (int k = 0; k < kGemvConsumerWarps; ++k) b = best_sh[k] > b ? best_sh[k] : b;
+            for (int k = 0; k < W; ++k) b = best_sh[k] > b ? best_sh[k] : b;
             if (b) atomicMax(p.argmax, b);
         }
     }
@@ -742,7 +748,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         // every row partial of this CTA is stored (at the peers too); the last
         // CTA to finish raises this rank's flag at every rank
         __threadfence_system();
-        consumers_sync();
+        consumers_sync<W>();
         if (ctid == 0 && atomicAdd(p.done_ctr, 1u) == gridDim.x - 1) {
             *p.done_ctr = 0u;
             __threadfence_system();
@@ -751,7 +757,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
         }
     }
     if (p.trace) {
-        consumers_sync();
+        consumers_sync<W>();
         if (ctid == 0) trace_mark(p.trace, 2);
     }
 }

@@ -603,39 +603,57 @@ static const void* gemv_kernel_for(uint32_t type, int pro, int epi) {
 constexpr size_t kSmemLimit = 227 * 1024;
 constexpr uint32_t kMaxStages = 32;
 
-// Tiles of 4 rows (one consumer warp each, released by that warp), as many
-// stages as shared memory holds after the staged x: for K = 4096 Q4_0 that
-// is ~23 tiles (~210 KB) in flight per SM.
-GemvPlan gemv_plan(const QMat& m) {
+// Consumer warps of the kernel for a tensor type (the formats' WARPS).
+static uint32_t gemv_warps(uint32_t type) {
+    switch (type) {
+        case SM_T_Q4_0: return FmtQ4_0::WARPS;
+        case SM_T_Q8_0: return FmtQ8_0::WARPS;
+        case SM_T_Q4_K: return FmtQ4K::WARPS;
+        case SM_T_Q6_K: return FmtQ6K::WARPS;
+        default: return FmtF32::WARPS;
+    }
+}
+
+// Tiles of 4 rows; as many stages as shared memory (at most smem_cap bytes,
+// 0 = the 227 KB limit) holds after the staged x.  The W consumer warps form
+// NG <= 8 groups with private rings of >= 2 stages each, NG as large as the
+// stages allow; a group has the fewest warps that still need the minimum
+// number of 32-unit sweeps over K (measured: 448-unit rows run faster on 7-8
+// warps with full sweeps than on 16 with 28 of 32 lanes busy).  Warps left
+// over idle in the tile loop but share the x staging (measured on Q4_0
+// 14336x4096: 11 groups of 2 warps, 9.51 us; 8 groups, 8.94 us).
+constexpr uint32_t kGemvMaxGroups = 8;
+GemvPlan gemv_plan(const QMat& m, size_t smem_cap) {
     GemvPlan pl;
+    const size_t limit = smem_cap && smem_cap < kSmemLimit ? smem_cap : kSmemLimit;
+    const uint32_t W = gemv_warps(m.type);
+    pl.warps = W;
     // x records: two digits for the 4-bit codes, three for the others
     const bool four_bit = m.type == SM_T_Q4_0 || m.type == SM_T_Q4_K;
     const size_t xrec = four_bit ? xrec_bytes<2>() : xrec_bytes<3>();
     pl.xbytes = m.type == SM_T_F32 ? (size_t)m.cols * 4 : (size_t)(m.cols / 32) * xrec;
     // per stage: the tile, three mbarriers, the group's partial sums
-    const size_t misc = kGemvConsumerWarps * 4 + kGemvConsumerWarps * 8 + 128;
+    const size_t misc = kGemvMaxWarps * 4 + kGemvMaxWarps * 8 + 128;
     const uint32_t rt = 4;
     const size_t sb = (size_t)rt * m.row_stride;
-    const size_t per_stage = sb + 24 + kGemvConsumerWarps * 4 * 4;
-    if (pl.xbytes + misc + per_stage > kSmemLimit)
+    const size_t per_stage = sb + 24 + (size_t)W * 4 * 4;
+    if (pl.xbytes + misc + 2 * per_stage > limit)
         throw Error(1, "gemv: rows of " + std::to_string(m.cols) + " columns do not fit the shared-memory pipeline");
-    uint32_t smax = (uint32_t)((kSmemLimit - pl.xbytes - misc) / per_stage);
+    uint32_t smax = (uint32_t)((limit - pl.xbytes - misc) / per_stage);
     if (smax > kMaxStages) smax = kMaxStages;
-    // NG groups of G warps, each group with a private ring of k >= 2 stages
-    // where shared memory allows; the G warps of a group split K, with at
-    // least one 32-unit sweep per warp (measured: 448-unit rows run faster on
-    // 8 warps with full sweeps than on 16 with 28 of 32 lanes busy).
-    uint32_t ng = 1;
-    while (ng * 2 <= (uint32_t)kGemvConsumerWarps && ng * 2 * 2 <= smax) ng *= 2;
-    uint32_t g = kGemvConsumerWarps / ng;
-    while (g > 1 && m.units / g < 32) g /= 2;
+    uint32_t ng = std::min(std::min(W / 2, kGemvMaxGroups), smax / 2);
+    if (ng < 1) ng = 1;
+    const uint32_t gmax = W / ng;
+    const uint32_t sweeps = (m.units + 32 * gmax - 1) / (32 * gmax);
+    uint32_t g = gmax;
+    while (g > 1 && (m.units + 32 * (g - 1) - 1) / (32 * (g - 1)) <= sweeps) --g;
     pl.ngroups = ng;
     pl.gsize = g;
     pl.kring = smax / ng;
     pl.rt = rt;
     pl.stages = ng * pl.kring;
-    pl.smem = pl.xbytes + (size_t)pl.stages * sb + 24 * (size_t)pl.stages + 8 + kGemvConsumerWarps * 4 +
-              kGemvConsumerWarps * 8 + (size_t)pl.stages * g * 4 * 4;
+    pl.smem = pl.xbytes + (size_t)pl.stages * sb + 24 * (size_t)pl.stages + 8 + kGemvMaxWarps * 4 +
+              kGemvMaxWarps * 8 + (size_t)pl.stages * g * 4 * 4;
     return pl;
 }
 
@@ -666,7 +684,7 @@ void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_
             configured[fn] = 1;
         }
     }
-    const GemvPlan pl = gemv_plan(m);
+    const GemvPlan pl = gemv_plan(m, a.smem_cap);
     const uint32_t ntiles = m.rows_pad / pl.rt;
     uint32_t grid = (uint32_t)device_sm_count();
     if (grid > ntiles) grid = ntiles;
@@ -722,7 +740,7 @@ void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_
          (pro == GEMV_PRO_RMS_SUM && (!a.x_res || !a.x_out || !a.rx || !a.rx_flag))))
         throw Error(1, "gemv: incomplete tensor-parallel arguments");
     void* args[] = {&p};
-    launch_kernel_ex(fn, dim3(grid), dim3(kGemvThreads), pl.smem, stream, pdl, args);
+    launch_kernel_ex(fn, dim3(grid), dim3((pl.warps + 1) * 32), pl.smem, stream, pdl, args);
 }
 
 unsigned int gemv_error_flags(bool clear) {

@@ -322,6 +322,17 @@ void Model::load(const std::string& path, const smallm_model_opts& o) {
     logits = static_cast<float*>(dalloc(4ull * vocab_l * tp_size));
     logits_local = tp_size > 1 ? static_cast<float*>(dalloc(4ull * vocab_l)) : logits;
     attn_cluster = attention_cluster_size(nh_l, nkv_l, hd);
+    {
+        // an attention CTA (dynamic + a little static shared memory) next to a
+        // GEMV CTA on one SM, each with the per-CTA reservation
+        int dev = 0, per_sm = 0, reserved = 0;
+        SM_CUDA(cudaGetDevice(&dev));
+        SM_CUDA(cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev));
+        SM_CUDA(cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev));
+        const size_t attn = attention_cluster_smem(nh_l, nkv_l, hd) + 256;
+        const size_t need = attn + 2 * (size_t)reserved;
+        gemv_cap_attn = (size_t)per_sm > need ? (size_t)per_sm - need : 0;
+    }
     st = static_cast<DecodeState*>(dalloc(sizeof(DecodeState)));
     SM_CUDA(cudaMemsetAsync(st, 0, sizeof(DecodeState), stream));
     keys = static_cast<unsigned long long*>(dalloc(8ull * tp_size));
@@ -442,6 +453,7 @@ void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
         a.rope = rope;
         a.pos = &st->pos;
         a.trace = slot(TK_QKV);
+        a.smem_cap = gemv_cap_attn;
         if (sum_in) gather(a, 2 * i - 1);
         launch_gemv(L.qkv, sum_in ? GEMV_PRO_RMS_SUM : GEMV_PRO_RMS, GEMV_EPI_QKV, a, s, pdl);
         if (!L.fused_v) {
@@ -471,6 +483,7 @@ void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
         ao.x = att;
         ao.y = x;
         ao.trace = slot(TK_O);
+        ao.smem_cap = gemv_cap_attn;
         if (tpx) send(ao, 2 * i);
         launch_gemv(L.o, GEMV_PRO_PLAIN, tpx ? GEMV_EPI_PEER : GEMV_EPI_RESIDUAL, ao, s, pdl);
 
