@@ -8,7 +8,7 @@
 // cp.async.bulk (completion through mbarrier transaction counts).
 //
 // Compute side -- warp groups with private rings.  A tile is 4 rows.  The W
-// consumer warps (Fmt::WARPS) form NG groups of G warps; group g owns a ring of k stages
+// consumer warps form NG groups of G warps; group g owns a ring of k stages
 // and takes tiles g, g+NG, g+2NG, ..., its j-th tile landing in stage
 // g*k + j%k, so every mbarrier wait is on the next phase of a stage only
 // that group uses (parity waits are only unambiguous that way).  Producer
@@ -49,11 +49,13 @@ enum { PRO_PLAIN = 0, PRO_RMS = 1, PRO_RMS_SUM = 2 };
 enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4, EPI_PEER = 5 };
 constexpr int kMaxTP = 8;
 
-// Consumer warps per CTA (one producer warp more): 22 for Q4_0, which fits
-// 72 registers per thread and still leaves room on the SM for the decode
-// attention's CTAs next to a QKV GEMV's (more warps hide the shared-memory
-// latency of the dot loop and share the x staging); 16 for the formats whose
-// dot needs more registers.
+// Consumer warps per CTA (one producer warp more; a kernel template
+// parameter): 16, or 22 for Q4_0 rows of >= 256 units (8192 columns), where
+// the extra warps share the x staging of the long row (measured on the
+// 4096x14336 down projection: 11.86 -> 10.86 us; on 4096-column rows they
+// cost 0.26 us).  22 warps fit 72 registers per thread with room left on the
+// SM for the decode attention's CTAs; the other formats' dots need more
+// registers than 22 warps allow (Fmt::WIDE).
 constexpr int kGemvMaxWarps = 22;
 constexpr int kMaxRT = 32;                                   // storage rows pad to this
 
@@ -245,7 +247,7 @@ __device__ __forceinline__ float combine(int s0, int s1, int s2) {
 // Q4_0: element i of a block is the low nibble of byte i, element i+16 the
 // high nibble (src/core/tensor.cpp:57-63); value (q - 8) * d.
 struct FmtQ4_0 {
-    static constexpr int UE = 32, SUBS = 1, ND = 2, WARPS = 22;
+    static constexpr int UE = 32, SUBS = 1, ND = 2, WIDE = 22;
     static constexpr bool F32X = false;
     struct Raw { uint4 q; uint32_t s; };
     __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t units, Raw& r) {
@@ -271,7 +273,7 @@ struct FmtQ4_0 {
 
 // Q8_0: int8 codes; value q * d.
 struct FmtQ8_0 {
-    static constexpr int UE = 32, SUBS = 1, ND = 3, WARPS = 16;
+    static constexpr int UE = 32, SUBS = 1, ND = 3, WIDE = 16;
     static constexpr bool F32X = false;
     struct Raw { uint4 a, b; uint32_t s; };
     __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t units, Raw& r) {
@@ -302,7 +304,7 @@ struct FmtQ8_0 {
 // nibbles of qs[32k..32k+32), sub-block 2k+1 = high nibbles.
 // Value: (d*sc)*q - dmin*m (gguf-py Q4_K.dequantize_blocks).
 struct FmtQ4K {
-    static constexpr int UE = 64, SUBS = 2, ND = 2, WARPS = 16;
+    static constexpr int UE = 64, SUBS = 2, ND = 2, WIDE = 16;
     static constexpr bool F32X = false;
     struct Raw { uint4 h, a, b; };
     __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t, Raw& r) {
@@ -348,7 +350,7 @@ struct FmtQ4K {
 // 6-7); 4 int8 scales per unit (element e of a super-block uses scale e/16);
 // f16 d per super-block.  Value: (d*sc)*(q - 32) (src/core/tensor.cpp:97-106).
 struct FmtQ6K {
-    static constexpr int UE = 64, SUBS = 2, ND = 3, WARPS = 16;
+    static constexpr int UE = 64, SUBS = 2, ND = 3, WIDE = 16;
     static constexpr bool F32X = false;
     struct Raw { uint4 n0, n1, hb; uint32_t sc; uint32_t d; };
     __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t units, Raw& r) {
@@ -392,7 +394,7 @@ struct FmtQ6K {
 // F32 (the reference's catch-all branch, ops.cpp:289-299): plain f32 FMAs
 // against an f32 copy of x.
 struct FmtF32 {
-    static constexpr int UE = 32, SUBS = 1, ND = 3, WARPS = 16;
+    static constexpr int UE = 32, SUBS = 1, ND = 3, WIDE = 16;
     static constexpr bool F32X = true;
 };
 
@@ -470,9 +472,9 @@ __device__ __forceinline__ void gemv_epilogue_row(const GemvParams& p, uint32_t 
 
 // ------------------------------------------------------------------ kernel --
 
-template <class Fmt, int PRO, int EPI>
-__global__ void __launch_bounds__((Fmt::WARPS + 1) * 32, 1) gemv_kernel(const GemvParams p) {
-    constexpr int W = Fmt::WARPS;  // consumer warps; warp W is the producer
+template <class Fmt, int PRO, int EPI, int W>  // W consumer warps; warp W is the producer
+__global__ void __launch_bounds__((W + 1) * 32, 1) gemv_kernel(const GemvParams p) {
+    static_assert(W <= kGemvMaxWarps && W <= Fmt::WIDE, "consumer warps");
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* xreg = smem;                                   // x records (or f32 x)
     uint8_t* stage0 = smem + p.xbytes;                      // S stages

@@ -573,29 +573,29 @@ void rope_table(uint32_t hd, uint32_t positions, float base, std::vector<float2>
 
 __device__ unsigned int g_gemv_err;  // set by a bounded wait that gave up
 
-template <class Fmt>
+template <class Fmt, int W>
 static const void* pick(int pro, int epi) {
-    if (pro == PRO_PLAIN && epi == EPI_STORE) return (const void*)gemv_kernel<Fmt, PRO_PLAIN, EPI_STORE>;
-    if (pro == PRO_PLAIN && epi == EPI_RESIDUAL) return (const void*)gemv_kernel<Fmt, PRO_PLAIN, EPI_RESIDUAL>;
-    if (pro == PRO_RMS && epi == EPI_STORE) return (const void*)gemv_kernel<Fmt, PRO_RMS, EPI_STORE>;
-    if (pro == PRO_RMS && epi == EPI_QKV) return (const void*)gemv_kernel<Fmt, PRO_RMS, EPI_QKV>;
-    if (pro == PRO_RMS && epi == EPI_SWIGLU) return (const void*)gemv_kernel<Fmt, PRO_RMS, EPI_SWIGLU>;
-    if (pro == PRO_RMS && epi == EPI_LOGITS) return (const void*)gemv_kernel<Fmt, PRO_RMS, EPI_LOGITS>;
+    if (pro == PRO_PLAIN && epi == EPI_STORE) return (const void*)gemv_kernel<Fmt, PRO_PLAIN, EPI_STORE, W>;
+    if (pro == PRO_PLAIN && epi == EPI_RESIDUAL) return (const void*)gemv_kernel<Fmt, PRO_PLAIN, EPI_RESIDUAL, W>;
+    if (pro == PRO_RMS && epi == EPI_STORE) return (const void*)gemv_kernel<Fmt, PRO_RMS, EPI_STORE, W>;
+    if (pro == PRO_RMS && epi == EPI_QKV) return (const void*)gemv_kernel<Fmt, PRO_RMS, EPI_QKV, W>;
+    if (pro == PRO_RMS && epi == EPI_SWIGLU) return (const void*)gemv_kernel<Fmt, PRO_RMS, EPI_SWIGLU, W>;
+    if (pro == PRO_RMS && epi == EPI_LOGITS) return (const void*)gemv_kernel<Fmt, PRO_RMS, EPI_LOGITS, W>;
     // tensor parallel: row-parallel partials to peers, and the GEMVs that sum them
-    if (pro == PRO_PLAIN && epi == EPI_PEER) return (const void*)gemv_kernel<Fmt, PRO_PLAIN, EPI_PEER>;
-    if (pro == PRO_RMS_SUM && epi == EPI_QKV) return (const void*)gemv_kernel<Fmt, PRO_RMS_SUM, EPI_QKV>;
-    if (pro == PRO_RMS_SUM && epi == EPI_SWIGLU) return (const void*)gemv_kernel<Fmt, PRO_RMS_SUM, EPI_SWIGLU>;
-    if (pro == PRO_RMS_SUM && epi == EPI_LOGITS) return (const void*)gemv_kernel<Fmt, PRO_RMS_SUM, EPI_LOGITS>;
+    if (pro == PRO_PLAIN && epi == EPI_PEER) return (const void*)gemv_kernel<Fmt, PRO_PLAIN, EPI_PEER, W>;
+    if (pro == PRO_RMS_SUM && epi == EPI_QKV) return (const void*)gemv_kernel<Fmt, PRO_RMS_SUM, EPI_QKV, W>;
+    if (pro == PRO_RMS_SUM && epi == EPI_SWIGLU) return (const void*)gemv_kernel<Fmt, PRO_RMS_SUM, EPI_SWIGLU, W>;
+    if (pro == PRO_RMS_SUM && epi == EPI_LOGITS) return (const void*)gemv_kernel<Fmt, PRO_RMS_SUM, EPI_LOGITS, W>;
     throw Error(1, "gemv: unsupported prologue/epilogue combination");
 }
 
-static const void* gemv_kernel_for(uint32_t type, int pro, int epi) {
+static const void* gemv_kernel_for(uint32_t type, int pro, int epi, uint32_t warps) {
     switch (type) {
-        case SM_T_F32: return pick<FmtF32>(pro, epi);
-        case SM_T_Q4_0: return pick<FmtQ4_0>(pro, epi);
-        case SM_T_Q8_0: return pick<FmtQ8_0>(pro, epi);
-        case SM_T_Q4_K: return pick<FmtQ4K>(pro, epi);
-        case SM_T_Q6_K: return pick<FmtQ6K>(pro, epi);
+        case SM_T_F32: return pick<FmtF32, 16>(pro, epi);
+        case SM_T_Q4_0: return warps == 22 ? pick<FmtQ4_0, 22>(pro, epi) : pick<FmtQ4_0, 16>(pro, epi);
+        case SM_T_Q8_0: return pick<FmtQ8_0, 16>(pro, epi);
+        case SM_T_Q4_K: return pick<FmtQ4K, 16>(pro, epi);
+        case SM_T_Q6_K: return pick<FmtQ6K, 16>(pro, epi);
         default: throw Error(2, "unsupported tensor type: " + std::to_string(type));
     }
 }
@@ -603,15 +603,9 @@ static const void* gemv_kernel_for(uint32_t type, int pro, int epi) {
 constexpr size_t kSmemLimit = 227 * 1024;
 constexpr uint32_t kMaxStages = 32;
 
-// Consumer warps of the kernel for a tensor type (the formats' WARPS).
-static uint32_t gemv_warps(uint32_t type) {
-    switch (type) {
-        case SM_T_Q4_0: return FmtQ4_0::WARPS;
-        case SM_T_Q8_0: return FmtQ8_0::WARPS;
-        case SM_T_Q4_K: return FmtQ4K::WARPS;
-        case SM_T_Q6_K: return FmtQ6K::WARPS;
-        default: return FmtF32::WARPS;
-    }
+// Consumer warps of the kernel for a matrix (gemv.cuh, kGemvMaxWarps).
+static uint32_t gemv_warps(const QMat& m) {
+    return m.type == SM_T_Q4_0 && m.units >= 256 ? 22u : 16u;
 }
 
 // Tiles of 4 rows; as many stages as shared memory (at most smem_cap bytes,
@@ -626,7 +620,7 @@ constexpr uint32_t kGemvMaxGroups = 8;
 GemvPlan gemv_plan(const QMat& m, size_t smem_cap) {
     GemvPlan pl;
     const size_t limit = smem_cap && smem_cap < kSmemLimit ? smem_cap : kSmemLimit;
-    const uint32_t W = gemv_warps(m.type);
+    const uint32_t W = gemv_warps(m);
     pl.warps = W;
     // x records: two digits for the 4-bit codes, three for the others
     const bool four_bit = m.type == SM_T_Q4_0 || m.type == SM_T_Q4_K;
@@ -675,7 +669,8 @@ unsigned int* device_error_flag() {
 void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_t stream, bool pdl) {
     static std::mutex mu;
     static std::unordered_map<const void*, int> configured;
-    const void* fn = gemv_kernel_for(m.type, pro, epi);
+    const GemvPlan pl = gemv_plan(m, a.smem_cap);
+    const void* fn = gemv_kernel_for(m.type, pro, epi, pl.warps);
     unsigned int* err = device_error_flag();
     {
         std::lock_guard<std::mutex> g(mu);
@@ -684,7 +679,6 @@ void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_
             configured[fn] = 1;
         }
     }
-    const GemvPlan pl = gemv_plan(m, a.smem_cap);
     const uint32_t ntiles = m.rows_pad / pl.rt;
     uint32_t grid = (uint32_t)device_sm_count();
     if (grid > ntiles) grid = ntiles;
