@@ -135,6 +135,28 @@ int smallm_qmatrix_bytes(const smallm_qmatrix* m, uint64_t* gguf_bytes, uint64_t
 int smallm_gemv(smallm_ctx* ctx, const smallm_qmatrix* W, const float* x_dev, float* y_dev,
                 void* stream);
 
+/* The tensor-parallel residual step of the decode path as one call (what the
+ * decode step's QKV, gate/up and lm_head GEMVs do under tensor parallelism):
+ *   x_out = x_res + parts[0] + ... + parts[n_parts-1]   (f32, in that order)
+ *   y     = W . (x_out * norm_w / rms(x_out))           (ops::rmsnorm, src/core/ops.cpp:29-40)
+ * once every arrival flag flags[r] equals *epoch + 1 (the value a sender
+ * stores after its part is complete).  parts is [n_parts][cols] f32,
+ * n_parts in 1..8; x_out may be written by any one CTA.  The flag wait is
+ * bounded (about one second): when it gives up, bit 3 of the device error
+ * word is raised and y / x_out are not valid (smallm_ctx_device_errors).
+ * Asynchronous on `stream` (NULL = the context stream); device pointers. */
+int smallm_gemv_residual_sum(smallm_ctx* ctx, const smallm_qmatrix* W, const float* x_res_dev,
+                             const float* parts_dev, uint32_t n_parts, const uint32_t* flags_dev,
+                             const uint32_t* epoch_dev, const float* norm_w_dev, float eps, float* x_out_dev,
+                             float* y_dev, void* stream);
+
+/* The device error word that the bounded waits of the GEMV and attention
+ * kernels raise when they give up (0 = none): bit 0 a GEMV producer's stage
+ * wait, bits 1-2 a GEMV or attention pipeline wait, bit 3 a residual part's
+ * arrival flag, bit 5 the decode position changed during a step.  Waits for
+ * the device; clear != 0 resets the word. */
+int smallm_ctx_device_errors(smallm_ctx* ctx, uint32_t* flags, int clear);
+
 /* Dequantize the matrix from its device layout into y_dev[rows * cols]
  * (row-major), bit-identical to the reference's dequantize_tensor
  * (src/core/tensor.cpp:115-138). */

@@ -314,6 +314,40 @@ int smallm_gemv(smallm_ctx* ctx, const smallm_qmatrix* W, const float* x_dev, fl
     });
 }
 
+int smallm_gemv_residual_sum(smallm_ctx* ctx, const smallm_qmatrix* W, const float* x_res_dev,
+                             const float* parts_dev, uint32_t n_parts, const uint32_t* flags_dev,
+                             const uint32_t* epoch_dev, const float* norm_w_dev, float eps, float* x_out_dev,
+                             float* y_dev, void* stream) {
+    return guard([&] {
+        need(ctx && W && x_res_dev && parts_dev && flags_dev && epoch_dev && norm_w_dev && x_out_dev && y_dev,
+             "NULL argument");
+        need(n_parts >= 1 && n_parts <= (uint32_t)smallm::kMaxTPRanks, "n_parts must be 1..8");
+        set_dev(ctx->device);
+        smallm::GemvArgs a;
+        a.x = x_res_dev;
+        a.x_res = x_res_dev;
+        a.rx = parts_dev;
+        a.rx_flag = flags_dev;
+        a.epoch = epoch_dev;
+        a.tp = n_parts;
+        a.norm_w = norm_w_dev;
+        a.eps = eps;
+        a.x_out = x_out_dev;
+        a.y = y_dev;
+        smallm::launch_gemv(W->m, smallm::GEMV_PRO_RMS_SUM, smallm::GEMV_EPI_STORE, a,
+                            stream ? (cudaStream_t)stream : ctx->stream);
+    });
+}
+
+int smallm_ctx_device_errors(smallm_ctx* ctx, uint32_t* flags, int clear) {
+    return guard([&] {
+        need(ctx && flags, "NULL argument");
+        set_dev(ctx->device);
+        SM_CUDA(cudaDeviceSynchronize());
+        *flags = smallm::gemv_error_flags(clear != 0);
+    });
+}
+
 int smallm_attention_noalloc(smallm_ctx* ctx, const float* q_dev, const float* kcache_dev,
                              const float* vcache_dev, uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
                              uint32_t max_ctx, uint32_t pos, float* out_dev, void* stream) {

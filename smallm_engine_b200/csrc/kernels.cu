@@ -583,6 +583,7 @@ static const void* pick(int pro, int epi) {
     if (pro == PRO_RMS && epi == EPI_LOGITS) return (const void*)gemv_kernel<Fmt, PRO_RMS, EPI_LOGITS, W>;
     // tensor parallel: row-parallel partials to peers, and the GEMVs that sum them
     if (pro == PRO_PLAIN && epi == EPI_PEER) return (const void*)gemv_kernel<Fmt, PRO_PLAIN, EPI_PEER, W>;
+    if (pro == PRO_RMS_SUM && epi == EPI_STORE) return (const void*)gemv_kernel<Fmt, PRO_RMS_SUM, EPI_STORE, W>;
     if (pro == PRO_RMS_SUM && epi == EPI_QKV) return (const void*)gemv_kernel<Fmt, PRO_RMS_SUM, EPI_QKV, W>;
     if (pro == PRO_RMS_SUM && epi == EPI_SWIGLU) return (const void*)gemv_kernel<Fmt, PRO_RMS_SUM, EPI_SWIGLU, W>;
     if (pro == PRO_RMS_SUM && epi == EPI_LOGITS) return (const void*)gemv_kernel<Fmt, PRO_RMS_SUM, EPI_LOGITS, W>;

@@ -216,3 +216,79 @@ def test_ops_vs_golden(be, golden):
 def test_softmax_empty_is_noop(be):
     x = np.zeros(0, dtype=np.float32)
     be.softmax(x)
+
+
+def _residual_sum(be, qm, x_res, parts, flags, epoch, norm_w, eps, x_out, y):
+    import ctypes
+    _lib.check(_lib.lib().smallm_gemv_residual_sum(
+        be.h, qm.h, x_res.data_ptr(), parts.data_ptr(), parts.shape[0], flags.data_ptr(), epoch.data_ptr(),
+        norm_w.data_ptr(), ctypes.c_float(eps), x_out.data_ptr(), y.data_ptr(), None))
+
+
+def _device_errors(be, clear=True):
+    import ctypes
+    f = ctypes.c_uint32(0)
+    _lib.check(_lib.lib().smallm_ctx_device_errors(be.h, ctypes.byref(f), 1 if clear else 0))
+    return f.value
+
+
+def test_gemv_residual_sum_vs_oracle(be, orc):
+    """The tensor-parallel residual step: x_out = x_res + parts in rank order
+    (bit-exact f32 adds), then the reference's RMSNorm and the GEMV, once
+    every arrival flag reads epoch + 1."""
+    rows, cols, n, eps = 96, 2048, 3, 1e-5
+    rng = np.random.default_rng(21)
+    W = synth.quantize(O.Q4_0, (rng.standard_normal(rows * cols) * 0.02).astype(np.float32))
+    qm = be.upload(W, O.Q4_0, rows, cols)
+    xr = rng.standard_normal(cols).astype(np.float32)
+    P = rng.standard_normal((n, cols)).astype(np.float32)
+    nw = (1.0 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+    dev = lambda a: torch.from_numpy(a).cuda()
+    epoch = torch.tensor([41], dtype=torch.int32, device="cuda")
+    flags = torch.full((n,), 42, dtype=torch.int32, device="cuda")
+    x_out = torch.empty(cols, device="cuda")
+    y = torch.empty(rows, device="cuda")
+    assert _device_errors(be) == 0
+    _residual_sum(be, qm, dev(xr), dev(P), flags, epoch, dev(nw), eps, x_out, y)
+    torch.cuda.synchronize()
+    assert _device_errors(be) == 0
+    want_x = xr.copy()
+    for r in range(n):
+        want_x = (want_x + P[r]).astype(np.float32)
+    assert np.array_equal(x_out.cpu().numpy().view(np.uint32), want_x.view(np.uint32))
+    xn = orc.rmsnorm(want_x, nw, eps)
+    want = orc.matmul_quantized(W, O.Q4_0, xn, rows, cols)
+    got = y.cpu().numpy().astype(np.float64)
+    # the GEMV bound plus the norm's own f32 rounding (1/rms applied to the row sums)
+    bound = gemv_bound(orc, W, O.Q4_0, xn, rows, cols) + 1e-6 * np.abs(want)
+    assert np.all(np.abs(got - want) <= bound)
+
+
+def test_gemv_residual_sum_flag_wait_gives_up(be, orc):
+    """A part whose arrival flag never comes up: the kernel's bounded wait
+    (about a second) gives up, raises bit 3 of the device error word and the
+    kernel ends; the context stays usable."""
+    rows, cols = 32, 512
+    rng = np.random.default_rng(22)
+    W = synth.quantize(O.Q4_0, (rng.standard_normal(rows * cols) * 0.02).astype(np.float32))
+    qm = be.upload(W, O.Q4_0, rows, cols)
+    x_res = torch.randn(cols, device="cuda")
+    parts = torch.randn(2, cols, device="cuda")
+    norm_w = torch.ones(cols, device="cuda")
+    epoch = torch.tensor([7], dtype=torch.int32, device="cuda")
+    flags = torch.tensor([8, 0], dtype=torch.int32, device="cuda")  # the second sender never arrives
+    x_out = torch.empty(cols, device="cuda")
+    y = torch.empty(rows, device="cuda")
+    assert _device_errors(be) == 0
+    _residual_sum(be, qm, x_res, parts, flags, epoch, norm_w, 1e-5, x_out, y)
+    torch.cuda.synchronize()
+    assert _device_errors(be) & 8
+    assert _device_errors(be) == 0  # cleared by the read above
+    # the context still runs kernels, with correct results
+    x = rng.standard_normal(cols).astype(np.float32)
+    xd = torch.from_numpy(x).cuda()
+    qm.gemv(xd.data_ptr(), y.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    want = orc.matmul_quantized(W, O.Q4_0, x, rows, cols)
+    assert np.all(np.abs(y.cpu().numpy().astype(np.float64) - want) <= gemv_bound(orc, W, O.Q4_0, x, rows, cols))
+    assert _device_errors(be) == 0
