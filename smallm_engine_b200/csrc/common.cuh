@@ -48,40 +48,6 @@ __device__ __forceinline__ float h2f(uint32_t h) {
     return __half2float(__ushort_as_half((unsigned short)h));
 }
 
-// Streaming 128-bit load that does not allocate in L1 (weights are read once
-// per step).
-__device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
-    uint4 v;
-    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
-__device__ __forceinline__ uint32_t ld_stream_u32(const void* p) {
-    uint32_t v;
-    asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
-    return v;
-}
-__device__ __forceinline__ uint32_t ld_stream_u16(const void* p) {
-    unsigned short v;
-    asm("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
-    return v;
-}
-__device__ __forceinline__ uint2 ld_stream_u2(const void* p) {
-    uint2 v;
-    asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
-                 : "=r"(v.x), "=r"(v.y)
-                 : "l"(p));
-    return v;
-}
-
-// Byte k (0..3) of w as an exact float offset by `bias`: builds 2^23 + byte
-// with a byte permute and subtracts 2^23 + bias (both exact in f32).
-template <int K>
-__device__ __forceinline__ float byte_f(uint32_t w, float magic_minus_bias) {
-    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | K)) - magic_minus_bias;
-}
-
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -208,16 +174,6 @@ __device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) 
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Non-blocking: has phase `parity` of the barrier completed?
-__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
 // Wait for phase `parity` of the barrier to complete; gives up after about
 // 2^31 SM cycles (~1 s) and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
