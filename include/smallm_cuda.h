@@ -135,6 +135,19 @@ int smallm_qmatrix_bytes(const smallm_qmatrix* m, uint64_t* gguf_bytes, uint64_t
 int smallm_gemv(smallm_ctx* ctx, const smallm_qmatrix* W, const float* x_dev, float* y_dev,
                 void* stream);
 
+/* Tensor-core GEMM (tcgen05, sm_100a) of the batched prefill on device
+ * operands: y_dev[t * ldy + n] = sum_k x_dev[t * K + k] * w_dev[n * K + k]
+ * for t < T, n < N.  w_dev [N][K] and x_dev [T][K] are row-major IEEE half
+ * (uint16 bit patterns, 16-byte aligned, K a positive multiple of 8); the
+ * products are exact and accumulate in f32.  This is the contraction the
+ * reference performs as matmul_quantized once per prompt token
+ * (src/core/ops.cpp:103-184 via src/runtime/generator.cpp:47-51), here over T
+ * tokens at once on dequantized (f16-rounded) weights.  A bounded wait that
+ * gives up raises bit 6 of the device error word (smallm_ctx_device_errors).
+ * Asynchronous on `stream` (NULL = the context stream). */
+int smallm_gemm_f16(smallm_ctx* ctx, const uint16_t* w_dev, const uint16_t* x_dev, uint32_t N, uint32_t K,
+                    uint32_t T, float* y_dev, uint32_t ldy, void* stream);
+
 /* The tensor-parallel residual step of the decode path as one call (what the
  * decode step's QKV, gate/up and lm_head GEMVs do under tensor parallelism):
  *   x_out = x_res + parts[0] + ... + parts[n_parts-1]   (f32, in that order)
@@ -277,8 +290,14 @@ int smallm_model_decode_ids(smallm_model* m, uint32_t* ids, uint32_t n);
  * cached_length becomes start_pos + n.  Single GPU (tp_size 1).  The first
  * call keeps an f32 copy of the layer weights on the device (4 bytes per
  * weight).  flags: SMALLM_PREFILL_TF32 runs the GEMMs on TF32 tensor cores
- * (10-bit mantissa inputs); without it they are exact f32. */
+ * (10-bit mantissa inputs) through cuBLAS; without a flag they are exact f32. */
 #define SMALLM_PREFILL_TF32 1u
+/* SMALLM_PREFILL_TC runs the GEMMs as the backend's own tcgen05 kernel
+ * (smallm_gemm_f16) on f16 copies of the layer weights (2 bytes per weight,
+ * made at the first such call) and f16-rounded activations (11-bit
+ * significands like TF32; f16 range, |x| < 65504); it takes precedence over
+ * SMALLM_PREFILL_TF32. */
+#define SMALLM_PREFILL_TC 2u
 int smallm_model_prefill(smallm_model* m, const uint32_t* tokens, uint32_t n, uint32_t start_pos, float* logits,
                          uint32_t* argmax, uint32_t flags);
 

@@ -66,6 +66,7 @@ SIGNATURES = {
     "smallm_qmatrix_free": (_I, [_P]),
     "smallm_qmatrix_bytes": (_I, [_P, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]),
     "smallm_gemv": (_I, [_P, _P, _P, _P, _P]),
+    "smallm_gemm_f16": (_I, [_P, _P, _P, _U32, _U32, _U32, _P, _U32, _P]),
     "smallm_gemv_residual_sum": (_I, [_P, _P, _P, _P, _U32, _P, _P, _P, ctypes.c_float, _P, _P, _P]),
     "smallm_ctx_device_errors": (_I, [_P, ctypes.POINTER(_U32), ctypes.c_int]),
     "smallm_qmatrix_dequantize": (_I, [_P, _P, _P, _P]),

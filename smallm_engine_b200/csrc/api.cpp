@@ -314,6 +314,16 @@ int smallm_gemv(smallm_ctx* ctx, const smallm_qmatrix* W, const float* x_dev, fl
     });
 }
 
+int smallm_gemm_f16(smallm_ctx* ctx, const uint16_t* w_dev, const uint16_t* x_dev, uint32_t N, uint32_t K,
+                    uint32_t T, float* y_dev, uint32_t ldy, void* stream) {
+    return guard([&] {
+        need(ctx && ((w_dev && x_dev && y_dev) || N == 0 || T == 0), "NULL argument");
+        set_dev(ctx->device);
+        smallm::launch_tc_gemm(reinterpret_cast<const __half*>(w_dev), N, K, reinterpret_cast<const __half*>(x_dev),
+                               T, y_dev, ldy, stream ? (cudaStream_t)stream : ctx->stream);
+    });
+}
+
 int smallm_gemv_residual_sum(smallm_ctx* ctx, const smallm_qmatrix* W, const float* x_res_dev,
                              const float* parts_dev, uint32_t n_parts, const uint32_t* flags_dev,
                              const uint32_t* epoch_dev, const float* norm_w_dev, float eps, float* x_out_dev,

@@ -1,6 +1,7 @@
 // Internal host-side interface of the CUDA backend (not part of the C ABI).
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -198,6 +199,17 @@ void launch_attention_prefill(const float* Q, const float* kc, const float* vc, 
                               uint32_t hd, uint32_t max_ctx, uint32_t pos0, uint32_t T, float* out, cudaStream_t s);
 void launch_swiglu_rows(const float* Y, uint32_t ffn, uint32_t T, float* H, cudaStream_t s);
 void launch_add_rows(float* X, const float* Y, uint64_t n, cudaStream_t s);
+
+// Tensor-core GEMM of the batched prefill (tc_gemm.cu, tcgen05 + TMA):
+// Y[t * ldy + n] = sum_k X[t][k] * W[n][k] for t < T, n < N; X [T][K] and
+// W [N][K] row-major f16 (16-byte aligned, K a multiple of 8), f32 result.
+// A bounded wait that gives up raises bit 6 of the device error word.
+void launch_tc_gemm(const __half* W, uint32_t N, uint32_t K, const __half* X, uint32_t T, float* Y, uint32_t ldy,
+                    cudaStream_t s);
+// Token-tile width (64 or 128) the GEMM uses for an N x T output.
+uint32_t tc_gemm_token_tile(uint32_t N, uint32_t T);
+// dst[i] = (f16) src[i], round to nearest even (src 16-byte, dst 8-byte aligned).
+void launch_f32_to_f16(const float* src, __half* dst, uint64_t n, cudaStream_t s);
 
 // One sample from n logits on the device (sampler.cu): kind 0 greedy, 1
 // temperature, 2 top-k, 3 top-p; r is the host's uniform draw; scratch holds

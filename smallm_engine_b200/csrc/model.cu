@@ -634,8 +634,9 @@ void Model::prefill(const uint32_t* tokens, uint32_t T, uint32_t pos0, float* ou
     for (uint32_t t = 0; t < T; ++t)
         if (tokens[t] >= vocab) throw Error(1, "token id out of range");
     if ((uint64_t)pos0 + T > max_ctx) throw Error(7, "prefill would run past the context length");
-    const bool tf32 = (flags & SMALLM_PREFILL_TF32) != 0;
-    if (!cublas) {
+    const bool tc = (flags & SMALLM_PREFILL_TC) != 0;
+    const bool tf32 = !tc && (flags & SMALLM_PREFILL_TF32) != 0;
+    if (!tc && !cublas) {
         cublas_check(cublasCreate(&cublas), "cublasCreate");
         cublas_check(cublasSetStream(cublas, stream), "cublasSetStream");
     }
@@ -645,7 +646,43 @@ void Model::prefill(const uint32_t* tokens, uint32_t T, uint32_t pos0, float* ou
         pre_allocs.push_back(p);
         return static_cast<float*>(p);
     };
-    if (layers_f32.empty()) {
+    if (tc && layers_f16.empty()) {
+        // dequantize each matrix (bit-exact) into one f32 staging buffer, then
+        // round it to f16 into its own copy (2 bytes per weight)
+        uint64_t most = 0;
+        for (uint32_t i = 0; i < n_layers; ++i)
+            for (const QMat* q : {&layers[i].qkv, &layers[i].v, &layers[i].o, &layers[i].gu, &layers[i].down})
+                if (q->base) most = std::max<uint64_t>(most, (uint64_t)q->rows * q->cols);
+        float* stage = nullptr;
+        SM_CUDA(cudaMalloc(&stage, 4 * most));
+        std::vector<LayerF16> made(n_layers);
+        auto deq16 = [&](const QMat& q) -> __half* {
+            if (!q.base) return nullptr;
+            __half* w = reinterpret_cast<__half*>(palloc(2ull * q.rows * q.cols));
+            launch_qmat_dequant(q, stage, stream);
+            launch_f32_to_f16(stage, w, (uint64_t)q.rows * q.cols, stream);
+            return w;
+        };
+        try {
+            for (uint32_t i = 0; i < n_layers; ++i) {
+                LayerW& L = layers[i];
+                LayerF16& F = made[i];
+                F.qkv = deq16(L.qkv);
+                F.v = L.fused_v ? nullptr : deq16(L.v);
+                F.o = deq16(L.o);
+                F.gu = deq16(L.gu);
+                F.down = deq16(L.down);
+            }
+            SM_CUDA(cudaStreamSynchronize(stream));
+        } catch (...) {
+            cudaStreamSynchronize(stream);
+            cudaFree(stage);
+            throw;
+        }
+        SM_CUDA(cudaFree(stage));
+        layers_f16 = std::move(made);
+    }
+    if (!tc && layers_f32.empty()) {
         layers_f32.resize(n_layers);
         auto deq = [&](const QMat& q) -> float* {
             if (!q.base) return nullptr;
@@ -676,28 +713,44 @@ void Model::prefill(const uint32_t* tokens, uint32_t T, uint32_t pos0, float* ou
         pre_tok = reinterpret_cast<uint32_t*>(palloc(4ull * T));
         pre_cap = T;
     }
+    if (tc && (uint64_t)T * std::max({embd, qrows, ffn_l}) > pre_xh_cap) {
+        pre_xh_cap = (uint64_t)T * std::max({embd, qrows, ffn_l});
+        pre_xh = reinterpret_cast<__half*>(palloc(2 * pre_xh_cap));
+    }
+    // Y[T][rows] = X[T][cols] . W^T: tcgen05 on f16 copies, or cuBLAS on f32 copies
+    auto linear = [&](const float* w32, const __half* w16, uint32_t rows, uint32_t cols, const float* X) {
+        if (tc) {
+            launch_f32_to_f16(X, pre_xh, (uint64_t)T * cols, stream);
+            launch_tc_gemm(w16, rows, cols, pre_xh, T, pre_y, rows, stream);
+        } else {
+            gemm(w32, rows, cols, X, T, pre_y, tf32);
+        }
+    };
+    static const LayerF32 kNo32;
+    static const LayerF16 kNo16;
     SM_CUDA(cudaMemcpyAsync(pre_tok, tokens, 4ull * T, cudaMemcpyHostToDevice, stream));
     launch_embed_rows(embd_m, pre_tok, T, pre_x, stream);
     for (uint32_t i = 0; i < n_layers; ++i) {
         LayerW& L = layers[i];
-        LayerF32& F = layers_f32[i];
+        const LayerF32& F = tc ? kNo32 : layers_f32[i];
+        const LayerF16& H = tc ? layers_f16[i] : kNo16;
         float* kc = kv + (size_t)(2 * i) * nkv_l * max_ctx * hd;
         float* vc = kv + (size_t)(2 * i + 1) * nkv_l * max_ctx * hd;
         launch_rmsnorm_rows(pre_x, L.attn_norm, embd, T, eps, pre_xn, stream);
-        gemm(F.qkv, L.qkv.rows, embd, pre_xn, T, pre_y, tf32);
+        linear(F.qkv, H.qkv, L.qkv.rows, embd, pre_xn);
         launch_qkv_post(pre_y, L.qkv.rows, T, qrows, krows, hd, L.bias, rope, pos0, max_ctx, pre_q, kc, vc, stream);
         if (!L.fused_v) {
-            gemm(F.v, L.v.rows, embd, pre_xn, T, pre_y, tf32);
+            linear(F.v, H.v, L.v.rows, embd, pre_xn);
             launch_qkv_post(pre_y, L.v.rows, T, 0, 0, hd, L.bias ? L.bias + qrows + krows : nullptr, rope, pos0,
                             max_ctx, pre_q, kc, vc, stream);
         }
         launch_attention_prefill(pre_q, kc, vc, nh_l, nkv_l, hd, max_ctx, pos0, T, pre_a, stream);
-        gemm(F.o, embd, qrows, pre_a, T, pre_y, tf32);
+        linear(F.o, H.o, embd, qrows, pre_a);
         launch_add_rows(pre_x, pre_y, (uint64_t)T * embd, stream);
         launch_rmsnorm_rows(pre_x, L.ffn_norm, embd, T, eps, pre_xn, stream);
-        gemm(F.gu, L.gu.rows, embd, pre_xn, T, pre_y, tf32);
+        linear(F.gu, H.gu, L.gu.rows, embd, pre_xn);
         launch_swiglu_rows(pre_y, ffn_l, T, pre_h, stream);
-        gemm(F.down, embd, ffn_l, pre_h, T, pre_y, tf32);
+        linear(F.down, H.down, embd, ffn_l, pre_h);
         launch_add_rows(pre_x, pre_y, (uint64_t)T * embd, stream);
     }
     SM_CUDA(cudaMemsetAsync(&st->argmax, 0, sizeof(unsigned long long), stream));

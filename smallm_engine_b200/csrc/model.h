@@ -91,6 +91,14 @@ struct Model {
         float *qkv = nullptr, *v = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
     };
     std::vector<LayerF32> layers_f32;
+    // f16 copies for the tensor-core GEMMs (SMALLM_PREFILL_TC), made at the
+    // first such prefill from the bit-exact dequantized values.
+    struct LayerF16 {
+        __half *qkv = nullptr, *v = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
+    };
+    std::vector<LayerF16> layers_f16;
+    __half* pre_xh = nullptr;  // f16 copy of a GEMM's input rows
+    uint64_t pre_xh_cap = 0;   // elements pre_xh holds
     cublasHandle_t cublas = nullptr;
     uint32_t pre_cap = 0;  // tokens the prefill buffers hold
     float *pre_x = nullptr, *pre_xn = nullptr, *pre_y = nullptr, *pre_q = nullptr, *pre_a = nullptr,

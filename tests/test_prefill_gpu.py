@@ -73,6 +73,51 @@ def test_prefill_tf32(orc, gguf_dir):
     assert close(got, want)
 
 
+@pytest.mark.parametrize("kind,seed", [("qwen2", 7), ("llama-q4_0", 8), ("llama-kq", 9)])
+def test_prefill_tensor_cores(orc, gguf_dir, kind, seed):
+    """The GEMMs on the backend's tcgen05 kernel over f16 weight copies: the
+    last logits within 1e-2 * max|logit| of the token-by-token restatement,
+    the same greedy id, and decode continuing from that cache matching it."""
+    spec = synth.tiny_spec(kind)
+    path = synth.write_gguf(spec, seed, gguf_dir / f"pre-tc-{kind}.gguf")
+    ref = O.OracleModel(path, orc)
+    rng = np.random.default_rng(seed)
+    toks = [int(t) for t in rng.integers(0, spec.vocab, size=21)]
+    want = None
+    for p, t in enumerate(toks):
+        want = ref.forward(t, p)
+    m = CudaModel(path)
+    got, am = m.prefill(toks, 0, tensor_cores=True)
+    assert close(got, want)
+    assert am == int(np.argmax(got)) == int(np.argmax(want))
+    ids = m.decode_greedy(am, len(toks), 8)
+    pos, n = len(toks), am
+    for k in range(8):
+        l = ref.forward(n, pos)
+        pos += 1
+        n = int(np.argmax(l))
+        assert int(ids[k]) == n
+
+
+def test_prefill_tensor_cores_wide(gguf_dir):
+    """A wider model and a 300-token prompt (several row and token tiles per
+    GEMM): tensor-core prefill against the exact-f32 prefill."""
+    spec = synth.tiny_spec("llama-q4_0", embd=1024, heads=8, kv_heads=2, ffn=2816, vocab=1024, ctx=512)
+    path = synth.write_gguf(spec, 11, gguf_dir / "pre-tc-wide.gguf")
+    toks = [int(t) for t in np.random.default_rng(11).integers(0, spec.vocab, size=300)]
+    m = CudaModel(path)
+    exact, am_exact = m.prefill(toks, 0)
+    m.reset_cache()
+    tc, am_tc = m.prefill(toks, 0, tensor_cores=True)
+    assert close(tc, exact)
+    assert am_tc == am_exact
+    # two tensor-core segments equal one pass
+    m.reset_cache()
+    m.prefill(toks[:170], 0, want_logits=False, tensor_cores=True)
+    two, _ = m.prefill(toks[170:], 170, tensor_cores=True)
+    assert close(two, tc, 1e-4)
+
+
 def test_prefill_errors(gguf_dir):
     spec = synth.tiny_spec("llama-q4_0")
     path = synth.write_gguf(spec, 8, gguf_dir / "pre-err.gguf")
