@@ -206,7 +206,7 @@ void launch_add_rows(float* X, const float* Y, uint64_t n, cudaStream_t s);
 // A bounded wait that gives up raises bit 6 of the device error word.
 void launch_tc_gemm(const __half* W, uint32_t N, uint32_t K, const __half* X, uint32_t T, float* Y, uint32_t ldy,
                     cudaStream_t s);
-// Token-tile width (64 or 128) the GEMM uses for an N x T output.
+// Token-tile width (64, 128 or 256) the GEMM uses for an N x T output.
 uint32_t tc_gemm_token_tile(uint32_t N, uint32_t T);
 // dst[i] = (f16) src[i], round to nearest even (src 16-byte, dst 8-byte aligned).
 void launch_f32_to_f16(const float* src, __half* dst, uint64_t n, cudaStream_t s);

@@ -6,6 +6,9 @@
 // RMSNorm (ops.cpp:29-40), bias + RoPE + KV append (qwen2_model.cpp:97-110),
 // causal GQA attention (qwen2_model.cpp:111-133), SiLU * up (ops.cpp:60-65,
 // 325-330) and the residual adds.
+#include <mutex>
+#include <unordered_map>
+
 #include "common.cuh"
 #include "engine.h"
 
@@ -70,130 +73,184 @@ __global__ void qkv_post_kernel(const float* Y, uint32_t rows, uint32_t T, uint3
     }
 }
 
-// Causal attention of token t (position pos0 + t) for the `group` query heads
-// of KV head g: one CTA per (t, g), keys 0..pos0 + t in chunks of 32 staged in
-// shared memory, online softmax across chunks (ops::softmax, ops.cpp:43-57).
-constexpr uint32_t kPreChunk = 32;
-constexpr int kPreMaxGroup = 8;
+// Causal attention over the prompt (the reference's per-token attention loop,
+// src/model/qwen2_model.cpp:111-133, with ops::softmax, ops.cpp:43-57, for
+// every prompt token at once).  One CTA of 8 warps per (block of 8 query
+// tokens, KV head g); warp w owns token t0 + w and its G query heads.
+// Chunks of 32 keys (K rows padded to HD + 4 floats, so the lanes' float4
+// reads of 32 different rows are conflict-free) are staged once in shared
+// memory and used by all 8 tokens.  Scores: lane = key, so each row's online
+// softmax (running max, sum, rescale) is a warp reduction; probabilities go
+// through a warp-private shared-memory row to the PV product, where lane owns
+// HD/32 output dimensions.  f32 throughout, expf as the reference.
+constexpr uint32_t kPreChunk = 32;   // keys per chunk (= lanes)
+constexpr uint32_t kPreTokens = 8;   // query tokens per CTA (= warps)
+constexpr int kPreMaxGroup = 8;      // query heads per KV head
 
-template <int HD>
-__global__ void __launch_bounds__(128) attention_prefill_kernel(const float* Q, const float* kc, const float* vc,
-                                                                uint32_t n_heads, uint32_t n_kv, uint32_t max_ctx,
-                                                                uint32_t pos0, float* out) {
-    constexpr int PARTS = 128 / HD;
-    constexpr int DL = HD / 8, DV = DL / 4;
-    __shared__ __align__(16) float ks[kPreChunk * HD];
-    __shared__ __align__(16) float vs[kPreChunk * HD];
-    __shared__ __align__(16) float qs[kPreMaxGroup * HD];
-    __shared__ float sc[kPreMaxGroup * kPreChunk];
-    __shared__ float corr[kPreMaxGroup], pm[kPreMaxGroup], pl[kPreMaxGroup];
-    __shared__ float red[(128 - 32) * kPreMaxGroup + kPreMaxGroup];
-    const uint32_t G = n_heads / n_kv;
-    const uint32_t t = blockIdx.x, g = blockIdx.y;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t n = pos0 + t + 1;
-    const float* q = Q + (size_t)t * n_heads * HD + (size_t)g * G * HD;
-    for (uint32_t i = tid; i < G * HD; i += 128) qs[i] = q[i];
-    if (tid < kPreMaxGroup) {
-        pm[tid] = -INFINITY;
-        pl[tid] = 0.f;
+template <int HD, int G>
+struct PreAttnSmem {
+    static constexpr int KSTR = HD + 4;
+    static constexpr size_t q = (size_t)kPreTokens * G * HD;  // [token][head][HD]
+    static constexpr size_t k = (size_t)kPreChunk * KSTR;      // [key][HD + 4]
+    static constexpr size_t v = (size_t)kPreChunk * HD;        // [key][HD]
+    static constexpr size_t p = (size_t)kPreTokens * G * kPreChunk;
+    static constexpr size_t bytes = 4 * (q + k + v + p);
+};
+
+template <int HD, int G>
+__global__ void __launch_bounds__(256) attention_prefill_kernel(const float* __restrict__ Q,
+                                                                const float* __restrict__ kc,
+                                                                const float* __restrict__ vc, uint32_t n_heads,
+                                                                uint32_t max_ctx, uint32_t pos0, uint32_t T,
+                                                                float* __restrict__ out) {
+    using S = PreAttnSmem<HD, G>;
+    constexpr int DPL = HD / 32;  // output dims per lane
+    extern __shared__ __align__(16) float pre_smem[];
+    float* qs = pre_smem;
+    float* ks = qs + S::q;
+    float* vs = ks + S::k;
+    float* ps = vs + S::v;
+    const uint32_t tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    // heaviest (last) token blocks first
+    const uint32_t t0 = (gridDim.x - 1 - blockIdx.x) * kPreTokens, g = blockIdx.y;
+    const uint32_t t = t0 + w;
+    const bool live = t < T;
+    const uint32_t t_last = min(t0 + kPreTokens, T) - 1;
+    const uint32_t n_keys = pos0 + t_last + 1;  // keys the block's last token attends to
+    const uint32_t my_keys = pos0 + t + 1;      // this warp's token (causal)
+
+    // q tile: [token][head][HD]
+    for (uint32_t i = tid; i < kPreTokens * G * HD / 4; i += 256) {
+        const uint32_t tok = i / (G * HD / 4), rem = i % (G * HD / 4);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t0 + tok < T)
+            v = reinterpret_cast<const float4*>(Q + (size_t)(t0 + tok) * n_heads * HD + (size_t)g * G * HD)[rem];
+        reinterpret_cast<float4*>(qs)[i] = v;
     }
     const float scale = 1.0f / sqrtf((float)HD);
-    const int d = tid % HD, part = tid / HD;
-    float acc[kPreMaxGroup];
+    float m[G], l[G], acc[G][DPL];
 #pragma unroll
-    for (int h = 0; h < kPreMaxGroup; ++h) acc[h] = 0.f;
+    for (int i = 0; i < G; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.f;
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) acc[i][j] = 0.f;
+    }
     const float* kb = kc + (size_t)g * max_ctx * HD;
     const float* vb = vc + (size_t)g * max_ctx * HD;
-    for (uint32_t c0 = 0; c0 < n; c0 += kPreChunk) {
-        const uint32_t len = min(kPreChunk, n - c0);
-        __syncthreads();
-        for (uint32_t i = tid; i < len * HD / 4; i += 128) {
-            reinterpret_cast<float4*>(ks)[i] = reinterpret_cast<const float4*>(kb + (size_t)c0 * HD)[i];
+    const float* qw = qs + (size_t)w * G * HD;
+    float* pw = ps + (size_t)w * G * kPreChunk;
+    for (uint32_t c0 = 0; c0 < n_keys; c0 += kPreChunk) {
+        const uint32_t len = min(kPreChunk, n_keys - c0);
+        __syncthreads();  // the previous chunk's K/V are no longer read
+        for (uint32_t i = tid; i < len * HD / 4; i += 256) {
+            const uint32_t key = i / (HD / 4), c4 = i % (HD / 4);
+            reinterpret_cast<float4*>(ks + key * S::KSTR)[c4] =
+                reinterpret_cast<const float4*>(kb + (size_t)(c0 + key) * HD)[c4];
             reinterpret_cast<float4*>(vs)[i] = reinterpret_cast<const float4*>(vb + (size_t)c0 * HD)[i];
         }
         __syncthreads();
-        // scores: 8 lanes per key, uniform pass loop (all lanes reach the shuffles)
-        const int l8 = tid & 7, grp = tid >> 3;
-        for (uint32_t tb = 0; tb < len; tb += 16) {
-            const uint32_t tt = tb + grp;
-            const bool act = tt < len;
-            float4 kv[DV];
+        // scores of key c0 + lane for the G heads of this warp's token
+        const bool valid = live && lane < len && c0 + lane < my_keys;
+        float sc[G];
 #pragma unroll
-            for (int j = 0; j < DV; ++j)
-                kv[j] = act ? reinterpret_cast<const float4*>(ks + tt * HD)[l8 + 8 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
-            float s[kPreMaxGroup];
+        for (int i = 0; i < G; ++i) sc[i] = 0.f;
+        if (lane < len) {
+            const float* kr = ks + lane * S::KSTR;
+#pragma unroll 4
+            for (int d = 0; d < HD; d += 4) {
+                const float4 k4 = *reinterpret_cast<const float4*>(kr + d);
 #pragma unroll
-            for (int h = 0; h < kPreMaxGroup; ++h) {
-                s[h] = 0.f;
-                if (h < (int)G) {
-#pragma unroll
-                    for (int j = 0; j < DV; ++j) {
-                        const float4 q4 = reinterpret_cast<const float4*>(qs + h * HD)[l8 + 8 * j];
-                        s[h] = fmaf(q4.x, kv[j].x, s[h]);
-                        s[h] = fmaf(q4.y, kv[j].y, s[h]);
-                        s[h] = fmaf(q4.z, kv[j].z, s[h]);
-                        s[h] = fmaf(q4.w, kv[j].w, s[h]);
-                    }
+                for (int i = 0; i < G; ++i) {
+                    const float4 q4 = *reinterpret_cast<const float4*>(qw + i * HD + d);
+                    sc[i] = fmaf(q4.x, k4.x, sc[i]);
+                    sc[i] = fmaf(q4.y, k4.y, sc[i]);
+                    sc[i] = fmaf(q4.z, k4.z, sc[i]);
+                    sc[i] = fmaf(q4.w, k4.w, sc[i]);
                 }
             }
+        }
+        // online softmax per head (all lanes hold the row state)
+        float corr[G];
 #pragma unroll
-            for (int o = 4; o >= 1; o >>= 1) {
+        for (int i = 0; i < G; ++i) {
+            const float sv = valid ? sc[i] * scale : -INFINITY;
+            const float m_new = fmaxf(m[i], warp_max(sv));
+            const float e = valid ? expf(sv - m_new) : 0.f;
+            const float cf = m[i] == -INFINITY ? 0.f : expf(m[i] - m_new);
+            l[i] = fmaf(l[i], cf, warp_sum(e));
+            m[i] = m_new;
+            corr[i] = cf;
+            pw[i * kPreChunk + lane] = e;
+        }
+        __syncwarp();
 #pragma unroll
-                for (int h = 0; h < kPreMaxGroup; ++h)
-                    if (h < (int)G) s[h] += __shfl_xor_sync(0xffffffffu, s[h], o);
+        for (int i = 0; i < G; ++i)
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) acc[i][j] *= corr[i];
+        for (uint32_t key = 0; key < len; ++key) {
+            float v[DPL];
+            if constexpr (DPL == 4) {
+                const float4 v4 = reinterpret_cast<const float4*>(vs + key * HD)[lane];
+                v[0] = v4.x, v[1] = v4.y, v[2] = v4.z, v[3] = v4.w;
+            } else if constexpr (DPL == 2) {
+                const float2 v2 = reinterpret_cast<const float2*>(vs + key * HD)[lane];
+                v[0] = v2.x, v[1] = v2.y;
+            } else {
+                v[0] = vs[key * HD + lane];
             }
-            if (l8 == 0 && act) {
 #pragma unroll
-                for (int h = 0; h < kPreMaxGroup; ++h)
-                    if (h < (int)G) sc[h * kPreChunk + tt] = s[h] * scale;
+            for (int i = 0; i < G; ++i) {
+                const float p = pw[i * kPreChunk + key];
+#pragma unroll
+                for (int j = 0; j < DPL; ++j) acc[i][j] = fmaf(p, v[j], acc[i][j]);
             }
         }
-        __syncthreads();
-        for (uint32_t h = warp; h < G; h += 4) {
-            const float sv = (uint32_t)lane < len ? sc[h * kPreChunk + lane] : -INFINITY;
-            const float m_old = pm[h];
-            const float m_new = fmaxf(m_old, warp_max(sv));
-            const float e = (uint32_t)lane < len ? expf(sv - m_new) : 0.f;
-            const float l = warp_sum(e);
-            if ((uint32_t)lane < len) sc[h * kPreChunk + lane] = e;
-            if (lane == 0) {
-                const float cf = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
-                corr[h] = cf;
-                pl[h] = fmaf(pl[h], cf, l);
-                pm[h] = m_new;
-            }
-        }
-        __syncthreads();
-#pragma unroll
-        for (int h = 0; h < kPreMaxGroup; ++h)
-            if (h < (int)G) acc[h] *= corr[h];
-        for (uint32_t tt = part; tt < len; tt += PARTS) {
-            const float v = vs[tt * HD + d];
-#pragma unroll
-            for (int h = 0; h < kPreMaxGroup; ++h)
-                if (h < (int)G) acc[h] = fmaf(sc[h * kPreChunk + tt], v, acc[h]);
-        }
+        __syncwarp();  // pw is rewritten by the next chunk
     }
-    if constexpr (PARTS > 1) {
-        __syncthreads();
-        if (part > 0) {
-#pragma unroll
-            for (int h = 0; h < kPreMaxGroup; ++h) red[((part - 1) * HD + d) * kPreMaxGroup + h] = acc[h];
-        }
-        __syncthreads();
-    }
-    if (part == 0) {
+    if (live) {
         float* o = out + (size_t)t * n_heads * HD + (size_t)g * G * HD;
 #pragma unroll
-        for (int h = 0; h < kPreMaxGroup; ++h) {
-            if (h < (int)G) {
-                float v = acc[h];
+        for (int i = 0; i < G; ++i)
 #pragma unroll
-                for (int k = 1; k < PARTS; ++k) v += red[((k - 1) * HD + d) * kPreMaxGroup + h];
-                o[h * HD + d] = v / pl[h];
-            }
+            for (int j = 0; j < DPL; ++j) o[i * HD + lane * DPL + j] = acc[i][j] / l[i];
+    }
+}
+
+template <int HD, int G>
+static void launch_pre_attn(const float* Q, const float* kc, const float* vc, uint32_t n_heads, uint32_t n_kv,
+                            uint32_t max_ctx, uint32_t pos0, uint32_t T, float* out, cudaStream_t s) {
+    using S = PreAttnSmem<HD, G>;
+    static std::mutex mu;
+    static std::unordered_map<int, bool> configured;
+    int dev = 0;
+    SM_CUDA(cudaGetDevice(&dev));
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!configured.count(dev)) {
+            SM_CUDA(cudaFuncSetAttribute(attention_prefill_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)S::bytes));
+            configured[dev] = true;
         }
+    }
+    const dim3 grid((T + kPreTokens - 1) / kPreTokens, n_kv);
+    attention_prefill_kernel<HD, G><<<grid, 256, S::bytes, s>>>(Q, kc, vc, n_heads, max_ctx, pos0, T, out);
+}
+
+template <int HD>
+static void launch_pre_attn_hd(uint32_t G, const float* Q, const float* kc, const float* vc, uint32_t n_heads,
+                               uint32_t n_kv, uint32_t max_ctx, uint32_t pos0, uint32_t T, float* out,
+                               cudaStream_t s) {
+    switch (G) {
+        case 1: return launch_pre_attn<HD, 1>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
+        case 2: return launch_pre_attn<HD, 2>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
+        case 3: return launch_pre_attn<HD, 3>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
+        case 4: return launch_pre_attn<HD, 4>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
+        case 5: return launch_pre_attn<HD, 5>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
+        case 6: return launch_pre_attn<HD, 6>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
+        case 7: return launch_pre_attn<HD, 7>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
+        case 8: return launch_pre_attn<HD, 8>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
+        default: throw Error(1, "prefill attention: unsupported head grouping");
     }
 }
 
@@ -233,10 +290,10 @@ void launch_attention_prefill(const float* Q, const float* kc, const float* vc, 
                               cudaStream_t s) {
     if (n_heads % n_kv || n_heads / n_kv > (uint32_t)kPreMaxGroup)
         throw Error(1, "prefill attention: unsupported head grouping");
-    const dim3 grid(T, n_kv);
-    if (hd == 32) attention_prefill_kernel<32><<<grid, 128, 0, s>>>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, out);
-    else if (hd == 64) attention_prefill_kernel<64><<<grid, 128, 0, s>>>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, out);
-    else if (hd == 128) attention_prefill_kernel<128><<<grid, 128, 0, s>>>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, out);
+    const uint32_t G = n_heads / n_kv;
+    if (hd == 32) launch_pre_attn_hd<32>(G, Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
+    else if (hd == 64) launch_pre_attn_hd<64>(G, Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
+    else if (hd == 128) launch_pre_attn_hd<128>(G, Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
     else throw Error(1, "prefill attention: head_dim must be 32, 64 or 128");
     SM_CUDA(cudaGetLastError());
 }

@@ -5,17 +5,20 @@
 // The prefill's linear layers are the one dense contraction of the engine
 // (the reference runs them as one matmul_quantized per token,
 // src/core/ops.cpp:103-184, called from Model::forward once per prompt token,
-// src/runtime/generator.cpp:47-51).  One CTA computes a 128 x BN tile of
-// W-rows x tokens:
+// src/runtime/generator.cpp:47-51).  A persistent grid (one CTA per SM)
+// walks 128 x BN output tiles of W-rows x tokens (BN = 64, 128 or 256):
 //   - warp 0, one lane: TMA producer.  2-D tiled bulk tensor copies of a
 //     128 x 64 W tile and a BN x 64 X tile per stage (64 f16 = one 128-byte
-//     row, 128-byte swizzle), completing on the stage's mbarrier;
+//     row, 128-byte swizzle) into a ring of stages, completing on the stage's
+//     mbarrier;
 //   - warp 1, one lane: MMA issuer.  Four tcgen05.mma kind::f16 (K = 16 each)
 //     per stage into an f32 accumulator in tensor memory; tcgen05.commit
-//     frees the stage when its MMAs have read it;
-//   - warp 2 allocates BN tensor-memory columns; all four warps then read
-//     their 32 accumulator lanes (tcgen05.ld 32x32b) and store them: lane =
-//     W row, so a warp's stores of one token's 32 outputs are one 128-byte line.
+//     frees the stage when its MMAs have read it.  Tiles alternate between two
+//     accumulators (2 x BN TMEM columns), so one tile's epilogue overlaps the
+//     next tile's MMAs;
+//   - warps 2..5: epilogue.  Each reads its 32 accumulator lanes (tcgen05.ld
+//     32x32b) and stores them: lane = W row, so a warp's stores of one
+//     token's 32 outputs are one 128-byte line.
 // Every mbarrier wait is bounded (mbar_wait: ~2^31 cycles); a wait that gives
 // up raises bit 6 of the device error word and the CTA finishes without
 // further MMAs, so the host sees an error instead of a hang.
@@ -44,14 +47,15 @@ constexpr unsigned kErrTcGemm = 64u;
 
 template <uint32_t BN>
 struct TcCfg {
-    static_assert(BN == 64 || BN == 128, "token tile");
+    static_assert(BN == 64 || BN == 128 || BN == 256, "token tile");
     static constexpr uint32_t a_bytes = kBM * kBK * 2;  // 16 KB
-    static constexpr uint32_t b_bytes = BN * kBK * 2;   // 8 / 16 KB
+    static constexpr uint32_t b_bytes = BN * kBK * 2;   // 8 / 16 / 32 KB
     static constexpr uint32_t stage_bytes = a_bytes + b_bytes;
-    static constexpr uint32_t stages = 192u * 1024u / stage_bytes;  // 8 / 6
-    static constexpr uint32_t tmem_cols = BN;                       // f32 accumulator columns
-    static constexpr size_t smem = 1024 + (size_t)stages * stage_bytes + 256;
+    static constexpr uint32_t stages = 192u * 1024u / stage_bytes;  // 8 / 6 / 4
+    static constexpr uint32_t tmem_cols = 2 * BN;                   // two f32 accumulators
+    static constexpr size_t smem = 1024 + (size_t)stages * stage_bytes + 512;
 };
+constexpr uint32_t kThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
 
 // ---- PTX wrappers ----------------------------------------------------------
 
@@ -112,7 +116,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 // ---- the kernel --------------------------------------------------------------
 
 template <uint32_t BN>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx,
                    float* __restrict__ y, uint32_t N, uint32_t T, uint32_t K, uint32_t ldy, unsigned int* err) {
     using C = TcCfg<BN>;
@@ -123,25 +127,30 @@ __global__ void __launch_bounds__(128, 1)
     uint8_t* sb = smem + C::stages * C::a_bytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(sb + C::stages * C::b_bytes);
     uint64_t* empty = full + C::stages;
-    uint64_t* done = empty + C::stages;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* acc_full = empty + C::stages;  // [2] MMA -> epilogue: accumulator b complete
+    uint64_t* acc_empty = acc_full + 2;      // [2] epilogue -> MMA: accumulator b drained
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t t0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
     const uint32_t nk = (K + kBK - 1) / kBK;
+    const uint32_t n_t = (T + BN - 1) / BN;                 // token tiles (fastest: CTAs running
+    const uint32_t tiles = n_t * ((N + kBM - 1) / kBM);     // together share W rows in L2)
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < C::stages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(done, 1);
+        for (uint32_t b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 128);
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tw)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tx)) : "memory");
     }
-    if (warp == 2) {
+    if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(C::tmem_cols)
                      : "memory");
@@ -152,61 +161,99 @@ __global__ void __launch_bounds__(128, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0 && lane == 0) {
-        // producer: stage s is refilled once the MMAs of its previous use completed
-        for (uint32_t kb = 0; kb < nk; ++kb) {
-            const uint32_t s = kb % C::stages, use = kb / C::stages;
-            if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) {
-                atomicOr(err, kErrTcGemm);
-                break;
+    if (warp == 0) {
+        if (lane == 0) {
+            // producer: a stage is refilled once the MMAs of its previous use completed
+            uint32_t it = 0;
+            for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+                const int32_t t0 = (int32_t)((tile % n_t) * BN), m0 = (int32_t)((tile / n_t) * kBM);
+                bool ok = true;
+                for (uint32_t kb = 0; kb < nk; ++kb, ++it) {
+                    const uint32_t s = it % C::stages, use = it / C::stages;
+                    if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], C::stage_bytes);
+                    tma_load_2d(sa + s * C::a_bytes, &tw, (int32_t)(kb * kBK), m0, &full[s]);
+                    tma_load_2d(sb + s * C::b_bytes, &tx, (int32_t)(kb * kBK), t0, &full[s]);
+                }
+                if (!ok) {
+                    atomicOr(err, kErrTcGemm);
+                    break;
+                }
             }
-            mbar_arrive_expect_tx(&full[s], C::stage_bytes);
-            tma_load_2d(sa + s * C::a_bytes, &tw, (int32_t)(kb * kBK), (int32_t)m0, &full[s]);
-            tma_load_2d(sb + s * C::b_bytes, &tx, (int32_t)(kb * kBK), (int32_t)t0, &full[s]);
         }
-    } else if (warp == 1 && lane == 0) {
-        // MMA issuer
-        constexpr uint32_t idesc = idesc_f16_f32<BN>();
-        for (uint32_t kb = 0; kb < nk; ++kb) {
-            const uint32_t s = kb % C::stages, use = kb / C::stages;
-            if (!mbar_wait(&full[s], use & 1)) {
-                atomicOr(err, kErrTcGemm);
-                break;
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // MMA issuer: tile j accumulates into TMEM columns (j & 1) * BN
+            constexpr uint32_t idesc = idesc_f16_f32<BN>();
+            uint32_t it = 0, j = 0;
+            for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++j) {
+                const uint32_t b = j & 1, buse = j >> 1;
+                if (buse > 0 && !mbar_wait(&acc_empty[b], (buse - 1) & 1)) {
+                    atomicOr(err, kErrTcGemm);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + b * BN;
+                bool ok = true;
+                for (uint32_t kb = 0; kb < nk; ++kb, ++it) {
+                    const uint32_t s = it % C::stages, use = it / C::stages;
+                    if (!mbar_wait(&full[s], use & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t da = smem_desc_sw128(sa + s * C::a_bytes);
+                    const uint64_t db = smem_desc_sw128(sb + s * C::b_bytes);
+#pragma unroll
+                    for (uint32_t k = 0; k < kBK / kUK; ++k)  // +32 bytes = +2 in the 16-byte address field
+                        mma_f16(d, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+                    mma_commit(&empty[s]);
+                }
+                mma_commit(&acc_full[b]);  // arrives when every MMA issued so far has completed
+                if (!ok) {
+                    atomicOr(err, kErrTcGemm);
+                    break;
+                }
             }
+        }
+    } else {
+        // epilogue warps 2..5: warp w reads TMEM lanes (W rows) 32 (w % 4) .. + 31
+        const uint32_t q = warp & 3;
+        const uint32_t lane_base = tmem + ((q * 32u) << 16);
+        uint32_t j = 0;
+        for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++j) {
+            const uint32_t b = j & 1, buse = j >> 1;
+            const uint32_t t0 = (tile % n_t) * BN, m = (tile / n_t) * kBM + q * 32 + lane;
+            const bool ok = mbar_wait(&acc_full[b], buse & 1);
+            __syncwarp();
             tc_fence_after();
-            const uint64_t da = smem_desc_sw128(sa + s * C::a_bytes);
-            const uint64_t db = smem_desc_sw128(sb + s * C::b_bytes);
-#pragma unroll
-            for (uint32_t k = 0; k < kBK / kUK; ++k)  // +32 bytes = +2 in the 16-byte address field
-                mma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
-            mma_commit(&empty[s]);
-        }
-        mma_commit(done);  // arrives when every MMA issued above has completed
-    }
-    __syncwarp();
-
-    // epilogue: warp w owns accumulator lanes (W rows) 32w .. 32w + 31
-    const bool ok = mbar_wait(done, 0);
-    if (!ok && lane == 0) atomicOr(err, kErrTcGemm);
-    __syncwarp();
-    tc_fence_after();
-    const uint32_t m = m0 + warp * 32 + lane;
-    const uint32_t taddr = tmem + ((warp * 32u) << 16);
 #pragma unroll 1
-    for (uint32_t c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(taddr + c, r);
-        if (ok && m < N) {
+            for (uint32_t c = 0; c < BN; c += 32) {
+                uint32_t r[32];
+                tmem_ld32(lane_base + b * BN + c, r);
+                if (ok && m < N) {
 #pragma unroll
-            for (uint32_t j = 0; j < 32; ++j) {
-                const uint32_t t = t0 + c + j;
-                if (t < T) y[(size_t)t * ldy + m] = __uint_as_float(r[j]);
+                    for (uint32_t i = 0; i < 32; ++i) {
+                        const uint32_t t = t0 + c + i;
+                        if (t < T) y[(size_t)t * ldy + m] = __uint_as_float(r[i]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&acc_empty[b]);
+            if (!ok) {
+                if (lane == 0) atomicOr(err, kErrTcGemm);
+                break;
             }
         }
     }
+    __syncwarp();
     tc_fence_before();
     __syncthreads();
-    if (warp == 2) {
+    if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::tmem_cols)
                      : "memory");
@@ -276,16 +323,33 @@ void launch_tc(const CUtensorMap& tw, const CUtensorMap& tx, float* Y, uint32_t 
             configured[dev] = true;
         }
     }
-    const dim3 grid((T + BN - 1) / BN, (N + kBM - 1) / kBM);
-    tc_gemm_kernel<BN><<<grid, 128, C::smem, s>>>(tw, tx, Y, N, T, K, ldy, device_error_flag());
+    const uint64_t tiles = (uint64_t)((T + BN - 1) / BN) * ((N + kBM - 1) / kBM);
+    const uint32_t grid = (uint32_t)std::min<uint64_t>(tiles, (uint64_t)device_sm_count());
+    tc_gemm_kernel<BN><<<grid, kThreads, C::smem, s>>>(tw, tx, Y, N, T, K, ldy, device_error_flag());
     SM_CUDA(cudaGetLastError());
 }
 
 }  // namespace
 
+// Token-tile width from a wave model of the persistent grid: per 64-wide K
+// stage a 128 x BN tile costs max(MMA, shared-memory operand reads) =
+// max(2 BN, 128 + BN) SM cycles (M=128, N=BN, K=16 MMAs at ~8 K flop/cycle;
+// 16 KB of W plus BN x 128 bytes of X read at 128 bytes/cycle), and the
+// grid runs ceil(tiles / SMs) rounds of tiles.  Ties go to the wider tile
+// (fewer re-reads of W).
 uint32_t tc_gemm_token_tile(uint32_t N, uint32_t T) {
-    const uint64_t tiles128 = (uint64_t)((T + 127) / 128) * ((N + kBM - 1) / kBM);
-    return tiles128 >= (uint64_t)device_sm_count() ? 128u : 64u;
+    const uint64_t sms = (uint64_t)device_sm_count(), n_m = (N + kBM - 1) / kBM;
+    uint32_t best = 64;
+    uint64_t best_cost = ~0ull;
+    for (uint32_t bn : {256u, 128u, 64u}) {
+        const uint64_t tiles = (uint64_t)((T + bn - 1) / bn) * n_m;
+        const uint64_t cost = (tiles + sms - 1) / sms * std::max<uint64_t>(2 * bn, 128 + bn);
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = bn;
+        }
+    }
+    return best;
 }
 
 void launch_tc_gemm(const __half* W, uint32_t N, uint32_t K, const __half* X, uint32_t T, float* Y, uint32_t ldy,
@@ -299,7 +363,8 @@ void launch_tc_gemm(const __half* W, uint32_t N, uint32_t K, const __half* X, ui
     const uint32_t bn = tc_gemm_token_tile(N, T);
     const CUtensorMap tw = f16_map(W, K, N, kBM);
     const CUtensorMap tx = f16_map(X, K, T, bn);
-    if (bn == 128) launch_tc<128>(tw, tx, Y, N, T, K, ldy, s);
+    if (bn == 256) launch_tc<256>(tw, tx, Y, N, T, K, ldy, s);
+    else if (bn == 128) launch_tc<128>(tw, tx, Y, N, T, K, ldy, s);
     else launch_tc<64>(tw, tx, Y, N, T, K, ldy, s);
 }
 

@@ -7,8 +7,8 @@ accumulation order and rounding of the f32 sum:
 (an operand-layout mistake gives errors of the size of y itself).  Shapes
 cover one tile, ragged N/K/T (partial tiles and a partial last K stage that
 the tensor map zero-fills), the prefill shapes of the Qwen2-1.5B and
-Llama-3-8B decoders (many trips around the stage ring) and both token-tile
-widths."""
+Llama-3-8B decoders (many trips around the stage ring), all three token-tile
+widths and persistent CTAs that take several tiles."""
 import ctypes
 
 import numpy as np
@@ -58,7 +58,10 @@ def check(y, w, x):
     (300, 200, 37),      # ragged rows, K (a partial last stage) and tokens
     (2048, 1536, 512),   # Qwen2-1.5B QKV over a 512-token prompt (64-token tiles)
     (4096, 14336, 128),  # Llama-3-8B down: 224 K stages around the ring
-    (28672, 4096, 256),  # Llama-3-8B gate/up: 128-token tiles
+    (4096, 1024, 384),   # 128-token tiles
+    (28672, 4096, 256),  # Llama-3-8B gate/up: 256-token tiles, some CTAs take two
+    (17920, 1536, 2048), # Qwen2-1.5B gate/up over 4 x 512 tokens: ~8 tiles per CTA,
+                         # both accumulators reused several times
 ])
 def test_tc_gemm_matches_f64(be, N, K, T):
     w, x = operands(N, K, T, seed=N + K + T)
