@@ -48,6 +48,22 @@ def build(ref: bool = True) -> None:
         raise RuntimeError("oracle build failed:\n" + r.stdout + r.stderr)
 
 
+DROPIN = HERE / "_ref" / "dropin_driver"
+
+
+def build_dropin() -> Path:
+    """make -C oracle dropin: the reference's sources + dropin_driver.cpp +
+    the C++ adapters, linked against the already built CUDA backend."""
+    r = subprocess.run(["make", "-s", "-C", str(HERE), "dropin"], capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("drop-in driver build failed:\n" + r.stdout + r.stderr)
+    return DROPIN
+
+
+def reference_sources_present() -> bool:
+    return Path("/root/reference/src/core/ops.cpp").exists()
+
+
 def type_nbytes(t: int, count: int) -> int:
     be, bb = _BLOCK[t]
     return count // be * bb

@@ -96,7 +96,7 @@ def cuda_sources() -> list[Path]:
 
 def cuda_headers() -> list[Path]:
     return sorted(list(CSRC.glob("*.h")) + list(CSRC.glob("*.cuh")) +
-                  list((ROOT / "include").glob("*.h")))
+                  list((ROOT / "include").glob("*.h")) + [CSRC / "exports.map"])
 
 
 def build_cuda(force: bool = False, jobs: int | None = None) -> Path:
@@ -137,7 +137,8 @@ def build_cuda(force: bool = False, jobs: int | None = None) -> Path:
     cuda_lib = Path(nvcc).resolve().parent.parent / "lib64"  # cuBLAS (prefill GEMMs)
     _run([nvcc, *ARCH, "-shared", "-cudart", "static", "-o", str(CUDA_LIB),
           *[str(o) for o in objs], "-L", str(lib_nccl), "-l:libnccl.so.2", "-L", str(cuda_lib), "-lcublas",
-          "-Xlinker", f"-rpath={lib_nccl}", "-Xlinker", f"-rpath={cuda_lib}"])
+          "-Xlinker", f"-rpath={lib_nccl}", "-Xlinker", f"-rpath={cuda_lib}",
+          "-Xlinker", f"--version-script={CSRC / 'exports.map'}"])
     return CUDA_LIB
 
 
