@@ -190,14 +190,17 @@ unsigned int* device_error_flag();
 // Batched prefill (prefill.cu and the embedding in kernels.cu): rows are
 // tokens, T of them at positions pos0 .. pos0 + T - 1.
 void launch_embed_rows(const QMat& emb, const uint32_t* tokens, uint32_t T, float* X, cudaStream_t stream);
+// The *_rows kernels and the attention write f16 to the last argument instead
+// of f32 when it is set (the tensor-core GEMM's input).
 void launch_rmsnorm_rows(const float* X, const float* w, uint32_t n, uint32_t T, float eps, float* Y,
-                         cudaStream_t s);
+                         cudaStream_t s, __half* Yh = nullptr);
 void launch_qkv_post(const float* Y, uint32_t rows, uint32_t T, uint32_t q_rows, uint32_t k_rows, uint32_t hd,
                      const float* bias, const float2* rope, uint32_t pos0, uint32_t max_ctx, float* Q, float* kc,
                      float* vc, cudaStream_t s);
 void launch_attention_prefill(const float* Q, const float* kc, const float* vc, uint32_t n_heads, uint32_t n_kv,
-                              uint32_t hd, uint32_t max_ctx, uint32_t pos0, uint32_t T, float* out, cudaStream_t s);
-void launch_swiglu_rows(const float* Y, uint32_t ffn, uint32_t T, float* H, cudaStream_t s);
+                              uint32_t hd, uint32_t max_ctx, uint32_t pos0, uint32_t T, float* out, cudaStream_t s,
+                              __half* out_h = nullptr);
+void launch_swiglu_rows(const float* Y, uint32_t ffn, uint32_t T, float* H, cudaStream_t s, __half* Hh = nullptr);
 void launch_add_rows(float* X, const float* Y, uint64_t n, cudaStream_t s);
 
 // Tensor-core GEMM of the batched prefill (tc_gemm.cu, tcgen05 + TMA):

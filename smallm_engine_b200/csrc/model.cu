@@ -717,15 +717,14 @@ void Model::prefill(const uint32_t* tokens, uint32_t T, uint32_t pos0, float* ou
         pre_xh_cap = (uint64_t)T * std::max({embd, qrows, ffn_l});
         pre_xh = reinterpret_cast<__half*>(palloc(2 * pre_xh_cap));
     }
-    // Y[T][rows] = X[T][cols] . W^T: tcgen05 on f16 copies, or cuBLAS on f32 copies
+    // Y[T][rows] = X[T][cols] . W^T: tcgen05 on the f16 copies (X is then in
+    // pre_xh, written as f16 by the kernel that produced it), or cuBLAS on the
+    // f32 copies with X in f32
     auto linear = [&](const float* w32, const __half* w16, uint32_t rows, uint32_t cols, const float* X) {
-        if (tc) {
-            launch_f32_to_f16(X, pre_xh, (uint64_t)T * cols, stream);
-            launch_tc_gemm(w16, rows, cols, pre_xh, T, pre_y, rows, stream);
-        } else {
-            gemm(w32, rows, cols, X, T, pre_y, tf32);
-        }
+        if (tc) launch_tc_gemm(w16, rows, cols, pre_xh, T, pre_y, rows, stream);
+        else gemm(w32, rows, cols, X, T, pre_y, tf32);
     };
+    __half* const xh = tc ? pre_xh : nullptr;
     static const LayerF32 kNo32;
     static const LayerF16 kNo16;
     SM_CUDA(cudaMemcpyAsync(pre_tok, tokens, 4ull * T, cudaMemcpyHostToDevice, stream));
@@ -736,7 +735,7 @@ void Model::prefill(const uint32_t* tokens, uint32_t T, uint32_t pos0, float* ou
         const LayerF16& H = tc ? layers_f16[i] : kNo16;
         float* kc = kv + (size_t)(2 * i) * nkv_l * max_ctx * hd;
         float* vc = kv + (size_t)(2 * i + 1) * nkv_l * max_ctx * hd;
-        launch_rmsnorm_rows(pre_x, L.attn_norm, embd, T, eps, pre_xn, stream);
+        launch_rmsnorm_rows(pre_x, L.attn_norm, embd, T, eps, pre_xn, stream, xh);
         linear(F.qkv, H.qkv, L.qkv.rows, embd, pre_xn);
         launch_qkv_post(pre_y, L.qkv.rows, T, qrows, krows, hd, L.bias, rope, pos0, max_ctx, pre_q, kc, vc, stream);
         if (!L.fused_v) {
@@ -744,12 +743,12 @@ void Model::prefill(const uint32_t* tokens, uint32_t T, uint32_t pos0, float* ou
             launch_qkv_post(pre_y, L.v.rows, T, 0, 0, hd, L.bias ? L.bias + qrows + krows : nullptr, rope, pos0,
                             max_ctx, pre_q, kc, vc, stream);
         }
-        launch_attention_prefill(pre_q, kc, vc, nh_l, nkv_l, hd, max_ctx, pos0, T, pre_a, stream);
+        launch_attention_prefill(pre_q, kc, vc, nh_l, nkv_l, hd, max_ctx, pos0, T, pre_a, stream, xh);
         linear(F.o, H.o, embd, qrows, pre_a);
         launch_add_rows(pre_x, pre_y, (uint64_t)T * embd, stream);
-        launch_rmsnorm_rows(pre_x, L.ffn_norm, embd, T, eps, pre_xn, stream);
+        launch_rmsnorm_rows(pre_x, L.ffn_norm, embd, T, eps, pre_xn, stream, xh);
         linear(F.gu, H.gu, L.gu.rows, embd, pre_xn);
-        launch_swiglu_rows(pre_y, ffn_l, T, pre_h, stream);
+        launch_swiglu_rows(pre_y, ffn_l, T, pre_h, stream, xh);
         linear(F.down, H.down, embd, ffn_l, pre_h);
         launch_add_rows(pre_x, pre_y, (uint64_t)T * embd, stream);
     }

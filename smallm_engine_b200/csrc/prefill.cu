@@ -17,15 +17,21 @@ namespace smallm {
 constexpr int kPreThreads = 256;
 
 // Y[t] = X[t] * (1 / sqrt(mean(X[t]^2) + eps)) * w, one CTA per token.
-__global__ void rmsnorm_rows_kernel(const float* X, const float* w, uint32_t n, float eps, float* Y) {
+// (Yh: the same values rounded to f16 instead, the tensor-core GEMM's input.)
+__global__ void rmsnorm_rows_kernel(const float* X, const float* w, uint32_t n, float eps, float* Y, __half* Yh) {
     __shared__ float red[32];
     const float* x = X + (size_t)blockIdx.x * n;
-    float* y = Y + (size_t)blockIdx.x * n;
     float ss = 0.f;
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) ss += x[i] * x[i];
     ss = block_sum(ss, red);
     const float inv = 1.0f / sqrtf(ss / (float)n + eps);
-    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) y[i] = (x[i] * inv) * w[i];
+    if (Yh) {
+        __half* y = Yh + (size_t)blockIdx.x * n;
+        for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) y[i] = __float2half_rn((x[i] * inv) * w[i]);
+    } else {
+        float* y = Y + (size_t)blockIdx.x * n;
+        for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) y[i] = (x[i] * inv) * w[i];
+    }
 }
 
 // The QKV GEMM's rows (storage order: query rotary pairs, key rotary pairs,
@@ -75,35 +81,38 @@ __global__ void qkv_post_kernel(const float* Y, uint32_t rows, uint32_t T, uint3
 
 // Causal attention over the prompt (the reference's per-token attention loop,
 // src/model/qwen2_model.cpp:111-133, with ops::softmax, ops.cpp:43-57, for
-// every prompt token at once).  One CTA of 8 warps per (block of 8 query
+// every prompt token at once).  One CTA of TOK warps (8, or 4 when 8-token
+// blocks would leave fewer than two CTAs per SM) per (block of TOK query
 // tokens, KV head g); warp w owns token t0 + w and its G query heads.
 // Chunks of 32 keys (K rows padded to HD + 4 floats, so the lanes' float4
 // reads of 32 different rows are conflict-free) are staged once in shared
-// memory and used by all 8 tokens.  Scores: lane = key, so each row's online
+// memory and used by all TOK tokens.  Scores: lane = key, so each row's online
 // softmax (running max, sum, rescale) is a warp reduction; probabilities go
 // through a warp-private shared-memory row to the PV product, where lane owns
 // HD/32 output dimensions.  f32 throughout, expf as the reference.
 constexpr uint32_t kPreChunk = 32;   // keys per chunk (= lanes)
-constexpr uint32_t kPreTokens = 8;   // query tokens per CTA (= warps)
 constexpr int kPreMaxGroup = 8;      // query heads per KV head
 
-template <int HD, int G>
+template <int HD, int G, int TOK>
 struct PreAttnSmem {
     static constexpr int KSTR = HD + 4;
-    static constexpr size_t q = (size_t)kPreTokens * G * HD;  // [token][head][HD]
+    static constexpr size_t q = (size_t)TOK * G * HD;          // [token][head][HD]
     static constexpr size_t k = (size_t)kPreChunk * KSTR;      // [key][HD + 4]
     static constexpr size_t v = (size_t)kPreChunk * HD;        // [key][HD]
-    static constexpr size_t p = (size_t)kPreTokens * G * kPreChunk;
+    static constexpr size_t p = (size_t)TOK * G * kPreChunk;
     static constexpr size_t bytes = 4 * (q + k + v + p);
 };
 
-template <int HD, int G>
-__global__ void __launch_bounds__(256) attention_prefill_kernel(const float* __restrict__ Q,
-                                                                const float* __restrict__ kc,
-                                                                const float* __restrict__ vc, uint32_t n_heads,
-                                                                uint32_t max_ctx, uint32_t pos0, uint32_t T,
-                                                                float* __restrict__ out) {
-    using S = PreAttnSmem<HD, G>;
+// out (f32) or, when out_h is set, out_h (the same values rounded to f16,
+// the tensor-core GEMM's input).
+template <int HD, int G, int TOK>
+__global__ void __launch_bounds__(32 * TOK) attention_prefill_kernel(const float* __restrict__ Q,
+                                                                     const float* __restrict__ kc,
+                                                                     const float* __restrict__ vc, uint32_t n_heads,
+                                                                     uint32_t max_ctx, uint32_t pos0, uint32_t T,
+                                                                     float* __restrict__ out, __half* out_h) {
+    using S = PreAttnSmem<HD, G, TOK>;
+    constexpr uint32_t NT = 32 * TOK;  // threads
     constexpr int DPL = HD / 32;  // output dims per lane
     extern __shared__ __align__(16) float pre_smem[];
     float* qs = pre_smem;
@@ -112,15 +121,15 @@ __global__ void __launch_bounds__(256) attention_prefill_kernel(const float* __r
     float* ps = vs + S::v;
     const uint32_t tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     // heaviest (last) token blocks first
-    const uint32_t t0 = (gridDim.x - 1 - blockIdx.x) * kPreTokens, g = blockIdx.y;
+    const uint32_t t0 = (gridDim.x - 1 - blockIdx.x) * TOK, g = blockIdx.y;
     const uint32_t t = t0 + w;
     const bool live = t < T;
-    const uint32_t t_last = min(t0 + kPreTokens, T) - 1;
+    const uint32_t t_last = min(t0 + TOK, T) - 1;
     const uint32_t n_keys = pos0 + t_last + 1;  // keys the block's last token attends to
     const uint32_t my_keys = pos0 + t + 1;      // this warp's token (causal)
 
     // q tile: [token][head][HD]
-    for (uint32_t i = tid; i < kPreTokens * G * HD / 4; i += 256) {
+    for (uint32_t i = tid; i < TOK * G * HD / 4; i += NT) {
         const uint32_t tok = i / (G * HD / 4), rem = i % (G * HD / 4);
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (t0 + tok < T)
@@ -143,7 +152,7 @@ __global__ void __launch_bounds__(256) attention_prefill_kernel(const float* __r
     for (uint32_t c0 = 0; c0 < n_keys; c0 += kPreChunk) {
         const uint32_t len = min(kPreChunk, n_keys - c0);
         __syncthreads();  // the previous chunk's K/V are no longer read
-        for (uint32_t i = tid; i < len * HD / 4; i += 256) {
+        for (uint32_t i = tid; i < len * HD / 4; i += NT) {
             const uint32_t key = i / (HD / 4), c4 = i % (HD / 4);
             reinterpret_cast<float4*>(ks + key * S::KSTR)[c4] =
                 reinterpret_cast<const float4*>(kb + (size_t)(c0 + key) * HD)[c4];
@@ -209,18 +218,23 @@ __global__ void __launch_bounds__(256) attention_prefill_kernel(const float* __r
         __syncwarp();  // pw is rewritten by the next chunk
     }
     if (live) {
-        float* o = out + (size_t)t * n_heads * HD + (size_t)g * G * HD;
+        const size_t o = (size_t)t * n_heads * HD + (size_t)g * G * HD;
 #pragma unroll
         for (int i = 0; i < G; ++i)
 #pragma unroll
-            for (int j = 0; j < DPL; ++j) o[i * HD + lane * DPL + j] = acc[i][j] / l[i];
+            for (int j = 0; j < DPL; ++j) {
+                const float v = acc[i][j] / l[i];
+                if (out_h) out_h[o + i * HD + lane * DPL + j] = __float2half_rn(v);
+                else out[o + i * HD + lane * DPL + j] = v;
+            }
     }
 }
 
-template <int HD, int G>
-static void launch_pre_attn(const float* Q, const float* kc, const float* vc, uint32_t n_heads, uint32_t n_kv,
-                            uint32_t max_ctx, uint32_t pos0, uint32_t T, float* out, cudaStream_t s) {
-    using S = PreAttnSmem<HD, G>;
+template <int HD, int G, int TOK>
+static void launch_pre_attn_tok(const float* Q, const float* kc, const float* vc, uint32_t n_heads, uint32_t n_kv,
+                                uint32_t max_ctx, uint32_t pos0, uint32_t T, float* out, __half* out_h,
+                                cudaStream_t s) {
+    using S = PreAttnSmem<HD, G, TOK>;
     static std::mutex mu;
     static std::unordered_map<int, bool> configured;
     int dev = 0;
@@ -228,39 +242,55 @@ static void launch_pre_attn(const float* Q, const float* kc, const float* vc, ui
     {
         std::lock_guard<std::mutex> lk(mu);
         if (!configured.count(dev)) {
-            SM_CUDA(cudaFuncSetAttribute(attention_prefill_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)S::bytes));
+            SM_CUDA(cudaFuncSetAttribute(attention_prefill_kernel<HD, G, TOK>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::bytes));
             configured[dev] = true;
         }
     }
-    const dim3 grid((T + kPreTokens - 1) / kPreTokens, n_kv);
-    attention_prefill_kernel<HD, G><<<grid, 256, S::bytes, s>>>(Q, kc, vc, n_heads, max_ctx, pos0, T, out);
+    const dim3 grid((T + TOK - 1) / TOK, n_kv);
+    attention_prefill_kernel<HD, G, TOK><<<grid, 32 * TOK, S::bytes, s>>>(Q, kc, vc, n_heads, max_ctx, pos0, T, out,
+                                                                          out_h);
+}
+
+template <int HD, int G>
+static void launch_pre_attn(const float* Q, const float* kc, const float* vc, uint32_t n_heads, uint32_t n_kv,
+                            uint32_t max_ctx, uint32_t pos0, uint32_t T, float* out, __half* out_h,
+                            cudaStream_t s) {
+    // 8-token CTAs when they give at least two CTAs per SM, else 4-token ones
+    // (more CTAs, so heavy and light causal blocks pack together)
+    if ((uint64_t)((T + 7) / 8) * n_kv >= 2ull * device_sm_count())
+        launch_pre_attn_tok<HD, G, 8>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
+    else
+        launch_pre_attn_tok<HD, G, 4>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
 }
 
 template <int HD>
 static void launch_pre_attn_hd(uint32_t G, const float* Q, const float* kc, const float* vc, uint32_t n_heads,
                                uint32_t n_kv, uint32_t max_ctx, uint32_t pos0, uint32_t T, float* out,
-                               cudaStream_t s) {
+                               __half* out_h, cudaStream_t s) {
     switch (G) {
-        case 1: return launch_pre_attn<HD, 1>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
-        case 2: return launch_pre_attn<HD, 2>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
-        case 3: return launch_pre_attn<HD, 3>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
-        case 4: return launch_pre_attn<HD, 4>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
-        case 5: return launch_pre_attn<HD, 5>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
-        case 6: return launch_pre_attn<HD, 6>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
-        case 7: return launch_pre_attn<HD, 7>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
-        case 8: return launch_pre_attn<HD, 8>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
+        case 1: return launch_pre_attn<HD, 1>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
+        case 2: return launch_pre_attn<HD, 2>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
+        case 3: return launch_pre_attn<HD, 3>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
+        case 4: return launch_pre_attn<HD, 4>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
+        case 5: return launch_pre_attn<HD, 5>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
+        case 6: return launch_pre_attn<HD, 6>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
+        case 7: return launch_pre_attn<HD, 7>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
+        case 8: return launch_pre_attn<HD, 8>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
         default: throw Error(1, "prefill attention: unsupported head grouping");
     }
 }
 
 // H[t][j] = silu(Y[t][2j]) * Y[t][2j+1] (gate / up rows interleaved).
-__global__ void swiglu_rows_kernel(const float* Y, uint32_t ffn, uint32_t T, float* H) {
+// (Hh: the same values rounded to f16 instead, the tensor-core GEMM's input.)
+__global__ void swiglu_rows_kernel(const float* Y, uint32_t ffn, uint32_t T, float* H, __half* Hh) {
     const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (uint64_t)T * ffn) return;
     const uint32_t t = (uint32_t)(idx / ffn), j = (uint32_t)(idx % ffn);
     const float gv = Y[(size_t)t * 2 * ffn + 2 * j], uv = Y[(size_t)t * 2 * ffn + 2 * j + 1];
-    H[idx] = (gv / (1.0f + expf(-gv))) * uv;
+    const float h = (gv / (1.0f + expf(-gv))) * uv;
+    if (Hh) Hh[idx] = __float2half_rn(h);
+    else H[idx] = h;
 }
 
 // X += Y (the residual, ops::axpy with a = 1).
@@ -272,8 +302,8 @@ __global__ void add_rows_kernel(float* X, const float* Y, uint64_t n) {
 static unsigned blocks_for(uint64_t n) { return (unsigned)((n + kPreThreads - 1) / kPreThreads); }
 
 void launch_rmsnorm_rows(const float* X, const float* w, uint32_t n, uint32_t T, float eps, float* Y,
-                         cudaStream_t s) {
-    rmsnorm_rows_kernel<<<T, 1024, 0, s>>>(X, w, n, eps, Y);
+                         cudaStream_t s, __half* Yh) {
+    rmsnorm_rows_kernel<<<T, 1024, 0, s>>>(X, w, n, eps, Y, Yh);
     SM_CUDA(cudaGetLastError());
 }
 
@@ -287,19 +317,19 @@ void launch_qkv_post(const float* Y, uint32_t rows, uint32_t T, uint32_t q_rows,
 
 void launch_attention_prefill(const float* Q, const float* kc, const float* vc, uint32_t n_heads, uint32_t n_kv,
                               uint32_t hd, uint32_t max_ctx, uint32_t pos0, uint32_t T, float* out,
-                              cudaStream_t s) {
+                              cudaStream_t s, __half* out_h) {
     if (n_heads % n_kv || n_heads / n_kv > (uint32_t)kPreMaxGroup)
         throw Error(1, "prefill attention: unsupported head grouping");
     const uint32_t G = n_heads / n_kv;
-    if (hd == 32) launch_pre_attn_hd<32>(G, Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
-    else if (hd == 64) launch_pre_attn_hd<64>(G, Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
-    else if (hd == 128) launch_pre_attn_hd<128>(G, Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, s);
+    if (hd == 32) launch_pre_attn_hd<32>(G, Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
+    else if (hd == 64) launch_pre_attn_hd<64>(G, Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
+    else if (hd == 128) launch_pre_attn_hd<128>(G, Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
     else throw Error(1, "prefill attention: head_dim must be 32, 64 or 128");
     SM_CUDA(cudaGetLastError());
 }
 
-void launch_swiglu_rows(const float* Y, uint32_t ffn, uint32_t T, float* H, cudaStream_t s) {
-    swiglu_rows_kernel<<<blocks_for((uint64_t)T * ffn), kPreThreads, 0, s>>>(Y, ffn, T, H);
+void launch_swiglu_rows(const float* Y, uint32_t ffn, uint32_t T, float* H, cudaStream_t s, __half* Hh) {
+    swiglu_rows_kernel<<<blocks_for((uint64_t)T * ffn), kPreThreads, 0, s>>>(Y, ffn, T, H, Hh);
     SM_CUDA(cudaGetLastError());
 }
 
