@@ -197,9 +197,15 @@ void launch_rmsnorm_rows(const float* X, const float* w, uint32_t n, uint32_t T,
 void launch_qkv_post(const float* Y, uint32_t rows, uint32_t T, uint32_t q_rows, uint32_t k_rows, uint32_t hd,
                      const float* bias, const float2* rope, uint32_t pos0, uint32_t max_ctx, float* Q, float* kc,
                      float* vc, cudaStream_t s);
+// Causal attention over the prompt; when the grid is small the keys of each
+// token block are split over prefill_attention_splits() CTAs whose partials
+// go to `part` (prefill_attention_scratch_floats() floats) and are merged.
 void launch_attention_prefill(const float* Q, const float* kc, const float* vc, uint32_t n_heads, uint32_t n_kv,
                               uint32_t hd, uint32_t max_ctx, uint32_t pos0, uint32_t T, float* out, cudaStream_t s,
-                              __half* out_h = nullptr);
+                              __half* out_h = nullptr, float* part = nullptr);
+uint32_t prefill_attention_tokens(uint32_t T, uint32_t n_kv);
+uint32_t prefill_attention_splits(uint32_t T, uint32_t n_kv, uint32_t pos0);
+size_t prefill_attention_scratch_floats(uint32_t T, uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t pos0);
 void launch_swiglu_rows(const float* Y, uint32_t ffn, uint32_t T, float* H, cudaStream_t s, __half* Hh = nullptr);
 void launch_add_rows(float* X, const float* Y, uint64_t n, cudaStream_t s);
 

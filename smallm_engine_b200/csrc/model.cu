@@ -725,6 +725,11 @@ void Model::prefill(const uint32_t* tokens, uint32_t T, uint32_t pos0, float* ou
         else gemm(w32, rows, cols, X, T, pre_y, tf32);
     };
     __half* const xh = tc ? pre_xh : nullptr;
+    const size_t part_floats = prefill_attention_scratch_floats(T, nh_l, nkv_l, hd, pos0);
+    if (part_floats > pre_part_cap) {
+        pre_part = palloc(4 * part_floats);
+        pre_part_cap = part_floats;
+    }
     static const LayerF32 kNo32;
     static const LayerF16 kNo16;
     SM_CUDA(cudaMemcpyAsync(pre_tok, tokens, 4ull * T, cudaMemcpyHostToDevice, stream));
@@ -743,7 +748,7 @@ void Model::prefill(const uint32_t* tokens, uint32_t T, uint32_t pos0, float* ou
             launch_qkv_post(pre_y, L.v.rows, T, 0, 0, hd, L.bias ? L.bias + qrows + krows : nullptr, rope, pos0,
                             max_ctx, pre_q, kc, vc, stream);
         }
-        launch_attention_prefill(pre_q, kc, vc, nh_l, nkv_l, hd, max_ctx, pos0, T, pre_a, stream, xh);
+        launch_attention_prefill(pre_q, kc, vc, nh_l, nkv_l, hd, max_ctx, pos0, T, pre_a, stream, xh, pre_part);
         linear(F.o, H.o, embd, qrows, pre_a);
         launch_add_rows(pre_x, pre_y, (uint64_t)T * embd, stream);
         launch_rmsnorm_rows(pre_x, L.ffn_norm, embd, T, eps, pre_xn, stream, xh);

@@ -99,6 +99,8 @@ struct Model {
     std::vector<LayerF16> layers_f16;
     __half* pre_xh = nullptr;  // f16 copy of a GEMM's input rows
     uint64_t pre_xh_cap = 0;   // elements pre_xh holds
+    float* pre_part = nullptr; // key-split partials of the prefill attention
+    size_t pre_part_cap = 0;   // floats pre_part holds
     cublasHandle_t cublas = nullptr;
     uint32_t pre_cap = 0;  // tokens the prefill buffers hold
     float *pre_x = nullptr, *pre_xn = nullptr, *pre_y = nullptr, *pre_q = nullptr, *pre_a = nullptr,

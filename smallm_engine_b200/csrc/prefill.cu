@@ -6,6 +6,7 @@
 // RMSNorm (ops.cpp:29-40), bias + RoPE + KV append (qwen2_model.cpp:97-110),
 // causal GQA attention (qwen2_model.cpp:111-133), SiLU * up (ops.cpp:60-65,
 // 325-330) and the residual adds.
+#include <algorithm>
 #include <mutex>
 #include <unordered_map>
 
@@ -110,7 +111,8 @@ __global__ void __launch_bounds__(32 * TOK) attention_prefill_kernel(const float
                                                                      const float* __restrict__ kc,
                                                                      const float* __restrict__ vc, uint32_t n_heads,
                                                                      uint32_t max_ctx, uint32_t pos0, uint32_t T,
-                                                                     float* __restrict__ out, __half* out_h) {
+                                                                     float* __restrict__ out, __half* out_h,
+                                                                     uint32_t n_split, float* __restrict__ part) {
     using S = PreAttnSmem<HD, G, TOK>;
     constexpr uint32_t NT = 32 * TOK;  // threads
     constexpr int DPL = HD / 32;  // output dims per lane
@@ -149,8 +151,11 @@ __global__ void __launch_bounds__(32 * TOK) attention_prefill_kernel(const float
     const float* vb = vc + (size_t)g * max_ctx * HD;
     const float* qw = qs + (size_t)w * G * HD;
     float* pw = ps + (size_t)w * G * kPreChunk;
-    for (uint32_t c0 = 0; c0 < n_keys; c0 += kPreChunk) {
-        const uint32_t len = min(kPreChunk, n_keys - c0);
+    // this CTA's whole chunks of the block's keys (split blockIdx.z of n_split)
+    const uint32_t per = ((n_keys + kPreChunk - 1) / kPreChunk + n_split - 1) / n_split * kPreChunk;
+    const uint32_t k_begin = min(blockIdx.z * per, n_keys), k_end = min(k_begin + per, n_keys);
+    for (uint32_t c0 = k_begin; c0 < k_end; c0 += kPreChunk) {
+        const uint32_t len = min(kPreChunk, k_end - c0);
         __syncthreads();  // the previous chunk's K/V are no longer read
         for (uint32_t i = tid; i < len * HD / 4; i += NT) {
             const uint32_t key = i / (HD / 4), c4 = i % (HD / 4);
@@ -217,7 +222,21 @@ __global__ void __launch_bounds__(32 * TOK) attention_prefill_kernel(const float
         }
         __syncwarp();  // pw is rewritten by the next chunk
     }
-    if (live) {
+    if (live && n_split > 1) {
+        // partial of this split: unnormalised output, running max and sum
+        // ([token][head][split][HD + 2]); rows without a key here keep
+        // m = -inf, l = 0 and weigh nothing in the merge
+#pragma unroll
+        for (int i = 0; i < G; ++i) {
+            float* pr = part + (((size_t)t * n_heads + g * G + i) * n_split + blockIdx.z) * (HD + 2);
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) pr[lane * DPL + j] = acc[i][j];
+            if (lane == 0) {
+                pr[HD] = m[i];
+                pr[HD + 1] = l[i];
+            }
+        }
+    } else if (live) {
         const size_t o = (size_t)t * n_heads * HD + (size_t)g * G * HD;
 #pragma unroll
         for (int i = 0; i < G; ++i)
@@ -230,10 +249,32 @@ __global__ void __launch_bounds__(32 * TOK) attention_prefill_kernel(const float
     }
 }
 
+// Merge of the key splits of one (token, head): out = sum_s acc_s e^(m_s - M)
+// / sum_s l_s e^(m_s - M), M = max_s m_s (split 0 holds key 0, so M is finite).
+__global__ void attention_prefill_merge_kernel(const float* __restrict__ part, uint32_t n_split, uint32_t hd,
+                                               float* __restrict__ out, __half* out_h) {
+    const size_t row = blockIdx.x;  // token * n_heads + head
+    const float* pr = part + row * n_split * (hd + 2);
+    float M = -INFINITY;
+    for (uint32_t s = 0; s < n_split; ++s) M = fmaxf(M, pr[s * (hd + 2) + hd]);
+    for (uint32_t d = threadIdx.x; d < hd; d += blockDim.x) {
+        float L = 0.f, O = 0.f;
+        for (uint32_t s = 0; s < n_split; ++s) {
+            const float* q = pr + s * (hd + 2);
+            const float wgt = q[hd] == -INFINITY ? 0.f : expf(q[hd] - M);
+            L = fmaf(q[hd + 1], wgt, L);
+            O = fmaf(q[d], wgt, O);
+        }
+        const float v = O / L;
+        if (out_h) out_h[row * hd + d] = __float2half_rn(v);
+        else out[row * hd + d] = v;
+    }
+}
+
 template <int HD, int G, int TOK>
 static void launch_pre_attn_tok(const float* Q, const float* kc, const float* vc, uint32_t n_heads, uint32_t n_kv,
                                 uint32_t max_ctx, uint32_t pos0, uint32_t T, float* out, __half* out_h,
-                                cudaStream_t s) {
+                                float* part, cudaStream_t s) {
     using S = PreAttnSmem<HD, G, TOK>;
     static std::mutex mu;
     static std::unordered_map<int, bool> configured;
@@ -247,36 +288,41 @@ static void launch_pre_attn_tok(const float* Q, const float* kc, const float* vc
             configured[dev] = true;
         }
     }
-    const dim3 grid((T + TOK - 1) / TOK, n_kv);
+    const uint32_t n_split = prefill_attention_splits(T, n_kv, pos0);
+    const dim3 grid((T + TOK - 1) / TOK, n_kv, n_split);
     attention_prefill_kernel<HD, G, TOK><<<grid, 32 * TOK, S::bytes, s>>>(Q, kc, vc, n_heads, max_ctx, pos0, T, out,
-                                                                          out_h);
+                                                                          out_h, n_split, part);
+    if (n_split > 1) {
+        SM_CUDA(cudaGetLastError());
+        attention_prefill_merge_kernel<<<T * n_heads, HD, 0, s>>>(part, n_split, HD, out, out_h);
+    }
 }
 
 template <int HD, int G>
 static void launch_pre_attn(const float* Q, const float* kc, const float* vc, uint32_t n_heads, uint32_t n_kv,
-                            uint32_t max_ctx, uint32_t pos0, uint32_t T, float* out, __half* out_h,
+                            uint32_t max_ctx, uint32_t pos0, uint32_t T, float* out, __half* out_h, float* part,
                             cudaStream_t s) {
     // 8-token CTAs when they give at least two CTAs per SM, else 4-token ones
     // (more CTAs, so heavy and light causal blocks pack together)
-    if ((uint64_t)((T + 7) / 8) * n_kv >= 2ull * device_sm_count())
-        launch_pre_attn_tok<HD, G, 8>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
+    if (prefill_attention_tokens(T, n_kv) == 8)
+        launch_pre_attn_tok<HD, G, 8>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, part, s);
     else
-        launch_pre_attn_tok<HD, G, 4>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
+        launch_pre_attn_tok<HD, G, 4>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, part, s);
 }
 
 template <int HD>
 static void launch_pre_attn_hd(uint32_t G, const float* Q, const float* kc, const float* vc, uint32_t n_heads,
                                uint32_t n_kv, uint32_t max_ctx, uint32_t pos0, uint32_t T, float* out,
-                               __half* out_h, cudaStream_t s) {
+                               __half* out_h, float* part, cudaStream_t s) {
     switch (G) {
-        case 1: return launch_pre_attn<HD, 1>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
-        case 2: return launch_pre_attn<HD, 2>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
-        case 3: return launch_pre_attn<HD, 3>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
-        case 4: return launch_pre_attn<HD, 4>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
-        case 5: return launch_pre_attn<HD, 5>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
-        case 6: return launch_pre_attn<HD, 6>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
-        case 7: return launch_pre_attn<HD, 7>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
-        case 8: return launch_pre_attn<HD, 8>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
+        case 1: return launch_pre_attn<HD, 1>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, part, s);
+        case 2: return launch_pre_attn<HD, 2>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, part, s);
+        case 3: return launch_pre_attn<HD, 3>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, part, s);
+        case 4: return launch_pre_attn<HD, 4>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, part, s);
+        case 5: return launch_pre_attn<HD, 5>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, part, s);
+        case 6: return launch_pre_attn<HD, 6>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, part, s);
+        case 7: return launch_pre_attn<HD, 7>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, part, s);
+        case 8: return launch_pre_attn<HD, 8>(Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, part, s);
         default: throw Error(1, "prefill attention: unsupported head grouping");
     }
 }
@@ -315,15 +361,38 @@ void launch_qkv_post(const float* Y, uint32_t rows, uint32_t T, uint32_t q_rows,
     SM_CUDA(cudaGetLastError());
 }
 
+uint32_t prefill_attention_tokens(uint32_t T, uint32_t n_kv) {
+    // 8-token CTAs when they give at least two CTAs per SM, else 4-token ones
+    return (uint64_t)((T + 7) / 8) * n_kv >= 2ull * device_sm_count() ? 8u : 4u;
+}
+
+uint32_t prefill_attention_splits(uint32_t T, uint32_t n_kv, uint32_t pos0) {
+    // split the keys of each token block until the grid has ~4 CTAs per SM,
+    // keeping at least two 32-key chunks per split of the longest block
+    const uint64_t ctas = (uint64_t)((T + prefill_attention_tokens(T, n_kv) - 1) / prefill_attention_tokens(T, n_kv)) *
+                          n_kv;
+    const uint64_t want = (4ull * device_sm_count() + ctas - 1) / ctas;
+    const uint64_t chunks = ((uint64_t)pos0 + T + kPreChunk - 1) / kPreChunk;
+    uint64_t n = std::min<uint64_t>(want, std::min<uint64_t>(8, chunks / 2));
+    return n < 2 ? 1u : (uint32_t)n;
+}
+
+size_t prefill_attention_scratch_floats(uint32_t T, uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t pos0) {
+    const uint32_t n = prefill_attention_splits(T, n_kv, pos0);
+    return n > 1 ? (size_t)T * n_heads * n * (hd + 2) : 0;
+}
+
 void launch_attention_prefill(const float* Q, const float* kc, const float* vc, uint32_t n_heads, uint32_t n_kv,
                               uint32_t hd, uint32_t max_ctx, uint32_t pos0, uint32_t T, float* out,
-                              cudaStream_t s, __half* out_h) {
+                              cudaStream_t s, __half* out_h, float* part) {
+    if (prefill_attention_splits(T, n_kv, pos0) > 1 && !part)
+        throw Error(1, "prefill attention: key splits need scratch (prefill_attention_scratch_floats)");
     if (n_heads % n_kv || n_heads / n_kv > (uint32_t)kPreMaxGroup)
         throw Error(1, "prefill attention: unsupported head grouping");
     const uint32_t G = n_heads / n_kv;
-    if (hd == 32) launch_pre_attn_hd<32>(G, Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
-    else if (hd == 64) launch_pre_attn_hd<64>(G, Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
-    else if (hd == 128) launch_pre_attn_hd<128>(G, Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, s);
+    if (hd == 32) launch_pre_attn_hd<32>(G, Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, part, s);
+    else if (hd == 64) launch_pre_attn_hd<64>(G, Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, part, s);
+    else if (hd == 128) launch_pre_attn_hd<128>(G, Q, kc, vc, n_heads, n_kv, max_ctx, pos0, T, out, out_h, part, s);
     else throw Error(1, "prefill attention: head_dim must be 32, 64 or 128");
     SM_CUDA(cudaGetLastError());
 }
