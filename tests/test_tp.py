@@ -1,10 +1,10 @@
-"""Tensor parallelism: host logic on CPU with world-size-2 gloo ranks, and
-2-GPU parity of the tensor-parallel model against the single-process oracle
-(skipped below two GPUs).
+"""Tensor parallelism: host logic on CPU with world-size-2 and -4 gloo ranks,
+and 2/4/8-GPU parity of the tensor-parallel model against the single-process
+oracle (each skipped when the machine has fewer GPUs).
 
 The reference has no multi-process path; the bar is the single-GPU one: the
-TP=2 model's logits agree with the oracle to 1e-2 * max|logit| and its greedy
-ids are identical, rank 0 reading the all-gathered logits."""
+tensor-parallel model's logits agree with the oracle to 1e-2 * max|logit| and
+its greedy ids are identical, rank 0 reading the all-gathered logits."""
 from __future__ import annotations
 
 import os
@@ -65,19 +65,20 @@ def _gloo_rank(rank, ws, port, out):
         dist.destroy_process_group()
 
 
-def test_world_size_2_gloo_handshake():
+@pytest.mark.parametrize("ws", [2, 4])
+def test_gloo_handshake(ws):
     """The multi-rank bench path on CPU: one NCCL id reaches every rank, the
     timing reduction returns the slowest rank, the shards are disjoint."""
-    ws = 2
     with mp.Manager() as mgr:
         out = mgr.dict()
         mp.start_processes(_gloo_rank, args=(ws, _free_port(), out), nprocs=ws, start_method="spawn")
         results = [out[r] for r in range(ws)]
+    per = 32 // ws
     for g in results:
         ids = {x[0] for x in g}
         assert len(ids) == 1 and len(next(iter(ids))) == 128
-        assert all(x[1] == 2.5 for x in g)
-        assert g[0][2].heads == (0, 16) and g[1][2].heads == (16, 32)
+        assert all(x[1] == 1.5 + (ws - 1) for x in g)
+        assert [x[2].heads for x in g] == [(r * per, (r + 1) * per) for r in range(ws)]
 
 
 def _tp_model_rank(rank, ws, path, nccl_id, steps, out):
@@ -103,16 +104,21 @@ def _tp_model_rank(rank, ws, path, nccl_id, steps, out):
 
 
 @pytest.mark.gpu
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="tensor parallelism needs two GPUs")
-def test_tp2_model_matches_oracle(orc, gguf_dir):
+@pytest.mark.parametrize("ws", [2, 4, 8])
+def test_tp_model_matches_oracle(orc, gguf_dir, ws):
+    if torch.cuda.device_count() < ws:
+        pytest.skip(f"tensor parallelism at {ws} needs {ws} GPUs")
     import oracle as O
     from smallm_engine_b200 import synth
-    spec = synth.tiny_spec("llama-q4_0")
-    path = synth.write_gguf(spec, 8, gguf_dir / "tp2-llama.gguf")
+    # 8 query and 8 KV heads of 64: every degree up to 8 splits heads, FFN
+    # rows (2 Q4_0 blocks of O/down columns per rank at 8) and vocabulary
+    spec = synth.tiny_spec("llama-q4_0") if ws == 2 else synth.tiny_spec("llama-q4_0", embd=512, heads=8,
+                                                                          kv_heads=8)
+    path = synth.write_gguf(spec, 8, gguf_dir / f"tp{ws}-llama.gguf")
     steps = 16
     with mp.Manager() as mgr:
         out = mgr.dict()
-        mp.start_processes(_tp_model_rank, args=(2, str(path), tp.new_nccl_id(), steps, out), nprocs=2,
+        mp.start_processes(_tp_model_rank, args=(ws, str(path), tp.new_nccl_id(), steps, out), nprocs=ws,
                            start_method="spawn")
         got, dev_ids, nxt = out["logits"], out["dev_ids"], out["next"]
     ref = O.OracleModel(path, orc)
