@@ -21,7 +21,10 @@
 //     token's 32 outputs are one 128-byte line.
 // Every mbarrier wait is bounded (mbar_wait: ~2^31 cycles); a wait that gives
 // up raises bit 6 of the device error word and the CTA finishes without
-// further MMAs, so the host sees an error instead of a hang.
+// further MMAs, so the host sees an error instead of a hang.  On every exit
+// path the producer first waits (bounded) for the last copy it issued into
+// each stage and the MMA thread for all of its MMAs, so nothing lands in
+// shared or tensor memory after the CTA has released them.
 //
 // Operands are f16 (11-bit significands, like TF32's): products are exact in
 // the f32 accumulator.  No cluster launch and no multicast.
@@ -129,7 +132,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* empty = full + C::stages;
     uint64_t* acc_full = empty + C::stages;  // [2] MMA -> epilogue: accumulator b complete
     uint64_t* acc_empty = acc_full + 2;      // [2] epilogue -> MMA: accumulator b drained
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    uint64_t* mma_done = acc_empty + 2;      // every MMA this CTA issued has completed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t nk = (K + kBK - 1) / kBK;
@@ -145,6 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], 128);
         }
+        mbar_init(mma_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tw)) : "memory");
@@ -165,6 +170,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             // producer: a stage is refilled once the MMAs of its previous use completed
             uint32_t it = 0;
+            uint32_t last[C::stages];  // last use issued into each stage
+#pragma unroll
+            for (uint32_t st = 0; st < C::stages; ++st) last[st] = ~0u;
             for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
                 const int32_t t0 = (int32_t)((tile % n_t) * BN), m0 = (int32_t)((tile / n_t) * kBM);
                 bool ok = true;
@@ -177,12 +185,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_arrive_expect_tx(&full[s], C::stage_bytes);
                     tma_load_2d(sa + s * C::a_bytes, &tw, (int32_t)(kb * kBK), m0, &full[s]);
                     tma_load_2d(sb + s * C::b_bytes, &tx, (int32_t)(kb * kBK), t0, &full[s]);
+                    last[s] = use;
                 }
                 if (!ok) {
                     atomicOr(err, kErrTcGemm);
                     break;
                 }
             }
+            // no copy may still be landing in shared memory when the CTA exits
+            // (immediate when the MMA warp has consumed them all)
+#pragma unroll
+            for (uint32_t st = 0; st < C::stages; ++st)
+                if (last[st] != ~0u && !mbar_wait(&full[st], last[st] & 1)) atomicOr(err, kErrTcGemm);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -218,6 +232,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
             }
+            // the tensor memory is freed below only after every MMA completed
+            mma_commit(mma_done);
+            if (!mbar_wait(mma_done, 0)) atomicOr(err, kErrTcGemm);
         }
     } else {
         // epilogue warps 2..5: warp w reads TMEM lanes (W rows) 32 (w % 4) .. + 31
