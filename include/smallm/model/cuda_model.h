@@ -87,6 +87,29 @@ public:
         return logits;
     }
 
+    // Beyond the reference's Model: a greedy continuation without a host
+    // round trip per token.  `prompt` is prefilled in one pass at positions
+    // start_pos.. (flags as prefill()); its greedy id is the first of the n
+    // returned ids, and the other n - 1 come from CUDA-graph steps chained on
+    // the device, each feeding the previous step's argmax.  The cache then
+    // holds start_pos + prompt.size() + n - 1 positions.
+    std::vector<uint32_t> generate_greedy(const std::vector<uint32_t>& prompt, uint32_t start_pos, uint32_t n,
+                                          uint32_t flags = 0) {
+        std::vector<uint32_t> ids(n);
+        if (n == 0) return ids;
+        uint32_t first = 0;
+        check(smallm_model_prefill(m_, prompt.data(), static_cast<uint32_t>(prompt.size()), start_pos, nullptr,
+                                   &first, flags));
+        ids[0] = first;
+        if (n > 1) {
+            const uint32_t pos = start_pos + static_cast<uint32_t>(prompt.size());
+            check(smallm_model_decode_greedy_async(m_, first, pos, n - 1));
+            check(smallm_model_decode_ids(m_, ids.data() + 1, n - 1));
+        }
+        cached_length_ = smallm_model_cached_length(m_);
+        return ids;
+    }
+
     smallm_model* handle() const { return m_; }
 
 private:

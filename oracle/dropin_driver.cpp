@@ -12,6 +12,9 @@
 //       Generator::generate (src/runtime/generator.cpp:22-72) twice, the
 //       second prompt sharing a prefix with the first (truncate_cache path);
 //       prints one line per call: "ids <reused> <prefilled> <generated ids...>".
+//   dropin_driver fastgen <model.gguf> <n_new> "<prompt ids>" <flags>
+//       CudaModel::generate_greedy (one-pass prefill, device-chained greedy
+//       steps); prints "fast <ids...>".
 //   dropin_driver ops <seed>
 //       CPUBackend vs CUDABackend on seeded inputs: rmsnorm, softmax, silu,
 //       rope, F32 matmul; prints "op <name> <max |diff|> <max |ref|> <bits equal 0/1>".
@@ -73,6 +76,14 @@ int generate(const char* path, uint32_t n_new, const char* p1, const char* p2) {
         const auto& st = gen.last_stats();
         std::printf("ids %u %u%s\n", st.reused_tokens, st.prefill_tokens, out.c_str());
     }
+    return 0;
+}
+
+int fastgen(const char* path, uint32_t n_new, const char* prompt, uint32_t flags) {
+    auto model = smallm::CudaModel::open(path);
+    IdTokenizer tok(model->config().vocab_size);
+    const auto ids = model->generate_greedy(tok.encode(prompt), 0, n_new, flags);
+    std::printf("fast%s\n", tok.decode(ids).c_str());
     return 0;
 }
 
@@ -138,9 +149,13 @@ int main(int argc, char** argv) {
     try {
         if (argc == 6 && std::strcmp(argv[1], "generate") == 0)
             return generate(argv[2], (uint32_t)std::strtoul(argv[3], nullptr, 10), argv[4], argv[5]);
+        if (argc == 6 && std::strcmp(argv[1], "fastgen") == 0)
+            return fastgen(argv[2], (uint32_t)std::strtoul(argv[3], nullptr, 10), argv[4],
+                           (uint32_t)std::strtoul(argv[5], nullptr, 10));
         if (argc == 3 && std::strcmp(argv[1], "ops") == 0)
             return ops((unsigned)std::strtoul(argv[2], nullptr, 10));
         std::fprintf(stderr, "usage: dropin_driver generate <gguf> <n_new> <prompt ids> <prompt ids>\n"
+                             "       dropin_driver fastgen <gguf> <n_new> <prompt ids> <flags>\n"
                              "       dropin_driver ops <seed>\n");
         return 1;
     } catch (const std::exception& e) {

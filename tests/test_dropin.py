@@ -80,6 +80,20 @@ def test_reference_generator_drives_cuda_model(driver, orc, gguf_dir, kind, seed
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("kind,seed", [("qwen2", 7), ("llama-q4_0", 8)])
+def test_cuda_model_generate_greedy(driver, orc, gguf_dir, kind, seed):
+    """CudaModel::generate_greedy: one-pass prefill (exact f32 GEMMs, flags 0)
+    and device-chained greedy steps give the oracle's greedy continuation."""
+    path = synth.write_gguf(synth.tiny_spec(kind), seed, gguf_dir / f"fastgen-{kind}.gguf")
+    p, n = [5, 9, 200, 31, 7], 12
+    r = run(driver, "fastgen", path, n, " ".join(map(str, p)), 0)
+    assert r.returncode == 0, r.stderr
+    line = [l.split() for l in r.stdout.splitlines() if l.startswith("fast")]
+    assert len(line) == 1
+    assert [int(i) for i in line[0][1:]] == greedy(path, orc, p, n)
+
+
+@pytest.mark.gpu
 def test_cpu_backend_vs_cuda_backend(driver):
     r = run(driver, "ops", 3)
     assert r.returncode == 0, r.stderr
