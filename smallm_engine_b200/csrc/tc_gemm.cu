@@ -376,7 +376,6 @@ void launch_tc_gemm(const __half* W, uint32_t N, uint32_t K, const __half* X, ui
     if (ldy < N) throw Error(SMALLM_ERR_INVALID, "tc_gemm: ldy < N");
     if ((reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(X)) & 15)
         throw Error(SMALLM_ERR_INVALID, "tc_gemm: W and X must be 16-byte aligned");
-    if ((N + kBM - 1) / kBM > 65535u) throw Error(SMALLM_ERR_INVALID, "tc_gemm: too many rows");
     const uint32_t bn = tc_gemm_token_tile(N, T);
     const CUtensorMap tw = f16_map(W, K, N, kBM);
     const CUtensorMap tx = f16_map(X, K, T, bn);
