@@ -290,6 +290,36 @@ class RefModel:
             self.h = None
 
 
+class RefGenerator:
+    """The reference's own smallm::Generator (src/runtime/generator.cpp:22-72)
+    over `model` and `sampler`, with the harness's id tokenizer (prompt and
+    output are token ids; `eos` < 0 disables the stop)."""
+
+    def __init__(self, ref: Reference, model: "RefModel", sampler: "RefSampler", eos: int = -1):
+        self.ref = ref
+        self.h = ref.L.ref_generator_new(model.h, sampler.h, eos)
+        if not self.h:
+            raise RuntimeError(ref.L.ref_last_error().decode())
+        self._keep = (model, sampler)
+
+    def generate(self, prompt, max_new: int):
+        """(generated ids, stats dict) of one Generator::generate call."""
+        p = np.ascontiguousarray(prompt, dtype=np.uint32)
+        out = np.zeros(max_new + 1, dtype=np.uint32)
+        n = np.zeros(1, dtype=np.uint32)
+        st = np.zeros(6, dtype=np.float64)
+        self.ref._check(self.ref.L.ref_generate(self.h, _ptr(p), p.size, max_new, _ptr(out), _ptr(n), _ptr(st)))
+        keys = ("prompt_tokens", "reused_tokens", "prefill_tokens", "generated_tokens")
+        return [int(i) for i in out[:int(n[0])]], {k: int(v) for k, v in zip(keys, st[:4])}
+
+    def __del__(self):
+        try:
+            if self.h:
+                self.ref.L.ref_generator_free(self.h)
+        except Exception:
+            pass
+
+
 class RefSampler:
     def __init__(self, ref, kind, k, p, temp, seed):
         self.ref = ref
