@@ -60,6 +60,18 @@ def build_dropin() -> Path:
     return DROPIN
 
 
+COMPAT = HERE / "_ref" / "compat_driver"
+
+
+def build_compat() -> Path:
+    """make -C oracle compat: the reference's sources with its two model files
+    compiled against compat/ (CPUBackend -> the CUDABackend adapter)."""
+    r = subprocess.run(["make", "-s", "-C", str(HERE), "compat"], capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("compat driver build failed:\n" + r.stdout + r.stderr)
+    return COMPAT
+
+
 def reference_sources_present() -> bool:
     return Path("/root/reference/src/core/ops.cpp").exists()
 

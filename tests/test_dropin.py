@@ -1,9 +1,12 @@
 """The C++ adapters (include/smallm/backend/cuda_backend.h,
 include/smallm/model/cuda_model.h) inside the reference engine: the
 reference's own Generator, GreedySampler, GGUF loader and config reader
-(unmodified sources, src/runtime/generator.cpp:22-72) drive CudaModel, and
-CPUBackend is compared with CUDABackend op by op.  The driver binary
-(oracle/_ref/dropin_driver) is built where the reference sources are present.
+(unmodified sources, src/runtime/generator.cpp:22-72) drive CudaModel,
+CPUBackend is compared with CUDABackend op by op, and the reference's own
+Qwen2Model / LlamaModel run their forward pass on CUDABackend (the compat
+driver, whose two model files see CPUBackend as CUDABackend through an
+include shim).  The driver binaries (oracle/_ref/dropin_driver,
+oracle/_ref/compat_driver) are built where the reference sources are present.
 
 Generator semantics checked: the first prompt is prefilled token by token
 and continued greedily; the second prompt shares a prefix with the cached
@@ -28,6 +31,15 @@ def _has_gpu():
 
 
 @pytest.fixture(scope="module")
+def compat():
+    if O.reference_sources_present():
+        return O.build_compat()
+    if not O.COMPAT.exists():
+        pytest.skip("compat driver not built (reference sources absent)")
+    return O.COMPAT
+
+
+@pytest.fixture(scope="module")
 def driver():
     if O.reference_sources_present():
         return O.build_dropin()
@@ -47,6 +59,17 @@ def test_dropin_fails_loudly_without_gpu(driver, gguf_dir):
     assert r.returncode == 2 and r.stderr.startswith("error: CudaModel:"), r.stderr
     r = run(driver, "ops", 1)
     assert r.returncode == 2 and r.stderr.startswith("error: CUDABackend:"), r.stderr
+
+
+@pytest.mark.skipif(_has_gpu(), reason="checks the no-GPU failure mode")
+def test_compat_model_code_constructs_cuda_backend(compat, gguf_dir, tmp_path):
+    """The reference's Qwen2Model / LlamaModel, compiled against the compat
+    shim, construct CUDABackend: without a GPU their constructor throws from
+    it (the stock build would run on the CPU)."""
+    for kind, seed in (("qwen2", 7), ("llama-q4_0", 8)):
+        path = synth.write_gguf(synth.tiny_spec(kind), seed, gguf_dir / f"compat-cpu-{kind}.gguf")
+        r = run(compat, path, 2, "5 9 200", tmp_path / "l.f32")
+        assert r.returncode == 2 and r.stderr.startswith("error: CUDABackend:"), r.stderr
 
 
 def greedy(path, orc, prompt, n):
