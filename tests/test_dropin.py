@@ -117,6 +117,29 @@ def test_cuda_model_generate_greedy(driver, orc, gguf_dir, kind, seed):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("kind,seed", [("qwen2", 7), ("llama-q4_0", 8)])
+def test_compat_reference_model_on_cuda_backend(compat, orc, gguf_dir, tmp_path, kind, seed):
+    """The reference's own forward pass (qwen2_model.cpp / llama_model.cpp,
+    unmodified) with every Backend call on the GPU: the last prompt token's
+    logits within 1e-2 * max|logit| of the restatement and the greedy ids
+    identical."""
+    path = synth.write_gguf(synth.tiny_spec(kind), seed, gguf_dir / f"compat-{kind}.gguf")
+    p, n = [5, 9, 200, 31, 7], 8
+    out = tmp_path / "logits.f32"
+    r = run(compat, path, n, " ".join(map(str, p)), out)
+    assert r.returncode == 0, r.stderr
+    got = np.fromfile(out, dtype=np.float32)
+    ref = O.OracleModel(path, orc)
+    want = None
+    for pos, t in enumerate(p):
+        want = ref.forward(t, pos)
+    assert got.shape == want.shape
+    assert np.abs(got.astype(np.float64) - want).max() <= 1e-2 * np.abs(want).max()
+    line = [l.split() for l in r.stdout.splitlines() if l.startswith("ids")]
+    assert [int(i) for i in line[0][1:]] == greedy(path, orc, p, n)
+
+
+@pytest.mark.gpu
 def test_cpu_backend_vs_cuda_backend(driver):
     r = run(driver, "ops", 3)
     assert r.returncode == 0, r.stderr
