@@ -188,14 +188,15 @@ int smallm_dequantize(smallm_ctx* ctx, uint32_t type, const uint8_t* src, uint64
  * a split-K decode-attention kernel (partials merged by the last CTA of each
  * KV head; a loaded model runs a cluster variant), on caller-owned device buffers
  * q_dev[n_heads * head_dim] and kcache_dev / vcache_dev laid out
- * [n_kv_heads][max_ctx][head_dim] (f32).  Asynchronous on `stream` (NULL =
- * the context stream).
+ * [n_kv_heads][max_ctx][head_dim] (f32; kcache_dev and vcache_dev 16-byte
+ * aligned, since their rows are bulk-copied, else SMALLM_ERR_INVALID).
+ * Asynchronous on `stream` (NULL = the context stream).
  *
  * For callers that cannot let the library allocate device memory (a serving
  * engine whose memory all belongs to its own KV pool; a loop that cannot absorb
  * the device synchronisation cudaMalloc / cudaFree may cause): the kernel's
- * scratch (split-K partials, per-KV-head tickets, the position word) is one
- * static 4 MiB + 1.25 KiB array inside the library, not a buffer.
+ * scratch (split-K partials, per-KV-head tickets) is one static 4 MiB + 1 KiB
+ * array inside the library, not a buffer; pos travels as a kernel parameter.
  *   - The first call on each device does one-time set-up on that device (looks
  *     up the array's address and zeroes the tickets on `stream`); make it
  *     before any stream capture begins.

@@ -19,6 +19,7 @@ Two checkers live here:
 from __future__ import annotations
 
 import ctypes
+import os
 import math
 import struct
 import subprocess
@@ -43,7 +44,7 @@ def _ptr(a: np.ndarray):
 def build(ref: bool = True) -> None:
     """make -C oracle (the reference part only where its sources exist)."""
     target = "all" if ref else "oracle"
-    r = subprocess.run(["make", "-s", "-C", str(HERE), target], capture_output=True, text=True)
+    r = subprocess.run(["make", "-s", "-C", str(HERE), f"REF={REF_SRC}", target], capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError("oracle build failed:\n" + r.stdout + r.stderr)
 
@@ -54,7 +55,7 @@ DROPIN = HERE / "_ref" / "dropin_driver"
 def build_dropin() -> Path:
     """make -C oracle dropin: the reference's sources + dropin_driver.cpp +
     the C++ adapters, linked against the already built CUDA backend."""
-    r = subprocess.run(["make", "-s", "-C", str(HERE), "dropin"], capture_output=True, text=True)
+    r = subprocess.run(["make", "-s", "-C", str(HERE), f"REF={REF_SRC}", "dropin"], capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError("drop-in driver build failed:\n" + r.stdout + r.stderr)
     return DROPIN
@@ -66,14 +67,19 @@ COMPAT = HERE / "_ref" / "compat_driver"
 def build_compat() -> Path:
     """make -C oracle compat: the reference's sources with its two model files
     compiled against compat/ (CPUBackend -> the CUDABackend adapter)."""
-    r = subprocess.run(["make", "-s", "-C", str(HERE), "compat"], capture_output=True, text=True)
+    r = subprocess.run(["make", "-s", "-C", str(HERE), f"REF={REF_SRC}", "compat"], capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError("compat driver build failed:\n" + r.stdout + r.stderr)
     return COMPAT
 
 
+# Where the reference's sources are read from when its build (oracle/_ref) is
+# made: $SMALLM_REF_SRC, by default the read-only checkout beside this repo.
+REF_SRC = Path(os.environ.get("SMALLM_REF_SRC", "/root/reference"))
+
+
 def reference_sources_present() -> bool:
-    return Path("/root/reference/src/core/ops.cpp").exists()
+    return (REF_SRC / "src" / "core" / "ops.cpp").exists()
 
 
 def type_nbytes(t: int, count: int) -> int:
@@ -211,7 +217,7 @@ class Reference:
         L.ref_generate.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
                                    ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         L.ref_decode_timed.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
-                                       ctypes.c_void_p, ctypes.c_void_p]
+                                       ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p]
         self.L = L
 
     def _check(self, rc):
@@ -288,11 +294,13 @@ class RefModel:
     def cached_length(self):
         return int(self.ref.L.ref_model_cached_length(self.h))
 
-    def decode_timed(self, prompt, steps):
+    def decode_timed(self, prompt, steps, warmup=0):
+        """Prompt token by token, `warmup` untimed greedy steps, then `steps`
+        timed ones: (all warmup + steps ids, ms of the timed steps)."""
         prompt = np.ascontiguousarray(prompt, np.uint32)
-        ids = np.empty(steps, dtype=np.uint32)
+        ids = np.empty(warmup + steps, dtype=np.uint32)
         ms = ctypes.c_double()
-        self.ref._check(self.ref.L.ref_decode_timed(self.h, _ptr(prompt), prompt.size, steps, _ptr(ids),
+        self.ref._check(self.ref.L.ref_decode_timed(self.h, _ptr(prompt), prompt.size, warmup, steps, _ptr(ids),
                                                     ctypes.byref(ms)))
         return ids, ms.value
 

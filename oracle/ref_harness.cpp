@@ -235,7 +235,12 @@ int ref_generate(void* g, const uint32_t* prompt, uint32_t n, uint32_t max_new, 
 // Greedy decode timed like generator.cpp:57-68 (steady_clock around the
 // decode loop only): prompt prefill untimed, then `steps` forward+argmax
 // steps.  ids[0..steps) receives the generated ids; *ms the decode time.
-int ref_decode_timed(void* h, const uint32_t* prompt, uint32_t n, uint32_t steps, uint32_t* ids,
+// The reference's decode loop (generator.cpp:47-67): the prompt through
+// Model::forward token by token, then greedy steps (GreedySampler).  The
+// first `warmup` greedy steps run untimed; the next `steps` are timed with
+// steady_clock around the loop, as the reference's Generator times it.
+// ids receives all warmup + steps greedy ids.
+int ref_decode_timed(void* h, const uint32_t* prompt, uint32_t n, uint32_t warmup, uint32_t steps, uint32_t* ids,
                      double* ms) {
     return guarded([&] {
         auto& m = *static_cast<RefModel*>(h)->model;
@@ -244,10 +249,15 @@ int ref_decode_timed(void* h, const uint32_t* prompt, uint32_t n, uint32_t steps
         std::vector<float> logits;
         uint32_t pos = 0;
         for (uint32_t i = 0; i < n; ++i) logits = m.forward(prompt[i], pos++);
+        for (uint32_t s = 0; s < warmup; ++s) {
+            uint32_t next = greedy.sample(logits);
+            ids[s] = next;
+            logits = m.forward(next, pos++);
+        }
         auto t0 = std::chrono::steady_clock::now();
         for (uint32_t s = 0; s < steps; ++s) {
             uint32_t next = greedy.sample(logits);
-            ids[s] = next;
+            ids[warmup + s] = next;
             logits = m.forward(next, pos++);
         }
         *ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();

@@ -55,7 +55,7 @@ __host__ __device__ static uint32_t attn_chunk_max(uint32_t max_ctx, uint32_t n_
 }
 
 template <int HD>
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads) smallm_attention_kernel(const AttnArgs a) {
     constexpr int EPL = HD / 32;               // head-dim elements per lane
     constexpr int PARTS = kAttnThreads / HD;   // position slices in the V pass
     extern __shared__ __align__(128) float sm[];
@@ -77,7 +77,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
     pdl_launch_dependents();
     pdl_wait();
     if (tid == 0) trace_mark(a.trace, 1);
-    const uint32_t n = *a.pos + 1;
+    const uint32_t n = (a.pos ? *a.pos : a.pos_value) + 1;
     const uint32_t chunk = attn_chunk(n, a.n_split);
     const uint32_t t0 = split * chunk;
     const uint32_t t1 = min(n, t0 + chunk);
@@ -99,7 +99,13 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
         for (uint32_t i = tid; i < G * HD; i += kAttnThreads) qs[i] = a.q[(size_t)g * G * HD + i];
         __syncthreads();
         const bool ok = mbar_wait(&bar, 0);
-        if (!ok && tid == 0 && a.err) atomicOr(a.err, 4u);
+        if (!ok) {
+            if (tid == 0 && a.err) atomicOr(a.err, 4u);
+            // the two copies may still be landing in ks / vs: wait once more
+            // (bounded) before the CTA reuses that memory or exits; the error
+            // bit stays raised and the math below skips the staged rows
+            mbar_wait(&bar, 0);
+        }
         const float scale = 1.0f / sqrtf((float)HD);
 
         // scores: one warp per position, lanes split the head dimension
@@ -233,17 +239,13 @@ void launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {
     AttnArgs aa = a;
     void* args[] = {&aa};
     const void* fn;
-    if (a.hd == 32) fn = (const void*)attention_kernel<32>;
-    else if (a.hd == 64) fn = (const void*)attention_kernel<64>;
-    else if (a.hd == 128) fn = (const void*)attention_kernel<128>;
+    if (a.hd == 32) fn = (const void*)smallm_attention_kernel<32>;
+    else if (a.hd == 64) fn = (const void*)smallm_attention_kernel<64>;
+    else if (a.hd == 128) fn = (const void*)smallm_attention_kernel<128>;
     else throw Error(1, "attention: head_dim must be 32, 64 or 128");
-    static bool attr_set = false;
-    if (!attr_set) {
-        SM_CUDA(cudaFuncSetAttribute(attention_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        SM_CUDA(cudaFuncSetAttribute(attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        SM_CUDA(cudaFuncSetAttribute(attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        attr_set = true;
-    }
+    // the shared-memory limit is a per-device attribute of each function: set
+    // it once per (device, kernel)
+    set_smem_limit_once(fn, 200 * 1024);
     launch_kernel_ex(fn, dim3(a.n_kv, a.n_split), dim3(kAttnThreads), smem, stream, pdl, args);
 }
 
@@ -288,7 +290,7 @@ __host__ __device__ constexpr size_t cattn_smem_floats(uint32_t G, uint32_t hd) 
 }
 
 template <int HD>
-__global__ void __launch_bounds__(kCAttnThreads) attention_cluster_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel(const AttnArgs a) {
     constexpr int PARTS = kCAttnThreads / HD;  // position slices in the V pass
     constexpr int DL = HD / 8;                 // head-dim elements per lane in the score pass
     constexpr int DV = DL / 4;                 // ... as float4
@@ -556,9 +558,9 @@ size_t attention_cluster_smem(uint32_t n_heads, uint32_t n_kv, uint32_t hd) {
 }
 
 static const void* cattn_fn(uint32_t hd) {
-    if (hd == 32) return (const void*)attention_cluster_kernel<32>;
-    if (hd == 64) return (const void*)attention_cluster_kernel<64>;
-    if (hd == 128) return (const void*)attention_cluster_kernel<128>;
+    if (hd == 32) return (const void*)smallm_attention_cluster_kernel<32>;
+    if (hd == 64) return (const void*)smallm_attention_cluster_kernel<64>;
+    if (hd == 128) return (const void*)smallm_attention_cluster_kernel<128>;
     throw Error(SMALLM_ERR_INVALID, "attention: head_dim must be 32, 64 or 128");
 }
 
@@ -626,21 +628,20 @@ void launch_attention_cluster(const AttnArgs& a, uint32_t C, cudaStream_t stream
 // the GPU's memory to its own KV-block pool has none left for cudaMalloc to
 // find, and cudaMalloc / cudaFree can synchronise the device, which a
 // latency-bound decode loop cannot absorb.  For those callers the split-K
-// partials, the per-KV-head tickets and the position word live in this one
+// partials and the per-KV-head tickets live in this one
 // fixed array of the module, so a call allocates nothing.
 //
 // Layout: [0, kAttnStaticPartialBytes) partials, then kAttnStaticMaxKv
 // tickets (u32, must be zero before a launch; the merging CTA of each KV head
-// puts its ticket back to zero), then the position word.  Tickets start at zero
-// because the first call on a device clears them on its stream before its
-// launch.  Every call on a device shares this array, so calls whose kernels
-// overlap in time (other streams, other threads) race on it; callers must order
-// them.
+// puts its ticket back to zero).  The position goes to the kernel as a
+// parameter.  Tickets start at zero because the first call on a device clears
+// them on its stream before its launch.  Every call on a device shares this
+// array, so calls whose kernels overlap in time (other streams, other threads)
+// race on it; callers must order them.
 constexpr size_t kAttnStaticPartialBytes = 4u << 20;  // 4 MiB
 constexpr uint32_t kAttnStaticMaxKv = 256;
 constexpr size_t kAttnStaticTicketOff = kAttnStaticPartialBytes;
-constexpr size_t kAttnStaticPosOff = kAttnStaticTicketOff + 4 * kAttnStaticMaxKv;
-constexpr size_t kAttnStaticBytes = kAttnStaticPosOff + 256;
+constexpr size_t kAttnStaticBytes = kAttnStaticTicketOff + 4 * kAttnStaticMaxKv;
 static __device__ __align__(256) unsigned char g_attn_scratch[kAttnStaticBytes];
 
 constexpr int kAttnStaticMaxDevices = 64;
@@ -685,9 +686,12 @@ void launch_attention_static(const float* q, const float* kcache, const float* v
                                           "; the static scratch holds 4194304 (lower max_ctx or n_heads)");
     if (attention_smem(n_heads, n_kv, hd, max_ctx, n_split) > 200 * 1024)
         throw Error(SMALLM_ERR_INVALID, "attention: chunk does not fit in shared memory");
+    // K and V rows reach shared memory through bulk copies, whose global
+    // source must be 16-byte aligned (row offsets are whole rows of head_dim
+    // floats, so the base pointers decide)
+    if ((reinterpret_cast<uintptr_t>(kcache) | reinterpret_cast<uintptr_t>(vcache)) & 15u)
+        throw Error(SMALLM_ERR_INVALID, "attention: kcache_dev and vcache_dev must be 16-byte aligned");
     unsigned char* base = attention_static_scratch(stream);
-    uint32_t* pos_dev = reinterpret_cast<uint32_t*>(base + kAttnStaticPosOff);
-    SM_CUDA(cudaMemcpyAsync(pos_dev, &pos, sizeof(pos), cudaMemcpyHostToDevice, stream));
     AttnArgs a;
     a.q = q;
     a.kcache = kcache;
@@ -695,7 +699,8 @@ void launch_attention_static(const float* q, const float* kcache, const float* v
     a.out = out;
     a.partial = reinterpret_cast<float*>(base);
     a.counter = reinterpret_cast<unsigned int*>(base + kAttnStaticTicketOff);
-    a.pos = pos_dev;
+    a.pos = nullptr;
+    a.pos_value = pos;
     a.n_heads = n_heads;
     a.n_kv = n_kv;
     a.hd = hd;

@@ -111,6 +111,10 @@ struct GemvArgs {
 
 void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_t stream, bool pdl = false);
 
+// cudaFuncAttributeMaxDynamicSharedMemorySize of `fn` on the current device,
+// set once per (device, kernel, size) under a lock.
+void set_smem_limit_once(const void* fn, int bytes);
+
 // Pipeline shape the GEMV uses for a matrix: rows per tile, stages of the
 // shared-memory ring, bytes of staged x, total dynamic shared memory.
 struct GemvPlan {
@@ -157,7 +161,8 @@ struct AttnArgs {
     float* out;            // [n_heads * hd]
     float* partial;        // scratch: [n_kv][n_split][group][hd + 2]
     unsigned int* counter; // scratch: [n_kv], zero between launches
-    const uint32_t* pos;   // attend over positions 0..*pos
+    const uint32_t* pos;   // attend over positions 0..*pos (null: 0..pos_value)
+    uint32_t pos_value = 0;
     uint32_t n_heads, n_kv, hd, max_ctx, n_split;
     unsigned int* err = nullptr;  // raised if a bounded wait gives up
     TraceSlot* trace = nullptr;   // traced steps only

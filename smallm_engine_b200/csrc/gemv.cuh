@@ -473,7 +473,7 @@ __device__ __forceinline__ void gemv_epilogue_row(const GemvParams& p, uint32_t 
 // ------------------------------------------------------------------ kernel --
 
 template <class Fmt, int PRO, int EPI, int W>  // W consumer warps; warp W is the producer
-__global__ void __launch_bounds__((W + 1) * 32, 1) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__((W + 1) * 32, 1) smallm_qgemv_kernel(const GemvParams p) {
     static_assert(W <= kGemvMaxWarps && W <= Fmt::WIDE, "consumer warps");
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* xreg = smem;                                   // x records (or f32 x)

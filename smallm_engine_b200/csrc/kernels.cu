@@ -3,6 +3,8 @@
 #include <cmath>
 #include <cstring>
 #include <mutex>
+#include <set>
+#include <tuple>
 #include <unordered_map>
 
 #include "engine.h"
@@ -95,7 +97,7 @@ void qmat_free(QMat& m) {
 // One thread per (storage row, 32-element unit) for Q4_0, Q8_0 and F32:
 // quants to the front of the row record, f16 scales after them.  Source
 // blocks are byte-addressed (18/34-byte GGUF blocks are not aligned).
-__global__ void repack_blocks_kernel(const uint8_t* src, uint64_t src_row_bytes, uint64_t col_byte0,
+__global__ void smallm_repack_blocks_kernel(const uint8_t* src, uint64_t src_row_bytes, uint64_t col_byte0,
                                      const uint32_t* row_map, uint32_t rows, uint32_t rows_pad,
                                      uint32_t nunits, uint32_t stride, uint32_t type, uint8_t* dst) {
     const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -117,7 +119,7 @@ __global__ void repack_blocks_kernel(const uint8_t* src, uint64_t src_row_bytes,
 }
 
 // Q4_K: super-blocks are copied whole (row permutation / column slice only).
-__global__ void repack_q4k_kernel(const uint8_t* src, uint64_t src_row_bytes, uint64_t col_byte0,
+__global__ void smallm_repack_q4k_kernel(const uint8_t* src, uint64_t src_row_bytes, uint64_t col_byte0,
                                   const uint32_t* row_map, uint32_t rows, uint32_t rows_pad, uint32_t nsb,
                                   uint32_t stride, uint8_t* dst) {
     const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -136,7 +138,7 @@ __global__ void repack_q4k_kernel(const uint8_t* src, uint64_t src_row_bytes, ui
 // 2-bit high parts (byte k: elements k, 16+k, 32+k, 48+k).  The 16 int8
 // scales keep their order (element e uses scale e/16) and d goes to the end
 // of the record.  Lossless: every code and scale bit is preserved.
-__global__ void repack_q6k_kernel(const uint8_t* src, uint64_t src_row_bytes, uint64_t col_byte0,
+__global__ void smallm_repack_q6k_kernel(const uint8_t* src, uint64_t src_row_bytes, uint64_t col_byte0,
                                   const uint32_t* row_map, uint32_t rows, uint32_t rows_pad, uint32_t nsb,
                                   uint32_t stride, uint8_t* dst) {
     const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -178,14 +180,14 @@ void qmat_repack(QMat& m, const RepackSource& s, cudaStream_t stream) {
         const uint32_t nsb = m.cols / 256;
         const uint64_t n = (uint64_t)m.rows_pad * nsb;
         if (m.type == SM_T_Q4_K)
-            repack_q4k_kernel<<<(unsigned)((n + T - 1) / T), T, 0, stream>>>(s.src, rb, cb0, s.row_map, m.rows,
+            smallm_repack_q4k_kernel<<<(unsigned)((n + T - 1) / T), T, 0, stream>>>(s.src, rb, cb0, s.row_map, m.rows,
                                                                               m.rows_pad, nsb, m.row_stride, m.base);
         else
-            repack_q6k_kernel<<<(unsigned)((n + T - 1) / T), T, 0, stream>>>(s.src, rb, cb0, s.row_map, m.rows,
+            smallm_repack_q6k_kernel<<<(unsigned)((n + T - 1) / T), T, 0, stream>>>(s.src, rb, cb0, s.row_map, m.rows,
                                                                               m.rows_pad, nsb, m.row_stride, m.base);
     } else {
         const uint64_t n = (uint64_t)m.rows_pad * m.units;
-        repack_blocks_kernel<<<(unsigned)((n + T - 1) / T), T, 0, stream>>>(
+        smallm_repack_blocks_kernel<<<(unsigned)((n + T - 1) / T), T, 0, stream>>>(
             s.src, rb, cb0, s.row_map, m.rows, m.rows_pad, m.units, m.row_stride, m.type, m.base);
     }
     SM_CUDA(cudaGetLastError());
@@ -297,7 +299,7 @@ __device__ void dequant_group(const QMat m, uint32_t r, uint32_t g, float* out) 
     }
 }
 
-__global__ void qmat_dequant_kernel(const QMat m, float* y) {
+__global__ void smallm_qmat_dequant_kernel(const QMat m, float* y) {
     const uint32_t groups = m.cols / 32;
     const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (uint64_t)m.rows * groups) return;
@@ -307,14 +309,14 @@ __global__ void qmat_dequant_kernel(const QMat m, float* y) {
 
 void launch_qmat_dequant(const QMat& m, float* y, cudaStream_t stream) {
     const uint64_t n = (uint64_t)m.rows * (m.cols / 32);
-    qmat_dequant_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(m, y);
+    smallm_qmat_dequant_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(m, y);
     SM_CUDA(cudaGetLastError());
 }
 
 
 // Raw GGUF blocks (contiguous, byte-addressed) -> f32, one thread per 32
 // elements, same arithmetic as dequant_group.
-__global__ void dequant_raw_kernel(uint32_t type, const uint8_t* src, uint64_t count, float* out) {
+__global__ void smallm_dequant_raw_kernel(uint32_t type, const uint8_t* src, uint64_t count, float* out) {
     const uint64_t g = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (g * 32 >= count) return;
     float* o = out + g * 32;
@@ -372,7 +374,7 @@ __global__ void dequant_raw_kernel(uint32_t type, const uint8_t* src, uint64_t c
 
 void launch_dequant_raw(uint32_t type, const uint8_t* src, uint64_t count, float* out, cudaStream_t stream) {
     const uint64_t groups = (count + 31) / 32;
-    dequant_raw_kernel<<<(unsigned)((groups + 255) / 256), 256, 0, stream>>>(type, src, count, out);
+    smallm_dequant_raw_kernel<<<(unsigned)((groups + 255) / 256), 256, 0, stream>>>(type, src, count, out);
     SM_CUDA(cudaGetLastError());
 }
 
@@ -398,7 +400,7 @@ void launch_kernel_ex(const void* fn, dim3 grid, dim3 block, size_t smem, cudaSt
 // ------------------------------------------------------------- embedding --
 
 // One thread per 32-element group of the token's row.
-__global__ void embed_kernel(const QMat m, DecodeState* st, float* x, TraceSlot* trace) {
+__global__ void smallm_embed_kernel(const QMat m, DecodeState* st, float* x, TraceSlot* trace) {
     if (threadIdx.x == 0) trace_mark(trace, 0);
     pdl_launch_dependents();
     pdl_wait();
@@ -415,12 +417,12 @@ void launch_embed(const QMat& emb, DecodeState* st, float* x, cudaStream_t strea
     QMat m = emb;
     void* args[] = {&m, &st, &x, &trace};
     const uint32_t groups = m.cols / 32;
-    launch_kernel_ex((const void*)embed_kernel, dim3((groups + 31) / 32), dim3(32), 0, stream, pdl, args);
+    launch_kernel_ex((const void*)smallm_embed_kernel, dim3((groups + 31) / 32), dim3(32), 0, stream, pdl, args);
 }
 
 // Prefill: X[t] = dequantized row tokens[t] for t < T (one thread per
 // 32-element group).  Ids were validated on the host.
-__global__ void embed_rows_kernel(const QMat m, const uint32_t* tokens, uint32_t T, float* X) {
+__global__ void smallm_embed_rows_kernel(const QMat m, const uint32_t* tokens, uint32_t T, float* X) {
     const uint32_t groups = m.cols / 32;
     const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (uint64_t)T * groups) return;
@@ -430,11 +432,11 @@ __global__ void embed_rows_kernel(const QMat m, const uint32_t* tokens, uint32_t
 
 void launch_embed_rows(const QMat& emb, const uint32_t* tokens, uint32_t T, float* X, cudaStream_t stream) {
     const uint64_t n = (uint64_t)T * (emb.cols / 32);
-    embed_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(emb, tokens, T, X);
+    smallm_embed_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(emb, tokens, T, X);
     SM_CUDA(cudaGetLastError());
 }
 
-__global__ void finalize_kernel(DecodeState* st, uint32_t* ids, uint32_t cap, TraceSlot* trace) {
+__global__ void smallm_finalize_kernel(DecodeState* st, uint32_t* ids, uint32_t cap, TraceSlot* trace) {
     trace_mark(trace, 0);
     pdl_launch_dependents();
     pdl_wait();
@@ -449,10 +451,10 @@ __global__ void finalize_kernel(DecodeState* st, uint32_t* ids, uint32_t cap, Tr
 
 void launch_finalize(DecodeState* st, uint32_t* ids, uint32_t cap, cudaStream_t stream, bool pdl, TraceSlot* trace) {
     void* args[] = {&st, &ids, &cap, &trace};
-    launch_kernel_ex((const void*)finalize_kernel, dim3(1), dim3(1), 0, stream, pdl, args);
+    launch_kernel_ex((const void*)smallm_finalize_kernel, dim3(1), dim3(1), 0, stream, pdl, args);
 }
 
-__global__ void finalize_tp_kernel(DecodeState* st, const unsigned long long* keys, int n, uint32_t* ids,
+__global__ void smallm_finalize_tp_kernel(DecodeState* st, const unsigned long long* keys, int n, uint32_t* ids,
                                    uint32_t cap, unsigned int* epoch) {
     pdl_wait();
     if (epoch) *epoch += 1u;
@@ -470,13 +472,13 @@ __global__ void finalize_tp_kernel(DecodeState* st, const unsigned long long* ke
 void launch_finalize_tp(DecodeState* st, const unsigned long long* keys, int n, uint32_t* ids, uint32_t cap,
                         unsigned int* epoch, cudaStream_t stream, bool pdl) {
     void* args[] = {&st, &keys, &n, &ids, &cap, &epoch};
-    launch_kernel_ex((const void*)finalize_tp_kernel, dim3(1), dim3(1), 0, stream, pdl, args);
+    launch_kernel_ex((const void*)smallm_finalize_tp_kernel, dim3(1), dim3(1), 0, stream, pdl, args);
 }
 
 // ------------------------------------------------------------- op level --
 
 // ops::rmsnorm (ops.cpp:29-40) on one CTA
-__global__ void rmsnorm_kernel(const float* x, const float* w, uint32_t n, float eps, float* y) {
+__global__ void smallm_rmsnorm_kernel(const float* x, const float* w, uint32_t n, float eps, float* y) {
     __shared__ float red[32];
     float ss = 0.f;
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) ss += x[i] * x[i];
@@ -486,7 +488,7 @@ __global__ void rmsnorm_kernel(const float* x, const float* w, uint32_t n, float
 }
 
 // ops::softmax (ops.cpp:43-57) in place on one CTA
-__global__ void softmax_kernel(float* x, uint32_t n) {
+__global__ void smallm_softmax_kernel(float* x, uint32_t n) {
     __shared__ float red[32];
     __shared__ float mx;
     float m = -INFINITY;
@@ -513,7 +515,7 @@ __global__ void softmax_kernel(float* x, uint32_t n) {
 }
 
 // ops::silu (ops.cpp:60-65)
-__global__ void silu_kernel(float* x, uint32_t n) {
+__global__ void smallm_silu_kernel(float* x, uint32_t n) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) {
         const float v = x[i];
@@ -522,7 +524,7 @@ __global__ void silu_kernel(float* x, uint32_t n) {
 }
 
 // ops::rope (ops.cpp:68-92) with the host table of (cos, sin)
-__global__ void rope_kernel(float* x, uint32_t n_heads, uint32_t hd, const float2* cs) {
+__global__ void smallm_rope_kernel(float* x, uint32_t n_heads, uint32_t hd, const float2* cs) {
     const uint32_t half = hd / 2;
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n_heads * half) return;
@@ -535,22 +537,22 @@ __global__ void rope_kernel(float* x, uint32_t n_heads, uint32_t hd, const float
 }
 
 void launch_rmsnorm(const float* x, const float* w, uint32_t n, float eps, float* y, cudaStream_t s) {
-    rmsnorm_kernel<<<1, 1024, 0, s>>>(x, w, n, eps, y);
+    smallm_rmsnorm_kernel<<<1, 1024, 0, s>>>(x, w, n, eps, y);
     SM_CUDA(cudaGetLastError());
 }
 void launch_softmax(float* x, uint32_t n, cudaStream_t s) {
-    softmax_kernel<<<1, 1024, 0, s>>>(x, n);
+    smallm_softmax_kernel<<<1, 1024, 0, s>>>(x, n);
     SM_CUDA(cudaGetLastError());
 }
 void launch_silu(float* x, uint32_t n, cudaStream_t s) {
     if (!n) return;
-    silu_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, n);
+    smallm_silu_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, n);
     SM_CUDA(cudaGetLastError());
 }
 void launch_rope(float* x, uint32_t n_heads, uint32_t head_dim, const float2* cs, cudaStream_t s) {
     const uint32_t n = n_heads * (head_dim / 2);
     if (!n) return;
-    rope_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, n_heads, head_dim, cs);
+    smallm_rope_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, n_heads, head_dim, cs);
     SM_CUDA(cudaGetLastError());
 }
 
@@ -575,18 +577,18 @@ __device__ unsigned int g_gemv_err;  // set by a bounded wait that gave up
 
 template <class Fmt, int W>
 static const void* pick(int pro, int epi) {
-    if (pro == PRO_PLAIN && epi == EPI_STORE) return (const void*)gemv_kernel<Fmt, PRO_PLAIN, EPI_STORE, W>;
-    if (pro == PRO_PLAIN && epi == EPI_RESIDUAL) return (const void*)gemv_kernel<Fmt, PRO_PLAIN, EPI_RESIDUAL, W>;
-    if (pro == PRO_RMS && epi == EPI_STORE) return (const void*)gemv_kernel<Fmt, PRO_RMS, EPI_STORE, W>;
-    if (pro == PRO_RMS && epi == EPI_QKV) return (const void*)gemv_kernel<Fmt, PRO_RMS, EPI_QKV, W>;
-    if (pro == PRO_RMS && epi == EPI_SWIGLU) return (const void*)gemv_kernel<Fmt, PRO_RMS, EPI_SWIGLU, W>;
-    if (pro == PRO_RMS && epi == EPI_LOGITS) return (const void*)gemv_kernel<Fmt, PRO_RMS, EPI_LOGITS, W>;
+    if (pro == PRO_PLAIN && epi == EPI_STORE) return (const void*)smallm_qgemv_kernel<Fmt, PRO_PLAIN, EPI_STORE, W>;
+    if (pro == PRO_PLAIN && epi == EPI_RESIDUAL) return (const void*)smallm_qgemv_kernel<Fmt, PRO_PLAIN, EPI_RESIDUAL, W>;
+    if (pro == PRO_RMS && epi == EPI_STORE) return (const void*)smallm_qgemv_kernel<Fmt, PRO_RMS, EPI_STORE, W>;
+    if (pro == PRO_RMS && epi == EPI_QKV) return (const void*)smallm_qgemv_kernel<Fmt, PRO_RMS, EPI_QKV, W>;
+    if (pro == PRO_RMS && epi == EPI_SWIGLU) return (const void*)smallm_qgemv_kernel<Fmt, PRO_RMS, EPI_SWIGLU, W>;
+    if (pro == PRO_RMS && epi == EPI_LOGITS) return (const void*)smallm_qgemv_kernel<Fmt, PRO_RMS, EPI_LOGITS, W>;
     // tensor parallel: row-parallel partials to peers, and the GEMVs that sum them
-    if (pro == PRO_PLAIN && epi == EPI_PEER) return (const void*)gemv_kernel<Fmt, PRO_PLAIN, EPI_PEER, W>;
-    if (pro == PRO_RMS_SUM && epi == EPI_STORE) return (const void*)gemv_kernel<Fmt, PRO_RMS_SUM, EPI_STORE, W>;
-    if (pro == PRO_RMS_SUM && epi == EPI_QKV) return (const void*)gemv_kernel<Fmt, PRO_RMS_SUM, EPI_QKV, W>;
-    if (pro == PRO_RMS_SUM && epi == EPI_SWIGLU) return (const void*)gemv_kernel<Fmt, PRO_RMS_SUM, EPI_SWIGLU, W>;
-    if (pro == PRO_RMS_SUM && epi == EPI_LOGITS) return (const void*)gemv_kernel<Fmt, PRO_RMS_SUM, EPI_LOGITS, W>;
+    if (pro == PRO_PLAIN && epi == EPI_PEER) return (const void*)smallm_qgemv_kernel<Fmt, PRO_PLAIN, EPI_PEER, W>;
+    if (pro == PRO_RMS_SUM && epi == EPI_STORE) return (const void*)smallm_qgemv_kernel<Fmt, PRO_RMS_SUM, EPI_STORE, W>;
+    if (pro == PRO_RMS_SUM && epi == EPI_QKV) return (const void*)smallm_qgemv_kernel<Fmt, PRO_RMS_SUM, EPI_QKV, W>;
+    if (pro == PRO_RMS_SUM && epi == EPI_SWIGLU) return (const void*)smallm_qgemv_kernel<Fmt, PRO_RMS_SUM, EPI_SWIGLU, W>;
+    if (pro == PRO_RMS_SUM && epi == EPI_LOGITS) return (const void*)smallm_qgemv_kernel<Fmt, PRO_RMS_SUM, EPI_LOGITS, W>;
     throw Error(1, "gemv: unsupported prologue/epilogue combination");
 }
 
@@ -667,19 +669,22 @@ unsigned int* device_error_flag() {
     return it->second;
 }
 
-void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_t stream, bool pdl) {
+void set_smem_limit_once(const void* fn, int bytes) {
     static std::mutex mu;
-    static std::unordered_map<const void*, int> configured;
+    static std::set<std::tuple<int, const void*, int>> done;  // (device, kernel, bytes)
+    int dev = 0;
+    SM_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> g(mu);
+    if (done.count({dev, fn, bytes})) return;
+    SM_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done.insert({dev, fn, bytes});
+}
+
+void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_t stream, bool pdl) {
     const GemvPlan pl = gemv_plan(m, a.smem_cap);
     const void* fn = gemv_kernel_for(m.type, pro, epi, pl.warps);
     unsigned int* err = device_error_flag();
-    {
-        std::lock_guard<std::mutex> g(mu);
-        if (!configured.count(fn)) {
-            SM_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit));
-            configured[fn] = 1;
-        }
-    }
+    set_smem_limit_once(fn, (int)kSmemLimit);
     const uint32_t ntiles = m.rows_pad / pl.rt;
     uint32_t grid = (uint32_t)device_sm_count();
     if (grid > ntiles) grid = ntiles;

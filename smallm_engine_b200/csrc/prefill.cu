@@ -19,7 +19,7 @@ constexpr int kPreThreads = 256;
 
 // Y[t] = X[t] * (1 / sqrt(mean(X[t]^2) + eps)) * w, one CTA per token.
 // (Yh: the same values rounded to f16 instead, the tensor-core GEMM's input.)
-__global__ void rmsnorm_rows_kernel(const float* X, const float* w, uint32_t n, float eps, float* Y, __half* Yh) {
+__global__ void smallm_rmsnorm_rows_kernel(const float* X, const float* w, uint32_t n, float eps, float* Y, __half* Yh) {
     __shared__ float red[32];
     const float* x = X + (size_t)blockIdx.x * n;
     float ss = 0.f;
@@ -39,7 +39,7 @@ __global__ void rmsnorm_rows_kernel(const float* X, const float* w, uint32_t n, 
 // value rows) of token t at position pos0 + t: bias, RoPE with the reference
 // build's rounding, query into Q[t], key and value into the cache.  One
 // thread per (token, even row of a pair or value row).
-__global__ void qkv_post_kernel(const float* Y, uint32_t rows, uint32_t T, uint32_t q_rows, uint32_t k_rows,
+__global__ void smallm_qkv_post_kernel(const float* Y, uint32_t rows, uint32_t T, uint32_t q_rows, uint32_t k_rows,
                                 uint32_t hd, const float* bias, const float2* rope, uint32_t pos0,
                                 uint32_t max_ctx, float* Q, float* kc, float* vc) {
     const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -107,7 +107,7 @@ struct PreAttnSmem {
 // out (f32) or, when out_h is set, out_h (the same values rounded to f16,
 // the tensor-core GEMM's input).
 template <int HD, int G, int TOK>
-__global__ void __launch_bounds__(32 * TOK) attention_prefill_kernel(const float* __restrict__ Q,
+__global__ void __launch_bounds__(32 * TOK) smallm_attention_prefill_kernel(const float* __restrict__ Q,
                                                                      const float* __restrict__ kc,
                                                                      const float* __restrict__ vc, uint32_t n_heads,
                                                                      uint32_t max_ctx, uint32_t pos0, uint32_t T,
@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(32 * TOK) attention_prefill_kernel(const float
 
 // Merge of the key splits of one (token, head): out = sum_s acc_s e^(m_s - M)
 // / sum_s l_s e^(m_s - M), M = max_s m_s (split 0 holds key 0, so M is finite).
-__global__ void attention_prefill_merge_kernel(const float* __restrict__ part, uint32_t n_split, uint32_t hd,
+__global__ void smallm_attention_prefill_merge_kernel(const float* __restrict__ part, uint32_t n_split, uint32_t hd,
                                                float* __restrict__ out, __half* out_h) {
     const size_t row = blockIdx.x;  // token * n_heads + head
     const float* pr = part + row * n_split * (hd + 2);
@@ -283,18 +283,18 @@ static void launch_pre_attn_tok(const float* Q, const float* kc, const float* vc
     {
         std::lock_guard<std::mutex> lk(mu);
         if (!configured.count(dev)) {
-            SM_CUDA(cudaFuncSetAttribute(attention_prefill_kernel<HD, G, TOK>,
+            SM_CUDA(cudaFuncSetAttribute(smallm_attention_prefill_kernel<HD, G, TOK>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::bytes));
             configured[dev] = true;
         }
     }
     const uint32_t n_split = prefill_attention_splits(T, n_kv, pos0);
     const dim3 grid((T + TOK - 1) / TOK, n_kv, n_split);
-    attention_prefill_kernel<HD, G, TOK><<<grid, 32 * TOK, S::bytes, s>>>(Q, kc, vc, n_heads, max_ctx, pos0, T, out,
+    smallm_attention_prefill_kernel<HD, G, TOK><<<grid, 32 * TOK, S::bytes, s>>>(Q, kc, vc, n_heads, max_ctx, pos0, T, out,
                                                                           out_h, n_split, part);
     if (n_split > 1) {
         SM_CUDA(cudaGetLastError());
-        attention_prefill_merge_kernel<<<T * n_heads, HD, 0, s>>>(part, n_split, HD, out, out_h);
+        smallm_attention_prefill_merge_kernel<<<T * n_heads, HD, 0, s>>>(part, n_split, HD, out, out_h);
     }
 }
 
@@ -329,7 +329,7 @@ static void launch_pre_attn_hd(uint32_t G, const float* Q, const float* kc, cons
 
 // H[t][j] = silu(Y[t][2j]) * Y[t][2j+1] (gate / up rows interleaved).
 // (Hh: the same values rounded to f16 instead, the tensor-core GEMM's input.)
-__global__ void swiglu_rows_kernel(const float* Y, uint32_t ffn, uint32_t T, float* H, __half* Hh) {
+__global__ void smallm_swiglu_rows_kernel(const float* Y, uint32_t ffn, uint32_t T, float* H, __half* Hh) {
     const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (uint64_t)T * ffn) return;
     const uint32_t t = (uint32_t)(idx / ffn), j = (uint32_t)(idx % ffn);
@@ -340,7 +340,7 @@ __global__ void swiglu_rows_kernel(const float* Y, uint32_t ffn, uint32_t T, flo
 }
 
 // X += Y (the residual, ops::axpy with a = 1).
-__global__ void add_rows_kernel(float* X, const float* Y, uint64_t n) {
+__global__ void smallm_add_rows_kernel(float* X, const float* Y, uint64_t n) {
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) X[i] += Y[i];
 }
@@ -349,14 +349,14 @@ static unsigned blocks_for(uint64_t n) { return (unsigned)((n + kPreThreads - 1)
 
 void launch_rmsnorm_rows(const float* X, const float* w, uint32_t n, uint32_t T, float eps, float* Y,
                          cudaStream_t s, __half* Yh) {
-    rmsnorm_rows_kernel<<<T, 1024, 0, s>>>(X, w, n, eps, Y, Yh);
+    smallm_rmsnorm_rows_kernel<<<T, 1024, 0, s>>>(X, w, n, eps, Y, Yh);
     SM_CUDA(cudaGetLastError());
 }
 
 void launch_qkv_post(const float* Y, uint32_t rows, uint32_t T, uint32_t q_rows, uint32_t k_rows, uint32_t hd,
                      const float* bias, const float2* rope, uint32_t pos0, uint32_t max_ctx, float* Q, float* kc,
                      float* vc, cudaStream_t s) {
-    qkv_post_kernel<<<blocks_for((uint64_t)T * rows), kPreThreads, 0, s>>>(Y, rows, T, q_rows, k_rows, hd, bias,
+    smallm_qkv_post_kernel<<<blocks_for((uint64_t)T * rows), kPreThreads, 0, s>>>(Y, rows, T, q_rows, k_rows, hd, bias,
                                                                           rope, pos0, max_ctx, Q, kc, vc);
     SM_CUDA(cudaGetLastError());
 }
@@ -398,12 +398,12 @@ void launch_attention_prefill(const float* Q, const float* kc, const float* vc, 
 }
 
 void launch_swiglu_rows(const float* Y, uint32_t ffn, uint32_t T, float* H, cudaStream_t s, __half* Hh) {
-    swiglu_rows_kernel<<<blocks_for((uint64_t)T * ffn), kPreThreads, 0, s>>>(Y, ffn, T, H, Hh);
+    smallm_swiglu_rows_kernel<<<blocks_for((uint64_t)T * ffn), kPreThreads, 0, s>>>(Y, ffn, T, H, Hh);
     SM_CUDA(cudaGetLastError());
 }
 
 void launch_add_rows(float* X, const float* Y, uint64_t n, cudaStream_t s) {
-    add_rows_kernel<<<blocks_for(n), kPreThreads, 0, s>>>(X, Y, n);
+    smallm_add_rows_kernel<<<blocks_for(n), kPreThreads, 0, s>>>(X, Y, n);
     SM_CUDA(cudaGetLastError());
 }
 

@@ -118,7 +118,7 @@ __device__ void radix_pass(const uint32_t* kin, const uint32_t* iin, uint32_t* k
 
 // kind 1 temperature, 2 top-k, 3 top-p.  scratch: 4 * n u32.
 __global__ void __launch_bounds__(kSampThreads, 1)
-    sample_kernel(const float* logits, uint32_t n, uint32_t kind, uint32_t k_arg, float p_arg, float temp, float r,
+    smallm_sample_kernel(const float* logits, uint32_t n, uint32_t kind, uint32_t k_arg, float p_arg, float temp, float r,
                   uint32_t* scratch, uint32_t* out) {
     __shared__ uint32_t hist[256 * kSampWarps];
     __shared__ float sh[64];
@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(kSampThreads, 1)
 
 void launch_sample(const float* logits, uint32_t n, uint32_t kind, uint32_t k, float p, float temp, float r,
                    uint32_t* scratch, uint32_t* out, cudaStream_t stream) {
-    sample_kernel<<<1, kSampThreads, 0, stream>>>(logits, n, kind, k, p, temp, r, scratch, out);
+    smallm_sample_kernel<<<1, kSampThreads, 0, stream>>>(logits, n, kind, k, p, temp, r, scratch, out);
     SM_CUDA(cudaGetLastError());
 }
 

@@ -120,7 +120,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 template <uint32_t BN>
 __global__ void __launch_bounds__(kThreads, 1)
-    tc_gemm_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx,
+    smallm_tc_gemm_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx,
                    float* __restrict__ y, uint32_t N, uint32_t T, uint32_t K, uint32_t ldy, unsigned int* err) {
     using C = TcCfg<BN>;
     extern __shared__ uint8_t smem_raw[];
@@ -277,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-__global__ void f32_to_f16_kernel(const float* __restrict__ src, __half* __restrict__ dst, uint64_t n) {
+__global__ void smallm_f32_to_f16_kernel(const float* __restrict__ src, __half* __restrict__ dst, uint64_t n) {
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t n4 = n / 4;
     const float4* s4 = reinterpret_cast<const float4*>(src);
@@ -335,14 +335,14 @@ void launch_tc(const CUtensorMap& tw, const CUtensorMap& tx, float* Y, uint32_t 
     {
         std::lock_guard<std::mutex> g(mu);
         if (!configured.count(dev)) {
-            SM_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            SM_CUDA(cudaFuncSetAttribute(smallm_tc_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)C::smem));
             configured[dev] = true;
         }
     }
     const uint64_t tiles = (uint64_t)((T + BN - 1) / BN) * ((N + kBM - 1) / kBM);
     const uint32_t grid = (uint32_t)std::min<uint64_t>(tiles, (uint64_t)device_sm_count());
-    tc_gemm_kernel<BN><<<grid, kThreads, C::smem, s>>>(tw, tx, Y, N, T, K, ldy, device_error_flag());
+    smallm_tc_gemm_kernel<BN><<<grid, kThreads, C::smem, s>>>(tw, tx, Y, N, T, K, ldy, device_error_flag());
     SM_CUDA(cudaGetLastError());
 }
 
@@ -390,7 +390,7 @@ void launch_f32_to_f16(const float* src, __half* dst, uint64_t n, cudaStream_t s
         throw Error(SMALLM_ERR_INVALID, "f32_to_f16: src must be 16-byte and dst 8-byte aligned");
     const uint64_t want = (n / 4 + 255) / 256;
     const uint32_t grid = (uint32_t)std::min<uint64_t>(std::max<uint64_t>(want, 1), 8ull * device_sm_count());
-    f32_to_f16_kernel<<<grid, 256, 0, s>>>(src, dst, n);
+    smallm_f32_to_f16_kernel<<<grid, 256, 0, s>>>(src, dst, n);
     SM_CUDA(cudaGetLastError());
 }
 

@@ -1,4 +1,3 @@
-import os
 import sys
 from pathlib import Path
 
@@ -13,7 +12,6 @@ sys.path.insert(0, str(ROOT / "oracle"))
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs an sm_100 GPU (run with -m gpu on a B200)")
-    config.addinivalue_line("markers", "slow: full-size workloads (opt in with SMALLM_FULL=1)")
 
 
 @pytest.fixture(scope="session")
@@ -53,6 +51,3 @@ def be():
     yield b
     b.close()
 
-
-def full_size() -> bool:
-    return os.environ.get("SMALLM_FULL", "") == "1"
