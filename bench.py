@@ -310,10 +310,10 @@ def gemv_legs(device: int, iters: int = 50, cpu: bool = True) -> list[dict]:
                 n += 1
             cms = (time.perf_counter() - t0) * 1e3 / n
             # the tests' GEMV bound: 1e-5 sum|w x| + sum|w| r, r = one unit of
-            # x's 15-bit block fixed point
+            # x's 21-bit block fixed point
             wd = np.abs(O.Oracle().dequantize(synth.Q4_0, Ws[0], rows * cols).reshape(rows, cols))
             m = np.abs(xh.astype(np.float64)).reshape(-1, 32).max(axis=1)
-            r = np.repeat(np.where(m >= 1e-30, np.ldexp(1.0, np.frexp(m)[1] - 15), 1e-30), 32)
+            r = np.repeat(np.where(m >= 1e-30, np.ldexp(1.0, np.frexp(m)[1] - 21), 1e-30), 32)
             bound = 1e-5 * (wd @ np.abs(xh.astype(np.float64))) + wd @ r + 1e-30
             err = np.abs(yg - yc.astype(np.float64))
             leg.update({"cpu_kind": kind, "cpu_ms": cms, "cpu_gbs": algo / (cms / 1e3) / 1e9,
@@ -418,9 +418,9 @@ def our_arm(args, ws, rank, local):
             "scaling": "strong",
             "vs_baseline": None,
             "dtype": "f32",
-            "x_repr": "activations enter the GEMVs as block fixed point per 32 elements: 15-bit (two int8 "
-                      "digits) for the Q4_0/Q4_K weights, 21-bit (three digits) for Q8_0/Q6_K; exact int32 "
-                      "dot per block, f32 scale and accumulation; attention, norms and residual in f32",
+            "x_repr": "activations enter the GEMVs as 21-bit block fixed point per 32 elements (three "
+                      "int8 digits, held to 2^-21 of the block maximum) for every weight format; exact int32 "
+                      "dot per digit and block, f32 scale and accumulation; attention, norms and residual in f32",
             "data": "synthetic (seeded random weights, random token ids)",
             "config": decode_config(args.workload, args.prompt, args.warmup, args.steps),
             "executor": f"tp{ws}" if ws > 1 else "single GPU",

@@ -23,17 +23,13 @@
 // Math side -- integer dot products.  In the prologue each CTA turns x (f32;
 // times the RMSNorm weight when the norm is fused, ops::rmsnorm,
 // src/core/ops.cpp:29-40) into block fixed point: per 32-element block,
-// X_i = rint(x_i * 2^(B-e)) with 2^e > max|x_i|, split into signed bytes
-// ("digits").  A block's integer weight codes q meet x through IDP4A, one
-// sum S_d = sum_i q_i D_d,i per digit, so the block needs one int->float
-// conversion and one float scale (weight scale * 2^(e-B)).
-//  - 8-bit and 6-bit codes: B = 21, three balanced digits
-//    X = D2*2^16 + D1*2^8 + D0; x is held to 2^-21 of the block maximum, the
-//    order of the f32 rounding of the reference's FMA chain.
-//  - 4-bit codes: B = 15, two digits X = D1*2^8 + D0 (D0 unsigned), x held to
-//    2^-15 of the block maximum.  High nibbles are masked in place (16 q, no
-//    shift) and their sums joined with the low ones as 16 S_lo + S_hi16, so a
-//    32-weight block costs 8 masks and 16 IDP4A; 16 sum q X stays below 2^28.
+// X_i = rint(x_i * 2^(21-e)) with 2^e > max|x_i|, split into three balanced
+// signed bytes ("digits"), so x is held to 2^-21 of the block maximum, the
+// order of the f32 rounding of the reference's FMA chain.  A block's integer
+// weight codes q meet x through IDP4A, one exact sum S_d = sum_i q_i D_d,i per
+// digit; the digits are joined in float and the block needs one float scale
+// (weight scale * 2^(e-21)).  4-bit codes are masked in place (the high
+// nibble as 16 q, no shift), so a 32-weight block costs 8 masks and 24 IDP4A.
 // The norm's 1/rms is a scalar and is applied to the row results in the
 // epilogue.
 //
@@ -114,19 +110,20 @@ struct GemvParams {
 
 // ------------------------------------------------------- x in fixed point --
 
-// Shared-memory record of one 32-element block of x with ND digits.
-template <int ND>
+// Shared-memory record of one 32-element block of x: X_i = rint(x_i 2^(21-e))
+// (2^e > the block's max |x|) as three balanced signed-byte digits,
+// X = D2 2^16 + D1 2^8 + D0, plus four format-specific words (XK below).
 struct XRec {
-    uint32_t d[ND][8];             // digits, 4 elements per word (d[0] least significant)
-    int32_t sx_lo, sx_hi;          // sum of X over elements 0-15 / 16-31
-    float xs;                      // x_i ~= X_i * 2^(e-B); 4-bit codes fold in 1/16 (see dot)
-    float xsum;                    // sum of the f32 x_i
+    uint32_t d[3][8];   // digits, 4 elements per word (d[0] least significant)
+    int32_t s0, s1;     // XK_PLAIN / XK_NIB: sum of X over elements 0-15 / 16-31;
+    uint32_t s2;        //   s2 = bits of the f32 sum of x.  XK_NIB_SD: s0, s1, s2 =
+                        //   sum over the block of D0, D1, D2
+    float xs;           // x_i ~= X_i xs; XK_NIB / XK_NIB_SD fold in 1/16 (see the dots)
 };
-template <int ND>
-__host__ __device__ constexpr int xrec_bytes() { return ND * 32 + 16; }
-template <int ND>
-__host__ __device__ constexpr int xrec_bits() { return ND == 3 ? 21 : 15; }
-static_assert(sizeof(XRec<3>) == xrec_bytes<3>() && sizeof(XRec<2>) == xrec_bytes<2>(), "XRec layout");
+constexpr int kXrecBytes = 112;
+constexpr int kXrecBits = 21;
+static_assert(sizeof(XRec) == kXrecBytes, "XRec layout");
+enum { XK_PLAIN = 0, XK_NIB = 1, XK_NIB_SD = 2 };
 
 // Exact int -> float for |v| < 2^22 (IADD + FADD, no conversion unit).
 __device__ __forceinline__ float i2f_small(int v) {
@@ -136,10 +133,11 @@ __device__ __forceinline__ float i2f_small(int v) {
 // Build the record of one 32-element block cooperatively: the 8 aligned lanes
 // of a group each hold one float4 (elements 4j..4j+3, j = lane & 7).  All 32
 // lanes must call it (shuffles); lanes with act == false hold zeros and write
-// nothing.
-template <int ND>
+// nothing.  x is held to 2^-21 of the block maximum, the order of the f32
+// rounding of the reference's FMA chain.
+template <int XK>
 __device__ __forceinline__ void build_xrec_lane(float4 q, int lane, bool act, uint8_t* rec) {
-    constexpr int B = xrec_bits<ND>();
+    constexpr int B = kXrecBits;
     const int j = lane & 7;
     float m = fmaxf(fmaxf(fabsf(q.x), fabsf(q.y)), fmaxf(fabsf(q.z), fabsf(q.w)));
     float s = (q.x + q.y) + (q.z + q.w);
@@ -157,65 +155,73 @@ __device__ __forceinline__ void build_xrec_lane(float4 q, int lane, bool act, ui
     const float up = m > 0.f ? __uint_as_float((uint32_t)(B - e + 127) << 23) : 0.f;
     // X = rint(x * 2^(B-e)): x * 2^(B-e) is exact and |X| <= 2^B < 2^22, so
     // one FMA with 1.5 * 2^23 rounds it (ties to even) into the low mantissa
-    // bits: bits = 0x4B400000 + X, and the low bytes of bits are those of X
+    // bits: bits = 0x4B400000 + X
     constexpr float kMagic = 12582912.0f;
     constexpr uint32_t kMagicBits = 0x4B400000u;
     const float v[4] = {q.x, q.y, q.z, q.w};
     uint32_t bits[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        float r = fmaf(v[k], up, kMagic);
-        if constexpr (ND == 2) r = fminf(r, kMagic + 32767.0f);  // x * up < 2^15 may round up to 2^15
-        bits[k] = __float_as_uint(r);
-    }
-    uint32_t p[ND];
-    if constexpr (ND == 2) {
-        // unsigned low digit = byte 0 of X, signed high digit = byte 1
-        const uint32_t t01 = __byte_perm(bits[0], bits[1], 0x5140);  // X0.b0 X1.b0 X0.b1 X1.b1
-        const uint32_t t23 = __byte_perm(bits[2], bits[3], 0x5140);
-        p[0] = __byte_perm(t01, t23, 0x5410);
-        p[1] = __byte_perm(t01, t23, 0x7632);
-    } else {
+    for (int k = 0; k < 4; ++k) bits[k] = __float_as_uint(fmaf(v[k], up, kMagic));
+    uint32_t p[3] = {0u, 0u, 0u};
+    int ds[3] = {0, 0, 0};  // this lane's digit sums (XK_NIB_SD)
 #pragma unroll
-        for (int d = 0; d < ND; ++d) p[d] = 0u;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {  // balanced digits: X = D2 2^16 + D1 2^8 + D0
-            const int X = (int)(bits[k] - kMagicBits);
-            const int a0 = (int)(int8_t)(X & 0xFF);
-            const int X1 = (X - a0) >> 8;
-            const int a1 = (int)(int8_t)(X1 & 0xFF);
-            const int a2 = (X1 - a1) >> 8;
-            p[0] |= (uint32_t)(a0 & 0xFF) << (8 * k);
-            p[1] |= (uint32_t)(a1 & 0xFF) << (8 * k);
-            p[2] |= (uint32_t)(a2 & 0xFF) << (8 * k);
+    for (int k = 0; k < 4; ++k) {  // balanced digits: X = D2 2^16 + D1 2^8 + D0
+        const int X = (int)(bits[k] - kMagicBits);
+        const int a0 = (int)(int8_t)(X & 0xFF);
+        const int X1 = (X - a0) >> 8;
+        const int a1 = (int)(int8_t)(X1 & 0xFF);
+        const int a2 = (X1 - a1) >> 8;
+        p[0] |= (uint32_t)(a0 & 0xFF) << (8 * k);
+        p[1] |= (uint32_t)(a1 & 0xFF) << (8 * k);
+        p[2] |= (uint32_t)(a2 & 0xFF) << (8 * k);
+        if constexpr (XK == XK_NIB_SD) {
+            ds[0] += a0;
+            ds[1] += a1;
+            ds[2] += a2;
         }
     }
-    int sx = (int)((bits[0] + bits[1]) + (bits[2] + bits[3]) - 4u * kMagicBits);
-    sx += __shfl_xor_sync(0xffffffffu, sx, 1);
-    sx += __shfl_xor_sync(0xffffffffu, sx, 2);  // lanes 0-3: elements 0-15, lanes 4-7: 16-31
-    const int sx_other = __shfl_xor_sync(0xffffffffu, sx, 4);
+    int t0, t1;
+    uint32_t t2;
+    if constexpr (XK == XK_NIB_SD) {
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+            ds[0] += __shfl_xor_sync(0xffffffffu, ds[0], o);
+            ds[1] += __shfl_xor_sync(0xffffffffu, ds[1], o);
+            ds[2] += __shfl_xor_sync(0xffffffffu, ds[2], o);
+        }
+        t0 = ds[0];
+        t1 = ds[1];
+        t2 = (uint32_t)ds[2];
+    } else {
+        int sx = (int)((bits[0] + bits[1]) + (bits[2] + bits[3]) - 4u * kMagicBits);
+        sx += __shfl_xor_sync(0xffffffffu, sx, 1);
+        sx += __shfl_xor_sync(0xffffffffu, sx, 2);  // lanes 0-3: elements 0-15, lanes 4-7: 16-31
+        const int sx_other = __shfl_xor_sync(0xffffffffu, sx, 4);
+        t0 = sx;
+        t1 = sx_other;
+        t2 = __float_as_uint(s);
+    }
     if (act) {
         uint32_t* w = reinterpret_cast<uint32_t*>(rec);
 #pragma unroll
-        for (int d = 0; d < ND; ++d) w[8 * d + j] = p[d];
+        for (int d = 0; d < 3; ++d) w[8 * d + j] = p[d];
         if (j == 0) {
             const float nan = __int_as_float(0x7FC00000);  // propagate like the reference's f32 math
             // 4-bit codes produce 16 sum q X (high nibbles stay in place)
-            const int scale_e = e - B - (ND == 2 ? 4 : 0);
-            w[8 * ND] = (uint32_t)sx;
-            w[8 * ND + 1] = (uint32_t)sx_other;
+            const int scale_e = e - B - (XK == XK_PLAIN ? 0 : 4);
             const float scale = __uint_as_float((uint32_t)(scale_e + 127) << 23);
-            reinterpret_cast<float*>(w)[8 * ND + 2] = !finite ? nan : (m > 0.f ? scale : 0.f);
-            reinterpret_cast<float*>(w)[8 * ND + 3] = !finite ? nan : s;
+            w[24] = (uint32_t)t0;
+            w[25] = (uint32_t)t1;
+            w[26] = !finite && XK != XK_NIB_SD ? __float_as_uint(nan) : t2;
+            reinterpret_cast<float*>(w)[27] = !finite ? nan : (m > 0.f ? scale : 0.f);
         }
     }
 }
 
-template <int ND>
-__device__ __forceinline__ void load_xrec(const uint8_t* base, uint32_t blk, XRec<ND>& r) {
-    const uint4* p = reinterpret_cast<const uint4*>(base + (size_t)blk * xrec_bytes<ND>());
+__device__ __forceinline__ void load_xrec(const uint8_t* base, uint32_t blk, XRec& r) {
+    const uint4* p = reinterpret_cast<const uint4*>(base + (size_t)blk * kXrecBytes);
 #pragma unroll
-    for (int i = 0; i < xrec_bytes<ND>() / 16; ++i) reinterpret_cast<uint4*>(&r)[i] = p[i];
+    for (int i = 0; i < kXrecBytes / 16; ++i) reinterpret_cast<uint4*>(&r)[i] = p[i];
 }
 
 // IDP4A with an unsigned first operand: unsigned x unsigned / unsigned x signed bytes.
@@ -245,35 +251,41 @@ __device__ __forceinline__ float combine(int s0, int s1, int s2) {
 //  F32   [cols][f32]                                   unit = 32 values
 
 // Q4_0: element i of a block is the low nibble of byte i, element i+16 the
-// high nibble (src/core/tensor.cpp:57-63); value (q - 8) * d.
+// high nibble (src/core/tensor.cpp:57-63); value (q - 8) * d.  Low nibbles
+// are masked to q, high nibbles masked in place to 16 q (no shift); per digit
+// 16 sum (q - 8) D = 16 L + H - 128 sum D is exact in int32 and below 2^21,
+// and the three digits are joined in float (the record's scale carries 1/16).
 struct FmtQ4_0 {
-    static constexpr int UE = 32, SUBS = 1, ND = 2, WIDE = 22;
+    static constexpr int UE = 32, SUBS = 1, WIDE = 22, XK = XK_NIB_SD;
     static constexpr bool F32X = false;
     struct Raw { uint4 q; uint32_t s; };
     __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t units, Raw& r) {
         r.q = *reinterpret_cast<const uint4*>(row + (size_t)u * 16);
         r.s = *reinterpret_cast<const uint16_t*>(row + (size_t)units * 16 + (size_t)u * 2);
     }
-    __device__ __forceinline__ static float dot(const Raw& r, int, const XRec<ND>& x, uint32_t) {
+    __device__ __forceinline__ static float dot(const Raw& r, int, const XRec& x, uint32_t) {
         const uint32_t w[4] = {r.q.x, r.q.y, r.q.z, r.q.w};
-        int l0 = 0, l1 = 0, h0 = 0, h1 = 0;  // low nibbles (q) / high nibbles in place (16 q)
+        int l0 = 0, l1 = 0, l2 = 0, h0 = 0, h1 = 0, h2 = 0;  // low nibbles (q) / high nibbles in place (16 q)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const uint32_t lo = w[j] & 0x0F0F0F0Fu, hi = w[j] & 0xF0F0F0F0u;
-            l0 = dp4a_uu(lo, x.d[0][j], l0);
+            l0 = dp4a_us(lo, x.d[0][j], l0);
             l1 = dp4a_us(lo, x.d[1][j], l1);
-            h0 = dp4a_uu(hi, x.d[0][4 + j], h0);
+            l2 = dp4a_us(lo, x.d[2][j], l2);
+            h0 = dp4a_us(hi, x.d[0][4 + j], h0);
             h1 = dp4a_us(hi, x.d[1][4 + j], h1);
+            h2 = dp4a_us(hi, x.d[2][4 + j], h2);
         }
-        // 16 sum (q - 8) X = (16 L1 + H1) 2^8 + 16 L0 + H0 - 128 sum X, exact in int32
-        const int v = ((l1 * 16 + h1) * 256 + (l0 * 16 + h0)) - 128 * (x.sx_lo + x.sx_hi);
-        return (float)v * (h2f(r.s) * x.xs);
+        const int v0 = 16 * l0 + h0 - 128 * x.s0;
+        const int v1 = 16 * l1 + h1 - 128 * x.s1;
+        const int v2 = 16 * l2 + h2 - 128 * (int)x.s2;
+        return combine(v0, v1, v2) * (h2f(r.s) * x.xs);
     }
 };
 
 // Q8_0: int8 codes; value q * d.
 struct FmtQ8_0 {
-    static constexpr int UE = 32, SUBS = 1, ND = 3, WIDE = 16;
+    static constexpr int UE = 32, SUBS = 1, WIDE = 16, XK = XK_PLAIN;
     static constexpr bool F32X = false;
     struct Raw { uint4 a, b; uint32_t s; };
     __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t units, Raw& r) {
@@ -286,7 +298,7 @@ struct FmtQ8_0 {
         r.b = f ? first : second;
         r.s = *reinterpret_cast<const uint16_t*>(row + (size_t)units * 32 + (size_t)u * 2);
     }
-    __device__ __forceinline__ static float dot(const Raw& r, int, const XRec<ND>& x, uint32_t) {
+    __device__ __forceinline__ static float dot(const Raw& r, int, const XRec& x, uint32_t) {
         const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
         int s0 = 0, s1 = 0, s2 = 0;
 #pragma unroll
@@ -304,7 +316,7 @@ struct FmtQ8_0 {
 // nibbles of qs[32k..32k+32), sub-block 2k+1 = high nibbles.
 // Value: (d*sc)*q - dmin*m (gguf-py Q4_K.dequantize_blocks).
 struct FmtQ4K {
-    static constexpr int UE = 64, SUBS = 2, ND = 2, WIDE = 16;
+    static constexpr int UE = 64, SUBS = 2, WIDE = 16, XK = XK_NIB;
     static constexpr bool F32X = false;
     struct Raw { uint4 h, a, b; };
     __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t, Raw& r) {
@@ -324,23 +336,24 @@ struct FmtQ4K {
             m = (byte(s2, j - 4) >> 4) | ((byte(s1, j - 4) >> 6) << 4);
         }
     }
-    __device__ __forceinline__ static float dot(const Raw& r, int sub, const XRec<ND>& x, uint32_t u) {
+    __device__ __forceinline__ static float dot(const Raw& r, int sub, const XRec& x, uint32_t u) {
         const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
         // sub-block 1's high nibbles stay in place: its sums are 16 sum q X
         const uint32_t mask = sub ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
-        int s0 = 0, s1 = 0;
+        int s0 = 0, s1 = 0, s2 = 0;  // each below 32 * 240 * 128 < 2^22
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const uint32_t n = w[j] & mask;
-            s0 = dp4a_uu(n, x.d[0][j], s0);
+            s0 = dp4a_us(n, x.d[0][j], s0);
             s1 = dp4a_us(n, x.d[1][j], s1);
+            s2 = dp4a_us(n, x.d[2][j], s2);
         }
         int sc, m;
         scale_min(r.h, 2 * (int)(u & 3) + sub, sc, m);
         const float d = h2f(r.h.x & 0xFFFFu), dmin = h2f(r.h.x >> 16);
         const float d1 = d * (float)sc, m1 = dmin * (float)m;
         const float xs = sub ? x.xs : x.xs * 16.0f;  // x.xs carries 1/16 for in-place high nibbles
-        return fmaf(d1 * xs, (float)(s1 * 256 + s0), -m1 * x.xsum);
+        return fmaf(d1 * xs, combine(s0, s1, s2), -m1 * __uint_as_float(x.s2));
     }
 };
 
@@ -350,7 +363,7 @@ struct FmtQ4K {
 // 6-7); 4 int8 scales per unit (element e of a super-block uses scale e/16);
 // f16 d per super-block.  Value: (d*sc)*(q - 32) (src/core/tensor.cpp:97-106).
 struct FmtQ6K {
-    static constexpr int UE = 64, SUBS = 2, ND = 3, WIDE = 16;
+    static constexpr int UE = 64, SUBS = 2, WIDE = 16, XK = XK_PLAIN;
     static constexpr bool F32X = false;
     struct Raw { uint4 n0, n1, hb; uint32_t sc; uint32_t d; };
     __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t units, Raw& r) {
@@ -361,7 +374,7 @@ struct FmtQ6K {
         r.sc = *reinterpret_cast<const uint32_t*>(row + (size_t)units * 48 + (size_t)u * 4);
         r.d = *reinterpret_cast<const uint16_t*>(row + (size_t)units * 52 + (size_t)(u >> 2) * 2);
     }
-    __device__ __forceinline__ static float dot(const Raw& r, int sub, const XRec<ND>& x, uint32_t) {
+    __device__ __forceinline__ static float dot(const Raw& r, int sub, const XRec& x, uint32_t) {
         const uint32_t n[8] = {r.n0.x, r.n0.y, r.n0.z, r.n0.w, r.n1.x, r.n1.y, r.n1.z, r.n1.w};
         const uint32_t h[4] = {r.hb.x, r.hb.y, r.hb.z, r.hb.w};
         int a0 = 0, a1 = 0, a2 = 0, b0 = 0, b1 = 0, b2 = 0;  // first / second 16 elements
@@ -383,8 +396,8 @@ struct FmtQ6K {
             }
         }
         // codes are q + 32: subtract 32 * sum X per 16-element group
-        const float va = fmaf(-32.0f, (float)x.sx_lo, combine(a0, a1, a2));
-        const float vb = fmaf(-32.0f, (float)x.sx_hi, combine(b0, b1, b2));
+        const float va = fmaf(-32.0f, (float)x.s0, combine(a0, a1, a2));
+        const float vb = fmaf(-32.0f, (float)x.s1, combine(b0, b1, b2));
         const float sa = (float)(int8_t)((r.sc >> (16 * sub)) & 0xFFu);
         const float sbv = (float)(int8_t)((r.sc >> (16 * sub + 8)) & 0xFFu);
         return (h2f(r.d) * x.xs) * fmaf(sbv, vb, sa * va);
@@ -394,7 +407,7 @@ struct FmtQ6K {
 // F32 (the reference's catch-all branch, ops.cpp:289-299): plain f32 FMAs
 // against an f32 copy of x.
 struct FmtF32 {
-    static constexpr int UE = 32, SUBS = 1, ND = 3, WIDE = 16;
+    static constexpr int UE = 32, SUBS = 1, WIDE = 16, XK = XK_PLAIN;
     static constexpr bool F32X = true;
 };
 
@@ -623,7 +636,7 @@ __global__ void __launch_bounds__((W + 1) * 32, 1) smallm_qgemv_kernel(const Gem
                 if (act) reinterpret_cast<float4*>(xreg)[g] = q;
             } else {
                 // uniform across the warp: all lanes reach the shuffles inside
-                build_xrec_lane<Fmt::ND>(q, lane, act, xreg + (size_t)(g >> 3) * xrec_bytes<Fmt::ND>());
+                build_xrec_lane<Fmt::XK>(q, lane, act, xreg + (size_t)(g >> 3) * kXrecBytes);
             }
         }
     }
@@ -695,8 +708,8 @@ __global__ void __launch_bounds__((W + 1) * 32, 1) smallm_qgemv_kernel(const Gem
                     for (int r = 0; r < 4; ++r) Fmt::load(rows4 + (size_t)r * p.row_stride, u, p.units, raw[r]);
 #pragma unroll
                     for (int sb = 0; sb < Fmt::SUBS; ++sb) {
-                        XRec<Fmt::ND> xr;
-                        load_xrec<Fmt::ND>(xreg, u * Fmt::SUBS + sb, xr);
+                        XRec xr;
+                        load_xrec(xreg, u * Fmt::SUBS + sb, xr);
 #pragma unroll
                         for (int r = 0; r < 4; ++r) acc[r] += Fmt::dot(raw[r], sb, xr, u);
                     }

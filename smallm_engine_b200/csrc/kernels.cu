@@ -625,10 +625,8 @@ GemvPlan gemv_plan(const QMat& m, size_t smem_cap) {
     const size_t limit = smem_cap && smem_cap < kSmemLimit ? smem_cap : kSmemLimit;
     const uint32_t W = gemv_warps(m);
     pl.warps = W;
-    // x records: two digits for the 4-bit codes, three for the others
-    const bool four_bit = m.type == SM_T_Q4_0 || m.type == SM_T_Q4_K;
-    const size_t xrec = four_bit ? xrec_bytes<2>() : xrec_bytes<3>();
-    pl.xbytes = m.type == SM_T_F32 ? (size_t)m.cols * 4 : (size_t)(m.cols / 32) * xrec;
+    // x records: three digits per 32-element block
+    pl.xbytes = m.type == SM_T_F32 ? (size_t)m.cols * 4 : (size_t)(m.cols / 32) * kXrecBytes;
     // per stage: the tile, three mbarriers, the group's partial sums
     const size_t misc = kGemvMaxWarps * 4 + kGemvMaxWarps * 8 + 128;
     const uint32_t rt = 4;

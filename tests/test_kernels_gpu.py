@@ -7,8 +7,8 @@ and reductions are floating point with a per-row bound
     |y_gpu - y_ref| <= 1e-5 * sum_i |w_i * x_i| + sum_i |w_i| * r_i
 (f32 accumulation in another order; the reference's own rounding error is
 ~1e-7 of the same sum).  r_i is the representation error of x_i in the
-4-bit formats' block fixed point, 2^(e-15) for a 32-block whose maximum lies
-in [2^(e-1), 2^e); the 8- and 6-bit formats keep x to 2^-21 (r = 0 here)."""
+GEMV's block fixed point, one unit 2^(e-21) for a 32-block whose maximum lies
+in [2^(e-1), 2^e) (zero for F32 weights, which meet x in f32)."""
 import numpy as np
 import pytest
 import torch
@@ -23,17 +23,16 @@ TYPES = [O.F32, O.Q4_0, O.Q8_0, O.Q6_K, O.Q4_K]
 
 
 def x_rep_err(t, x):
-    """Per-element bound on |x_i - X_i 2^(e-15)| for Q4_0 / Q4_K (one unit of
-    the 15-bit block fixed point: half a unit of rounding, plus the clamp of
-    2^15 to 2^15 - 1); zero for the other formats."""
+    """Per-element bound on |x_i - X_i 2^(e-21)| (one unit of the 21-bit block
+    fixed point, twice the rounding error); zero for F32 weights."""
     x = np.asarray(x, np.float64)
     out = np.zeros_like(x)
-    if t not in (O.Q4_0, O.Q4_K):
+    if t == O.F32:
         return out
     n = x.size // 32 * 32
     m = np.abs(x[:n]).reshape(-1, 32).max(axis=1)
     e = np.frexp(m)[1]
-    out[:n] = np.repeat(np.where(m >= 1e-30, np.ldexp(1.0, e - 15), 1e-30), 32)
+    out[:n] = np.repeat(np.where(m >= 1e-30, np.ldexp(1.0, e - 21), 1e-30), 32)
     return out
 
 
