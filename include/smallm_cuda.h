@@ -250,6 +250,9 @@ typedef struct smallm_model_info {
     uint64_t weight_bytes_per_token; /* GGUF bytes of every matrix a decode step reads
                                         (this rank's share under tensor parallelism) */
     uint64_t device_bytes; /* device memory held by the model */
+    uint32_t step_launches; /* kernel launches of one decode step: 1 when the whole
+                               step runs as one persistent kernel, else one per op */
+    uint32_t reserved;
 } smallm_model_info;
 
 /* Parse `gguf_path` (src/core/gguf.cpp:116-183, src/config/common/config.cpp

@@ -40,7 +40,8 @@ class ModelInfo(ctypes.Structure):
                 ("n_heads", ctypes.c_uint32), ("n_kv_heads", ctypes.c_uint32), ("head_dim", ctypes.c_uint32),
                 ("vocab", ctypes.c_uint32), ("context_length", ctypes.c_uint32), ("max_ctx", ctypes.c_uint32),
                 ("rope_freq_base", ctypes.c_float), ("rms_eps", ctypes.c_float),
-                ("weight_bytes_per_token", ctypes.c_uint64), ("device_bytes", ctypes.c_uint64)]
+                ("weight_bytes_per_token", ctypes.c_uint64), ("device_bytes", ctypes.c_uint64),
+                ("step_launches", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
 
 
 _P = ctypes.c_void_p

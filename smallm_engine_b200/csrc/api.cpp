@@ -503,6 +503,7 @@ int smallm_model_get_info(const smallm_model* m, smallm_model_info* o) {
         o->rms_eps = M.eps;
         o->weight_bytes_per_token = M.weight_bytes;
         o->device_bytes = M.dev_bytes;
+        o->step_launches = M.step_launch_count();
     });
 }
 

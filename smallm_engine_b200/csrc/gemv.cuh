@@ -420,8 +420,8 @@ __device__ __forceinline__ void consumers_sync() {
 // Fused epilogue of one finished row (v = the row's W.x after 1/rms).  The
 // pair epilogues (RoPE, SwiGLU) run on the even row of a pair and read the
 // odd row's value from v_next; `best` collects the LOGITS argmax key.
-template <int EPI>
-__device__ __forceinline__ void gemv_epilogue_row(const GemvParams& p, uint32_t row, float v, float v_next,
+template <int EPI, class P>  // P: GemvParams, or any struct with the same output fields
+__device__ __forceinline__ void gemv_epilogue_row(const P& p, uint32_t row, float v, float v_next,
                                                   unsigned long long& best) {
     if constexpr (EPI == EPI_STORE) {
         if (row < p.rows) p.y[row] = v;
@@ -429,7 +429,9 @@ __device__ __forceinline__ void gemv_epilogue_row(const GemvParams& p, uint32_t 
         if (row < p.rows)
             for (uint32_t r = 0; r < p.tp; ++r) p.peer_out[r][row] = v;  // NVLink stores to peers
     } else if constexpr (EPI == EPI_RESIDUAL) {
-        if (row < p.rows) p.y[row] += v;  // x += W.h (ops::axpy, qwen2_model.cpp:178,184)
+        // x += W.h (ops::axpy, qwen2_model.cpp:178,184); the residual is read
+        // from L2, where other CTAs of a persistent step may have updated it
+        if (row < p.rows) p.y[row] = __ldcg(p.y + row) + v;
     } else if constexpr (EPI == EPI_LOGITS) {
         if (row < p.rows) {
             p.y[row] = v;

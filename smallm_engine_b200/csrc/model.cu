@@ -384,6 +384,10 @@ void Model::load(const std::string& path, const smallm_model_opts& o) {
         nccl_check(ncclAllGather(hbuf_dev, hbuf_dev + sizeof(mine), sizeof(mine), ncclUint8, comm, stream),
                    "ncclAllGather");
     }
+    if (tp_size == 1) {
+        alloc_step_buffers();
+        build_step();
+    }
     SM_CUDA(cudaStreamSynchronize(stream));
     capture(&exec, nullptr);
 }
@@ -397,6 +401,10 @@ enum TraceKind { TK_EMBED = 1, TK_QKV = 2, TK_V = 3, TK_ATTN = 4, TK_O = 5, TK_G
 // With `trace`, kernel k of the step stamps slot trace[k] and its kind is
 // recorded in trace_kinds.
 void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
+    if (step_on && !trace) {  // the whole step as one persistent kernel (step.cu)
+        launch_step(s);
+        return;
+    }
     const bool pdl = true;  // programmatic dependent launch between the step's kernels
     uint32_t nslot = 0;
     if (trace) trace_kinds.clear();
@@ -591,6 +599,7 @@ void Model::check_step_errors() {
     if (!e) return;
     *h_err = 0;
     gemv_error_flags(true);
+    reset_step_state();
     throw Error(SMALLM_ERR_CUDA, "a bounded device wait gave up during the step (flags " + std::to_string(e) +
                                      "); its results are invalid");
 }

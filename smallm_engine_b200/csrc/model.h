@@ -13,6 +13,7 @@
 namespace smallm {
 
 class GGUFFile;
+struct StepOp;
 
 struct LayerW {
     QMat qkv;              // Q pairs | K pairs | V rows (V only when it shares Q's type)
@@ -109,6 +110,25 @@ struct Model {
     std::vector<void*> pre_allocs;
     void gemm(const float* W, uint32_t rows, uint32_t cols, const float* X, uint32_t T, float* Y, bool tf32);
     void enqueue_step(cudaStream_t s, TraceSlot* trace = nullptr);
+    // The persistent decode step (step.cu): the whole token step as one
+    // cooperative kernel when the model's shapes and formats allow it
+    // (step_on; otherwise step_why says why and the per-op kernels run).
+    bool step_on = false;
+    std::string step_why;
+    StepOp* step_ops = nullptr;
+    uint32_t step_nops = 0, step_nsig = 0, step_xbytes = 0, step_ring = 0, step_grid = 0;
+    size_t step_smem = 0;
+    const void* step_fn = nullptr;
+    unsigned int* step_bar = nullptr;    // grid barrier counter; step_bar + 1 is the abort flag
+    unsigned int* step_abort = nullptr;
+    float* step_part = nullptr;          // attention item partials
+    unsigned int* step_tickets = nullptr;
+    std::string step_unsupported() const;
+    void alloc_step_buffers();
+    void build_step();
+    void launch_step(cudaStream_t s);
+    void reset_step_state();
+    uint32_t step_launch_count() const;
     void trace_step(uint32_t token, uint32_t pos, std::vector<TraceSlot>& out);
 
 private:

@@ -1,0 +1,957 @@
+// Persistent decode step: the whole token step (src/model/llama_model.cpp:148-177,
+// src/model/qwen2_model.cpp:163-198) as ONE cooperative kernel.
+//
+// Why.  Batch-1 decode streams every weight byte once per token; what keeps
+// it from the HBM roofline is the time HBM sits idle between dependent
+// matrices (kernel boundaries, x staging, tails).  Here every SM keeps one
+// resident CTA for the whole step, and the weight pieces of ALL the step's
+// matrices stream, in order, through one shared-memory byte ring that never
+// waits on a data dependency -- only on ring space: whichever warp frees a
+// piece's space starts the copies of the next pieces that fit (ring_issue),
+// so there is no producer warp and the 16 warps keep 128 registers each.  The
+// warps walk the op list; between dependent ops they meet at a grid-wide
+// barrier (a release counter in global memory), stage the new x and continue
+// on pieces that are often already in shared memory.
+//
+// Ops, in order: EMBED, then per layer QKV -> ATTN -> O -> GATE/UP -> DOWN,
+// then LM_HEAD + greedy argmax; the last CTA to finish advances the decode
+// state (token, position, id list).  Each op ends with a grid barrier arrival
+// ("signal"); an op that reads the previous ops' results first waits for the
+// barrier count (counter >= signals so far x grid).  The counter is reset by
+// the last CTA of the step, so a captured graph replays the kernel as is.
+//
+// GEMV ops (same block formats and fused epilogues as gemv.cuh): x is staged
+// as three-digit block fixed point (gemv.cuh, XRec) and every consumer thread
+// keeps the record of ONE 32-element unit of x in registers for the whole
+// op ("x-stationary"): thread (warp w, lane l) owns unit u = (w % WS) * 32 + l
+// of the row slot w / WS (WS = warps per row, ceil(units / 32)), and the RS
+// = 16 / WS row slots of the CTA take RPT rows each of every piece.  A piece
+// is R = RS * RPT consecutive rows (one contiguous range: one bulk copy).
+// Per piece each warp reduces its RPT rows with shuffles, the partials meet
+// in shared memory, and one warp (rotating with the piece) sums them and runs
+// the fused epilogue.
+//
+// ATTN op (qwen2_model.cpp:111-133): split-K over (KV head, position range)
+// items, one item per CTA; 16 warps x 128/hd sub-warps walk the item's
+// positions with an online softmax; a CTA merges its warps in shared memory
+// and, when a head has several items, the last of them (atomic ticket) merges
+// the items' partials.  K/V rows are read straight from the cache (L2-coherent
+// loads): the QKV op's epilogue wrote this step's row moments earlier.
+//
+// Every wait is bounded (~1 s of SM clock).  A wait that gives up raises bit
+// 4 of the device error word and the model's abort flag; every other wait in
+// the grid then returns at once, thread 0 waits (bounded) for the CTA's copies
+// in flight, and the kernel ends.  The host reads the error word after the
+// step and raises.
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "dequant.cuh"
+#include "engine.h"
+#include "gemv.cuh"
+#include "model.h"
+
+namespace smallm {
+
+enum { SOP_EMBED = 0, SOP_GEMV = 1, SOP_ATTN = 2 };
+
+constexpr int kStepW = 16;                    // warps per CTA (all consume; see ring_issue)
+constexpr int kStepThreads = kStepW * 32;
+constexpr uint32_t kStepSlots = 16;           // ring pieces in flight at most
+constexpr uint32_t kStepPartRows = 64;        // rows of one piece's partials (R <= 64)
+constexpr unsigned int kStepErrBit = 16u;
+constexpr int kStepMaxGroup = 8;           // query heads per KV head
+
+// One op of the step (device memory).  The GEMV output fields carry the same
+// names as GemvParams so the fused epilogue (gemv_epilogue_row) reads them.
+struct StepOp {
+    uint32_t kind, fmt, pro, epi, wait, signal;
+    // GEMV: matrix and piece geometry
+    const uint8_t* w;
+    uint32_t row_stride, rows, rows_pad, cols, units;
+    uint32_t ws, rs, rpt, prows, npieces;
+    // GEMV inputs / fused epilogue outputs
+    const float* x;
+    const float* norm_w;
+    float eps;
+    float* y;
+    const float* bias;
+    uint32_t q_rows, k_rows, head_dim, max_ctx;
+    float* qout;
+    float* kcache;
+    float* vcache;
+    const float2* rope;
+    const uint32_t* pos;
+    unsigned long long* argmax;
+    uint32_t row_offset;
+    float* peer_out[kMaxTP];  // unused here (EPI_PEER is not a step op)
+    uint32_t tp;
+    // ATTN
+    const float* q;
+    float* out;
+    float* part;               // [n_kv * S][G][hd + 2] item partials
+    unsigned int* tickets;     // [n_kv], zero between steps
+    uint32_t n_heads, n_kv;
+    // EMBED
+    QMat emb;
+};
+
+static_assert(sizeof(StepOp) % 8 == 0, "StepOp is copied in 8-byte words");
+
+struct StepArgs {
+    const StepOp* ops;
+    uint32_t nops, nsig;       // ops, signalling ops
+    DecodeState* st;
+    uint32_t* ids;
+    uint32_t ids_cap;
+    unsigned int* bar;         // grid barrier counter (zero between steps)
+    unsigned int* abort_flag;  // set when any wait of the step gave up
+    unsigned int* err;         // device error word
+    uint32_t xbytes, ring_bytes;
+};
+
+// ------------------------------------------------------------- waiting --
+
+__device__ __forceinline__ void step_raise(const StepArgs& a) {
+    atomicOr(a.err, kStepErrBit);
+    *(volatile unsigned int*)a.abort_flag = 1u;
+    __threadfence();
+}
+
+// mbarrier phase wait, bounded (~2^31 cycles) and abandoned as soon as the
+// step's abort flag is up.
+__device__ __forceinline__ bool step_wait(uint64_t* bar, uint32_t parity, const unsigned int* abort_flag) {
+    const uint32_t addr = smem_u32(bar);
+    const long long t0 = clock64();
+    for (;;) {
+        uint32_t ok;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+            : "=r"(ok)
+            : "r"(addr), "r"(parity), "r"(20000u)
+            : "memory");
+        if (ok) return true;
+        if (abort_flag && *(const volatile unsigned int*)abort_flag) return false;
+        if (clock64() - t0 > (1ll << 31)) return false;
+    }
+}
+
+// Grid barrier: wait until the counter reaches `target` (wrap-safe compare).
+__device__ __forceinline__ bool grid_wait(const unsigned int* bar, unsigned int target,
+                                          const unsigned int* abort_flag) {
+    const long long t0 = clock64();
+    for (;;) {
+        unsigned int v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
+        if ((int)(v - target) >= 0) return true;
+        if (*(const volatile unsigned int*)abort_flag) return false;
+        if (clock64() - t0 > (1ll << 31)) return false;
+        __nanosleep(32);
+    }
+}
+
+__device__ __forceinline__ void step_sync() { __syncthreads(); }
+
+// ---------------------------------------------------------------- GEMV --
+
+// The CTA's piece ring.  Pieces are issued in the step's order (op by op,
+// this CTA's pieces p = blockIdx.x, + gridDim.x, ...) and retired in the same
+// order; piece j uses slot j % kStepSlots.  Only the lane that holds the
+// retire turn (retired == j) touches the issue state, so no lock is needed.
+struct StepRing {
+    uint32_t retired;  // pieces whose space is free again
+    uint32_t issued;   // pieces whose copy has been started
+    uint32_t head;     // ring offset just past the newest issued piece
+    uint32_t op, p;    // next piece to issue: op index and piece index
+    uint32_t pstart[kStepSlots];  // ring offset of each in-flight piece
+};
+
+struct StepShared {
+    uint64_t* full;
+    uint64_t* done;
+    float* part;
+    float* red;
+    uint8_t* xreg;
+    uint8_t* ring;
+    StepRing* rs;
+};
+
+// Issue the next pieces while a slot is free and the ring has room for them
+// (one lane, holding the retire turn).  Placement: a piece goes right after
+// the newest one, or at offset 0 when it would run past the end; it may not
+// overlap the span [tail, head) of pieces in flight (tail = oldest's start).
+__device__ void ring_issue(const StepArgs& a, const StepShared& sh) {
+    StepRing& r = *sh.rs;
+    const uint32_t RB = a.ring_bytes;
+    while (r.issued - r.retired < kStepSlots) {
+        const StepOp* op = a.ops + r.op;
+        while (r.op < a.nops && (op->kind != SOP_GEMV || r.p >= op->npieces)) {
+            ++r.op;
+            r.p = blockIdx.x;
+            op = a.ops + r.op;
+        }
+        if (r.op >= a.nops) return;
+        const uint32_t R = op->prows, stride = op->row_stride;
+        const uint32_t bytes = min(R, op->rows_pad - r.p * R) * stride;
+        const uint32_t off = r.head + bytes <= RB ? r.head : 0u;
+        if (r.issued != r.retired) {
+            const uint32_t tail = r.pstart[r.retired % kStepSlots];
+            const bool clash = tail < r.head ? (off < r.head && tail < off + bytes)  // occupied [tail, head)
+                                             : (off < r.head || off + bytes > tail); // [tail, RB) + [0, head)
+            if (clash) return;
+        }
+        const uint32_t s = r.issued % kStepSlots;
+        r.pstart[s] = off;
+        r.head = off + bytes;
+        mbar_arrive_expect_tx(&sh.full[s], bytes);
+        bulk_g2s(sh.ring + off, op->w + (size_t)r.p * R * stride, bytes, &sh.full[s]);
+        ++r.issued;
+        r.p += gridDim.x;
+    }
+}
+
+// Piece j is done (every warp has read it): wait for the retire turn, free its
+// space, issue what now fits, pass the turn on.  One lane.
+__device__ bool ring_retire(const StepArgs& a, const StepShared& sh, uint32_t j) {
+    volatile uint32_t* ret = &sh.rs->retired;
+    const long long t0 = clock64();
+    while (*ret != j) {
+        if (*(const volatile unsigned int*)a.abort_flag) return false;
+        if (clock64() - t0 > (1ll << 31)) return false;
+    }
+    __threadfence_block();
+    sh.rs->retired = j + 1;
+    ring_issue(a, sh);
+    __threadfence_block();
+    return true;
+}
+
+// x -> three-digit records of every 32-element block (times the norm weight
+// when the RMSNorm is fused; its 1/rms is returned and applied per row).
+template <class Fmt>
+__device__ float step_stage_x(const StepOp& op, const StepShared& sh, int warp, int lane) {
+    const int ctid = warp * 32 + lane;
+    constexpr uint32_t kStride = kStepW * 32;
+    constexpr int kB = 4;
+    const uint32_t ngr = op.cols / 4;  // a multiple of 8: whole blocks
+    const float4* x4 = reinterpret_cast<const float4*>(op.x);
+    const float4* w4 = reinterpret_cast<const float4*>(op.norm_w);
+    const bool rms = op.pro == PRO_RMS;
+    float ss = 0.f;
+    for (uint32_t g0 = 0; g0 < ngr; g0 += kB * kStride) {
+        float4 xq[kB], wq[kB];
+#pragma unroll
+        for (int k = 0; k < kB; ++k) {
+            const uint32_t g = g0 + ctid + k * kStride;
+            const bool in = g < ngr;
+            xq[k] = in ? __ldcg(x4 + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+            wq[k] = (in && rms) ? __ldg(w4 + g) : make_float4(1.f, 1.f, 1.f, 1.f);
+        }
+#pragma unroll
+        for (int k = 0; k < kB; ++k) {
+            // a warp whose first granule lies past the end has no block here
+            // (warp-uniform, so the shuffles inside stay whole-warp)
+            if (g0 + (uint32_t)warp * 32 + k * kStride >= ngr) continue;
+            const uint32_t g = g0 + ctid + k * kStride;
+            float4 q = xq[k];
+            ss += q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w;
+            q.x *= wq[k].x;
+            q.y *= wq[k].y;
+            q.z *= wq[k].z;
+            q.w *= wq[k].w;
+            build_xrec_lane<Fmt::XK>(q, lane, g < ngr, sh.xreg + (size_t)(g >> 3) * kXrecBytes);
+        }
+    }
+    if (rms) {
+        ss = warp_sum(ss);
+        if (lane == 0) sh.red[warp] = ss;
+    }
+    step_sync();
+    float inv = 1.0f;
+    if (rms) {
+        float t = 0.f;
+#pragma unroll
+        for (int k = 0; k < kStepW; ++k) t += sh.red[k];
+        inv = 1.0f / sqrtf(t / (float)op.cols + op.eps);  // ops::rmsnorm (ops.cpp:29-40)
+    }
+    return inv;
+}
+
+__device__ __forceinline__ void step_epilogue(const StepOp& op, uint32_t row, float v, float v_next,
+                                              unsigned long long& best) {
+    switch (op.epi) {
+        case EPI_STORE: gemv_epilogue_row<EPI_STORE>(op, row, v, v_next, best); break;
+        case EPI_RESIDUAL: gemv_epilogue_row<EPI_RESIDUAL>(op, row, v, v_next, best); break;
+        case EPI_QKV: gemv_epilogue_row<EPI_QKV>(op, row, v, v_next, best); break;
+        case EPI_SWIGLU: gemv_epilogue_row<EPI_SWIGLU>(op, row, v, v_next, best); break;
+        case EPI_LOGITS: gemv_epilogue_row<EPI_LOGITS>(op, row, v, v_next, best); break;
+        default: break;
+    }
+}
+
+// This CTA's position in its piece sequence (piece counter j and ring
+// placement head, identical to ring_issue's), the abandon flag and the
+// greedy-argmax key of a logits op.
+struct PieceCursor {
+    uint32_t j, head, dead;
+    unsigned long long best;
+};
+
+// One GEMV op.  Not inlined: each op variant gets its own register
+// allocation (the kernel holds six of them plus the attention).
+template <class Fmt, int RPT>
+__device__ __noinline__ PieceCursor step_gemv(const StepOp& op, const StepArgs& a, const StepShared sh, int warp,
+                                              int lane, PieceCursor cur) {
+    uint32_t j = cur.j, head = cur.head;
+    bool dead = cur.dead != 0;
+    unsigned long long best = cur.best;
+    const float inv = step_stage_x<Fmt>(op, sh, warp, lane);
+    const uint32_t U = op.units, WS = op.ws, RS = op.rs, R = op.prows, stride = op.row_stride;
+    const uint32_t slot = (uint32_t)warp / WS, wi = (uint32_t)warp % WS;
+    const bool active = slot < RS;
+    const uint32_t u = wi * 32 + (uint32_t)lane;
+    const bool uact = active && u < U;
+    XRec xr;
+    if (uact) load_xrec(sh.xreg, u, xr);
+    constexpr int LPR = 32 / RPT;
+    for (uint32_t p = blockIdx.x; p < op.npieces; p += gridDim.x, ++j) {
+        const uint32_t rows_here = min(R, op.rows_pad - p * R);
+        const uint32_t bytes = rows_here * stride;
+        const uint32_t off = head + bytes <= a.ring_bytes ? head : 0u;
+        head = off + bytes;
+        const uint32_t s = j % kStepSlots, ph = (j / kStepSlots) & 1u;
+        if (!dead && !step_wait(&sh.full[s], ph, a.abort_flag)) {
+            dead = true;
+            step_raise(a);
+        }
+        dead = __any_sync(0xffffffffu, dead);  // warp-uniform (the shuffles below)
+        float acc[RPT];
+#pragma unroll
+        for (int k = 0; k < RPT; ++k) acc[k] = 0.f;
+        if (uact && !dead) {
+            const uint32_t r0 = slot * RPT;
+            const uint8_t* base = sh.ring + off + (size_t)r0 * stride;
+#pragma unroll
+            for (int k = 0; k < RPT; ++k) {
+                if (r0 + k < rows_here) {
+                    typename Fmt::Raw raw;
+                    Fmt::load(base + (size_t)k * stride, u, U, raw);
+                    acc[k] = Fmt::dot(raw, 0, xr, u);
+                }
+            }
+        }
+        // lanes k*LPR .. k*LPR + LPR-1 end with this warp's part of row k
+        const float v = warp_reduce_rows<RPT>(acc, lane);
+        if (active && (lane % LPR) == 0)
+            sh.part[s * kStepPartRows + (slot * RPT + (uint32_t)lane / LPR) * WS + wi] = v;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.done[s]);
+        if ((uint32_t)warp == j % kStepW) {
+            // this warp closes the piece: sum the row partials, fused epilogue,
+            // free its ring space and issue the next pieces
+            if (!dead && !step_wait(&sh.done[s], ph, a.abort_flag)) {
+                dead = true;
+                step_raise(a);
+            }
+            dead = __any_sync(0xffffffffu, dead);
+            for (uint32_t rb = 0; rb < R; rb += 32) {
+                const uint32_t r = rb + (uint32_t)lane;
+                float val = 0.f;
+                if (r < R)
+                    for (uint32_t k = 0; k < WS; ++k) val += sh.part[s * kStepPartRows + r * WS + k];
+                val *= inv;  // 1/rms of the fused RMSNorm (1 if plain)
+                const float v_next = __shfl_down_sync(0xffffffffu, val, 1);  // partner row of a pair
+                if (r < rows_here && !dead) step_epilogue(op, p * R + r, val, v_next, best);
+            }
+            __syncwarp();
+            if (lane == 0 && !dead && !ring_retire(a, sh, j)) {
+                dead = true;
+                step_raise(a);
+            }
+            dead = __shfl_sync(0xffffffffu, dead ? 1 : 0, 0) != 0;
+        }
+    }
+    return PieceCursor{j, head, dead ? 1u : 0u, best};
+}
+
+template <class Fmt>
+__device__ __forceinline__ PieceCursor step_gemv_fmt(const StepOp& op, const StepArgs& a, const StepShared& sh,
+                                                     int warp, int lane, PieceCursor cur) {
+    if (op.rpt == 4) return step_gemv<Fmt, 4>(op, a, sh, warp, lane, cur);
+    if (op.rpt == 2) return step_gemv<Fmt, 2>(op, a, sh, warp, lane, cur);
+    return step_gemv<Fmt, 1>(op, a, sh, warp, lane, cur);
+}
+
+// ----------------------------------------------------------- attention --
+
+// Online-softmax state of one head over some positions: running max m, sum
+// of exp(score - m) l, unnormalised output o (4 dims of one lane).
+__device__ __forceinline__ void attn_merge(float& m, float& l, float4& o, float m2, float l2, float4 o2) {
+    const float M = fmaxf(m, m2);
+    const float a1 = M == -INFINITY ? 0.f : expf(m - M);
+    const float a2 = M == -INFINITY ? 0.f : expf(m2 - M);
+    l = a1 * l + a2 * l2;
+    o.x = a1 * o.x + a2 * o2.x;
+    o.y = a1 * o.y + a2 * o2.y;
+    o.z = a1 * o.z + a2 * o2.z;
+    o.w = a1 * o.w + a2 * o2.w;
+    m = M;
+}
+
+template <int HD>
+__device__ __noinline__ uint32_t step_attn(const StepOp& op, const StepArgs& a, const StepShared sh, int warp,
+                                           int lane, uint32_t dead_in) {
+    const bool dead = dead_in != 0;
+    constexpr int RPI = 128 / HD;   // positions per warp instruction (sub-warps)
+    constexpr int LPR = 32 / RPI;   // lanes per position: 4 dims each
+    constexpr int kHP = 4;          // heads per pass
+    constexpr uint32_t SR = HD + 4; // scratch row: HD outputs, max, sum, pad to 16 bytes
+    const int ctid = warp * 32 + lane;
+    const uint32_t G = op.n_heads / op.n_kv;
+    const uint32_t n = min(*op.pos + 1, op.max_ctx);
+    const uint32_t grid = gridDim.x;
+    uint32_t S = grid / op.n_kv;
+    if (S < 1) S = 1;
+    const uint32_t smax = (n + 15) / 16;
+    if (S > smax) S = smax;
+    const uint32_t L = (n + S - 1) / S;
+    const uint32_t items = op.n_kv * S;
+    const float scale = 1.0f / sqrtf((float)HD);
+    const int sub = lane / LPR, dl = lane % LPR;
+    float* scr = reinterpret_cast<float*>(sh.xreg);  // [kStepW][G][SR]
+    __shared__ int last_item;
+    for (uint32_t item = blockIdx.x; item < items; item += grid) {
+        const uint32_t kvh = item / S, sidx = item % S;
+        const uint32_t b = sidx * L, e = min(n, b + L);
+        const float* kb = op.kcache + (size_t)kvh * op.max_ctx * HD;
+        const float* vb = op.vcache + (size_t)kvh * op.max_ctx * HD;
+        constexpr uint32_t NRL = kStepW * RPI;  // position lanes of the CTA
+        const uint32_t first = b + (uint32_t)warp * RPI;
+        const uint32_t trips = (!dead && first < e) ? (e - first + NRL - 1) / NRL : 0u;  // warp-uniform
+        // heads in passes of kHP (register budget); a second pass re-reads the
+        // item's K/V rows from L2
+        for (uint32_t h0 = 0; h0 < G; h0 += kHP) {
+            float4 qv[kHP];
+            float m[kHP], l[kHP];
+            float4 o[kHP];
+#pragma unroll
+            for (int h = 0; h < kHP; ++h) {
+                qv[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (h0 + h < G)
+                    qv[h] = __ldcg(reinterpret_cast<const float4*>(op.q + ((size_t)kvh * G + h0 + h) * HD) + dl);
+                m[h] = -INFINITY;
+                l[h] = 0.f;
+                o[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            for (uint32_t i = 0; i < trips; i += 4) {
+                float4 kk[4], vv[4];
+                bool ok[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const uint32_t t = first + (i + c) * NRL + (uint32_t)sub;
+                    ok[c] = i + c < trips && t < e;
+                    kk[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    vv[c] = kk[c];
+                    if (ok[c]) {
+                        kk[c] = __ldcg(reinterpret_cast<const float4*>(kb + (size_t)t * HD) + dl);
+                        vv[c] = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)t * HD) + dl);
+                    }
+                }
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    if (i + c >= trips) break;  // warp-uniform
+#pragma unroll
+                    for (int h = 0; h < kHP; ++h) {
+                        if (h0 + h >= G) break;  // uniform
+                        float sc = qv[h].x * kk[c].x + qv[h].y * kk[c].y + qv[h].z * kk[c].z + qv[h].w * kk[c].w;
+#pragma unroll
+                        for (int off = 1; off < LPR; off <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, off);
+                        sc *= scale;
+                        if (ok[c]) {
+                            const float mn = fmaxf(m[h], sc);
+                            const float co = expf(m[h] - mn);  // 0 for the first position (m = -inf)
+                            const float pr = expf(sc - mn);
+                            l[h] = l[h] * co + pr;
+                            o[h].x = o[h].x * co + pr * vv[c].x;
+                            o[h].y = o[h].y * co + pr * vv[c].y;
+                            o[h].z = o[h].z * co + pr * vv[c].z;
+                            o[h].w = o[h].w * co + pr * vv[c].w;
+                            m[h] = mn;
+                        }
+                    }
+                }
+            }
+            // merge the sub-warps (same dims, other positions)
+#pragma unroll
+            for (int off = LPR; off < 32; off <<= 1) {
+#pragma unroll
+                for (int h = 0; h < kHP; ++h) {
+                    const float m2 = __shfl_xor_sync(0xffffffffu, m[h], off);
+                    const float l2 = __shfl_xor_sync(0xffffffffu, l[h], off);
+                    float4 o2;
+                    o2.x = __shfl_xor_sync(0xffffffffu, o[h].x, off);
+                    o2.y = __shfl_xor_sync(0xffffffffu, o[h].y, off);
+                    o2.z = __shfl_xor_sync(0xffffffffu, o[h].z, off);
+                    o2.w = __shfl_xor_sync(0xffffffffu, o[h].w, off);
+                    attn_merge(m[h], l[h], o[h], m2, l2, o2);
+                }
+            }
+            if (sub == 0) {
+#pragma unroll
+                for (int h = 0; h < kHP; ++h) {
+                    if (h0 + h >= G) break;
+                    float* r = scr + ((size_t)warp * G + h0 + h) * SR;  // SR floats: 16-byte rows
+                    reinterpret_cast<float4*>(r)[dl] = o[h];
+                    if (dl == 0) {
+                        r[HD] = m[h];
+                        r[HD + 1] = l[h];
+                    }
+                }
+            }
+        }
+        step_sync();
+        // merge the 16 warps: thread -> (head, dim)
+        float* part = op.part + (size_t)(kvh * S + sidx) * G * (HD + 2);
+        for (uint32_t idx = ctid; idx < G * HD; idx += kStepW * 32) {
+            const uint32_t h = idx / HD, d = idx % HD;
+            float M = -INFINITY;
+            for (int w = 0; w < kStepW; ++w) M = fmaxf(M, scr[((size_t)w * G + h) * SR + HD]);
+            float O = 0.f, Ls = 0.f;
+            if (M != -INFINITY) {
+                for (int w = 0; w < kStepW; ++w) {
+                    const float* r = scr + ((size_t)w * G + h) * SR;
+                    const float wt = expf(r[HD] - M);  // 0 for a warp without positions
+                    O = fmaf(wt, r[d], O);
+                    Ls = fmaf(wt, r[HD + 1], Ls);
+                }
+            }
+            if (S == 1) {
+                op.out[((size_t)kvh * G + h) * HD + d] = O / Ls;
+            } else {
+                part[(size_t)h * (HD + 2) + d] = O;
+                if (d == 0) {
+                    part[(size_t)h * (HD + 2) + HD] = M;
+                    part[(size_t)h * (HD + 2) + HD + 1] = Ls;
+                }
+            }
+        }
+        if (S > 1) {
+            // the last item of this KV head merges all of its items
+            __threadfence();
+            step_sync();
+            if (ctid == 0) last_item = atomicAdd(op.tickets + kvh, 1u) == S - 1 ? 1 : 0;
+            step_sync();
+            if (last_item) {
+                __threadfence();
+                const float* hp = op.part + (size_t)kvh * S * G * (HD + 2);
+                for (uint32_t idx = ctid; idx < G * HD; idx += kStepW * 32) {
+                    const uint32_t h = idx / HD, d = idx % HD;
+                    float M = -INFINITY;
+                    for (uint32_t s2 = 0; s2 < S; ++s2) M = fmaxf(M, __ldcg(hp + ((size_t)s2 * G + h) * (HD + 2) + HD));
+                    float O = 0.f, Ls = 0.f;
+                    for (uint32_t s2 = 0; s2 < S; ++s2) {
+                        const float* r = hp + ((size_t)s2 * G + h) * (HD + 2);
+                        const float mm = __ldcg(r + HD);
+                        const float wt = mm == -INFINITY ? 0.f : expf(mm - M);
+                        O = fmaf(wt, __ldcg(r + d), O);
+                        Ls = fmaf(wt, __ldcg(r + HD + 1), Ls);
+                    }
+                    op.out[((size_t)kvh * G + h) * HD + d] = O / Ls;
+                }
+                if (ctid == 0) op.tickets[kvh] = 0u;
+            }
+        }
+        step_sync();  // the scratch is reused by the next item
+    }
+    return dead_in;
+}
+
+// -------------------------------------------------------------- kernel --
+
+template <class FA, class FB>
+__global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const StepArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full[kStepSlots], done[kStepSlots];
+    __shared__ float part[kStepSlots * kStepPartRows];
+    __shared__ StepRing ring_state;
+    __shared__ float red[32];
+    __shared__ unsigned long long best_sh[kStepW];
+    __shared__ __align__(16) StepOp op_sh;
+    __shared__ int cta_dead;  // some wait of this CTA gave up (read after a barrier: CTA-uniform)
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    StepShared sh;
+    sh.full = full;
+    sh.done = done;
+    sh.part = part;
+    sh.red = red;
+    sh.xreg = smem;
+    sh.ring = smem + a.xbytes;
+    sh.rs = &ring_state;
+    if (tid == 0) {
+        for (uint32_t s = 0; s < kStepSlots; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&done[s], kStepW);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        ring_state.retired = ring_state.issued = ring_state.head = 0u;
+        ring_state.op = 0u;
+        ring_state.p = blockIdx.x;
+        cta_dead = 0;
+        ring_issue(a, sh);  // fill the ring: weights depend on nothing
+    }
+    __syncthreads();
+
+    const int ctid = tid;
+    uint32_t j = 0, head = 0, nsig = 0;
+    bool dead = false;
+    for (uint32_t k = 0; k < a.nops; ++k) {
+        // this op's descriptor into shared memory (8-byte words)
+        if (dead) cta_dead = 1;
+        step_sync();
+        for (uint32_t i = ctid; i < sizeof(StepOp) / 8; i += kStepW * 32)
+            reinterpret_cast<unsigned long long*>(&op_sh)[i] =
+                __ldg(reinterpret_cast<const unsigned long long*>(a.ops + k) + i);
+        step_sync();
+        dead = cta_dead != 0;
+        const StepOp& op = op_sh;
+        if (op.wait) {  // CTA-uniform condition: every thread reaches the barrier below
+            if (ctid == 0 && !dead && !grid_wait(a.bar, nsig * gridDim.x, a.abort_flag)) {
+                cta_dead = 1;
+                step_raise(a);
+            }
+            step_sync();
+            dead = cta_dead != 0;
+        }
+        if (op.kind == SOP_GEMV) {
+            PieceCursor cur{j, head, dead ? 1u : 0u, 0ull};
+            cur = op.fmt == 0 ? step_gemv_fmt<FA>(op, a, sh, warp, lane, cur)
+                              : step_gemv_fmt<FB>(op, a, sh, warp, lane, cur);
+            j = cur.j;
+            head = cur.head;
+            dead = cur.dead != 0;
+            unsigned long long best = cur.best;
+            if (op.epi == EPI_LOGITS) {
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+                    best = other > best ? other : best;
+                }
+                if (lane == 0) best_sh[warp] = best;
+                step_sync();
+                if (ctid == 0) {
+                    unsigned long long b = 0ull;
+                    for (int w = 0; w < kStepW; ++w) b = best_sh[w] > b ? best_sh[w] : b;
+                    if (b && !dead) atomicMax(op.argmax, b);
+                }
+            }
+        } else if (op.kind == SOP_ATTN) {
+            const uint32_t d = dead ? 1u : 0u;
+            if (op.head_dim == 128) step_attn<128>(op, a, sh, warp, lane, d);
+            else if (op.head_dim == 64) step_attn<64>(op, a, sh, warp, lane, d);
+            else step_attn<32>(op, a, sh, warp, lane, d);
+        } else if (op.kind == SOP_EMBED && !dead) {
+            uint32_t tok = a.st->token;
+            if (tok >= op.emb.rows) tok = 0;  // the host validates ids; never read outside the table
+            const uint32_t ng = op.emb.cols / 32;
+            for (uint32_t g = blockIdx.x + ctid * gridDim.x; g < ng; g += kStepW * 32 * gridDim.x)
+                dequant_group(op.emb, tok, g, op.y + (size_t)g * 32);
+            if (blockIdx.x == 0 && ctid == 0) a.st->argmax = 0ull;
+        }
+        if (op.signal) {
+            step_sync();  // every warp's writes of this op are issued
+            if (ctid == 0) {
+                __threadfence();
+                const unsigned int old = atomicAdd(a.bar, 1u);
+                if (k + 1 == a.nops && old == a.nsig * gridDim.x - 1u && !dead) {
+                    // the step's last CTA: advance the decode state
+                    __threadfence();
+                    const unsigned long long key = *(volatile unsigned long long*)&a.st->argmax;
+                    const uint32_t tok = argmax_key_index(key);
+                    DecodeState* st = a.st;
+                    st->token = tok;
+                    if (a.ids && st->step < a.ids_cap) a.ids[st->step] = tok;
+                    st->step += 1;
+                    st->pos += 1;
+                    *a.bar = 0u;
+                }
+            }
+            ++nsig;
+        }
+    }
+    if (dead) cta_dead = 1;
+    step_sync();
+    if (cta_dead) {
+        // copies still in flight land before the CTA's shared memory goes away
+        if (ctid == 0) {
+            const StepRing& r = ring_state;
+            for (uint32_t q = r.retired; q < r.issued; ++q)
+                step_wait(&full[q % kStepSlots], (q / kStepSlots) & 1u, nullptr);
+        }
+    }
+}
+
+// ---------------------------------------------------------------- host --
+
+static const void* step_kernel_for(uint32_t fa, uint32_t fb) {
+    if (fa == SM_T_Q4_0 && fb == SM_T_Q8_0) return (const void*)smallm_step_kernel<FmtQ4_0, FmtQ8_0>;
+    if (fa == SM_T_Q8_0 && fb == SM_T_Q8_0) return (const void*)smallm_step_kernel<FmtQ8_0, FmtQ8_0>;
+    if (fa == SM_T_Q4_0 && fb == SM_T_Q4_0) return (const void*)smallm_step_kernel<FmtQ4_0, FmtQ4_0>;
+    if (fa == SM_T_Q8_0 && fb == SM_T_Q4_0) return (const void*)smallm_step_kernel<FmtQ8_0, FmtQ4_0>;
+    return nullptr;
+}
+
+// Why the persistent step cannot run this model ("" if it can).
+std::string Model::step_unsupported() const {
+    if (tp_size != 1) return "tensor parallel";
+    if (n_layers == 0) return "no layers";
+    const uint32_t fa = layers[0].qkv.type;
+    for (const LayerW& L : layers) {
+        if (!L.fused_v) return "separate V matrix";
+        for (const QMat* m : {&L.qkv, &L.o, &L.gu, &L.down})
+            if (m->type != fa) return "mixed layer formats";
+    }
+    if (!step_kernel_for(fa, out_m.type)) return "weight formats";
+    if (embd_m.type != SM_T_Q4_0 && embd_m.type != SM_T_Q8_0 && embd_m.type != SM_T_F32 && embd_m.type != SM_T_Q4_K &&
+        embd_m.type != SM_T_Q6_K)
+        return "embedding format";
+    if (hd != 32 && hd != 64 && hd != 128) return "head_dim";
+    if (nh_l % nkv_l || nh_l / nkv_l > (uint32_t)kStepMaxGroup) return "head grouping";
+    for (const QMat* m : {&layers[0].qkv, &layers[0].o, &layers[0].gu, &layers[0].down, &out_m})
+        if (m->units > 32u * kStepW) return "rows longer than the step's x registers";
+    if (std::getenv("SMALLM_STEP_KERNELS")) return "disabled by SMALLM_STEP_KERNELS";
+    return "";
+}
+
+void Model::build_step() {
+    step_on = false;
+    step_why = step_unsupported();
+    if (!step_why.empty()) return;
+    const void* fn = step_kernel_for(layers[0].qkv.type, out_m.type);
+    cudaFuncAttributes fa{};
+    SM_CUDA(cudaFuncGetAttributes(&fa, fn));
+    int dev = 0, optin = 0;
+    SM_CUDA(cudaGetDevice(&dev));
+    SM_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    const size_t dyn_max = (size_t)optin - fa.sharedSizeBytes;
+
+    // x region: the largest op's records, or the attention's per-warp scratch
+    const uint32_t G = nh_l / nkv_l;
+    size_t xbytes = (size_t)kStepW * G * (hd + 4) * 4;
+    for (const QMat* m : {&layers[0].qkv, &layers[0].o, &layers[0].gu, &layers[0].down, &out_m})
+        xbytes = std::max(xbytes, (size_t)m->units * kXrecBytes);
+    xbytes = (xbytes + 127) / 128 * 128;
+    if (xbytes + 64 * 1024 > dyn_max) {
+        step_why = "shared memory";
+        return;
+    }
+    const size_t ring = (dyn_max - xbytes) / 128 * 128;
+
+    // piece geometry of a matrix: WS warps per row, RS row slots, RPT rows
+    // per slot (R = RS * RPT rows per piece, even, at most 64, a piece at most
+    // a third of the ring)
+    auto geometry = [&](const QMat& m, StepOp& op) {
+        const uint32_t WS = (m.units + 31) / 32;
+        uint32_t RS = kStepW / WS;
+        uint32_t rpt = 4;
+        while (rpt > 1 && ((size_t)RS * rpt * m.row_stride > ring / 3 || RS * rpt > kStepPartRows)) rpt /= 2;
+        if ((RS * rpt) % 2) {
+            if (rpt < 4 && (size_t)RS * rpt * 2 * m.row_stride <= ring / 3 && RS * rpt * 2 <= kStepPartRows) rpt *= 2;
+            else RS -= 1;  // RS >= 2 here (RS * rpt odd with rpt = 1 needs RS odd and > 1, or RS = 1, rpt = 1)
+        }
+        if (RS == 0 || (RS * rpt) % 2 || (size_t)RS * rpt * m.row_stride > ring / 2)
+            throw Error(1, "persistent step: no piece geometry for a matrix of " + std::to_string(m.cols) + " columns");
+        op.w = m.base;
+        op.row_stride = m.row_stride;
+        op.rows = m.rows;
+        op.rows_pad = m.rows_pad;
+        op.cols = m.cols;
+        op.units = m.units;
+        op.ws = WS;
+        op.rs = RS;
+        op.rpt = rpt;
+        op.prows = RS * rpt;
+        op.npieces = (m.rows_pad + op.prows - 1) / op.prows;
+    };
+
+    std::vector<StepOp> ops;
+    auto blank = [] {
+        StepOp o;
+        std::memset(&o, 0, sizeof(o));
+        return o;
+    };
+    {
+        StepOp e = blank();
+        e.kind = SOP_EMBED;
+        e.signal = 1;
+        e.emb = embd_m;
+        e.y = x;
+        ops.push_back(e);
+    }
+    const uint32_t qrows = nh_l * hd, krows = nkv_l * hd;
+    for (uint32_t i = 0; i < n_layers; ++i) {
+        LayerW& L = layers[i];
+        float* kc = kv + (size_t)(2 * i) * nkv_l * max_ctx * hd;
+        float* vc = kv + (size_t)(2 * i + 1) * nkv_l * max_ctx * hd;
+        StepOp g = blank();
+        g.kind = SOP_GEMV;
+        g.wait = g.signal = 1;
+        g.pro = PRO_RMS;
+        g.epi = EPI_QKV;
+        geometry(L.qkv, g);
+        g.x = x;
+        g.norm_w = L.attn_norm;
+        g.eps = eps;
+        g.bias = L.bias;
+        g.q_rows = qrows;
+        g.k_rows = krows;
+        g.head_dim = hd;
+        g.max_ctx = max_ctx;
+        g.qout = q;
+        g.kcache = kc;
+        g.vcache = vc;
+        g.rope = rope;
+        g.pos = &st->pos;
+        ops.push_back(g);
+
+        StepOp t = blank();
+        t.kind = SOP_ATTN;
+        t.wait = t.signal = 1;
+        t.q = q;
+        t.kcache = kc;
+        t.vcache = vc;
+        t.out = att;
+        t.part = step_part;
+        t.tickets = step_tickets;
+        t.n_heads = nh_l;
+        t.n_kv = nkv_l;
+        t.head_dim = hd;
+        t.max_ctx = max_ctx;
+        t.pos = &st->pos;
+        ops.push_back(t);
+
+        StepOp o = blank();
+        o.kind = SOP_GEMV;
+        o.wait = o.signal = 1;
+        o.pro = PRO_PLAIN;
+        o.epi = EPI_RESIDUAL;
+        geometry(L.o, o);
+        o.x = att;
+        o.y = x;
+        ops.push_back(o);
+
+        StepOp u = blank();
+        u.kind = SOP_GEMV;
+        u.wait = u.signal = 1;
+        u.pro = PRO_RMS;
+        u.epi = EPI_SWIGLU;
+        geometry(L.gu, u);
+        u.x = x;
+        u.norm_w = L.ffn_norm;
+        u.eps = eps;
+        u.y = hbuf;
+        ops.push_back(u);
+
+        StepOp d = blank();
+        d.kind = SOP_GEMV;
+        d.wait = d.signal = 1;
+        d.pro = PRO_PLAIN;
+        d.epi = EPI_RESIDUAL;
+        geometry(L.down, d);
+        d.x = hbuf;
+        d.y = x;
+        ops.push_back(d);
+    }
+    {
+        StepOp h = blank();
+        h.kind = SOP_GEMV;
+        h.fmt = 1;
+        h.wait = h.signal = 1;
+        h.pro = PRO_RMS;
+        h.epi = EPI_LOGITS;
+        geometry(out_m, h);
+        h.x = x;
+        h.norm_w = out_norm;
+        h.eps = eps;
+        h.y = logits_local;
+        h.argmax = &st->argmax;
+        h.row_offset = v0;
+        ops.push_back(h);
+    }
+    step_ops = static_cast<StepOp*>(dalloc(sizeof(StepOp) * ops.size()));
+    SM_CUDA(cudaMemcpy(step_ops, ops.data(), sizeof(StepOp) * ops.size(), cudaMemcpyHostToDevice));
+    step_nops = (uint32_t)ops.size();
+    step_nsig = 0;
+    for (const StepOp& o : ops) step_nsig += o.signal;
+    step_xbytes = (uint32_t)xbytes;
+    step_ring = (uint32_t)ring;
+    step_smem = xbytes + ring;
+    step_fn = fn;
+    set_smem_limit_once(fn, (int)step_smem);
+    int per_sm = 0;
+    SM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kStepThreads, step_smem));
+    if (per_sm < 1) {
+        step_why = "occupancy";
+        return;
+    }
+    step_grid = (uint32_t)sm_count;
+    step_on = true;
+}
+
+// Per-model device buffers of the persistent step (made at load).
+void Model::alloc_step_buffers() {
+    const uint32_t G = nkv_l ? nh_l / nkv_l : 1;
+    step_part = static_cast<float*>(dalloc(4ull * (size_t)sm_count * G * (hd + 2)));
+    step_tickets = static_cast<unsigned int*>(dalloc(4ull * std::max(1u, nkv_l)));
+    step_bar = static_cast<unsigned int*>(dalloc(64));
+    step_abort = step_bar + 1;
+    SM_CUDA(cudaMemsetAsync(step_tickets, 0, 4ull * std::max(1u, nkv_l), stream));
+    SM_CUDA(cudaMemsetAsync(step_bar, 0, 64, stream));
+}
+
+void Model::launch_step(cudaStream_t s) {
+    StepArgs a;
+    a.ops = step_ops;
+    a.nops = step_nops;
+    a.nsig = step_nsig;
+    a.st = st;
+    a.ids = ids;
+    a.ids_cap = ids_cap;
+    a.bar = step_bar;
+    a.abort_flag = step_abort;
+    a.err = device_error_flag();
+    a.xbytes = step_xbytes;
+    a.ring_bytes = step_ring;
+    void* args[] = {&a};
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(step_grid);
+    cfg.blockDim = dim3(kStepThreads);
+    cfg.dynamicSmemBytes = step_smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: they wait on one another
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    SM_CUDA(cudaLaunchKernelExC(&cfg, step_fn, args));
+}
+
+uint32_t Model::step_launch_count() const {
+    if (step_on) return 1;
+    uint32_t n = 1 + 1 + 1;  // embed, lm_head, finalize
+    for (const LayerW& L : layers) n += L.fused_v ? 5 : 6;  // QKV [+ V], attention, O, gate/up, down
+    return n + (tp_size > 1 ? 1 : 0);  // the argmax all-gather
+}
+
+// After a step whose bounded waits gave up: clear the barrier, the abort
+// flag and the attention tickets so the next step starts clean.
+void Model::reset_step_state() {
+    if (!step_bar) return;
+    SM_CUDA(cudaMemsetAsync(step_bar, 0, 64, stream));
+    SM_CUDA(cudaMemsetAsync(step_tickets, 0, 4ull * std::max(1u, nkv_l), stream));
+}
+
+}  // namespace smallm

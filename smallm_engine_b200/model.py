@@ -37,6 +37,7 @@ class ModelConfig:
     max_ctx: int
     weight_bytes_per_token: int
     device_bytes: int
+    step_launches: int = 0
 
 
 class CudaModel:
@@ -56,7 +57,7 @@ class CudaModel:
         self._config = ModelConfig(info.arch.decode(), info.n_layers, info.embd, info.ffn, info.n_heads,
                                    info.n_kv_heads, info.vocab, info.context_length, info.rope_freq_base,
                                    info.rms_eps, info.head_dim, info.max_ctx, info.weight_bytes_per_token,
-                                   info.device_bytes)
+                                   info.device_bytes, info.step_launches)
         self._logits = np.empty(self._config.vocab_size, dtype=np.float32)
 
     def config(self) -> ModelConfig:
