@@ -78,7 +78,7 @@ public:
 
     // Beyond the reference's Model: the prompt in one pass per layer (the
     // same cache contents as tokens.size() forward calls) -> last logits.
-    // flags: SMALLM_PREFILL_TC (tcgen05 GEMMs), SMALLM_PREFILL_TF32, or 0.
+    // The GEMMs run on the backend's tcgen05 tensor-core kernel; flags: 0.
     std::vector<float> prefill(const std::vector<uint32_t>& tokens, uint32_t start_pos, uint32_t flags = 0) {
         std::vector<float> logits(config().vocab_size);
         check(smallm_model_prefill(m_, tokens.data(), static_cast<uint32_t>(tokens.size()), start_pos,

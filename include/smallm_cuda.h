@@ -291,16 +291,13 @@ int smallm_model_decode_ids(smallm_model* m, uint32_t* ids, uint32_t n);
  * Model::forward once per prompt token, src/runtime/generator.cpp:47-51).
  * Fills the KV cache like n forward calls and returns the last token's
  * logits (host `logits`, may be NULL) and greedy id (`argmax`, may be NULL);
- * cached_length becomes start_pos + n.  Single GPU (tp_size 1).  The first
- * call keeps an f32 copy of the layer weights on the device (4 bytes per
- * weight).  flags: SMALLM_PREFILL_TF32 runs the GEMMs on TF32 tensor cores
- * (10-bit mantissa inputs) through cuBLAS; without a flag they are exact f32. */
-#define SMALLM_PREFILL_TF32 1u
-/* SMALLM_PREFILL_TC runs the GEMMs as the backend's own tcgen05 kernel
- * (smallm_gemm_f16) on f16 copies of the layer weights (2 bytes per weight,
- * made at the first such call) and f16-rounded activations (11-bit
- * significands like TF32; f16 range, |x| < 65504); it takes precedence over
- * SMALLM_PREFILL_TF32. */
+ * cached_length becomes start_pos + n.  Single GPU (tp_size 1).  The GEMMs
+ * run on the backend's own tcgen05 tensor-core kernel (smallm_gemm_f16) over
+ * f16 copies of the layer weights (2 bytes per weight, made at the first
+ * call from the exactly dequantized values) and f16-rounded activations
+ * (11-bit significands; f16 range, |x| < 65504), with f32 accumulation.
+ * flags: 0, or SMALLM_PREFILL_TC (the same path, named); any other bit is
+ * SMALLM_ERR_INVALID. */
 #define SMALLM_PREFILL_TC 2u
 int smallm_model_prefill(smallm_model* m, const uint32_t* tokens, uint32_t n, uint32_t start_pos, float* logits,
                          uint32_t* argmax, uint32_t flags);

@@ -134,10 +134,9 @@ def build_cuda(force: bool = False, jobs: int | None = None) -> Path:
     if failed:
         sys.stderr.write("\n".join(failed))
         raise RuntimeError("nvcc compilation failed")
-    cuda_lib = Path(nvcc).resolve().parent.parent / "lib64"  # cuBLAS (prefill GEMMs)
     _run([nvcc, *ARCH, "-shared", "-cudart", "static", "-o", str(CUDA_LIB),
-          *[str(o) for o in objs], "-L", str(lib_nccl), "-l:libnccl.so.2", "-L", str(cuda_lib), "-lcublas",
-          "-Xlinker", f"-rpath={lib_nccl}", "-Xlinker", f"-rpath={cuda_lib}",
+          *[str(o) for o in objs], "-L", str(lib_nccl), "-l:libnccl.so.2",
+          "-Xlinker", f"-rpath={lib_nccl}",
           "-Xlinker", f"--version-script={CSRC / 'exports.map'}"])
     return CUDA_LIB
 

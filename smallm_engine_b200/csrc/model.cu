@@ -50,7 +50,6 @@ void* Model::dalloc(size_t bytes) {
 
 Model::~Model() {
     if (stream) cudaStreamSynchronize(stream);
-    if (cublas) cublasDestroy(cublas);
     for (void* p : pre_allocs) cudaFree(p);
     for (int r = 0; r < tp_size && r < kMaxTPRanks; ++r)
         if (peer_xchg[r] && peer_xchg[r] != xchg) cudaIpcCloseMemHandle(peer_xchg[r]);
@@ -549,6 +548,10 @@ void Model::capture(cudaGraphExec_t* out, TraceSlot* trace) {
 void Model::trace_step(uint32_t token, uint32_t pos, std::vector<TraceSlot>& out) {
     if (token >= vocab) throw Error(1, "token id out of range");
     if (pos >= max_ctx) throw Error(7, "position " + std::to_string(pos) + " is beyond the context length");
+    if (step_on) {
+        trace_step_persistent(token, pos, out);
+        return;
+    }
     const uint32_t nmax = 8 + 6 * n_layers;
     if (!trace_dev) {
         trace_dev = static_cast<TraceSlot*>(dalloc(sizeof(TraceSlot) * nmax));
@@ -617,20 +620,6 @@ void Model::decode_async(uint32_t token, uint32_t pos, uint32_t n_steps) {
 
 // ------------------------------------------------------------ prefill --
 
-static void cublas_check(cublasStatus_t r, const char* what) {
-    if (r != CUBLAS_STATUS_SUCCESS) throw Error(3, std::string(what) + ": cuBLAS status " + std::to_string((int)r));
-}
-
-// Y[T][rows] = X[T][cols] . W[rows][cols]^T (all row-major f32).  A plain
-// library GEMM: exact f32 (pedantic) or TF32 tensor cores.
-void Model::gemm(const float* W, uint32_t rows, uint32_t cols, const float* X, uint32_t T, float* Y, bool tf32) {
-    const float one = 1.0f, zero = 0.0f;
-    cublas_check(cublasGemmEx(cublas, CUBLAS_OP_T, CUBLAS_OP_N, (int)rows, (int)T, (int)cols, &one, W, CUDA_R_32F,
-                              (int)cols, X, CUDA_R_32F, (int)cols, &zero, Y, CUDA_R_32F, (int)rows,
-                              tf32 ? CUBLAS_COMPUTE_32F_FAST_TF32 : CUBLAS_COMPUTE_32F_PEDANTIC, CUBLAS_GEMM_DEFAULT),
-                 "cublasGemmEx");
-}
-
 // The prompt tokens[0..T) at positions pos0 .. pos0 + T - 1 in one pass per
 // layer: every linear layer is a GEMM over the T tokens (the reference runs
 // Model::forward once per token, generator.cpp:47-51); the KV cache receives
@@ -643,19 +632,14 @@ void Model::prefill(const uint32_t* tokens, uint32_t T, uint32_t pos0, float* ou
     for (uint32_t t = 0; t < T; ++t)
         if (tokens[t] >= vocab) throw Error(1, "token id out of range");
     if ((uint64_t)pos0 + T > max_ctx) throw Error(7, "prefill would run past the context length");
-    const bool tc = (flags & SMALLM_PREFILL_TC) != 0;
-    const bool tf32 = !tc && (flags & SMALLM_PREFILL_TF32) != 0;
-    if (!tc && !cublas) {
-        cublas_check(cublasCreate(&cublas), "cublasCreate");
-        cublas_check(cublasSetStream(cublas, stream), "cublasSetStream");
-    }
+    if (flags & ~SMALLM_PREFILL_TC) throw Error(SMALLM_ERR_INVALID, "unknown prefill flags");
     auto palloc = [&](size_t bytes) {
         void* p = nullptr;
         SM_CUDA(cudaMalloc(&p, bytes));
         pre_allocs.push_back(p);
         return static_cast<float*>(p);
     };
-    if (tc && layers_f16.empty()) {
+    if (layers_f16.empty()) {
         // dequantize each matrix (bit-exact) into one f32 staging buffer, then
         // round it to f16 into its own copy (2 bytes per weight)
         uint64_t most = 0;
@@ -691,24 +675,6 @@ void Model::prefill(const uint32_t* tokens, uint32_t T, uint32_t pos0, float* ou
         SM_CUDA(cudaFree(stage));
         layers_f16 = std::move(made);
     }
-    if (!tc && layers_f32.empty()) {
-        layers_f32.resize(n_layers);
-        auto deq = [&](const QMat& q) -> float* {
-            if (!q.base) return nullptr;
-            float* w = palloc(4ull * q.rows * q.cols);
-            launch_qmat_dequant(q, w, stream);
-            return w;
-        };
-        for (uint32_t i = 0; i < n_layers; ++i) {
-            LayerW& L = layers[i];
-            LayerF32& F = layers_f32[i];
-            F.qkv = deq(L.qkv);
-            F.v = L.fused_v ? nullptr : deq(L.v);
-            F.o = deq(L.o);
-            F.gu = deq(L.gu);
-            F.down = deq(L.down);
-        }
-    }
     const uint32_t qrows = nh_l * hd, krows = nkv_l * hd;
     if (T > pre_cap) {
         for (float** b : {&pre_x, &pre_xn, &pre_y, &pre_q, &pre_a, &pre_h}) *b = nullptr;
@@ -722,48 +688,43 @@ void Model::prefill(const uint32_t* tokens, uint32_t T, uint32_t pos0, float* ou
         pre_tok = reinterpret_cast<uint32_t*>(palloc(4ull * T));
         pre_cap = T;
     }
-    if (tc && (uint64_t)T * std::max({embd, qrows, ffn_l}) > pre_xh_cap) {
+    if ((uint64_t)T * std::max({embd, qrows, ffn_l}) > pre_xh_cap) {
         pre_xh_cap = (uint64_t)T * std::max({embd, qrows, ffn_l});
         pre_xh = reinterpret_cast<__half*>(palloc(2 * pre_xh_cap));
     }
-    // Y[T][rows] = X[T][cols] . W^T: tcgen05 on the f16 copies (X is then in
-    // pre_xh, written as f16 by the kernel that produced it), or cuBLAS on the
-    // f32 copies with X in f32
-    auto linear = [&](const float* w32, const __half* w16, uint32_t rows, uint32_t cols, const float* X) {
-        if (tc) launch_tc_gemm(w16, rows, cols, pre_xh, T, pre_y, rows, stream);
-        else gemm(w32, rows, cols, X, T, pre_y, tf32);
+    // Y[T][rows] = X[T][cols] . W^T on the tcgen05 kernel over the f16
+    // copies; X is in pre_xh, written as f16 by the kernel that produced it
+    auto linear = [&](const __half* w16, uint32_t rows, uint32_t cols) {
+        launch_tc_gemm(w16, rows, cols, pre_xh, T, pre_y, rows, stream);
     };
-    __half* const xh = tc ? pre_xh : nullptr;
+    __half* const xh = pre_xh;
     const size_t part_floats = prefill_attention_scratch_floats(T, nh_l, nkv_l, hd, pos0);
     if (part_floats > pre_part_cap) {
         pre_part = palloc(4 * part_floats);
         pre_part_cap = part_floats;
     }
-    static const LayerF32 kNo32;
-    static const LayerF16 kNo16;
     SM_CUDA(cudaMemcpyAsync(pre_tok, tokens, 4ull * T, cudaMemcpyHostToDevice, stream));
     launch_embed_rows(embd_m, pre_tok, T, pre_x, stream);
     for (uint32_t i = 0; i < n_layers; ++i) {
         LayerW& L = layers[i];
-        const LayerF32& F = tc ? kNo32 : layers_f32[i];
-        const LayerF16& H = tc ? layers_f16[i] : kNo16;
+        const LayerF16& H = layers_f16[i];
         float* kc = kv + (size_t)(2 * i) * nkv_l * max_ctx * hd;
         float* vc = kv + (size_t)(2 * i + 1) * nkv_l * max_ctx * hd;
         launch_rmsnorm_rows(pre_x, L.attn_norm, embd, T, eps, pre_xn, stream, xh);
-        linear(F.qkv, H.qkv, L.qkv.rows, embd, pre_xn);
+        linear(H.qkv, L.qkv.rows, embd);
         launch_qkv_post(pre_y, L.qkv.rows, T, qrows, krows, hd, L.bias, rope, pos0, max_ctx, pre_q, kc, vc, stream);
         if (!L.fused_v) {
-            linear(F.v, H.v, L.v.rows, embd, pre_xn);
+            linear(H.v, L.v.rows, embd);
             launch_qkv_post(pre_y, L.v.rows, T, 0, 0, hd, L.bias ? L.bias + qrows + krows : nullptr, rope, pos0,
                             max_ctx, pre_q, kc, vc, stream);
         }
         launch_attention_prefill(pre_q, kc, vc, nh_l, nkv_l, hd, max_ctx, pos0, T, pre_a, stream, xh, pre_part);
-        linear(F.o, H.o, embd, qrows, pre_a);
+        linear(H.o, embd, qrows);
         launch_add_rows(pre_x, pre_y, (uint64_t)T * embd, stream);
         launch_rmsnorm_rows(pre_x, L.ffn_norm, embd, T, eps, pre_xn, stream, xh);
-        linear(F.gu, H.gu, L.gu.rows, embd, pre_xn);
+        linear(H.gu, L.gu.rows, embd);
         launch_swiglu_rows(pre_y, ffn_l, T, pre_h, stream, xh);
-        linear(F.down, H.down, embd, ffn_l, pre_h);
+        linear(H.down, embd, ffn_l);
         launch_add_rows(pre_x, pre_y, (uint64_t)T * embd, stream);
     }
     SM_CUDA(cudaMemsetAsync(&st->argmax, 0, sizeof(unsigned long long), stream));

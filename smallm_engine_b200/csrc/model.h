@@ -1,7 +1,6 @@
 // Device-resident decoder model (internal).
 #pragma once
 
-#include <cublas_v2.h>
 #include <nccl.h>
 
 #include <string>
@@ -84,16 +83,11 @@ struct Model {
     // One sample (sampler.cu) from the last step's logits.
     uint32_t sample(uint32_t kind, uint32_t k, float p, float temperature, float u);
     uint32_t* samp_scratch = nullptr;  // 4 * vocab + 4 u32
-    // Batched prefill: f32 copies of the layer matrices in storage row order
-    // (made at the first prefill), GEMMs over the T tokens.
+    // Batched prefill: f16 copies of the layer matrices in storage row order
+    // (made at the first prefill from the bit-exact dequantized values), GEMMs
+    // over the T tokens on the tcgen05 kernel.
     void prefill(const uint32_t* tokens, uint32_t T, uint32_t pos0, float* out_logits, uint32_t* out_argmax,
                  uint32_t flags);
-    struct LayerF32 {
-        float *qkv = nullptr, *v = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
-    };
-    std::vector<LayerF32> layers_f32;
-    // f16 copies for the tensor-core GEMMs (SMALLM_PREFILL_TC), made at the
-    // first such prefill from the bit-exact dequantized values.
     struct LayerF16 {
         __half *qkv = nullptr, *v = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
     };
@@ -102,13 +96,11 @@ struct Model {
     uint64_t pre_xh_cap = 0;   // elements pre_xh holds
     float* pre_part = nullptr; // key-split partials of the prefill attention
     size_t pre_part_cap = 0;   // floats pre_part holds
-    cublasHandle_t cublas = nullptr;
     uint32_t pre_cap = 0;  // tokens the prefill buffers hold
     float *pre_x = nullptr, *pre_xn = nullptr, *pre_y = nullptr, *pre_q = nullptr, *pre_a = nullptr,
           *pre_h = nullptr;
     uint32_t* pre_tok = nullptr;
     std::vector<void*> pre_allocs;
-    void gemm(const float* W, uint32_t rows, uint32_t cols, const float* X, uint32_t T, float* Y, bool tf32);
     void enqueue_step(cudaStream_t s, TraceSlot* trace = nullptr);
     // The persistent decode step (step.cu): the whole token step as one
     // cooperative kernel when the model's shapes and formats allow it
@@ -126,7 +118,9 @@ struct Model {
     std::string step_unsupported() const;
     void alloc_step_buffers();
     void build_step();
-    void launch_step(cudaStream_t s);
+    void launch_step(cudaStream_t s, TraceSlot* trace = nullptr);
+    void trace_step_persistent(uint32_t token, uint32_t pos, std::vector<TraceSlot>& out);
+    TraceSlot* trace_dev_step = nullptr;
     void reset_step_state();
     uint32_t step_launch_count() const;
     void trace_step(uint32_t token, uint32_t pos, std::vector<TraceSlot>& out);

@@ -69,6 +69,7 @@ constexpr int kStepMaxGroup = 8;           // query heads per KV head
 // names as GemvParams so the fused epilogue (gemv_epilogue_row) reads them.
 struct StepOp {
     uint32_t kind, fmt, pro, epi, wait, signal;
+    uint32_t trace_kind, pad0;  // kind code of this op's slot in a traced step
     // GEMV: matrix and piece geometry
     const uint8_t* w;
     uint32_t row_stride, rows, rows_pad, cols, units;
@@ -111,6 +112,7 @@ struct StepArgs {
     unsigned int* abort_flag;  // set when any wait of the step gave up
     unsigned int* err;         // device error word
     uint32_t xbytes, ring_bytes;
+    TraceSlot* trace;          // [nops] in a traced step, else null
 };
 
 // ------------------------------------------------------------- waiting --
@@ -166,6 +168,9 @@ struct StepRing {
     uint32_t issued;   // pieces whose copy has been started
     uint32_t head;     // ring offset just past the newest issued piece
     uint32_t op, p;    // next piece to issue: op index and piece index
+    // geometry of op `op` (read from global memory once per op)
+    uint32_t kind, np, R, stride, rows_pad;
+    const uint8_t* w;
     uint32_t pstart[kStepSlots];  // ring offset of each in-flight piece
 };
 
@@ -183,19 +188,29 @@ struct StepShared {
 // (one lane, holding the retire turn).  Placement: a piece goes right after
 // the newest one, or at offset 0 when it would run past the end; it may not
 // overlap the span [tail, head) of pieces in flight (tail = oldest's start).
+__device__ void ring_load_op(const StepArgs& a, StepRing& r) {
+    if (r.op >= a.nops) return;
+    const StepOp* op = a.ops + r.op;
+    r.kind = op->kind;
+    r.np = op->npieces;
+    r.R = op->prows;
+    r.stride = op->row_stride;
+    r.rows_pad = op->rows_pad;
+    r.w = op->w;
+}
+
 __device__ void ring_issue(const StepArgs& a, const StepShared& sh) {
     StepRing& r = *sh.rs;
     const uint32_t RB = a.ring_bytes;
     while (r.issued - r.retired < kStepSlots) {
-        const StepOp* op = a.ops + r.op;
-        while (r.op < a.nops && (op->kind != SOP_GEMV || r.p >= op->npieces)) {
+        while (r.op < a.nops && (r.kind != SOP_GEMV || r.p >= r.np)) {
             ++r.op;
             r.p = blockIdx.x;
-            op = a.ops + r.op;
+            ring_load_op(a, r);
         }
         if (r.op >= a.nops) return;
-        const uint32_t R = op->prows, stride = op->row_stride;
-        const uint32_t bytes = min(R, op->rows_pad - r.p * R) * stride;
+        const uint32_t R = r.R, stride = r.stride;
+        const uint32_t bytes = min(R, r.rows_pad - r.p * R) * stride;
         const uint32_t off = r.head + bytes <= RB ? r.head : 0u;
         if (r.issued != r.retired) {
             const uint32_t tail = r.pstart[r.retired % kStepSlots];
@@ -207,7 +222,7 @@ __device__ void ring_issue(const StepArgs& a, const StepShared& sh) {
         r.pstart[s] = off;
         r.head = off + bytes;
         mbar_arrive_expect_tx(&sh.full[s], bytes);
-        bulk_g2s(sh.ring + off, op->w + (size_t)r.p * R * stride, bytes, &sh.full[s]);
+        bulk_g2s(sh.ring + off, r.w + (size_t)r.p * R * stride, bytes, &sh.full[s]);
         ++r.issued;
         r.p += gridDim.x;
     }
@@ -280,14 +295,85 @@ __device__ float step_stage_x(const StepOp& op, const StepShared& sh, int warp, 
     return inv;
 }
 
+// Epilogue operands that do not depend on the row's dot product (rotary
+// cos/sin, biases), loaded before the piece's partial sums are complete so
+// their latency hides behind the other warps' work.
+struct EpiPre {
+    float2 cs;
+    float b0, b1;
+};
+
+__device__ __forceinline__ EpiPre step_epi_pre(const StepOp& op, uint32_t row, uint32_t pos) {
+    EpiPre e{make_float2(0.f, 0.f), 0.f, 0.f};
+    if (op.epi != EPI_QKV || row >= op.rows) return e;
+    const uint32_t hd = op.head_dim, half = hd >> 1;
+    if (row < op.q_rows + op.k_rows) {
+        if ((row & 1) == 0 && row + 1 < op.rows) {
+            const bool isq = row < op.q_rows;
+            const uint32_t pr = (isq ? row : row - op.q_rows) >> 1;  // rotary pair index
+            const uint32_t ii = pr % half;
+            e.cs = __ldg(op.rope + (size_t)pos * half + ii);
+            if (op.bias) {
+                const uint32_t la = (pr / half) * hd + ii, bo = isq ? 0u : op.q_rows;
+                e.b0 = __ldg(op.bias + bo + la);
+                e.b1 = __ldg(op.bias + bo + la + half);
+            }
+        }
+    } else if (op.bias) {
+        e.b0 = __ldg(op.bias + row);  // V rows follow Q and K in the bias vector too
+    }
+    return e;
+}
+
+// The fused epilogue of one finished row (v = W.x after 1/rms): the same
+// arithmetic as gemv.cuh's, with the residual added by a single atomic add
+// (each row is added once per op, so the sum is the plain f32 add) and the
+// rotary/bias operands taken from `e`.
 __device__ __forceinline__ void step_epilogue(const StepOp& op, uint32_t row, float v, float v_next,
-                                              unsigned long long& best) {
+                                              const EpiPre& e, unsigned long long& best) {
     switch (op.epi) {
-        case EPI_STORE: gemv_epilogue_row<EPI_STORE>(op, row, v, v_next, best); break;
-        case EPI_RESIDUAL: gemv_epilogue_row<EPI_RESIDUAL>(op, row, v, v_next, best); break;
-        case EPI_QKV: gemv_epilogue_row<EPI_QKV>(op, row, v, v_next, best); break;
+        case EPI_STORE:
+            if (row < op.rows) op.y[row] = v;
+            break;
+        case EPI_RESIDUAL:  // x += W.h (ops::axpy, qwen2_model.cpp:178,184)
+            if (row < op.rows) atomicAdd(op.y + row, v);
+            break;
         case EPI_SWIGLU: gemv_epilogue_row<EPI_SWIGLU>(op, row, v, v_next, best); break;
         case EPI_LOGITS: gemv_epilogue_row<EPI_LOGITS>(op, row, v, v_next, best); break;
+        case EPI_QKV: {
+            const uint32_t hd = op.head_dim, half = hd >> 1;
+            const uint32_t pos = *op.pos;
+            if (row < op.q_rows + op.k_rows) {
+                if ((row & 1) == 0 && row + 1 < op.rows) {
+                    const bool isq = row < op.q_rows;
+                    const uint32_t pr = (isq ? row : row - op.q_rows) >> 1;
+                    const uint32_t head = pr / half, ii = pr % half;
+                    const uint32_t la = head * hd + ii, lb = la + half;
+                    float x0 = v, x1 = v_next;
+                    if (op.bias) {
+                        x0 += e.b0;
+                        x1 += e.b1;
+                    }
+                    // ops::rope (ops.cpp:84-89) with the reference build's fused rounding
+                    const float o0 = fmaf(x0, e.cs.x, -__fmul_rn(x1, e.cs.y));
+                    const float o1 = fmaf(x0, e.cs.y, __fmul_rn(x1, e.cs.x));
+                    if (isq) {
+                        op.qout[la] = o0;
+                        op.qout[lb] = o1;
+                    } else {
+                        float* kr = op.kcache + ((size_t)head * op.max_ctx + pos) * hd;
+                        kr[ii] = o0;
+                        kr[ii + half] = o1;
+                    }
+                }
+            } else if (row < op.rows) {
+                const uint32_t lv = row - op.q_rows - op.k_rows;
+                float vv = v;
+                if (op.bias) vv += e.b0;
+                op.vcache[((size_t)(lv / hd) * op.max_ctx + pos) * hd + lv % hd] = vv;
+            }
+            break;
+        }
         default: break;
     }
 }
@@ -316,6 +402,7 @@ __device__ __noinline__ PieceCursor step_gemv(const StepOp& op, const StepArgs& 
     const bool uact = active && u < U;
     XRec xr;
     if (uact) load_xrec(sh.xreg, u, xr);
+    const uint32_t pos_op = op.epi == EPI_QKV ? *op.pos : 0u;  // the step's position (RoPE row)
     constexpr int LPR = 32 / RPT;
     for (uint32_t p = blockIdx.x; p < op.npieces; p += gridDim.x, ++j) {
         const uint32_t rows_here = min(R, op.rows_pad - p * R);
@@ -352,19 +439,27 @@ __device__ __noinline__ PieceCursor step_gemv(const StepOp& op, const StepArgs& 
         if ((uint32_t)warp == j % kStepW) {
             // this warp closes the piece: sum the row partials, fused epilogue,
             // free its ring space and issue the next pieces
+            EpiPre pre[2];
+#pragma unroll
+            for (int ib = 0; ib < 2; ++ib) {
+                const uint32_t r = ib * 32 + (uint32_t)lane;
+                pre[ib] = r < rows_here ? step_epi_pre(op, p * R + r, pos_op) : EpiPre{make_float2(0.f, 0.f), 0.f, 0.f};
+            }
             if (!dead && !step_wait(&sh.done[s], ph, a.abort_flag)) {
                 dead = true;
                 step_raise(a);
             }
             dead = __any_sync(0xffffffffu, dead);
-            for (uint32_t rb = 0; rb < R; rb += 32) {
-                const uint32_t r = rb + (uint32_t)lane;
+#pragma unroll
+            for (int ib = 0; ib < 2; ++ib) {
+                if ((uint32_t)ib * 32 >= R) break;  // uniform
+                const uint32_t r = ib * 32 + (uint32_t)lane;
                 float val = 0.f;
                 if (r < R)
                     for (uint32_t k = 0; k < WS; ++k) val += sh.part[s * kStepPartRows + r * WS + k];
                 val *= inv;  // 1/rms of the fused RMSNorm (1 if plain)
                 const float v_next = __shfl_down_sync(0xffffffffu, val, 1);  // partner row of a pair
-                if (r < rows_here && !dead) step_epilogue(op, p * R + r, val, v_next, best);
+                if (r < rows_here && !dead) step_epilogue(op, p * R + r, val, v_next, pre[ib], best);
             }
             __syncwarp();
             if (lane == 0 && !dead && !ring_retire(a, sh, j)) {
@@ -600,6 +695,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
         ring_state.retired = ring_state.issued = ring_state.head = 0u;
         ring_state.op = 0u;
         ring_state.p = blockIdx.x;
+        ring_load_op(a, ring_state);
         cta_dead = 0;
         ring_issue(a, sh);  // fill the ring: weights depend on nothing
     }
@@ -618,6 +714,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
         step_sync();
         dead = cta_dead != 0;
         const StepOp& op = op_sh;
+        TraceSlot* slot = a.trace ? a.trace + k : nullptr;
+        if (ctid == 0) trace_mark(slot, 0);
         if (op.wait) {  // CTA-uniform condition: every thread reaches the barrier below
             if (ctid == 0 && !dead && !grid_wait(a.bar, nsig * gridDim.x, a.abort_flag)) {
                 cta_dead = 1;
@@ -626,6 +724,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
             step_sync();
             dead = cta_dead != 0;
         }
+        if (ctid == 0) trace_mark(slot, 1);
         if (op.kind == SOP_GEMV) {
             PieceCursor cur{j, head, dead ? 1u : 0u, 0ull};
             cur = op.fmt == 0 ? step_gemv_fmt<FA>(op, a, sh, warp, lane, cur)
@@ -663,6 +762,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
         }
         if (op.signal) {
             step_sync();  // every warp's writes of this op are issued
+            if (ctid == 0) trace_mark(slot, 2);
             if (ctid == 0) {
                 __threadfence();
                 const unsigned int old = atomicAdd(a.bar, 1u);
@@ -786,6 +886,7 @@ void Model::build_step() {
     {
         StepOp e = blank();
         e.kind = SOP_EMBED;
+        e.trace_kind = 1;
         e.signal = 1;
         e.emb = embd_m;
         e.y = x;
@@ -801,6 +902,7 @@ void Model::build_step() {
         g.wait = g.signal = 1;
         g.pro = PRO_RMS;
         g.epi = EPI_QKV;
+        g.trace_kind = 2;
         geometry(L.qkv, g);
         g.x = x;
         g.norm_w = L.attn_norm;
@@ -819,6 +921,7 @@ void Model::build_step() {
 
         StepOp t = blank();
         t.kind = SOP_ATTN;
+        t.trace_kind = 4;
         t.wait = t.signal = 1;
         t.q = q;
         t.kcache = kc;
@@ -838,6 +941,7 @@ void Model::build_step() {
         o.wait = o.signal = 1;
         o.pro = PRO_PLAIN;
         o.epi = EPI_RESIDUAL;
+        o.trace_kind = 5;
         geometry(L.o, o);
         o.x = att;
         o.y = x;
@@ -848,6 +952,7 @@ void Model::build_step() {
         u.wait = u.signal = 1;
         u.pro = PRO_RMS;
         u.epi = EPI_SWIGLU;
+        u.trace_kind = 6;
         geometry(L.gu, u);
         u.x = x;
         u.norm_w = L.ffn_norm;
@@ -860,6 +965,7 @@ void Model::build_step() {
         d.wait = d.signal = 1;
         d.pro = PRO_PLAIN;
         d.epi = EPI_RESIDUAL;
+        d.trace_kind = 7;
         geometry(L.down, d);
         d.x = hbuf;
         d.y = x;
@@ -872,6 +978,7 @@ void Model::build_step() {
         h.wait = h.signal = 1;
         h.pro = PRO_RMS;
         h.epi = EPI_LOGITS;
+        h.trace_kind = 8;
         geometry(out_m, h);
         h.x = x;
         h.norm_w = out_norm;
@@ -912,7 +1019,7 @@ void Model::alloc_step_buffers() {
     SM_CUDA(cudaMemsetAsync(step_bar, 0, 64, stream));
 }
 
-void Model::launch_step(cudaStream_t s) {
+void Model::launch_step(cudaStream_t s, TraceSlot* trace) {
     StepArgs a;
     a.ops = step_ops;
     a.nops = step_nops;
@@ -925,6 +1032,7 @@ void Model::launch_step(cudaStream_t s) {
     a.err = device_error_flag();
     a.xbytes = step_xbytes;
     a.ring_bytes = step_ring;
+    a.trace = trace;
     void* args[] = {&a};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(step_grid);
@@ -937,6 +1045,28 @@ void Model::launch_step(cudaStream_t s) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     SM_CUDA(cudaLaunchKernelExC(&cfg, step_fn, args));
+}
+
+// One step of the persistent kernel with per-op timestamps (earliest CTA at
+// the op's start, earliest past its barrier wait, latest at its end); the
+// slots' kind codes follow the per-op kernels' trace kinds.
+void Model::trace_step_persistent(uint32_t token, uint32_t pos, std::vector<TraceSlot>& out) {
+    if (!trace_dev_step) trace_dev_step = static_cast<TraceSlot*>(dalloc(sizeof(TraceSlot) * step_nops));
+    std::vector<StepOp> ops(step_nops);
+    SM_CUDA(cudaMemcpy(ops.data(), step_ops, sizeof(StepOp) * step_nops, cudaMemcpyDeviceToHost));
+    std::vector<TraceSlot> init(step_nops);
+    for (uint32_t k = 0; k < step_nops; ++k) init[k] = TraceSlot{~0ull, ~0ull, 0ull, ops[k].trace_kind};
+    SM_CUDA(cudaMemcpyAsync(trace_dev_step, init.data(), sizeof(TraceSlot) * step_nops, cudaMemcpyHostToDevice,
+                            stream));
+    set_state(token, pos);
+    launch_step(stream, trace_dev_step);
+    out.resize(step_nops);
+    SM_CUDA(cudaMemcpyAsync(out.data(), trace_dev_step, sizeof(TraceSlot) * step_nops, cudaMemcpyDeviceToHost,
+                            stream));
+    SM_CUDA(cudaMemcpyAsync(h_err, device_error_flag(), 4, cudaMemcpyDeviceToHost, stream));
+    SM_CUDA(cudaStreamSynchronize(stream));
+    check_step_errors();
+    cached = pos + 1;
 }
 
 uint32_t Model::step_launch_count() const {

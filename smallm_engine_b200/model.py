@@ -103,19 +103,16 @@ class CudaModel:
         self.decode_greedy_async(token, pos, n_steps)
         return self.decode_ids(n_steps)
 
-    def prefill(self, tokens, start_pos: int, want_logits: bool = True, tf32: bool = False,
-                tensor_cores: bool = False):
+    def prefill(self, tokens, start_pos: int, want_logits: bool = True):
         """Batched prefill (smallm_model_prefill): tokens at positions
-        start_pos.. in one pass per layer.  tensor_cores runs the GEMMs on the
-        backend's tcgen05 kernel over f16 weight copies (SMALLM_PREFILL_TC),
-        tf32 on cuBLAS TF32; neither: exact f32.  Returns (last logits or None,
-        greedy id of the last token)."""
+        start_pos.. in one pass per layer, the GEMMs on the backend's tcgen05
+        tensor-core kernel over f16 weight copies.  Returns (last logits or
+        None, greedy id of the last token)."""
         toks = np.ascontiguousarray(tokens, dtype=np.uint32)
         out = np.empty(self._config.vocab_size, dtype=np.float32) if want_logits else None
         am = ctypes.c_uint32()
         check(lib().smallm_model_prefill(self.h, toks.ctypes.data, toks.size, int(start_pos),
-                                         out.ctypes.data if want_logits else None, ctypes.byref(am),
-                                         (2 if tensor_cores else 0) | (1 if tf32 else 0)))
+                                         out.ctypes.data if want_logits else None, ctypes.byref(am), 0))
         return out, int(am.value)
 
     def logits_device_ptr(self) -> int:

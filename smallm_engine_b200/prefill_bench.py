@@ -2,15 +2,15 @@
 whole model (the dense-contraction path).
 
     python -m smallm_engine_b200.prefill_bench [--workload qwen2-1.5b-q8_0]
-        [--seqs 4] [--tokens 512] [--decode 64] [--modes tc,tf32,f32] [--gemm-only]
+        [--seqs 4] [--tokens 512] [--decode 64] [--gemm-only]
 
 GEMM leg: smallm_gemm_f16 (tcgen05) on seeded f16 operands with the
 workload's layer shapes over seqs x tokens rows, `iters` launches timed with
 CUDA events on the launching stream after warm-up; TFLOP/s counts 2*N*K*T
 per launch.  Model leg: `seqs` independent seeded prompts of `tokens` ids,
-each prefilled in one pass (smallm_model_prefill, after reset_cache) and
-then decoded greedily for `decode` steps from its prefilled cache; CUDA
-events on the model stream around each prefill.  Linear-layer FLOPs per
+each prefilled in one pass (smallm_model_prefill on the tcgen05 GEMMs, after
+reset_cache) and then decoded greedily for `decode` steps from its prefilled
+cache; CUDA events on the model stream around each prefill and each decode.  Linear-layer FLOPs per
 token are 2 x the layer weights (the lm_head runs once, for the last token).
 One JSON line.
 """
@@ -81,7 +81,7 @@ def gemm_run(spec, T: int, iters: int = 20, device: int = 0) -> list[dict]:
     return out
 
 
-def model_run(workload: str, seqs: int, tokens: int, decode: int, modes: list[str], device: int = 0) -> dict:
+def model_run(workload: str, seqs: int, tokens: int, decode: int, device: int = 0) -> dict:
     import numpy as np
     import torch
 
@@ -93,38 +93,34 @@ def model_run(workload: str, seqs: int, tokens: int, decode: int, modes: list[st
     prompts = [rng.integers(0, spec.vocab, size=tokens).tolist() for _ in range(seqs)]
     s = torch.cuda.ExternalStream(m.stream, device=f"cuda:{device}")
     flops_tok = 2.0 * spec.layers * sum(r * c for _, r, c in layer_shapes(spec))
-    res = {}
-    first_ids = {}
-    for mode in modes:
-        kw = {"tensor_cores": mode == "tc", "tf32": mode == "tf32"}
+    m.reset_cache()
+    m.prefill(prompts[0], 0, want_logits=False)  # makes the weight copies; warm-up
+    ms, dec_ms, ids, heads = [], [], [], []
+    for p in prompts:
         m.reset_cache()
-        m.prefill(prompts[0], 0, want_logits=False, **kw)  # makes the weight copies; warm-up
-        ms, dec_ms, ids = [], [], []
-        for p in prompts:
-            m.reset_cache()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        _, am = m.prefill(p, 0, want_logits=False)
+        e1.record(s)
+        e1.synchronize()
+        ms.append(e0.elapsed_time(e1))
+        ids.append(am)
+        if decode:
             e0.record(s)
-            _, am = m.prefill(p, 0, want_logits=False, **kw)
+            m.decode_greedy_async(am, tokens, decode)
             e1.record(s)
             e1.synchronize()
-            ms.append(e0.elapsed_time(e1))
-            ids.append(am)
-            if decode:
-                e0.record(s)
-                m.decode_greedy(am, tokens, decode)
-                e1.record(s)
-                e1.synchronize()
-                dec_ms.append(e0.elapsed_time(e1))
-        tot = sum(ms)
-        res[mode] = {"prefill_ms_per_seq": [round(v, 3) for v in ms],
-                     "prefill_tok_s": seqs * tokens / (tot / 1e3),
-                     "linear_tflops": flops_tok * seqs * tokens / (tot / 1e3) / 1e12,
-                     "decode_tok_s": (seqs * decode / (sum(dec_ms) / 1e3)) if dec_ms else None}
-        first_ids[mode] = ids
+            dec_ms.append(e0.elapsed_time(e1))
+            heads.append([int(v) for v in m.decode_ids(decode)[:4]])
     m.close()
-    base = modes[-1]
-    return {"workload": workload, "seqs": seqs, "tokens": tokens, "decode_steps": decode, "modes": res,
-            "same_first_ids_as_" + base: {k: v == first_ids[base] for k, v in first_ids.items()}}
+    tot = sum(ms)
+    return {"workload": workload, "seqs": seqs, "tokens": tokens, "decode_steps": decode,
+            "prefill_ms_per_seq": [round(v, 3) for v in ms],
+            "prefill_tok_s": seqs * tokens / (tot / 1e3),
+            "linear_tflops": flops_tok * seqs * tokens / (tot / 1e3) / 1e12,
+            "decode_tok_s": (seqs * decode / (sum(dec_ms) / 1e3)) if dec_ms else None,
+            "decode_ms_per_seq": [round(v, 3) for v in dec_ms],
+            "first_ids": ids, "decode_ids_head": heads}
 
 
 def main(argv=None):
@@ -133,7 +129,6 @@ def main(argv=None):
     ap.add_argument("--seqs", type=int, default=4)
     ap.add_argument("--tokens", type=int, default=512)
     ap.add_argument("--decode", type=int, default=64)
-    ap.add_argument("--modes", default="tc,tf32,f32")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--gemm-only", action="store_true")
     a = ap.parse_args(argv)
@@ -145,9 +140,8 @@ def main(argv=None):
         r["frac_of_" + kind + "_peak"] = r["tflops"] / peak
     line = {"gemm": g, "tensor_peak_tflops": peak, "peak_kind": kind}
     if not a.gemm_only:
-        line["model"] = model_run(a.workload, a.seqs, a.tokens, a.decode, a.modes.split(","))
-        for v in line["model"]["modes"].values():
-            v["linear_frac_of_" + kind + "_peak"] = v["linear_tflops"] / peak
+        line["model"] = model_run(a.workload, a.seqs, a.tokens, a.decode)
+        line["model"]["linear_frac_of_" + kind + "_peak"] = line["model"]["linear_tflops"] / peak
     print(json.dumps(line), flush=True)
 
 
