@@ -123,11 +123,24 @@ __device__ __forceinline__ void step_raise(const StepArgs& a) {
     __threadfence();
 }
 
-// mbarrier phase wait, bounded (~2^31 cycles) and abandoned as soon as the
-// step's abort flag is up.
+// The abort flag lives in global memory: a wait looks at it only once it has
+// waited for ~2^16 cycles (~33 us), and then every 2^12 cycles, so a wait that
+// completes normally never pays for that load.
+constexpr long long kAbortLookAfter = 1ll << 16;
+constexpr long long kGiveUp = 1ll << 31;  // ~1 s
+
+__device__ __forceinline__ bool abort_seen(const unsigned int* abort_flag, long long waited, long long& next) {
+    if (!abort_flag || waited < next) return false;
+    next = waited + 4096;
+    return *(const volatile unsigned int*)abort_flag != 0u;
+}
+
+// mbarrier phase wait, bounded (~2^31 cycles) and abandoned when the step's
+// abort flag is up.
 __device__ __forceinline__ bool step_wait(uint64_t* bar, uint32_t parity, const unsigned int* abort_flag) {
     const uint32_t addr = smem_u32(bar);
     const long long t0 = clock64();
+    long long next = kAbortLookAfter;
     for (;;) {
         uint32_t ok;
         asm volatile(
@@ -136,8 +149,8 @@ __device__ __forceinline__ bool step_wait(uint64_t* bar, uint32_t parity, const 
             : "r"(addr), "r"(parity), "r"(20000u)
             : "memory");
         if (ok) return true;
-        if (abort_flag && *(const volatile unsigned int*)abort_flag) return false;
-        if (clock64() - t0 > (1ll << 31)) return false;
+        const long long waited = clock64() - t0;
+        if (waited > kGiveUp || abort_seen(abort_flag, waited, next)) return false;
     }
 }
 
@@ -145,13 +158,13 @@ __device__ __forceinline__ bool step_wait(uint64_t* bar, uint32_t parity, const 
 __device__ __forceinline__ bool grid_wait(const unsigned int* bar, unsigned int target,
                                           const unsigned int* abort_flag) {
     const long long t0 = clock64();
+    long long next = kAbortLookAfter;
     for (;;) {
         unsigned int v;
         asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
         if ((int)(v - target) >= 0) return true;
-        if (*(const volatile unsigned int*)abort_flag) return false;
-        if (clock64() - t0 > (1ll << 31)) return false;
-        __nanosleep(32);
+        const long long waited = clock64() - t0;
+        if (waited > kGiveUp || abort_seen(abort_flag, waited, next)) return false;
     }
 }
 
@@ -233,9 +246,10 @@ __device__ void ring_issue(const StepArgs& a, const StepShared& sh) {
 __device__ bool ring_retire(const StepArgs& a, const StepShared& sh, uint32_t j) {
     volatile uint32_t* ret = &sh.rs->retired;
     const long long t0 = clock64();
+    long long next = kAbortLookAfter;
     while (*ret != j) {
-        if (*(const volatile unsigned int*)a.abort_flag) return false;
-        if (clock64() - t0 > (1ll << 31)) return false;
+        const long long waited = clock64() - t0;
+        if (waited > kGiveUp || abort_seen(a.abort_flag, waited, next)) return false;
     }
     __threadfence_block();
     sh.rs->retired = j + 1;
@@ -496,120 +510,148 @@ __device__ __forceinline__ void attn_merge(float& m, float& l, float4& o, float 
     m = M;
 }
 
+// One attention item per CTA: KV head kvh, positions [b, e).  The op's
+// barrier (on the QKV op) is taken in here: the item's first batch of cached
+// K/V rows (every position but the newest, which this step's QKV op writes)
+// is loaded before it, so that latency overlaps the wait.
 template <int HD>
 __device__ __noinline__ uint32_t step_attn(const StepOp& op, const StepArgs& a, const StepShared sh, int warp,
-                                           int lane, uint32_t dead_in) {
-    const bool dead = dead_in != 0;
-    constexpr int RPI = 128 / HD;   // positions per warp instruction (sub-warps)
-    constexpr int LPR = 32 / RPI;   // lanes per position: 4 dims each
-    constexpr int kHP = 4;          // heads per pass
-    constexpr uint32_t SR = HD + 4; // scratch row: HD outputs, max, sum, pad to 16 bytes
+                                           int lane, uint32_t dead_in, uint32_t target, int* cta_dead) {
+    constexpr int RPI = 128 / HD;            // positions per warp instruction (sub-warps)
+    constexpr int LPR = 32 / RPI;            // lanes per position: 4 dims each
+    constexpr int kHP = 4;                   // heads per pass (register budget)
+    constexpr int kB = 4;                    // positions per position-lane and load batch
+    constexpr uint32_t SR = HD + 4;          // scratch row: HD outputs, max, sum, pad to 16 bytes
+    constexpr uint32_t NRL = kStepW * RPI;   // position lanes of the CTA
     const int ctid = warp * 32 + lane;
     const uint32_t G = op.n_heads / op.n_kv;
-    const uint32_t n = min(*op.pos + 1, op.max_ctx);
-    const uint32_t grid = gridDim.x;
-    uint32_t S = grid / op.n_kv;
-    if (S < 1) S = 1;
-    const uint32_t smax = (n + 15) / 16;
+    const uint32_t n = min(*op.pos + 1, op.max_ctx);  // fixed for the whole step
+    const uint32_t newest = n - 1;
+    // items of at most one load batch of positions each, as many as the grid allows
+    uint32_t smax = gridDim.x / op.n_kv;
+    if (smax < 1) smax = 1;
+    uint32_t S = (n + NRL * kB - 1) / (NRL * kB);
     if (S > smax) S = smax;
+    if (S < 1) S = 1;
     const uint32_t L = (n + S - 1) / S;
-    const uint32_t items = op.n_kv * S;
-    const float scale = 1.0f / sqrtf((float)HD);
+    const uint32_t item = blockIdx.x;
+    const bool has = item < op.n_kv * S;
+    const uint32_t kvh = has ? item / S : 0u, sidx = has ? item % S : 0u;
+    const uint32_t b = sidx * L, e = has ? min(n, b + L) : 0u;
     const int sub = lane / LPR, dl = lane % LPR;
+    const float* kb = op.kcache + (size_t)kvh * op.max_ctx * HD;
+    const float* vb = op.vcache + (size_t)kvh * op.max_ctx * HD;
+    const uint32_t first = b + (uint32_t)warp * RPI;
+    uint32_t trips = first < e ? (e - first + NRL - 1) / NRL : 0u;  // warp-uniform
+    float4 kk[kB], vv[kB];
+    auto load_batch = [&](uint32_t i, bool cached_only) {
+#pragma unroll
+        for (int c = 0; c < kB; ++c) {
+            const uint32_t t = first + (i + c) * NRL + (uint32_t)sub;
+            const bool in = i + c < trips && t < e && !(cached_only && t == newest);
+            if (in) {
+                kk[c] = __ldcg(reinterpret_cast<const float4*>(kb + (size_t)t * HD) + dl);
+                vv[c] = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)t * HD) + dl);
+            } else if (!cached_only || i + c >= trips || t >= e) {
+                kk[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+                vv[c] = kk[c];
+            }
+        }
+    };
+    load_batch(0, true);
+    // the QKV op's results (q, the newest K/V row) are complete past this barrier
+    bool dead = dead_in != 0;
+    if (ctid == 0 && !dead && !grid_wait(a.bar, target, a.abort_flag)) {
+        *cta_dead = 1;
+        step_raise(a);
+    }
+    step_sync();
+    dead = *cta_dead != 0;
+    if (dead) trips = 0u;
+#pragma unroll
+    for (int c = 0; c < kB; ++c) {
+        const uint32_t t = first + c * NRL + (uint32_t)sub;
+        if ((uint32_t)c < trips && t == newest) {
+            kk[c] = __ldcg(reinterpret_cast<const float4*>(kb + (size_t)t * HD) + dl);
+            vv[c] = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)t * HD) + dl);
+        }
+    }
+    const float scale = 1.0f / sqrtf((float)HD);
     float* scr = reinterpret_cast<float*>(sh.xreg);  // [kStepW][G][SR]
-    __shared__ int last_item;
-    for (uint32_t item = blockIdx.x; item < items; item += grid) {
-        const uint32_t kvh = item / S, sidx = item % S;
-        const uint32_t b = sidx * L, e = min(n, b + L);
-        const float* kb = op.kcache + (size_t)kvh * op.max_ctx * HD;
-        const float* vb = op.vcache + (size_t)kvh * op.max_ctx * HD;
-        constexpr uint32_t NRL = kStepW * RPI;  // position lanes of the CTA
-        const uint32_t first = b + (uint32_t)warp * RPI;
-        const uint32_t trips = (!dead && first < e) ? (e - first + NRL - 1) / NRL : 0u;  // warp-uniform
-        // heads in passes of kHP (register budget); a second pass re-reads the
-        // item's K/V rows from L2
-        for (uint32_t h0 = 0; h0 < G; h0 += kHP) {
-            float4 qv[kHP];
-            float m[kHP], l[kHP];
-            float4 o[kHP];
+    for (uint32_t h0 = 0; h0 < G; h0 += kHP) {
+        float4 qv[kHP];
+        float m[kHP], l[kHP];
+        float4 o[kHP];
 #pragma unroll
-            for (int h = 0; h < kHP; ++h) {
-                qv[h] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (h0 + h < G)
-                    qv[h] = __ldcg(reinterpret_cast<const float4*>(op.q + ((size_t)kvh * G + h0 + h) * HD) + dl);
-                m[h] = -INFINITY;
-                l[h] = 0.f;
-                o[h] = make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-            for (uint32_t i = 0; i < trips; i += 4) {
-                float4 kk[4], vv[4];
-                bool ok[4];
+        for (int h = 0; h < kHP; ++h) {
+            qv[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (has && h0 + h < G)
+                qv[h] = __ldcg(reinterpret_cast<const float4*>(op.q + ((size_t)kvh * G + h0 + h) * HD) + dl);
+            m[h] = -INFINITY;
+            l[h] = 0.f;
+            o[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        for (uint32_t i = 0; i < trips; i += kB) {
+            if (i > 0 || (h0 > 0 && trips > (uint32_t)kB)) load_batch(i, false);  // batch 0 is still in registers otherwise
+            bool ok[kB];
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const uint32_t t = first + (i + c) * NRL + (uint32_t)sub;
-                    ok[c] = i + c < trips && t < e;
-                    kk[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-                    vv[c] = kk[c];
+            for (int c = 0; c < kB; ++c) ok[c] = i + c < trips && first + (i + c) * NRL + (uint32_t)sub < e;
+#pragma unroll
+            for (int c = 0; c < kB; ++c) {
+                if (i + c >= trips) break;  // warp-uniform
+#pragma unroll
+                for (int h = 0; h < kHP; ++h) {
+                    if (h0 + h >= G) break;  // uniform
+                    float sc = qv[h].x * kk[c].x + qv[h].y * kk[c].y + qv[h].z * kk[c].z + qv[h].w * kk[c].w;
+#pragma unroll
+                    for (int off = 1; off < LPR; off <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, off);
+                    sc *= scale;
                     if (ok[c]) {
-                        kk[c] = __ldcg(reinterpret_cast<const float4*>(kb + (size_t)t * HD) + dl);
-                        vv[c] = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)t * HD) + dl);
-                    }
-                }
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    if (i + c >= trips) break;  // warp-uniform
-#pragma unroll
-                    for (int h = 0; h < kHP; ++h) {
-                        if (h0 + h >= G) break;  // uniform
-                        float sc = qv[h].x * kk[c].x + qv[h].y * kk[c].y + qv[h].z * kk[c].z + qv[h].w * kk[c].w;
-#pragma unroll
-                        for (int off = 1; off < LPR; off <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, off);
-                        sc *= scale;
-                        if (ok[c]) {
-                            const float mn = fmaxf(m[h], sc);
-                            const float co = expf(m[h] - mn);  // 0 for the first position (m = -inf)
-                            const float pr = expf(sc - mn);
-                            l[h] = l[h] * co + pr;
-                            o[h].x = o[h].x * co + pr * vv[c].x;
-                            o[h].y = o[h].y * co + pr * vv[c].y;
-                            o[h].z = o[h].z * co + pr * vv[c].z;
-                            o[h].w = o[h].w * co + pr * vv[c].w;
-                            m[h] = mn;
-                        }
-                    }
-                }
-            }
-            // merge the sub-warps (same dims, other positions)
-#pragma unroll
-            for (int off = LPR; off < 32; off <<= 1) {
-#pragma unroll
-                for (int h = 0; h < kHP; ++h) {
-                    const float m2 = __shfl_xor_sync(0xffffffffu, m[h], off);
-                    const float l2 = __shfl_xor_sync(0xffffffffu, l[h], off);
-                    float4 o2;
-                    o2.x = __shfl_xor_sync(0xffffffffu, o[h].x, off);
-                    o2.y = __shfl_xor_sync(0xffffffffu, o[h].y, off);
-                    o2.z = __shfl_xor_sync(0xffffffffu, o[h].z, off);
-                    o2.w = __shfl_xor_sync(0xffffffffu, o[h].w, off);
-                    attn_merge(m[h], l[h], o[h], m2, l2, o2);
-                }
-            }
-            if (sub == 0) {
-#pragma unroll
-                for (int h = 0; h < kHP; ++h) {
-                    if (h0 + h >= G) break;
-                    float* r = scr + ((size_t)warp * G + h0 + h) * SR;  // SR floats: 16-byte rows
-                    reinterpret_cast<float4*>(r)[dl] = o[h];
-                    if (dl == 0) {
-                        r[HD] = m[h];
-                        r[HD + 1] = l[h];
+                        const float mn = fmaxf(m[h], sc);
+                        const float co = expf(m[h] - mn);  // 0 for the first position (m = -inf)
+                        const float pr = expf(sc - mn);
+                        l[h] = l[h] * co + pr;
+                        o[h].x = o[h].x * co + pr * vv[c].x;
+                        o[h].y = o[h].y * co + pr * vv[c].y;
+                        o[h].z = o[h].z * co + pr * vv[c].z;
+                        o[h].w = o[h].w * co + pr * vv[c].w;
+                        m[h] = mn;
                     }
                 }
             }
         }
-        step_sync();
-        // merge the 16 warps: thread -> (head, dim)
-        float* part = op.part + (size_t)(kvh * S + sidx) * G * (HD + 2);
+        // merge the sub-warps (same dims, other positions)
+#pragma unroll
+        for (int off = LPR; off < 32; off <<= 1) {
+#pragma unroll
+            for (int h = 0; h < kHP; ++h) {
+                const float m2 = __shfl_xor_sync(0xffffffffu, m[h], off);
+                const float l2 = __shfl_xor_sync(0xffffffffu, l[h], off);
+                float4 o2;
+                o2.x = __shfl_xor_sync(0xffffffffu, o[h].x, off);
+                o2.y = __shfl_xor_sync(0xffffffffu, o[h].y, off);
+                o2.z = __shfl_xor_sync(0xffffffffu, o[h].z, off);
+                o2.w = __shfl_xor_sync(0xffffffffu, o[h].w, off);
+                attn_merge(m[h], l[h], o[h], m2, l2, o2);
+            }
+        }
+        if (sub == 0) {
+#pragma unroll
+            for (int h = 0; h < kHP; ++h) {
+                if (h0 + h >= G) break;
+                float* r = scr + ((size_t)warp * G + h0 + h) * SR;  // SR floats: 16-byte rows
+                reinterpret_cast<float4*>(r)[dl] = o[h];
+                if (dl == 0) {
+                    r[HD] = m[h];
+                    r[HD + 1] = l[h];
+                }
+            }
+        }
+    }
+    step_sync();
+    // merge the 16 warps: thread -> (head, dim)
+    float* part = op.part + (size_t)(kvh * S + sidx) * G * (HD + 2);
+    if (has && !dead) {
         for (uint32_t idx = ctid; idx < G * HD; idx += kStepW * 32) {
             const uint32_t h = idx / HD, d = idx % HD;
             float M = -INFINITY;
@@ -633,35 +675,36 @@ __device__ __noinline__ uint32_t step_attn(const StepOp& op, const StepArgs& a, 
                 }
             }
         }
-        if (S > 1) {
-            // the last item of this KV head merges all of its items
-            __threadfence();
-            step_sync();
-            if (ctid == 0) last_item = atomicAdd(op.tickets + kvh, 1u) == S - 1 ? 1 : 0;
-            step_sync();
-            if (last_item) {
-                __threadfence();
-                const float* hp = op.part + (size_t)kvh * S * G * (HD + 2);
-                for (uint32_t idx = ctid; idx < G * HD; idx += kStepW * 32) {
-                    const uint32_t h = idx / HD, d = idx % HD;
-                    float M = -INFINITY;
-                    for (uint32_t s2 = 0; s2 < S; ++s2) M = fmaxf(M, __ldcg(hp + ((size_t)s2 * G + h) * (HD + 2) + HD));
-                    float O = 0.f, Ls = 0.f;
-                    for (uint32_t s2 = 0; s2 < S; ++s2) {
-                        const float* r = hp + ((size_t)s2 * G + h) * (HD + 2);
-                        const float mm = __ldcg(r + HD);
-                        const float wt = mm == -INFINITY ? 0.f : expf(mm - M);
-                        O = fmaf(wt, __ldcg(r + d), O);
-                        Ls = fmaf(wt, __ldcg(r + HD + 1), Ls);
-                    }
-                    op.out[((size_t)kvh * G + h) * HD + d] = O / Ls;
-                }
-                if (ctid == 0) op.tickets[kvh] = 0u;
-            }
-        }
-        step_sync();  // the scratch is reused by the next item
     }
-    return dead_in;
+    if (S > 1) {
+        // the last item of this KV head merges all of its items
+        __shared__ int last_item;
+        __threadfence();
+        step_sync();
+        if (ctid == 0) last_item = (has && !dead) ? (atomicAdd(op.tickets + kvh, 1u) == S - 1 ? 1 : 0) : 0;
+        step_sync();
+        if (last_item) {
+            __threadfence();
+            const float* hp = op.part + (size_t)kvh * S * G * (HD + 2);
+            for (uint32_t idx = ctid; idx < G * HD; idx += kStepW * 32) {
+                const uint32_t h = idx / HD, d = idx % HD;
+                float M = -INFINITY;
+                for (uint32_t s2 = 0; s2 < S; ++s2) M = fmaxf(M, __ldcg(hp + ((size_t)s2 * G + h) * (HD + 2) + HD));
+                float O = 0.f, Ls = 0.f;
+                for (uint32_t s2 = 0; s2 < S; ++s2) {
+                    const float* r = hp + ((size_t)s2 * G + h) * (HD + 2);
+                    const float mm = __ldcg(r + HD);
+                    const float wt = mm == -INFINITY ? 0.f : expf(mm - M);
+                    O = fmaf(wt, __ldcg(r + d), O);
+                    Ls = fmaf(wt, __ldcg(r + HD + 1), Ls);
+                }
+                op.out[((size_t)kvh * G + h) * HD + d] = O / Ls;
+            }
+            if (ctid == 0) op.tickets[kvh] = 0u;
+        }
+    }
+    step_sync();  // the scratch (x region) is reused by the next op
+    return dead ? 1u : 0u;
 }
 
 // -------------------------------------------------------------- kernel --
@@ -716,7 +759,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
         const StepOp& op = op_sh;
         TraceSlot* slot = a.trace ? a.trace + k : nullptr;
         if (ctid == 0) trace_mark(slot, 0);
-        if (op.wait) {  // CTA-uniform condition: every thread reaches the barrier below
+        if (op.wait && op.kind != SOP_ATTN) {  // CTA-uniform: every thread reaches the barrier below
             if (ctid == 0 && !dead && !grid_wait(a.bar, nsig * gridDim.x, a.abort_flag)) {
                 cta_dead = 1;
                 step_raise(a);
@@ -748,10 +791,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
                 }
             }
         } else if (op.kind == SOP_ATTN) {
-            const uint32_t d = dead ? 1u : 0u;
-            if (op.head_dim == 128) step_attn<128>(op, a, sh, warp, lane, d);
-            else if (op.head_dim == 64) step_attn<64>(op, a, sh, warp, lane, d);
-            else step_attn<32>(op, a, sh, warp, lane, d);
+            // takes the op's barrier itself, after loading cached K/V rows
+            const uint32_t d = dead ? 1u : 0u, target = nsig * gridDim.x;
+            uint32_t r;
+            if (op.head_dim == 128) r = step_attn<128>(op, a, sh, warp, lane, d, target, &cta_dead);
+            else if (op.head_dim == 64) r = step_attn<64>(op, a, sh, warp, lane, d, target, &cta_dead);
+            else r = step_attn<32>(op, a, sh, warp, lane, d, target, &cta_dead);
+            dead = r != 0u;
         } else if (op.kind == SOP_EMBED && !dead) {
             uint32_t tok = a.st->token;
             if (tok >= op.emb.rows) tok = 0;  // the host validates ids; never read outside the table
@@ -852,12 +898,15 @@ void Model::build_step() {
 
     // piece geometry of a matrix: WS warps per row, RS row slots, RPT rows
     // per slot (R = RS * RPT rows per piece, even, at most 64, a piece at most
-    // a third of the ring)
+    // `cap` bytes: 40 KB, or SMALLM_STEP_PIECE_KB, and a third of the ring)
+    size_t cap = ring / 3;
+    if (const char* e = std::getenv("SMALLM_STEP_PIECE_KB")) cap = std::min(cap, (size_t)std::atoi(e) * 1024);
+    else cap = std::min(cap, (size_t)40 * 1024);
     auto geometry = [&](const QMat& m, StepOp& op) {
         const uint32_t WS = (m.units + 31) / 32;
         uint32_t RS = kStepW / WS;
         uint32_t rpt = 4;
-        while (rpt > 1 && ((size_t)RS * rpt * m.row_stride > ring / 3 || RS * rpt > kStepPartRows)) rpt /= 2;
+        while (rpt > 1 && ((size_t)RS * rpt * m.row_stride > cap || RS * rpt > kStepPartRows)) rpt /= 2;
         if ((RS * rpt) % 2) {
             if (rpt < 4 && (size_t)RS * rpt * 2 * m.row_stride <= ring / 3 && RS * rpt * 2 <= kStepPartRows) rpt *= 2;
             else RS -= 1;  // RS >= 2 here (RS * rpt odd with rpt = 1 needs RS odd and > 1, or RS = 1, rpt = 1)
