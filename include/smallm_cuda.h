@@ -319,7 +319,13 @@ const float* smallm_model_logits_device(smallm_model* m);
  * start of the kernel's first CTA, first CTA past its wait on the previous
  * kernel, end of its last CTA (ns, relative to the first record's start),
  * and a kind code (1 embed, 2 QKV, 3 V, 4 attention, 5 O, 6 gate/up,
- * 7 down, 8 lm_head, 9 finalize).  *n receives the number of kernels. */
+ * 7 down, 8 lm_head, 9 finalize).  *n receives the number of kernels.
+ * When the model runs the persistent step (one kernel per step), there is one
+ * record per op of that kernel instead (earliest CTA at the op, earliest CTA
+ * past its barrier, latest CTA done), followed by CTA 0's weight pieces: kind
+ * 1000 records hold (copy started, data seen in shared memory, piece
+ * retired) and the kind 1001 record after each holds, as its start, the time
+ * the piece's last warp finished it. */
 int smallm_model_trace_step(smallm_model* m, uint32_t token, uint32_t pos, uint64_t* out, uint32_t cap,
                             uint32_t* n);
 

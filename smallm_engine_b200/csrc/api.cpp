@@ -1,6 +1,7 @@
 // extern "C" entry points of include/smallm_cuda.h.
 #include <nccl.h>
 
+#include <algorithm>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -559,7 +560,8 @@ int smallm_model_trace_step(smallm_model* m, uint32_t token, uint32_t pos, uint6
         std::vector<smallm::TraceSlot> t;
         m->m.trace_step(token, pos, t);
         *n = (uint32_t)t.size();
-        const uint64_t t0 = t.empty() ? 0 : t[0].t_start;
+        uint64_t t0 = t.empty() ? 0 : t[0].t_start;
+        for (const auto& r : t) t0 = std::min<uint64_t>(t0, r.t_start);
         for (uint32_t i = 0; i < t.size() && i < cap; ++i) {
             out[4 * i] = t[i].t_start - t0;
             out[4 * i + 1] = t[i].t_ready - t0;

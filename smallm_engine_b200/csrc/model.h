@@ -118,9 +118,11 @@ struct Model {
     std::string step_unsupported() const;
     void alloc_step_buffers();
     void build_step();
-    void launch_step(cudaStream_t s, TraceSlot* trace = nullptr);
+    void launch_step(cudaStream_t s, TraceSlot* trace = nullptr, unsigned long long* pieces = nullptr,
+                     uint32_t piece_cap = 0);
     void trace_step_persistent(uint32_t token, uint32_t pos, std::vector<TraceSlot>& out);
     TraceSlot* trace_dev_step = nullptr;
+    unsigned long long* trace_dev_pieces = nullptr;
     void reset_step_state();
     uint32_t step_launch_count() const;
     void trace_step(uint32_t token, uint32_t pos, std::vector<TraceSlot>& out);

@@ -113,6 +113,8 @@ struct StepArgs {
     unsigned int* err;         // device error word
     uint32_t xbytes, ring_bytes;
     TraceSlot* trace;          // [nops] in a traced step, else null
+    unsigned long long* pieces;  // traced step: CTA 0's pieces [piece_cap][4], else null
+    uint32_t piece_cap;
 };
 
 // ------------------------------------------------------------- waiting --
@@ -234,6 +236,7 @@ __device__ void ring_issue(const StepArgs& a, const StepShared& sh) {
         const uint32_t s = r.issued % kStepSlots;
         r.pstart[s] = off;
         r.head = off + bytes;
+        if (a.pieces && blockIdx.x == 0 && r.issued < a.piece_cap) a.pieces[4 * r.issued] = global_ns();
         mbar_arrive_expect_tx(&sh.full[s], bytes);
         bulk_g2s(sh.ring + off, r.w + (size_t)r.p * R * stride, bytes, &sh.full[s]);
         ++r.issued;
@@ -429,6 +432,9 @@ __device__ __noinline__ PieceCursor step_gemv(const StepOp& op, const StepArgs& 
             step_raise(a);
         }
         dead = __any_sync(0xffffffffu, dead);  // warp-uniform (the shuffles below)
+        const bool stamp = a.pieces && blockIdx.x == 0 && lane == 0 && (uint32_t)warp == j % kStepW &&
+                           j < a.piece_cap;
+        if (stamp) a.pieces[4 * j + 1] = global_ns();
         float acc[RPT];
 #pragma unroll
         for (int k = 0; k < RPT; ++k) acc[k] = 0.f;
@@ -464,6 +470,7 @@ __device__ __noinline__ PieceCursor step_gemv(const StepOp& op, const StepArgs& 
                 step_raise(a);
             }
             dead = __any_sync(0xffffffffu, dead);
+            if (stamp) a.pieces[4 * j + 2] = global_ns();
 #pragma unroll
             for (int ib = 0; ib < 2; ++ib) {
                 if ((uint32_t)ib * 32 >= R) break;  // uniform
@@ -480,6 +487,7 @@ __device__ __noinline__ PieceCursor step_gemv(const StepOp& op, const StepArgs& 
                 dead = true;
                 step_raise(a);
             }
+            if (stamp) a.pieces[4 * j + 3] = global_ns();
             dead = __shfl_sync(0xffffffffu, dead ? 1 : 0, 0) != 0;
         }
     }
@@ -1068,7 +1076,7 @@ void Model::alloc_step_buffers() {
     SM_CUDA(cudaMemsetAsync(step_bar, 0, 64, stream));
 }
 
-void Model::launch_step(cudaStream_t s, TraceSlot* trace) {
+void Model::launch_step(cudaStream_t s, TraceSlot* trace, unsigned long long* pieces, uint32_t piece_cap) {
     StepArgs a;
     a.ops = step_ops;
     a.nops = step_nops;
@@ -1082,6 +1090,8 @@ void Model::launch_step(cudaStream_t s, TraceSlot* trace) {
     a.xbytes = step_xbytes;
     a.ring_bytes = step_ring;
     a.trace = trace;
+    a.pieces = pieces;
+    a.piece_cap = piece_cap;
     void* args[] = {&a};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(step_grid);
@@ -1100,22 +1110,33 @@ void Model::launch_step(cudaStream_t s, TraceSlot* trace) {
 // the op's start, earliest past its barrier wait, latest at its end); the
 // slots' kind codes follow the per-op kernels' trace kinds.
 void Model::trace_step_persistent(uint32_t token, uint32_t pos, std::vector<TraceSlot>& out) {
-    if (!trace_dev_step) trace_dev_step = static_cast<TraceSlot*>(dalloc(sizeof(TraceSlot) * step_nops));
+    constexpr uint32_t kPieceCap = 8192;
+    if (!trace_dev_step) {
+        trace_dev_step = static_cast<TraceSlot*>(dalloc(sizeof(TraceSlot) * step_nops));
+        trace_dev_pieces = static_cast<unsigned long long*>(dalloc(32ull * kPieceCap));
+    }
     std::vector<StepOp> ops(step_nops);
     SM_CUDA(cudaMemcpy(ops.data(), step_ops, sizeof(StepOp) * step_nops, cudaMemcpyDeviceToHost));
     std::vector<TraceSlot> init(step_nops);
     for (uint32_t k = 0; k < step_nops; ++k) init[k] = TraceSlot{~0ull, ~0ull, 0ull, ops[k].trace_kind};
     SM_CUDA(cudaMemcpyAsync(trace_dev_step, init.data(), sizeof(TraceSlot) * step_nops, cudaMemcpyHostToDevice,
                             stream));
+    SM_CUDA(cudaMemsetAsync(trace_dev_pieces, 0, 32ull * kPieceCap, stream));
     set_state(token, pos);
-    launch_step(stream, trace_dev_step);
+    launch_step(stream, trace_dev_step, trace_dev_pieces, kPieceCap);
     out.resize(step_nops);
+    std::vector<unsigned long long> pc(4ull * kPieceCap);
     SM_CUDA(cudaMemcpyAsync(out.data(), trace_dev_step, sizeof(TraceSlot) * step_nops, cudaMemcpyDeviceToHost,
                             stream));
+    SM_CUDA(cudaMemcpyAsync(pc.data(), trace_dev_pieces, 32ull * kPieceCap, cudaMemcpyDeviceToHost, stream));
     SM_CUDA(cudaMemcpyAsync(h_err, device_error_flag(), 4, cudaMemcpyDeviceToHost, stream));
     SM_CUDA(cudaStreamSynchronize(stream));
     check_step_errors();
     cached = pos + 1;
+    for (uint32_t j = 0; j < kPieceCap && pc[4 * j]; ++j) {
+        out.push_back(TraceSlot{pc[4 * j], pc[4 * j + 1], pc[4 * j + 3], 1000});
+        out.push_back(TraceSlot{pc[4 * j + 2], pc[4 * j + 2], pc[4 * j + 2], 1001});
+    }
 }
 
 uint32_t Model::step_launch_count() const {

@@ -119,11 +119,11 @@ class CudaModel:
         return lib().smallm_model_logits_device(self.h) or 0
 
     TRACE_KINDS = {1: "embed", 2: "qkv", 3: "v", 4: "attention", 5: "o", 6: "gate_up", 7: "down",
-                   8: "lm_head", 9: "finalize"}
+                   8: "lm_head", 9: "finalize", 1000: "piece", 1001: "piece_done"}
 
     def trace_step(self, token: int, pos: int) -> list[dict]:
         """One step with GPU timestamps per kernel (ns from the step start)."""
-        cap = 16 + 6 * self._config.n_layers
+        cap = 16 + 6 * self._config.n_layers + 2 * 8192  # persistent step: ops, then CTA 0's pieces
         buf = np.zeros(4 * cap, dtype=np.uint64)
         n = ctypes.c_uint32()
         check(lib().smallm_model_trace_step(self.h, int(token), int(pos), buf.ctypes.data, cap, ctypes.byref(n)))

@@ -45,6 +45,21 @@ def main(argv=None):
         tok = int(np.argmax(m.forward(tok, pos - 1)))  # keep the cache consistent; feed greedy
         steps.append(tr)
         prev_end = 0
+        pieces = [k for k in tr if k["kind"] in ("piece", "piece_done")]
+        tr = [k for k in tr if k["kind"] not in ("piece", "piece_done")]
+        steps[-1] = tr
+        if pieces:
+            # CTA 0's weight pieces: copy latency (start -> data seen), time to
+            # the last warp's finish, and to retirement
+            lat = [p["ready"] - p["start"] for p in pieces if p["kind"] == "piece"]
+            ends = [p["end"] for p in pieces if p["kind"] == "piece"]
+            dn = [p["start"] for p in pieces if p["kind"] == "piece_done"]
+            rd = [p["ready"] for p in pieces if p["kind"] == "piece"]
+            agg.setdefault("_pieces", []).append({
+                "n": len(lat), "copy_to_seen_us": float(np.median(lat)) / 1e3,
+                "seen_to_done_us": float(np.median(np.array(dn) - np.array(rd))) / 1e3,
+                "done_to_retired_us": float(np.median(np.array(ends) - np.array(dn))) / 1e3,
+                "interval_us": float(np.median(np.diff(ends))) / 1e3 if len(ends) > 1 else None})
         for k in tr:
             d = agg.setdefault(k["kind"], {"n": 0, "dur": 0.0, "wait": 0.0, "gap": 0.0})
             d["n"] += 1
@@ -54,6 +69,8 @@ def main(argv=None):
             prev_end = k["end"]
     step_ns = np.mean([s[-1]["end"] for s in steps])
     out = {"workload": a.workload, "prompt": a.prompt, "step_us": step_ns / 1e3, "kernels": {}}
+    if "_pieces" in agg:
+        out["pieces_cta0"] = agg.pop("_pieces")[-1]
     for kind, d in agg.items():
         out["kernels"][kind] = {"per_step": d["n"] / a.steps, "mean_us": d["dur"] / d["n"] / 1e3,
                                 "mean_wait_us": d["wait"] / d["n"] / 1e3, "mean_gap_us": d["gap"] / d["n"] / 1e3,
