@@ -140,3 +140,118 @@ def test_tp_model_matches_oracle(orc, gguf_dir, ws):
         pos += 1
         n = int(np.argmax(l))
         assert int(dev_ids[k]) == n
+
+
+# ---------------------------------------------------- sharded math on CPU --
+
+def _dequant_model(path):
+    """All weights of a GGUF as float64 arrays (rows x cols), via the oracle's
+    exact dequantisation."""
+    import oracle as O
+    orc = O.Oracle()
+    g = O.GGUFFile(path)
+
+    def deq(name, shape=None):
+        dims, t, _ = g.info(name)
+        v = orc.dequantize(t, g.raw(name), int(np.prod(dims))).astype(np.float64)
+        return v.reshape(dims[::-1]) if shape is None else v.reshape(shape)
+    return g, deq
+
+
+def _rope(x, n_heads, hd, pos, base):
+    """NeoX rotation of (i, i + hd/2) per head (ops::rope, src/core/ops.cpp:68-92)."""
+    half = hd // 2
+    i = np.arange(half)
+    ang = pos * (1.0 / np.power(base, 2.0 * i / hd))
+    c, s = np.cos(ang), np.sin(ang)
+    x = x.reshape(n_heads, hd).copy()
+    a, b = x[:, :half].copy(), x[:, half:].copy()
+    x[:, :half] = a * c - b * s
+    x[:, half:] = a * s + b * c
+    return x.ravel()
+
+
+def _tp_forward(path, spec, tp_size, tokens):
+    """The tensor-parallel decode step as the library splits it (tp_plan):
+    each rank runs its heads, FFN rows and vocabulary rows on its own shard of
+    the weights; the row-parallel O and down partials are summed over ranks in
+    rank order (the all-reduce) and the logits shards concatenated.  float64
+    throughout.  Returns the logits after each token."""
+    _, deq = _dequant_model(path)
+    e, hd, nh, nkv, f, V = spec.embd, spec.head_dim, spec.heads, spec.kv_heads, spec.ffn, spec.vocab
+    G = nh // nkv
+    shards = [tp.tp_plan(nh, nkv, f, V, tp_size, r) for r in range(tp_size)]
+    emb = deq("token_embd.weight")
+    out_w, out_n = deq("output.weight"), deq("output_norm.weight")
+    L = []
+    for i in range(spec.layers):
+        p = f"blk.{i}."
+        L.append({k: deq(p + k + ".weight") for k in ("attn_norm", "ffn_norm", "attn_q", "attn_k", "attn_v",
+                                                       "attn_output", "ffn_gate", "ffn_up", "ffn_down")})
+    eps = float(np.float32(spec.eps))
+    kc = [[np.zeros((spec.ctx, nkv * hd)) for _ in range(spec.layers)] for _ in range(tp_size)]
+    vc = [[np.zeros((spec.ctx, nkv * hd)) for _ in range(spec.layers)] for _ in range(tp_size)]
+
+    def rms(x, w):
+        return x / np.sqrt(np.mean(x * x) + eps) * w
+
+    outs = []
+    for pos, tok in enumerate(tokens):
+        x = emb[tok].copy()
+        for li, W in enumerate(L):
+            xn = rms(x, W["attn_norm"])
+            parts = []
+            for r, sh in enumerate(shards):
+                h0, h1 = sh.heads
+                g0, g1 = sh.kv_heads
+                q = _rope(W["attn_q"][h0 * hd:h1 * hd] @ xn, h1 - h0, hd, pos, spec.rope_base)
+                k = _rope(W["attn_k"][g0 * hd:g1 * hd] @ xn, g1 - g0, hd, pos, spec.rope_base)
+                v = W["attn_v"][g0 * hd:g1 * hd] @ xn
+                kc[r][li][pos, :(g1 - g0) * hd] = k
+                vc[r][li][pos, :(g1 - g0) * hd] = v
+                att = np.zeros((h1 - h0) * hd)
+                for h in range(h1 - h0):
+                    g = h // G
+                    K = kc[r][li][:pos + 1, g * hd:(g + 1) * hd]
+                    Vv = vc[r][li][:pos + 1, g * hd:(g + 1) * hd]
+                    sc = K @ q[h * hd:(h + 1) * hd] / np.sqrt(hd)
+                    pr = np.exp(sc - sc.max())
+                    att[h * hd:(h + 1) * hd] = (pr / pr.sum()) @ Vv
+                parts.append(W["attn_output"][:, h0 * hd:h1 * hd] @ att)  # row-parallel O
+            for pt in parts:  # all-reduce, rank order
+                x = x + pt
+            xn = rms(x, W["ffn_norm"])
+            parts = []
+            for sh in shards:
+                a, b = sh.ffn_rows
+                gate = W["ffn_gate"][a:b] @ xn
+                up = W["ffn_up"][a:b] @ xn
+                hh = gate / (1.0 + np.exp(-gate)) * up
+                parts.append(W["ffn_down"][:, a:b] @ hh)  # row-parallel down
+            for pt in parts:
+                x = x + pt
+        xn = rms(x, out_n)
+        outs.append(np.concatenate([out_w[sh.vocab_rows[0]:sh.vocab_rows[1]] @ xn for sh in shards]))
+    return outs
+
+
+@pytest.mark.parametrize("tp_size", [1, 2, 4, 8])
+def test_tp_sharded_math_matches_oracle(tmp_path, tp_size):
+    """The split the library runs under tensor parallelism (column-parallel
+    Q/K/V by head and gate/up by FFN row, row-parallel O and down summed over
+    ranks, vocab-parallel lm_head), restated in numpy on a tiny GQA model and
+    run shard by shard, gives the oracle's logits (the reference's single-
+    process forward, src/model/llama_model.cpp:148-177) to f32 rounding, with
+    the same greedy ids."""
+    import oracle as O
+    from smallm_engine_b200 import synth
+    spec = synth.tiny_spec("llama-q4_0", embd=512, heads=16, kv_heads=8, ffn=1024, vocab=392, ctx=32,
+                           name="tiny-llama-q4_0-tp")
+    path = synth.write_gguf(spec, 17, tmp_path / "tp-emu.gguf")
+    toks = [int(t) for t in np.random.default_rng(17).integers(0, spec.vocab, size=6)]
+    got = _tp_forward(path, spec, tp_size, toks)
+    ref = O.OracleModel(path)
+    for pos, t in enumerate(toks):
+        want = ref.forward(t, pos).astype(np.float64)
+        assert np.abs(got[pos] - want).max() <= 1e-4 * np.abs(want).max(), pos
+        assert int(np.argmax(got[pos])) == int(np.argmax(want))
