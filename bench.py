@@ -435,7 +435,9 @@ def our_arm(args, ws, rank, local):
             "step_roofline": {"bytes_per_token": bytes_tok, "achieved_gbs_per_gpu": step_gbs,
                               "frac": step_gbs / peak, "note": "weights + f32 KV at mid position; "
                               "per-GPU share under tensor parallelism"},
-            "gpu_launches": args.steps * (1 + 5 * cfg.n_layers + 2),
+            "gpu_launches": args.steps * cfg.step_launches,
+            "step_path": "persistent step kernel (one cooperative launch per token)" if cfg.step_launches == 1
+                         else f"per-op kernels ({cfg.step_launches} launches per token)",
             "clocks": clk.summary(),
             "greedy_ids_head": head[:8],
         }
