@@ -257,6 +257,7 @@ __device__ __forceinline__ float combine(int s0, int s1, int s2) {
 // and the three digits are joined in float (the record's scale carries 1/16).
 struct FmtQ4_0 {
     static constexpr int UE = 32, SUBS = 1, WIDE = 22, XK = XK_NIB_SD;
+    static constexpr int STEP_RPT = 4;  // rows per thread and piece in the persistent step
     static constexpr bool F32X = false;
     struct Raw { uint4 q; uint32_t s; };
     __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t units, Raw& r) {
@@ -286,6 +287,7 @@ struct FmtQ4_0 {
 // Q8_0: int8 codes; value q * d.
 struct FmtQ8_0 {
     static constexpr int UE = 32, SUBS = 1, WIDE = 16, XK = XK_PLAIN;
+    static constexpr int STEP_RPT = 2;  // rows per thread and piece in the persistent step (registers)
     static constexpr bool F32X = false;
     struct Raw { uint4 a, b; uint32_t s; };
     __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t units, Raw& r) {

@@ -181,6 +181,8 @@ __device__ __forceinline__ void step_sync() { __syncthreads(); }
 struct StepRing {
     uint32_t retired;  // pieces whose space is free again
     uint32_t issued;   // pieces whose copy has been started
+    uint32_t lock;     // held by the lane retiring pieces and issuing copies
+    uint32_t freed[kStepSlots];  // j + 1 once piece j (slot j % kStepSlots) is done with
     uint32_t head;     // ring offset just past the newest issued piece
     uint32_t op, p;    // next piece to issue: op index and piece index
     // geometry of op `op` (read from global memory once per op)
@@ -244,21 +246,33 @@ __device__ void ring_issue(const StepArgs& a, const StepShared& sh) {
     }
 }
 
-// Piece j is done (every warp has read it): wait for the retire turn, free its
-// space, issue what now fits, pass the turn on.  One lane.
-__device__ bool ring_retire(const StepArgs& a, const StepShared& sh, uint32_t j) {
-    volatile uint32_t* ret = &sh.rs->retired;
-    const long long t0 = clock64();
-    long long next = kAbortLookAfter;
-    while (*ret != j) {
-        const long long waited = clock64() - t0;
-        if (waited > kGiveUp || abort_seen(a.abort_flag, waited, next)) return false;
+// Piece j is done (every warp has read it, its epilogue has run): mark it, then
+// retire every piece that is done, in order, and issue the copies that now
+// fit -- unless another lane holds the lock, in which case that lane picks the
+// mark up (it looks again after unlocking).  One lane; never waits.
+__device__ void ring_retire(const StepArgs& a, const StepShared& sh, uint32_t j) {
+    StepRing& r = *sh.rs;
+    volatile uint32_t* fr = r.freed;
+    __threadfence_block();
+    fr[j % kStepSlots] = j + 1;
+    for (;;) {
+        __threadfence_block();
+        if (atomicCAS(&r.lock, 0u, 1u) != 0u) return;
+        __threadfence_block();
+        const uint32_t before = *(volatile uint32_t*)&r.retired;
+        uint32_t q = before;
+        while (fr[q % kStepSlots] == q + 1) ++q;
+        if (q != before) {
+            *(volatile uint32_t*)&r.retired = q;
+            ring_issue(a, sh);
+        }
+        __threadfence_block();
+        atomicExch(&r.lock, 0u);
+        __threadfence_block();
+        // a mark set while the lock was held is not lost: its lane failed to
+        // take the lock after setting it, so this read sees it
+        if (fr[q % kStepSlots] != q + 1) return;
     }
-    __threadfence_block();
-    sh.rs->retired = j + 1;
-    ring_issue(a, sh);
-    __threadfence_block();
-    return true;
 }
 
 // x -> three-digit records of every 32-element block (times the norm weight
@@ -403,22 +417,21 @@ struct PieceCursor {
     unsigned long long best;
 };
 
-// One GEMV op.  Not inlined: each op variant gets its own register
-// allocation (the kernel holds six of them plus the attention).
-template <class Fmt, int RPT>
-__device__ __noinline__ PieceCursor step_gemv(const StepOp& op, const StepArgs& a, const StepShared sh, int warp,
-                                              int lane, PieceCursor cur) {
+// One GEMV op (rows per slot op.rpt <= 4: the row loop and the shuffle
+// reduction run for 4 rows, the missing ones as zeros).
+template <class Fmt>
+__device__ __forceinline__ PieceCursor step_gemv(const StepOp& op, const StepArgs& a, const StepShared& sh,
+                                                 int warp, int lane, PieceCursor cur) {
+    constexpr int RPT = Fmt::STEP_RPT;  // rows per slot at most (register budget)
     uint32_t j = cur.j, head = cur.head;
     bool dead = cur.dead != 0;
     unsigned long long best = cur.best;
     const float inv = step_stage_x<Fmt>(op, sh, warp, lane);
-    const uint32_t U = op.units, WS = op.ws, RS = op.rs, R = op.prows, stride = op.row_stride;
+    const uint32_t U = op.units, WS = op.ws, RS = op.rs, R = op.prows, stride = op.row_stride, rpt = op.rpt;
     const uint32_t slot = (uint32_t)warp / WS, wi = (uint32_t)warp % WS;
     const bool active = slot < RS;
     const uint32_t u = wi * 32 + (uint32_t)lane;
     const bool uact = active && u < U;
-    XRec xr;
-    if (uact) load_xrec(sh.xreg, u, xr);
     const uint32_t pos_op = op.epi == EPI_QKV ? *op.pos : 0u;  // the step's position (RoPE row)
     constexpr int LPR = 32 / RPT;
     for (uint32_t p = blockIdx.x; p < op.npieces; p += gridDim.x, ++j) {
@@ -439,11 +452,15 @@ __device__ __noinline__ PieceCursor step_gemv(const StepOp& op, const StepArgs& 
 #pragma unroll
         for (int k = 0; k < RPT; ++k) acc[k] = 0.f;
         if (uact && !dead) {
-            const uint32_t r0 = slot * RPT;
+            // this thread's unit of x (three-digit record), from shared memory
+            // per piece rather than held across the epilogue (registers)
+            XRec xr;
+            load_xrec(sh.xreg, u, xr);
+            const uint32_t r0 = slot * rpt;
             const uint8_t* base = sh.ring + off + (size_t)r0 * stride;
 #pragma unroll
             for (int k = 0; k < RPT; ++k) {
-                if (r0 + k < rows_here) {
+                if ((uint32_t)k < rpt && r0 + k < rows_here) {
                     typename Fmt::Raw raw;
                     Fmt::load(base + (size_t)k * stride, u, U, raw);
                     acc[k] = Fmt::dot(raw, 0, xr, u);
@@ -452,8 +469,8 @@ __device__ __noinline__ PieceCursor step_gemv(const StepOp& op, const StepArgs& 
         }
         // lanes k*LPR .. k*LPR + LPR-1 end with this warp's part of row k
         const float v = warp_reduce_rows<RPT>(acc, lane);
-        if (active && (lane % LPR) == 0)
-            sh.part[s * kStepPartRows + (slot * RPT + (uint32_t)lane / LPR) * WS + wi] = v;
+        if (active && (lane % LPR) == 0 && (uint32_t)lane / LPR < rpt)
+            sh.part[s * kStepPartRows + (slot * rpt + (uint32_t)lane / LPR) * WS + wi] = v;
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh.done[s]);
         if ((uint32_t)warp == j % kStepW) {
@@ -483,10 +500,7 @@ __device__ __noinline__ PieceCursor step_gemv(const StepOp& op, const StepArgs& 
                 if (r < rows_here && !dead) step_epilogue(op, p * R + r, val, v_next, pre[ib], best);
             }
             __syncwarp();
-            if (lane == 0 && !dead && !ring_retire(a, sh, j)) {
-                dead = true;
-                step_raise(a);
-            }
+            if (lane == 0 && !dead) ring_retire(a, sh, j);
             if (stamp) a.pieces[4 * j + 3] = global_ns();
             dead = __shfl_sync(0xffffffffu, dead ? 1 : 0, 0) != 0;
         }
@@ -494,13 +508,6 @@ __device__ __noinline__ PieceCursor step_gemv(const StepOp& op, const StepArgs& 
     return PieceCursor{j, head, dead ? 1u : 0u, best};
 }
 
-template <class Fmt>
-__device__ __forceinline__ PieceCursor step_gemv_fmt(const StepOp& op, const StepArgs& a, const StepShared& sh,
-                                                     int warp, int lane, PieceCursor cur) {
-    if (op.rpt == 4) return step_gemv<Fmt, 4>(op, a, sh, warp, lane, cur);
-    if (op.rpt == 2) return step_gemv<Fmt, 2>(op, a, sh, warp, lane, cur);
-    return step_gemv<Fmt, 1>(op, a, sh, warp, lane, cur);
-}
 
 // ----------------------------------------------------------- attention --
 
@@ -523,7 +530,7 @@ __device__ __forceinline__ void attn_merge(float& m, float& l, float4& o, float 
 // K/V rows (every position but the newest, which this step's QKV op writes)
 // is loaded before it, so that latency overlaps the wait.
 template <int HD>
-__device__ __noinline__ uint32_t step_attn(const StepOp& op, const StepArgs& a, const StepShared sh, int warp,
+__device__ __forceinline__ uint32_t step_attn(const StepOp& op, const StepArgs& a, const StepShared& sh, int warp,
                                            int lane, uint32_t dead_in, uint32_t target, int* cta_dead) {
     constexpr int RPI = 128 / HD;            // positions per warp instruction (sub-warps)
     constexpr int LPR = 32 / RPI;            // lanes per position: 4 dims each
@@ -717,8 +724,8 @@ __device__ __noinline__ uint32_t step_attn(const StepOp& op, const StepArgs& a, 
 
 // -------------------------------------------------------------- kernel --
 
-template <class FA, class FB>
-__global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const StepArgs a) {
+template <class FA, class FB, int HD>
+__global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const StepArgs args) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[kStepSlots], done[kStepSlots];
     __shared__ float part[kStepSlots * kStepPartRows];
@@ -728,15 +735,24 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
     __shared__ __align__(16) StepOp op_sh;
     __shared__ int cta_dead;  // some wait of this CTA gave up (read after a barrier: CTA-uniform)
 
+    // The arguments and the shared-memory map live in shared memory: the
+    // non-inlined op functions take them by reference, and a per-thread copy
+    // would sit in local memory, which the ~29 KB of L1 left beside the ring
+    // cannot hold.
+    __shared__ StepArgs a;
+    __shared__ StepShared sh;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    StepShared sh;
-    sh.full = full;
-    sh.done = done;
-    sh.part = part;
-    sh.red = red;
-    sh.xreg = smem;
-    sh.ring = smem + a.xbytes;
-    sh.rs = &ring_state;
+    if (tid == 0) {
+        a = args;
+        sh.full = full;
+        sh.done = done;
+        sh.part = part;
+        sh.red = red;
+        sh.xreg = smem;
+        sh.ring = smem + args.xbytes;
+        sh.rs = &ring_state;
+    }
+    __syncthreads();
     if (tid == 0) {
         for (uint32_t s = 0; s < kStepSlots; ++s) {
             mbar_init(&full[s], 1);
@@ -744,6 +760,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         ring_state.retired = ring_state.issued = ring_state.head = 0u;
+        ring_state.lock = 0u;
+        for (uint32_t q = 0; q < kStepSlots; ++q) ring_state.freed[q] = 0u;
         ring_state.op = 0u;
         ring_state.p = blockIdx.x;
         ring_load_op(a, ring_state);
@@ -778,8 +796,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
         if (ctid == 0) trace_mark(slot, 1);
         if (op.kind == SOP_GEMV) {
             PieceCursor cur{j, head, dead ? 1u : 0u, 0ull};
-            cur = op.fmt == 0 ? step_gemv_fmt<FA>(op, a, sh, warp, lane, cur)
-                              : step_gemv_fmt<FB>(op, a, sh, warp, lane, cur);
+            if (op.fmt == 0) cur = step_gemv<FA>(op, a, sh, warp, lane, cur);
+            else cur = step_gemv<FB>(op, a, sh, warp, lane, cur);
             j = cur.j;
             head = cur.head;
             dead = cur.dead != 0;
@@ -801,11 +819,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
         } else if (op.kind == SOP_ATTN) {
             // takes the op's barrier itself, after loading cached K/V rows
             const uint32_t d = dead ? 1u : 0u, target = nsig * gridDim.x;
-            uint32_t r;
-            if (op.head_dim == 128) r = step_attn<128>(op, a, sh, warp, lane, d, target, &cta_dead);
-            else if (op.head_dim == 64) r = step_attn<64>(op, a, sh, warp, lane, d, target, &cta_dead);
-            else r = step_attn<32>(op, a, sh, warp, lane, d, target, &cta_dead);
-            dead = r != 0u;
+            dead = step_attn<HD>(op, a, sh, warp, lane, d, target, &cta_dead) != 0u;
         } else if (op.kind == SOP_EMBED && !dead) {
             uint32_t tok = a.st->token;
             if (tok >= op.emb.rows) tok = 0;  // the host validates ids; never read outside the table
@@ -850,11 +864,19 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
 
 // ---------------------------------------------------------------- host --
 
-static const void* step_kernel_for(uint32_t fa, uint32_t fb) {
-    if (fa == SM_T_Q4_0 && fb == SM_T_Q8_0) return (const void*)smallm_step_kernel<FmtQ4_0, FmtQ8_0>;
-    if (fa == SM_T_Q8_0 && fb == SM_T_Q8_0) return (const void*)smallm_step_kernel<FmtQ8_0, FmtQ8_0>;
-    if (fa == SM_T_Q4_0 && fb == SM_T_Q4_0) return (const void*)smallm_step_kernel<FmtQ4_0, FmtQ4_0>;
-    if (fa == SM_T_Q8_0 && fb == SM_T_Q4_0) return (const void*)smallm_step_kernel<FmtQ8_0, FmtQ4_0>;
+template <int HD>
+static const void* step_kernel_hd(uint32_t fa, uint32_t fb) {
+    if (fa == SM_T_Q4_0 && fb == SM_T_Q8_0) return (const void*)smallm_step_kernel<FmtQ4_0, FmtQ8_0, HD>;
+    if (fa == SM_T_Q8_0 && fb == SM_T_Q8_0) return (const void*)smallm_step_kernel<FmtQ8_0, FmtQ8_0, HD>;
+    if (fa == SM_T_Q4_0 && fb == SM_T_Q4_0) return (const void*)smallm_step_kernel<FmtQ4_0, FmtQ4_0, HD>;
+    if (fa == SM_T_Q8_0 && fb == SM_T_Q4_0) return (const void*)smallm_step_kernel<FmtQ8_0, FmtQ4_0, HD>;
+    return nullptr;
+}
+
+static const void* step_kernel_for(uint32_t fa, uint32_t fb, uint32_t hd) {
+    if (hd == 128) return step_kernel_hd<128>(fa, fb);
+    if (hd == 64) return step_kernel_hd<64>(fa, fb);
+    if (hd == 32) return step_kernel_hd<32>(fa, fb);
     return nullptr;
 }
 
@@ -868,7 +890,7 @@ std::string Model::step_unsupported() const {
         for (const QMat* m : {&L.qkv, &L.o, &L.gu, &L.down})
             if (m->type != fa) return "mixed layer formats";
     }
-    if (!step_kernel_for(fa, out_m.type)) return "weight formats";
+    if (!step_kernel_for(fa, out_m.type, hd)) return "weight formats or head_dim";
     if (embd_m.type != SM_T_Q4_0 && embd_m.type != SM_T_Q8_0 && embd_m.type != SM_T_F32 && embd_m.type != SM_T_Q4_K &&
         embd_m.type != SM_T_Q6_K)
         return "embedding format";
@@ -884,7 +906,7 @@ void Model::build_step() {
     step_on = false;
     step_why = step_unsupported();
     if (!step_why.empty()) return;
-    const void* fn = step_kernel_for(layers[0].qkv.type, out_m.type);
+    const void* fn = step_kernel_for(layers[0].qkv.type, out_m.type, hd);
     cudaFuncAttributes fa{};
     SM_CUDA(cudaFuncGetAttributes(&fa, fn));
     int dev = 0, optin = 0;
@@ -913,10 +935,12 @@ void Model::build_step() {
     auto geometry = [&](const QMat& m, StepOp& op) {
         const uint32_t WS = (m.units + 31) / 32;
         uint32_t RS = kStepW / WS;
-        uint32_t rpt = 4;
+        uint32_t rpt = m.type == SM_T_Q4_0 ? FmtQ4_0::STEP_RPT : FmtQ8_0::STEP_RPT;
         while (rpt > 1 && ((size_t)RS * rpt * m.row_stride > cap || RS * rpt > kStepPartRows)) rpt /= 2;
+        const uint32_t rpt_max = m.type == SM_T_Q4_0 ? FmtQ4_0::STEP_RPT : FmtQ8_0::STEP_RPT;
         if ((RS * rpt) % 2) {
-            if (rpt < 4 && (size_t)RS * rpt * 2 * m.row_stride <= ring / 3 && RS * rpt * 2 <= kStepPartRows) rpt *= 2;
+            if (rpt < rpt_max && (size_t)RS * rpt * 2 * m.row_stride <= ring / 3 && RS * rpt * 2 <= kStepPartRows)
+                rpt *= 2;
             else RS -= 1;  // RS >= 2 here (RS * rpt odd with rpt = 1 needs RS odd and > 1, or RS = 1, rpt = 1)
         }
         if (RS == 0 || (RS * rpt) % 2 || (size_t)RS * rpt * m.row_stride > ring / 2)
