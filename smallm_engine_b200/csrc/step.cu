@@ -898,7 +898,9 @@ std::string Model::step_unsupported() const {
     if (nh_l % nkv_l || nh_l / nkv_l > (uint32_t)kStepMaxGroup) return "head grouping";
     for (const QMat* m : {&layers[0].qkv, &layers[0].o, &layers[0].gu, &layers[0].down, &out_m})
         if (m->units > 32u * kStepW) return "rows longer than the step's x registers";
-    if (std::getenv("SMALLM_STEP_KERNELS")) return "disabled by SMALLM_STEP_KERNELS";
+    // opt-in while the per-op kernels are faster on the measured workloads
+    const char* want = std::getenv("SMALLM_STEP");
+    if (!want || std::strcmp(want, "persistent") != 0) return "per-op kernels (SMALLM_STEP=persistent selects it)";
     return "";
 }
 

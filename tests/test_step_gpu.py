@@ -1,12 +1,13 @@
 """The persistent decode step (csrc/step.cu): the whole token step as one
-cooperative kernel, the default for models whose layer matrices share one of
-the 32-element block formats (Q4_0, Q8_0).
+cooperative kernel, for models whose layer matrices share one of the
+32-element block formats (Q4_0, Q8_0); selected at load with
+SMALLM_STEP=persistent.
 
 Checked against the oracle's restatement of the reference's forward pass
 (src/model/qwen2_model.cpp:163-198, src/model/llama_model.cpp:148-177) with
 the model-level bar (logits within 1e-2 * max|logit| per step, observed far
 inside it, and identical greedy ids), and against the per-op kernel path of
-the same library on the same model (SMALLM_STEP_KERNELS set at load)."""
+the same library on the same model (the default at load)."""
 import os
 
 import numpy as np
@@ -19,12 +20,12 @@ pytestmark = pytest.mark.gpu
 
 
 def _load(path, per_op: bool = False, **kw) -> CudaModel:
-    if per_op:
-        os.environ["SMALLM_STEP_KERNELS"] = "1"
+    if not per_op:
+        os.environ["SMALLM_STEP"] = "persistent"
     try:
         return CudaModel(path, **kw)
     finally:
-        os.environ.pop("SMALLM_STEP_KERNELS", None)
+        os.environ.pop("SMALLM_STEP", None)
 
 
 @pytest.mark.parametrize("kind,seed", [("qwen2", 21), ("llama-q4_0", 22)])
