@@ -191,21 +191,31 @@ struct StepRing {
     uint32_t pstart[kStepSlots];  // ring offset of each in-flight piece
 };
 
-struct StepShared {
-    uint64_t* full;
-    uint64_t* done;
-    float* part;
-    float* red;
-    uint8_t* xreg;
-    uint8_t* ring;
-    StepRing* rs;
-};
+// The CTA's shared state, at file scope so every access compiles to a
+// shared-memory instruction (a pointer passed through a struct or a
+// non-inlined call would become a generic one, which waits on the long
+// scoreboard).
+extern __shared__ __align__(128) uint8_t s_dyn[];  // x region (records / attention scratch), then the ring
+__shared__ __align__(8) uint64_t s_full[kStepSlots];  // piece landed in the ring (count 1 + bytes)
+__shared__ __align__(8) uint64_t s_done[kStepSlots];  // every warp finished the piece (count kStepW)
+__shared__ float s_part[kStepSlots * kStepPartRows];  // row partials of each piece in flight
+__shared__ StepRing s_ring;
+__shared__ float s_red[32];
+__shared__ unsigned long long s_best[kStepW];
+// the current op's descriptor (raw storage: StepOp has default member initializers)
+__shared__ __align__(16) unsigned long long s_op_raw[sizeof(StepOp) / 8];
+#define s_op (*reinterpret_cast<StepOp*>(s_op_raw))
+__shared__ StepArgs s_args;
+__shared__ int s_cta_dead;  // some wait of this CTA gave up (read after a barrier: CTA-uniform)
+__shared__ int s_last_item;
+
+__device__ __forceinline__ uint8_t* step_ring() { return s_dyn + s_args.xbytes; }
 
 // Issue the next pieces while a slot is free and the ring has room for them
 // (one lane, holding the retire turn).  Placement: a piece goes right after
 // the newest one, or at offset 0 when it would run past the end; it may not
 // overlap the span [tail, head) of pieces in flight (tail = oldest's start).
-__device__ void ring_load_op(const StepArgs& a, StepRing& r) {
+__device__ __forceinline__ void ring_load_op(const StepArgs& a, StepRing& r) {
     if (r.op >= a.nops) return;
     const StepOp* op = a.ops + r.op;
     r.kind = op->kind;
@@ -216,8 +226,10 @@ __device__ void ring_load_op(const StepArgs& a, StepRing& r) {
     r.w = op->w;
 }
 
-__device__ void ring_issue(const StepArgs& a, const StepShared& sh) {
-    StepRing& r = *sh.rs;
+__device__ __forceinline__ void ring_issue() {
+    const StepArgs& a = s_args;
+    StepRing& r = s_ring;
+    uint8_t* ring = step_ring();
     const uint32_t RB = a.ring_bytes;
     while (r.issued - r.retired < kStepSlots) {
         while (r.op < a.nops && (r.kind != SOP_GEMV || r.p >= r.np)) {
@@ -239,8 +251,8 @@ __device__ void ring_issue(const StepArgs& a, const StepShared& sh) {
         r.pstart[s] = off;
         r.head = off + bytes;
         if (a.pieces && blockIdx.x == 0 && r.issued < a.piece_cap) a.pieces[4 * r.issued] = global_ns();
-        mbar_arrive_expect_tx(&sh.full[s], bytes);
-        bulk_g2s(sh.ring + off, r.w + (size_t)r.p * R * stride, bytes, &sh.full[s]);
+        mbar_arrive_expect_tx(&s_full[s], bytes);
+        bulk_g2s(ring + off, r.w + (size_t)r.p * R * stride, bytes, &s_full[s]);
         ++r.issued;
         r.p += gridDim.x;
     }
@@ -250,8 +262,8 @@ __device__ void ring_issue(const StepArgs& a, const StepShared& sh) {
 // retire every piece that is done, in order, and issue the copies that now
 // fit -- unless another lane holds the lock, in which case that lane picks the
 // mark up (it looks again after unlocking).  One lane; never waits.
-__device__ void ring_retire(const StepArgs& a, const StepShared& sh, uint32_t j) {
-    StepRing& r = *sh.rs;
+__device__ __forceinline__ void ring_retire(uint32_t j) {
+    StepRing& r = s_ring;
     volatile uint32_t* fr = r.freed;
     __threadfence_block();
     fr[j % kStepSlots] = j + 1;
@@ -264,7 +276,7 @@ __device__ void ring_retire(const StepArgs& a, const StepShared& sh, uint32_t j)
         while (fr[q % kStepSlots] == q + 1) ++q;
         if (q != before) {
             *(volatile uint32_t*)&r.retired = q;
-            ring_issue(a, sh);
+            ring_issue();
         }
         __threadfence_block();
         atomicExch(&r.lock, 0u);
@@ -278,7 +290,7 @@ __device__ void ring_retire(const StepArgs& a, const StepShared& sh, uint32_t j)
 // x -> three-digit records of every 32-element block (times the norm weight
 // when the RMSNorm is fused; its 1/rms is returned and applied per row).
 template <class Fmt>
-__device__ float step_stage_x(const StepOp& op, const StepShared& sh, int warp, int lane) {
+__device__ __forceinline__ float step_stage_x(const StepOp& op, int warp, int lane) {
     const int ctid = warp * 32 + lane;
     constexpr uint32_t kStride = kStepW * 32;
     constexpr int kB = 4;
@@ -308,19 +320,19 @@ __device__ float step_stage_x(const StepOp& op, const StepShared& sh, int warp, 
             q.y *= wq[k].y;
             q.z *= wq[k].z;
             q.w *= wq[k].w;
-            build_xrec_lane<Fmt::XK>(q, lane, g < ngr, sh.xreg + (size_t)(g >> 3) * kXrecBytes);
+            build_xrec_lane<Fmt::XK>(q, lane, g < ngr, s_dyn + (size_t)(g >> 3) * kXrecBytes);
         }
     }
     if (rms) {
         ss = warp_sum(ss);
-        if (lane == 0) sh.red[warp] = ss;
+        if (lane == 0) s_red[warp] = ss;
     }
     step_sync();
     float inv = 1.0f;
     if (rms) {
         float t = 0.f;
 #pragma unroll
-        for (int k = 0; k < kStepW; ++k) t += sh.red[k];
+        for (int k = 0; k < kStepW; ++k) t += s_red[k];
         inv = 1.0f / sqrtf(t / (float)op.cols + op.eps);  // ops::rmsnorm (ops.cpp:29-40)
     }
     return inv;
@@ -420,13 +432,17 @@ struct PieceCursor {
 // One GEMV op (rows per slot op.rpt <= 4: the row loop and the shuffle
 // reduction run for 4 rows, the missing ones as zeros).
 template <class Fmt>
-__device__ __forceinline__ PieceCursor step_gemv(const StepOp& op, const StepArgs& a, const StepShared& sh,
-                                                 int warp, int lane, PieceCursor cur) {
+__device__ __forceinline__ PieceCursor step_gemv(int warp, int lane, PieceCursor cur) {
     constexpr int RPT = Fmt::STEP_RPT;  // rows per slot at most (register budget)
+    const StepOp& op = s_op;
+    const StepArgs& a = s_args;
+    uint8_t* const ring = step_ring();
+    const unsigned int* const abort_flag = a.abort_flag;
+    const uint32_t RB = a.ring_bytes;
     uint32_t j = cur.j, head = cur.head;
     bool dead = cur.dead != 0;
     unsigned long long best = cur.best;
-    const float inv = step_stage_x<Fmt>(op, sh, warp, lane);
+    const float inv = step_stage_x<Fmt>(op, warp, lane);
     const uint32_t U = op.units, WS = op.ws, RS = op.rs, R = op.prows, stride = op.row_stride, rpt = op.rpt;
     const uint32_t slot = (uint32_t)warp / WS, wi = (uint32_t)warp % WS;
     const bool active = slot < RS;
@@ -434,13 +450,14 @@ __device__ __forceinline__ PieceCursor step_gemv(const StepOp& op, const StepArg
     const bool uact = active && u < U;
     const uint32_t pos_op = op.epi == EPI_QKV ? *op.pos : 0u;  // the step's position (RoPE row)
     constexpr int LPR = 32 / RPT;
-    for (uint32_t p = blockIdx.x; p < op.npieces; p += gridDim.x, ++j) {
-        const uint32_t rows_here = min(R, op.rows_pad - p * R);
+    const uint32_t npieces = op.npieces, rows_pad = op.rows_pad;
+    for (uint32_t p = blockIdx.x; p < npieces; p += gridDim.x, ++j) {
+        const uint32_t rows_here = min(R, rows_pad - p * R);
         const uint32_t bytes = rows_here * stride;
-        const uint32_t off = head + bytes <= a.ring_bytes ? head : 0u;
+        const uint32_t off = head + bytes <= RB ? head : 0u;
         head = off + bytes;
         const uint32_t s = j % kStepSlots, ph = (j / kStepSlots) & 1u;
-        if (!dead && !step_wait(&sh.full[s], ph, a.abort_flag)) {
+        if (!dead && !step_wait(&s_full[s], ph, abort_flag)) {
             dead = true;
             step_raise(a);
         }
@@ -455,9 +472,9 @@ __device__ __forceinline__ PieceCursor step_gemv(const StepOp& op, const StepArg
             // this thread's unit of x (three-digit record), from shared memory
             // per piece rather than held across the epilogue (registers)
             XRec xr;
-            load_xrec(sh.xreg, u, xr);
+            load_xrec(s_dyn, u, xr);
             const uint32_t r0 = slot * rpt;
-            const uint8_t* base = sh.ring + off + (size_t)r0 * stride;
+            const uint8_t* base = ring + off + (size_t)r0 * stride;
 #pragma unroll
             for (int k = 0; k < RPT; ++k) {
                 if ((uint32_t)k < rpt && r0 + k < rows_here) {
@@ -470,9 +487,9 @@ __device__ __forceinline__ PieceCursor step_gemv(const StepOp& op, const StepArg
         // lanes k*LPR .. k*LPR + LPR-1 end with this warp's part of row k
         const float v = warp_reduce_rows<RPT>(acc, lane);
         if (active && (lane % LPR) == 0 && (uint32_t)lane / LPR < rpt)
-            sh.part[s * kStepPartRows + (slot * rpt + (uint32_t)lane / LPR) * WS + wi] = v;
+            s_part[s * kStepPartRows + (slot * rpt + (uint32_t)lane / LPR) * WS + wi] = v;
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sh.done[s]);
+        if (lane == 0) mbar_arrive(&s_done[s]);
         if ((uint32_t)warp == j % kStepW) {
             // this warp closes the piece: sum the row partials, fused epilogue,
             // free its ring space and issue the next pieces
@@ -482,7 +499,7 @@ __device__ __forceinline__ PieceCursor step_gemv(const StepOp& op, const StepArg
                 const uint32_t r = ib * 32 + (uint32_t)lane;
                 pre[ib] = r < rows_here ? step_epi_pre(op, p * R + r, pos_op) : EpiPre{make_float2(0.f, 0.f), 0.f, 0.f};
             }
-            if (!dead && !step_wait(&sh.done[s], ph, a.abort_flag)) {
+            if (!dead && !step_wait(&s_done[s], ph, abort_flag)) {
                 dead = true;
                 step_raise(a);
             }
@@ -494,13 +511,13 @@ __device__ __forceinline__ PieceCursor step_gemv(const StepOp& op, const StepArg
                 const uint32_t r = ib * 32 + (uint32_t)lane;
                 float val = 0.f;
                 if (r < R)
-                    for (uint32_t k = 0; k < WS; ++k) val += sh.part[s * kStepPartRows + r * WS + k];
+                    for (uint32_t k = 0; k < WS; ++k) val += s_part[s * kStepPartRows + r * WS + k];
                 val *= inv;  // 1/rms of the fused RMSNorm (1 if plain)
                 const float v_next = __shfl_down_sync(0xffffffffu, val, 1);  // partner row of a pair
                 if (r < rows_here && !dead) step_epilogue(op, p * R + r, val, v_next, pre[ib], best);
             }
             __syncwarp();
-            if (lane == 0 && !dead) ring_retire(a, sh, j);
+            if (lane == 0 && !dead) ring_retire(j);
             if (stamp) a.pieces[4 * j + 3] = global_ns();
             dead = __shfl_sync(0xffffffffu, dead ? 1 : 0, 0) != 0;
         }
@@ -530,8 +547,9 @@ __device__ __forceinline__ void attn_merge(float& m, float& l, float4& o, float 
 // K/V rows (every position but the newest, which this step's QKV op writes)
 // is loaded before it, so that latency overlaps the wait.
 template <int HD>
-__device__ __forceinline__ uint32_t step_attn(const StepOp& op, const StepArgs& a, const StepShared& sh, int warp,
-                                           int lane, uint32_t dead_in, uint32_t target, int* cta_dead) {
+__device__ __forceinline__ uint32_t step_attn(int warp, int lane, uint32_t dead_in, uint32_t target) {
+    const StepOp& op = s_op;
+    const StepArgs& a = s_args;
     constexpr int RPI = 128 / HD;            // positions per warp instruction (sub-warps)
     constexpr int LPR = 32 / RPI;            // lanes per position: 4 dims each
     constexpr int kHP = 4;                   // heads per pass (register budget)
@@ -577,11 +595,11 @@ __device__ __forceinline__ uint32_t step_attn(const StepOp& op, const StepArgs& 
     // the QKV op's results (q, the newest K/V row) are complete past this barrier
     bool dead = dead_in != 0;
     if (ctid == 0 && !dead && !grid_wait(a.bar, target, a.abort_flag)) {
-        *cta_dead = 1;
+        s_cta_dead = 1;
         step_raise(a);
     }
     step_sync();
-    dead = *cta_dead != 0;
+    dead = s_cta_dead != 0;
     if (dead) trips = 0u;
 #pragma unroll
     for (int c = 0; c < kB; ++c) {
@@ -592,7 +610,7 @@ __device__ __forceinline__ uint32_t step_attn(const StepOp& op, const StepArgs& 
         }
     }
     const float scale = 1.0f / sqrtf((float)HD);
-    float* scr = reinterpret_cast<float*>(sh.xreg);  // [kStepW][G][SR]
+    float* scr = reinterpret_cast<float*>(s_dyn);  // [kStepW][G][SR]
     for (uint32_t h0 = 0; h0 < G; h0 += kHP) {
         float4 qv[kHP];
         float m[kHP], l[kHP];
@@ -693,12 +711,11 @@ __device__ __forceinline__ uint32_t step_attn(const StepOp& op, const StepArgs& 
     }
     if (S > 1) {
         // the last item of this KV head merges all of its items
-        __shared__ int last_item;
         __threadfence();
         step_sync();
-        if (ctid == 0) last_item = (has && !dead) ? (atomicAdd(op.tickets + kvh, 1u) == S - 1 ? 1 : 0) : 0;
+        if (ctid == 0) s_last_item = (has && !dead) ? (atomicAdd(op.tickets + kvh, 1u) == S - 1 ? 1 : 0) : 0;
         step_sync();
-        if (last_item) {
+        if (s_last_item) {
             __threadfence();
             const float* hp = op.part + (size_t)kvh * S * G * (HD + 2);
             for (uint32_t idx = ctid; idx < G * HD; idx += kStepW * 32) {
@@ -726,78 +743,55 @@ __device__ __forceinline__ uint32_t step_attn(const StepOp& op, const StepArgs& 
 
 template <class FA, class FB, int HD>
 __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const StepArgs args) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t full[kStepSlots], done[kStepSlots];
-    __shared__ float part[kStepSlots * kStepPartRows];
-    __shared__ StepRing ring_state;
-    __shared__ float red[32];
-    __shared__ unsigned long long best_sh[kStepW];
-    __shared__ __align__(16) StepOp op_sh;
-    __shared__ int cta_dead;  // some wait of this CTA gave up (read after a barrier: CTA-uniform)
-
-    // The arguments and the shared-memory map live in shared memory: the
-    // non-inlined op functions take them by reference, and a per-thread copy
-    // would sit in local memory, which the ~29 KB of L1 left beside the ring
-    // cannot hold.
-    __shared__ StepArgs a;
-    __shared__ StepShared sh;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) {
-        a = args;
-        sh.full = full;
-        sh.done = done;
-        sh.part = part;
-        sh.red = red;
-        sh.xreg = smem;
-        sh.ring = smem + args.xbytes;
-        sh.rs = &ring_state;
-    }
-    __syncthreads();
-    if (tid == 0) {
+        s_args = args;
         for (uint32_t s = 0; s < kStepSlots; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&done[s], kStepW);
+            mbar_init(&s_full[s], 1);
+            mbar_init(&s_done[s], kStepW);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        ring_state.retired = ring_state.issued = ring_state.head = 0u;
-        ring_state.lock = 0u;
-        for (uint32_t q = 0; q < kStepSlots; ++q) ring_state.freed[q] = 0u;
-        ring_state.op = 0u;
-        ring_state.p = blockIdx.x;
-        ring_load_op(a, ring_state);
-        cta_dead = 0;
-        ring_issue(a, sh);  // fill the ring: weights depend on nothing
+        StepRing& r = s_ring;
+        r.retired = r.issued = r.head = 0u;
+        r.lock = 0u;
+        for (uint32_t q = 0; q < kStepSlots; ++q) r.freed[q] = 0u;
+        r.op = 0u;
+        r.p = blockIdx.x;
+        ring_load_op(s_args, r);
+        s_cta_dead = 0;
+        ring_issue();  // fill the ring: weights depend on nothing
     }
     __syncthreads();
+    const StepArgs& a = s_args;
 
     const int ctid = tid;
     uint32_t j = 0, head = 0, nsig = 0;
     bool dead = false;
     for (uint32_t k = 0; k < a.nops; ++k) {
         // this op's descriptor into shared memory (8-byte words)
-        if (dead) cta_dead = 1;
+        if (dead) s_cta_dead = 1;
         step_sync();
         for (uint32_t i = ctid; i < sizeof(StepOp) / 8; i += kStepW * 32)
-            reinterpret_cast<unsigned long long*>(&op_sh)[i] =
+            s_op_raw[i] =
                 __ldg(reinterpret_cast<const unsigned long long*>(a.ops + k) + i);
         step_sync();
-        dead = cta_dead != 0;
-        const StepOp& op = op_sh;
+        dead = s_cta_dead != 0;
+        const StepOp& op = s_op;
         TraceSlot* slot = a.trace ? a.trace + k : nullptr;
         if (ctid == 0) trace_mark(slot, 0);
         if (op.wait && op.kind != SOP_ATTN) {  // CTA-uniform: every thread reaches the barrier below
             if (ctid == 0 && !dead && !grid_wait(a.bar, nsig * gridDim.x, a.abort_flag)) {
-                cta_dead = 1;
+                s_cta_dead = 1;
                 step_raise(a);
             }
             step_sync();
-            dead = cta_dead != 0;
+            dead = s_cta_dead != 0;
         }
         if (ctid == 0) trace_mark(slot, 1);
         if (op.kind == SOP_GEMV) {
             PieceCursor cur{j, head, dead ? 1u : 0u, 0ull};
-            if (op.fmt == 0) cur = step_gemv<FA>(op, a, sh, warp, lane, cur);
-            else cur = step_gemv<FB>(op, a, sh, warp, lane, cur);
+            if (op.fmt == 0) cur = step_gemv<FA>(warp, lane, cur);
+            else cur = step_gemv<FB>(warp, lane, cur);
             j = cur.j;
             head = cur.head;
             dead = cur.dead != 0;
@@ -808,18 +802,18 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
                     const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
                     best = other > best ? other : best;
                 }
-                if (lane == 0) best_sh[warp] = best;
+                if (lane == 0) s_best[warp] = best;
                 step_sync();
                 if (ctid == 0) {
                     unsigned long long b = 0ull;
-                    for (int w = 0; w < kStepW; ++w) b = best_sh[w] > b ? best_sh[w] : b;
+                    for (int w = 0; w < kStepW; ++w) b = s_best[w] > b ? s_best[w] : b;
                     if (b && !dead) atomicMax(op.argmax, b);
                 }
             }
         } else if (op.kind == SOP_ATTN) {
             // takes the op's barrier itself, after loading cached K/V rows
             const uint32_t d = dead ? 1u : 0u, target = nsig * gridDim.x;
-            dead = step_attn<HD>(op, a, sh, warp, lane, d, target, &cta_dead) != 0u;
+            dead = step_attn<HD>(warp, lane, d, target) != 0u;
         } else if (op.kind == SOP_EMBED && !dead) {
             uint32_t tok = a.st->token;
             if (tok >= op.emb.rows) tok = 0;  // the host validates ids; never read outside the table
@@ -850,14 +844,14 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
             ++nsig;
         }
     }
-    if (dead) cta_dead = 1;
+    if (dead) s_cta_dead = 1;
     step_sync();
-    if (cta_dead) {
+    if (s_cta_dead) {
         // copies still in flight land before the CTA's shared memory goes away
         if (ctid == 0) {
-            const StepRing& r = ring_state;
+            const StepRing& r = s_ring;
             for (uint32_t q = r.retired; q < r.issued; ++q)
-                step_wait(&full[q % kStepSlots], (q / kStepSlots) & 1u, nullptr);
+                step_wait(&s_full[q % kStepSlots], (q / kStepSlots) & 1u, nullptr);
         }
     }
 }
