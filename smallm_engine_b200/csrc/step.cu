@@ -60,7 +60,7 @@ enum { SOP_EMBED = 0, SOP_GEMV = 1, SOP_ATTN = 2 };
 
 constexpr int kStepW = 16;                    // warps per CTA (all consume; see ring_issue)
 constexpr int kStepThreads = kStepW * 32;
-constexpr uint32_t kStepSlots = 16;           // ring pieces in flight at most
+constexpr uint32_t kStepSlots = 32;           // ring pieces in flight at most
 constexpr uint32_t kStepPartRows = 64;        // rows of one piece's partials (R <= 64)
 constexpr unsigned int kStepErrBit = 16u;
 constexpr int kStepMaxGroup = 8;           // query heads per KV head
@@ -145,10 +145,12 @@ __device__ __forceinline__ bool step_wait(uint64_t* bar, uint32_t parity, const 
     long long next = kAbortLookAfter;
     for (;;) {
         uint32_t ok;
+        // no suspend-time hint: a suspended warp resumes late after the phase
+        // completes, and these waits are on the piece pipeline's critical path
         asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
             : "=r"(ok)
-            : "r"(addr), "r"(parity), "r"(20000u)
+            : "r"(addr), "r"(parity)
             : "memory");
         if (ok) return true;
         const long long waited = clock64() - t0;
@@ -197,7 +199,7 @@ struct StepRing {
 // scoreboard).
 extern __shared__ __align__(128) uint8_t s_dyn[];  // x region (records / attention scratch), then the ring
 __shared__ __align__(8) uint64_t s_full[kStepSlots];  // piece landed in the ring (count 1 + bytes)
-__shared__ __align__(8) uint64_t s_done[kStepSlots];  // every warp finished the piece (count kStepW)
+__shared__ uint32_t s_cnt[kStepSlots];                // warps of the piece's row slot done with it
 __shared__ float s_part[kStepSlots * kStepPartRows];  // row partials of each piece in flight
 __shared__ StepRing s_ring;
 __shared__ float s_red[32];
@@ -433,7 +435,8 @@ struct PieceCursor {
 // reduction run for 4 rows, the missing ones as zeros).
 template <class Fmt>
 __device__ __forceinline__ PieceCursor step_gemv(int warp, int lane, PieceCursor cur) {
-    constexpr int RPT = Fmt::STEP_RPT;  // rows per slot at most (register budget)
+    constexpr int RPT = Fmt::STEP_RPT;  // rows per piece at most (register budget)
+    constexpr int LPR = 32 / RPT;
     const StepOp& op = s_op;
     const StepArgs& a = s_args;
     uint8_t* const ring = step_ring();
@@ -443,41 +446,40 @@ __device__ __forceinline__ PieceCursor step_gemv(int warp, int lane, PieceCursor
     bool dead = cur.dead != 0;
     unsigned long long best = cur.best;
     const float inv = step_stage_x<Fmt>(op, warp, lane);
-    const uint32_t U = op.units, WS = op.ws, RS = op.rs, R = op.prows, stride = op.row_stride, rpt = op.rpt;
+    // row slot `slot` (WS warps, one unit of x per lane) owns every RS-th of
+    // this CTA's pieces; a piece is rpt rows
+    const uint32_t U = op.units, WS = op.ws, RS = op.rs, R = op.prows, stride = op.row_stride;
     const uint32_t slot = (uint32_t)warp / WS, wi = (uint32_t)warp % WS;
     const bool active = slot < RS;
     const uint32_t u = wi * 32 + (uint32_t)lane;
     const bool uact = active && u < U;
     const uint32_t pos_op = op.epi == EPI_QKV ? *op.pos : 0u;  // the step's position (RoPE row)
-    constexpr int LPR = 32 / RPT;
     const uint32_t npieces = op.npieces, rows_pad = op.rows_pad;
-    for (uint32_t p = blockIdx.x; p < npieces; p += gridDim.x, ++j) {
+    uint32_t i = 0;
+    for (uint32_t p = blockIdx.x; p < npieces; p += gridDim.x, ++j, ++i) {
         const uint32_t rows_here = min(R, rows_pad - p * R);
         const uint32_t bytes = rows_here * stride;
-        const uint32_t off = head + bytes <= RB ? head : 0u;
+        const uint32_t off = head + bytes <= RB ? head : 0u;  // the ring placement, as ring_issue makes it
         head = off + bytes;
+        if (!active || i % RS != slot) continue;  // another row slot's piece
         const uint32_t s = j % kStepSlots, ph = (j / kStepSlots) & 1u;
         if (!dead && !step_wait(&s_full[s], ph, abort_flag)) {
             dead = true;
             step_raise(a);
         }
         dead = __any_sync(0xffffffffu, dead);  // warp-uniform (the shuffles below)
-        const bool stamp = a.pieces && blockIdx.x == 0 && lane == 0 && (uint32_t)warp == j % kStepW &&
-                           j < a.piece_cap;
-        if (stamp) a.pieces[4 * j + 1] = global_ns();
+        const bool stamp = a.pieces && blockIdx.x == 0 && lane == 0 && j < a.piece_cap;
+        if (stamp && wi == 0) a.pieces[4 * j + 1] = global_ns();
         float acc[RPT];
 #pragma unroll
         for (int k = 0; k < RPT; ++k) acc[k] = 0.f;
         if (uact && !dead) {
-            // this thread's unit of x (three-digit record), from shared memory
-            // per piece rather than held across the epilogue (registers)
-            XRec xr;
+            XRec xr;  // this thread's unit of x (three-digit record)
             load_xrec(s_dyn, u, xr);
-            const uint32_t r0 = slot * rpt;
-            const uint8_t* base = ring + off + (size_t)r0 * stride;
+            const uint8_t* base = ring + off;
 #pragma unroll
             for (int k = 0; k < RPT; ++k) {
-                if ((uint32_t)k < rpt && r0 + k < rows_here) {
+                if ((uint32_t)k < rows_here) {
                     typename Fmt::Raw raw;
                     Fmt::load(base + (size_t)k * stride, u, U, raw);
                     acc[k] = Fmt::dot(raw, 0, xr, u);
@@ -486,41 +488,34 @@ __device__ __forceinline__ PieceCursor step_gemv(int warp, int lane, PieceCursor
         }
         // lanes k*LPR .. k*LPR + LPR-1 end with this warp's part of row k
         const float v = warp_reduce_rows<RPT>(acc, lane);
-        if (active && (lane % LPR) == 0 && (uint32_t)lane / LPR < rpt)
-            s_part[s * kStepPartRows + (slot * rpt + (uint32_t)lane / LPR) * WS + wi] = v;
+        if ((lane % LPR) == 0 && (uint32_t)lane / LPR < R) s_part[s * kStepPartRows + (lane / LPR) * WS + wi] = v;
         __syncwarp();
-        if (lane == 0) mbar_arrive(&s_done[s]);
-        if ((uint32_t)warp == j % kStepW) {
-            // this warp closes the piece: sum the row partials, fused epilogue,
-            // free its ring space and issue the next pieces
-            EpiPre pre[2];
-#pragma unroll
-            for (int ib = 0; ib < 2; ++ib) {
-                const uint32_t r = ib * 32 + (uint32_t)lane;
-                pre[ib] = r < rows_here ? step_epi_pre(op, p * R + r, pos_op) : EpiPre{make_float2(0.f, 0.f), 0.f, 0.f};
+        // the slot's last warp to finish closes the piece: no warp waits for another
+        uint32_t last = 1u;
+        if (WS > 1) {
+            if (lane == 0) {
+                __threadfence_block();
+                last = atomicAdd(&s_cnt[s], 1u) == WS - 1 ? 1u : 0u;
             }
-            if (!dead && !step_wait(&s_done[s], ph, abort_flag)) {
-                dead = true;
-                step_raise(a);
-            }
-            dead = __any_sync(0xffffffffu, dead);
-            if (stamp) a.pieces[4 * j + 2] = global_ns();
-#pragma unroll
-            for (int ib = 0; ib < 2; ++ib) {
-                if ((uint32_t)ib * 32 >= R) break;  // uniform
-                const uint32_t r = ib * 32 + (uint32_t)lane;
-                float val = 0.f;
-                if (r < R)
-                    for (uint32_t k = 0; k < WS; ++k) val += s_part[s * kStepPartRows + r * WS + k];
-                val *= inv;  // 1/rms of the fused RMSNorm (1 if plain)
-                const float v_next = __shfl_down_sync(0xffffffffu, val, 1);  // partner row of a pair
-                if (r < rows_here && !dead) step_epilogue(op, p * R + r, val, v_next, pre[ib], best);
-            }
-            __syncwarp();
-            if (lane == 0 && !dead) ring_retire(j);
-            if (stamp) a.pieces[4 * j + 3] = global_ns();
-            dead = __shfl_sync(0xffffffffu, dead ? 1 : 0, 0) != 0;
+            last = __shfl_sync(0xffffffffu, last, 0);
         }
+        if (!last) continue;
+        __threadfence_block();
+        if (stamp) a.pieces[4 * j + 2] = global_ns();
+        if (lane == 0) s_cnt[s] = 0u;
+        const uint32_t r = (uint32_t)lane;
+        float val = 0.f;
+        if (r < R)
+            for (uint32_t k = 0; k < WS; ++k) val += s_part[s * kStepPartRows + r * WS + k];
+        val *= inv;  // 1/rms of the fused RMSNorm (1 if plain)
+        const float v_next = __shfl_down_sync(0xffffffffu, val, 1);  // partner row of a pair
+        if (r < rows_here && !dead) {
+            const EpiPre e = step_epi_pre(op, p * R + r, pos_op);
+            step_epilogue(op, p * R + r, val, v_next, e, best);
+        }
+        __syncwarp();
+        if (lane == 0 && !dead) ring_retire(j);
+        if (stamp) a.pieces[4 * j + 3] = global_ns();
     }
     return PieceCursor{j, head, dead ? 1u : 0u, best};
 }
@@ -748,7 +743,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
         s_args = args;
         for (uint32_t s = 0; s < kStepSlots; ++s) {
             mbar_init(&s_full[s], 1);
-            mbar_init(&s_done[s], kStepW);
+            s_cnt[s] = 0u;
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         StepRing& r = s_ring;
@@ -929,17 +924,15 @@ void Model::build_step() {
     if (const char* e = std::getenv("SMALLM_STEP_PIECE_KB")) cap = std::min(cap, (size_t)std::atoi(e) * 1024);
     else cap = std::min(cap, (size_t)40 * 1024);
     auto geometry = [&](const QMat& m, StepOp& op) {
+        // WS warps cover a row's units (one per lane), RS = 16 / WS row slots
+        // take turns with this CTA's pieces; a piece is rpt rows (even: the
+        // rotary and SwiGLU row pairs stay in one piece), at most `cap` bytes
         const uint32_t WS = (m.units + 31) / 32;
-        uint32_t RS = kStepW / WS;
-        uint32_t rpt = m.type == SM_T_Q4_0 ? FmtQ4_0::STEP_RPT : FmtQ8_0::STEP_RPT;
-        while (rpt > 1 && ((size_t)RS * rpt * m.row_stride > cap || RS * rpt > kStepPartRows)) rpt /= 2;
+        const uint32_t RS = kStepW / WS;
         const uint32_t rpt_max = m.type == SM_T_Q4_0 ? FmtQ4_0::STEP_RPT : FmtQ8_0::STEP_RPT;
-        if ((RS * rpt) % 2) {
-            if (rpt < rpt_max && (size_t)RS * rpt * 2 * m.row_stride <= ring / 3 && RS * rpt * 2 <= kStepPartRows)
-                rpt *= 2;
-            else RS -= 1;  // RS >= 2 here (RS * rpt odd with rpt = 1 needs RS odd and > 1, or RS = 1, rpt = 1)
-        }
-        if (RS == 0 || (RS * rpt) % 2 || (size_t)RS * rpt * m.row_stride > ring / 2)
+        uint32_t rpt = rpt_max;
+        while (rpt > 2 && (size_t)rpt * m.row_stride > cap) rpt /= 2;
+        if (RS == 0 || rpt < 2 || (size_t)rpt * m.row_stride > ring / 3)
             throw Error(1, "persistent step: no piece geometry for a matrix of " + std::to_string(m.cols) + " columns");
         op.w = m.base;
         op.row_stride = m.row_stride;
@@ -950,8 +943,8 @@ void Model::build_step() {
         op.ws = WS;
         op.rs = RS;
         op.rpt = rpt;
-        op.prows = RS * rpt;
-        op.npieces = (m.rows_pad + op.prows - 1) / op.prows;
+        op.prows = rpt;
+        op.npieces = (m.rows_pad + rpt - 1) / rpt;
     };
 
     std::vector<StepOp> ops;
