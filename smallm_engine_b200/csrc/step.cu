@@ -58,8 +58,8 @@ namespace smallm {
 
 enum { SOP_EMBED = 0, SOP_GEMV = 1, SOP_ATTN = 2 };
 
-constexpr int kStepW = 16;                    // warps per CTA (all consume; see ring_issue)
-constexpr int kStepThreads = kStepW * 32;
+constexpr int kStepW = 16;                    // consumer warps (one producer warp more)
+constexpr int kStepThreads = (kStepW + 1) * 32;
 constexpr uint32_t kStepSlots = 32;           // ring pieces in flight at most
 constexpr uint32_t kStepPartRows = 64;        // rows of one piece's partials (R <= 64)
 constexpr unsigned int kStepErrBit = 16u;
@@ -172,7 +172,9 @@ __device__ __forceinline__ bool grid_wait(const unsigned int* bar, unsigned int 
     }
 }
 
-__device__ __forceinline__ void step_sync() { __syncthreads(); }
+__device__ __forceinline__ void step_sync() {  // the consumer warps (the producer never joins)
+    asm volatile("bar.sync 1, %0;" ::"n"(kStepW * 32) : "memory");
+}
 
 // ---------------------------------------------------------------- GEMV --
 
@@ -183,7 +185,6 @@ __device__ __forceinline__ void step_sync() { __syncthreads(); }
 struct StepRing {
     uint32_t retired;  // pieces whose space is free again
     uint32_t issued;   // pieces whose copy has been started
-    uint32_t lock;     // held by the lane retiring pieces and issuing copies
     uint32_t freed[kStepSlots];  // j + 1 once piece j (slot j % kStepSlots) is done with
     uint32_t head;     // ring offset just past the newest issued piece
     uint32_t op, p;    // next piece to issue: op index and piece index
@@ -260,32 +261,48 @@ __device__ __forceinline__ void ring_issue() {
     }
 }
 
-// Piece j is done (every warp has read it, its epilogue has run): mark it, then
-// retire every piece that is done, in order, and issue the copies that now
-// fit -- unless another lane holds the lock, in which case that lane picks the
-// mark up (it looks again after unlocking).  One lane; never waits.
-__device__ __forceinline__ void ring_retire(uint32_t j) {
+// Piece j is done (its slot's warps have read it, its epilogue has run): mark
+// it for the producer, which retires pieces in order and reuses their space.
+__device__ __forceinline__ void ring_mark_done(uint32_t j) {
+    __threadfence_block();
+    reinterpret_cast<volatile uint32_t*>(s_ring.freed)[j % kStepSlots] = j + 1;
+}
+
+// The producer warp's lane 0: retire the pieces marked done, in order, and
+// start the copies of the next pieces that fit, until every piece of the step
+// is issued and consumed.  A copy's issue can stall the issuing thread, which
+// is why no consumer does it.  Gives up (bounded) when no piece retires for
+// ~1 s or the step's abort flag is up, then waits for its copies in flight.
+__device__ __forceinline__ void step_producer() {
     StepRing& r = s_ring;
     volatile uint32_t* fr = r.freed;
-    __threadfence_block();
-    fr[j % kStepSlots] = j + 1;
+    const StepArgs& a = s_args;
+    long long t0 = clock64();
+    long long next = kAbortLookAfter;
+    bool dead = false;
     for (;;) {
-        __threadfence_block();
-        if (atomicCAS(&r.lock, 0u, 1u) != 0u) return;
-        __threadfence_block();
-        const uint32_t before = *(volatile uint32_t*)&r.retired;
-        uint32_t q = before;
-        while (fr[q % kStepSlots] == q + 1) ++q;
-        if (q != before) {
-            *(volatile uint32_t*)&r.retired = q;
-            ring_issue();
+        uint32_t q = r.retired;
+        while (q != r.issued && fr[q % kStepSlots] == q + 1) ++q;
+        const bool progress = q != r.retired;
+        r.retired = q;
+        const uint32_t issued_before = r.issued;
+        ring_issue();
+        if (r.op >= a.nops && r.retired == r.issued) break;  // all issued, all consumed
+        if (progress || r.issued != issued_before) {
+            t0 = clock64();
+            next = kAbortLookAfter;
+        } else {
+            const long long waited = clock64() - t0;
+            if (waited > kGiveUp || abort_seen(a.abort_flag, waited, next)) {
+                dead = true;
+                break;
+            }
         }
-        __threadfence_block();
-        atomicExch(&r.lock, 0u);
-        __threadfence_block();
-        // a mark set while the lock was held is not lost: its lane failed to
-        // take the lock after setting it, so this read sees it
-        if (fr[q % kStepSlots] != q + 1) return;
+    }
+    if (dead) {
+        step_raise(a);
+        for (uint32_t q2 = r.retired; q2 < r.issued; ++q2)
+            step_wait(&s_full[q2 % kStepSlots], (q2 / kStepSlots) & 1u, nullptr);
     }
 }
 
@@ -514,7 +531,7 @@ __device__ __forceinline__ PieceCursor step_gemv(int warp, int lane, PieceCursor
             step_epilogue(op, p * R + r, val, v_next, e, best);
         }
         __syncwarp();
-        if (lane == 0 && !dead) ring_retire(j);
+        if (lane == 0 && !dead) ring_mark_done(j);
         if (stamp) a.pieces[4 * j + 3] = global_ns();
     }
     return PieceCursor{j, head, dead ? 1u : 0u, best};
@@ -548,7 +565,7 @@ __device__ __forceinline__ uint32_t step_attn(int warp, int lane, uint32_t dead_
     constexpr int RPI = 128 / HD;            // positions per warp instruction (sub-warps)
     constexpr int LPR = 32 / RPI;            // lanes per position: 4 dims each
     constexpr int kHP = 4;                   // heads per pass (register budget)
-    constexpr int kB = 4;                    // positions per position-lane and load batch
+    constexpr int kB = 2;                    // positions per position-lane and load batch (registers)
     constexpr uint32_t SR = HD + 4;          // scratch row: HD outputs, max, sum, pad to 16 bytes
     constexpr uint32_t NRL = kStepW * RPI;   // position lanes of the CTA
     const int ctid = warp * 32 + lane;
@@ -748,15 +765,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         StepRing& r = s_ring;
         r.retired = r.issued = r.head = 0u;
-        r.lock = 0u;
         for (uint32_t q = 0; q < kStepSlots; ++q) r.freed[q] = 0u;
         r.op = 0u;
         r.p = blockIdx.x;
         ring_load_op(s_args, r);
         s_cta_dead = 0;
-        ring_issue();  // fill the ring: weights depend on nothing
     }
     __syncthreads();
+    if (warp == kStepW) {  // the producer: weights depend on nothing, so it streams ahead
+        if (lane == 0) step_producer();
+        return;
+    }
     const StepArgs& a = s_args;
 
     const int ctid = tid;
@@ -839,16 +858,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
             ++nsig;
         }
     }
-    if (dead) s_cta_dead = 1;
-    step_sync();
-    if (s_cta_dead) {
-        // copies still in flight land before the CTA's shared memory goes away
-        if (ctid == 0) {
-            const StepRing& r = s_ring;
-            for (uint32_t q = r.retired; q < r.issued; ++q)
-                step_wait(&s_full[q % kStepSlots], (q / kStepSlots) & 1u, nullptr);
-        }
-    }
+    // (a CTA whose wait gave up leaves its copies in flight to the producer,
+    // which waits for them before it returns: the CTA stays until then)
 }
 
 // ---------------------------------------------------------------- host --
