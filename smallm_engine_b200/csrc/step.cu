@@ -7,7 +7,7 @@
 // resident CTA for the whole step, and the weight pieces of ALL the step's
 // matrices stream, in order, through one shared-memory byte ring that never
 // waits on a data dependency -- only on ring space: whichever warp frees a
-// piece's space starts the copies of the next pieces that fit (ring_issue),
+// piece's space starts the copies of the next pieces that fit (ring_plan),
 // so there is no producer warp and the 16 warps keep 128 registers each.  The
 // warps walk the op list; between dependent ops they meet at a grid-wide
 // barrier (a release counter in global memory), stage the new x and continue
@@ -229,18 +229,25 @@ __device__ __forceinline__ void ring_load_op(const StepArgs& a, StepRing& r) {
     r.w = op->w;
 }
 
-__device__ __forceinline__ void ring_issue() {
+// Plan the next pieces while a slot is free and the ring has room for them
+// (the producer's lane 0): their ring offsets, sizes and sources go to
+// s_plan_*, and the ring state advances as if they were issued.  Returns how
+// many (at most 32: one per producer lane, which issue them at once).
+__shared__ uint32_t s_plan_off[32], s_plan_bytes[32];
+__shared__ const uint8_t* s_plan_src[32];
+
+__device__ __forceinline__ uint32_t ring_plan() {
     const StepArgs& a = s_args;
     StepRing& r = s_ring;
-    uint8_t* ring = step_ring();
     const uint32_t RB = a.ring_bytes;
-    while (r.issued - r.retired < kStepSlots) {
+    uint32_t n = 0;
+    while (n < 32 && r.issued - r.retired < kStepSlots) {
         while (r.op < a.nops && (r.kind != SOP_GEMV || r.p >= r.np)) {
             ++r.op;
             r.p = blockIdx.x;
             ring_load_op(a, r);
         }
-        if (r.op >= a.nops) return;
+        if (r.op >= a.nops) break;
         const uint32_t R = r.R, stride = r.stride;
         const uint32_t bytes = min(R, r.rows_pad - r.p * R) * stride;
         const uint32_t off = r.head + bytes <= RB ? r.head : 0u;
@@ -248,17 +255,18 @@ __device__ __forceinline__ void ring_issue() {
             const uint32_t tail = r.pstart[r.retired % kStepSlots];
             const bool clash = tail < r.head ? (off < r.head && tail < off + bytes)  // occupied [tail, head)
                                              : (off < r.head || off + bytes > tail); // [tail, RB) + [0, head)
-            if (clash) return;
+            if (clash) break;
         }
-        const uint32_t s = r.issued % kStepSlots;
-        r.pstart[s] = off;
+        r.pstart[r.issued % kStepSlots] = off;
         r.head = off + bytes;
-        if (a.pieces && blockIdx.x == 0 && r.issued < a.piece_cap) a.pieces[4 * r.issued] = global_ns();
-        mbar_arrive_expect_tx(&s_full[s], bytes);
-        bulk_g2s(ring + off, r.w + (size_t)r.p * R * stride, bytes, &s_full[s]);
+        s_plan_off[n] = off;
+        s_plan_bytes[n] = bytes;
+        s_plan_src[n] = r.w + (size_t)r.p * R * stride;
+        ++n;
         ++r.issued;
         r.p += gridDim.x;
     }
+    return n;
 }
 
 // Piece j is done (its slot's warps have read it, its epilogue has run): mark
@@ -273,33 +281,51 @@ __device__ __forceinline__ void ring_mark_done(uint32_t j) {
 // is issued and consumed.  A copy's issue can stall the issuing thread, which
 // is why no consumer does it.  Gives up (bounded) when no piece retires for
 // ~1 s or the step's abort flag is up, then waits for its copies in flight.
-__device__ __forceinline__ void step_producer() {
+__device__ __forceinline__ void step_producer(int lane) {
     StepRing& r = s_ring;
     volatile uint32_t* fr = r.freed;
     const StepArgs& a = s_args;
+    uint8_t* const ring = step_ring();
     long long t0 = clock64();
     long long next = kAbortLookAfter;
     bool dead = false;
     for (;;) {
-        uint32_t q = r.retired;
-        while (q != r.issued && fr[q % kStepSlots] == q + 1) ++q;
-        const bool progress = q != r.retired;
-        r.retired = q;
-        const uint32_t issued_before = r.issued;
-        ring_issue();
-        if (r.op >= a.nops && r.retired == r.issued) break;  // all issued, all consumed
-        if (progress || r.issued != issued_before) {
-            t0 = clock64();
-            next = kAbortLookAfter;
-        } else {
-            const long long waited = clock64() - t0;
-            if (waited > kGiveUp || abort_seen(a.abort_flag, waited, next)) {
-                dead = true;
-                break;
+        uint32_t n = 0, first = 0, state = 0;  // state: 1 all done, 2 gave up
+        if (lane == 0) {
+            uint32_t q = r.retired;
+            while (q != r.issued && fr[q % kStepSlots] == q + 1) ++q;
+            const bool progress = q != r.retired;
+            r.retired = q;
+            first = r.issued;
+            n = ring_plan();
+            if (r.op >= a.nops && r.retired == r.issued) {
+                state = 1;  // all issued, all consumed
+            } else if (progress || n) {
+                t0 = clock64();
+                next = kAbortLookAfter;
+            } else {
+                const long long waited = clock64() - t0;
+                if (waited > kGiveUp || abort_seen(a.abort_flag, waited, next)) state = 2;
             }
         }
+        __syncwarp();
+        n = __shfl_sync(0xffffffffu, n, 0);
+        first = __shfl_sync(0xffffffffu, first, 0);
+        state = __shfl_sync(0xffffffffu, state, 0);
+        if ((uint32_t)lane < n) {  // the planned copies, one per lane
+            const uint32_t j = first + lane, s = j % kStepSlots;
+            if (a.pieces && blockIdx.x == 0 && j < a.piece_cap) a.pieces[4 * j] = global_ns();
+            mbar_arrive_expect_tx(&s_full[s], s_plan_bytes[lane]);
+            bulk_g2s(ring + s_plan_off[lane], s_plan_src[lane], s_plan_bytes[lane], &s_full[s]);
+        }
+        __syncwarp();
+        if (state == 1) break;
+        if (state == 2) {
+            dead = true;
+            break;
+        }
     }
-    if (dead) {
+    if (dead && lane == 0) {
         step_raise(a);
         for (uint32_t q2 = r.retired; q2 < r.issued; ++q2)
             step_wait(&s_full[q2 % kStepSlots], (q2 / kStepSlots) & 1u, nullptr);
@@ -441,7 +467,7 @@ __device__ __forceinline__ void step_epilogue(const StepOp& op, uint32_t row, fl
 }
 
 // This CTA's position in its piece sequence (piece counter j and ring
-// placement head, identical to ring_issue's), the abandon flag and the
+// placement head, identical to ring_plan's), the abandon flag and the
 // greedy-argmax key of a logits op.
 struct PieceCursor {
     uint32_t j, head, dead;
@@ -476,7 +502,7 @@ __device__ __forceinline__ PieceCursor step_gemv(int warp, int lane, PieceCursor
     for (uint32_t p = blockIdx.x; p < npieces; p += gridDim.x, ++j, ++i) {
         const uint32_t rows_here = min(R, rows_pad - p * R);
         const uint32_t bytes = rows_here * stride;
-        const uint32_t off = head + bytes <= RB ? head : 0u;  // the ring placement, as ring_issue makes it
+        const uint32_t off = head + bytes <= RB ? head : 0u;  // the ring placement, as ring_plan makes it
         head = off + bytes;
         if (!active || i % RS != slot) continue;  // another row slot's piece
         const uint32_t s = j % kStepSlots, ph = (j / kStepSlots) & 1u;
@@ -773,7 +799,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
     }
     __syncthreads();
     if (warp == kStepW) {  // the producer: weights depend on nothing, so it streams ahead
-        if (lane == 0) step_producer();
+        step_producer(lane);
         return;
     }
     const StepArgs& a = s_args;
