@@ -200,7 +200,8 @@ struct StepRing {
 // scoreboard).
 extern __shared__ __align__(128) uint8_t s_dyn[];  // x region (records / attention scratch), then the ring
 __shared__ __align__(8) uint64_t s_full[kStepSlots];  // piece landed in the ring (count 1 + bytes)
-__shared__ uint32_t s_cnt[kStepSlots];                // warps of the piece's row slot done with it
+__shared__ uint32_t s_cnt[kStepSlots * kStepW];       // warps of a row slot done with the piece
+__shared__ uint32_t s_slots[kStepSlots];              // row slots done with the piece
 __shared__ float s_part[kStepSlots * kStepPartRows];  // row partials of each piece in flight
 __shared__ StepRing s_ring;
 __shared__ float s_red[32];
@@ -478,7 +479,7 @@ struct PieceCursor {
 // reduction run for 4 rows, the missing ones as zeros).
 template <class Fmt>
 __device__ __forceinline__ PieceCursor step_gemv(int warp, int lane, PieceCursor cur) {
-    constexpr int RPT = Fmt::STEP_RPT;  // rows per piece at most (register budget)
+    constexpr int RPT = Fmt::STEP_RPT;  // rows per slot at most (register budget)
     constexpr int LPR = 32 / RPT;
     const StepOp& op = s_op;
     const StepArgs& a = s_args;
@@ -489,22 +490,22 @@ __device__ __forceinline__ PieceCursor step_gemv(int warp, int lane, PieceCursor
     bool dead = cur.dead != 0;
     unsigned long long best = cur.best;
     const float inv = step_stage_x<Fmt>(op, warp, lane);
-    // row slot `slot` (WS warps, one unit of x per lane) owns every RS-th of
-    // this CTA's pieces; a piece is rpt rows
-    const uint32_t U = op.units, WS = op.ws, RS = op.rs, R = op.prows, stride = op.row_stride;
+    // A piece is R = RS * rpt consecutive rows (one bulk copy of ~32 KB: the
+    // per-SM copy engine needs copies that large to keep up with HBM); row
+    // slot `slot` (WS warps, one unit of x per lane) takes its rpt rows.
+    const uint32_t U = op.units, WS = op.ws, RS = op.rs, R = op.prows, stride = op.row_stride, rpt = op.rpt;
     const uint32_t slot = (uint32_t)warp / WS, wi = (uint32_t)warp % WS;
     const bool active = slot < RS;
     const uint32_t u = wi * 32 + (uint32_t)lane;
-    const bool uact = active && u < U;
+    const uint32_t r0 = slot * rpt;  // this slot's first row in a piece
     const uint32_t pos_op = op.epi == EPI_QKV ? *op.pos : 0u;  // the step's position (RoPE row)
     const uint32_t npieces = op.npieces, rows_pad = op.rows_pad;
-    uint32_t i = 0;
-    for (uint32_t p = blockIdx.x; p < npieces; p += gridDim.x, ++j, ++i) {
+    for (uint32_t p = blockIdx.x; p < npieces; p += gridDim.x, ++j) {
         const uint32_t rows_here = min(R, rows_pad - p * R);
         const uint32_t bytes = rows_here * stride;
         const uint32_t off = head + bytes <= RB ? head : 0u;  // the ring placement, as ring_plan makes it
         head = off + bytes;
-        if (!active || i % RS != slot) continue;  // another row slot's piece
+        if (!active) continue;
         const uint32_t s = j % kStepSlots, ph = (j / kStepSlots) & 1u;
         if (!dead && !step_wait(&s_full[s], ph, abort_flag)) {
             dead = true;
@@ -512,17 +513,17 @@ __device__ __forceinline__ PieceCursor step_gemv(int warp, int lane, PieceCursor
         }
         dead = __any_sync(0xffffffffu, dead);  // warp-uniform (the shuffles below)
         const bool stamp = a.pieces && blockIdx.x == 0 && lane == 0 && j < a.piece_cap;
-        if (stamp && wi == 0) a.pieces[4 * j + 1] = global_ns();
+        if (stamp && warp == 0) a.pieces[4 * j + 1] = global_ns();
         float acc[RPT];
 #pragma unroll
         for (int k = 0; k < RPT; ++k) acc[k] = 0.f;
-        if (uact && !dead) {
+        if (u < U && r0 < rows_here && !dead) {
             XRec xr;  // this thread's unit of x (three-digit record)
             load_xrec(s_dyn, u, xr);
-            const uint8_t* base = ring + off;
+            const uint8_t* base = ring + off + (size_t)r0 * stride;
 #pragma unroll
             for (int k = 0; k < RPT; ++k) {
-                if ((uint32_t)k < rows_here) {
+                if ((uint32_t)k < rpt && r0 + k < rows_here) {
                     typename Fmt::Raw raw;
                     Fmt::load(base + (size_t)k * stride, u, U, raw);
                     acc[k] = Fmt::dot(raw, 0, xr, u);
@@ -531,34 +532,45 @@ __device__ __forceinline__ PieceCursor step_gemv(int warp, int lane, PieceCursor
         }
         // lanes k*LPR .. k*LPR + LPR-1 end with this warp's part of row k
         const float v = warp_reduce_rows<RPT>(acc, lane);
-        if ((lane % LPR) == 0 && (uint32_t)lane / LPR < R) s_part[s * kStepPartRows + (lane / LPR) * WS + wi] = v;
+        if ((lane % LPR) == 0 && (uint32_t)lane / LPR < rpt)
+            s_part[s * kStepPartRows + (r0 + lane / LPR) * WS + wi] = v;
         __syncwarp();
-        // the slot's last warp to finish closes the piece: no warp waits for another
+        // the slot's last warp to finish closes the slot's rows, and the last
+        // slot to close hands the piece back: no warp waits for another
         uint32_t last = 1u;
         if (WS > 1) {
             if (lane == 0) {
                 __threadfence_block();
-                last = atomicAdd(&s_cnt[s], 1u) == WS - 1 ? 1u : 0u;
+                last = atomicAdd(&s_cnt[s * kStepW + slot], 1u) == WS - 1 ? 1u : 0u;
             }
             last = __shfl_sync(0xffffffffu, last, 0);
         }
         if (!last) continue;
         __threadfence_block();
-        if (stamp) a.pieces[4 * j + 2] = global_ns();
-        if (lane == 0) s_cnt[s] = 0u;
-        const uint32_t r = (uint32_t)lane;
-        float val = 0.f;
-        if (r < R)
-            for (uint32_t k = 0; k < WS; ++k) val += s_part[s * kStepPartRows + r * WS + k];
-        val *= inv;  // 1/rms of the fused RMSNorm (1 if plain)
-        const float v_next = __shfl_down_sync(0xffffffffu, val, 1);  // partner row of a pair
-        if (r < rows_here && !dead) {
-            const EpiPre e = step_epi_pre(op, p * R + r, pos_op);
-            step_epilogue(op, p * R + r, val, v_next, e, best);
+        if (lane == 0) s_cnt[s * kStepW + slot] = 0u;
+        {
+            const uint32_t r = r0 + (uint32_t)lane;  // lanes 0..rpt-1: this slot's rows
+            float val = 0.f;
+            if ((uint32_t)lane < rpt)
+                for (uint32_t k = 0; k < WS; ++k) val += s_part[s * kStepPartRows + r * WS + k];
+            val *= inv;  // 1/rms of the fused RMSNorm (1 if plain)
+            const float v_next = __shfl_down_sync(0xffffffffu, val, 1);  // partner row of a pair
+            if ((uint32_t)lane < rpt && r < rows_here && !dead) {
+                const EpiPre e = step_epi_pre(op, p * R + r, pos_op);
+                step_epilogue(op, p * R + r, val, v_next, e, best);
+            }
         }
         __syncwarp();
-        if (lane == 0 && !dead) ring_mark_done(j);
-        if (stamp) a.pieces[4 * j + 3] = global_ns();
+        if (lane == 0) {
+            __threadfence_block();
+            const bool piece_done = RS == 1 || atomicAdd(&s_slots[s], 1u) == RS - 1;
+            if (piece_done) {
+                if (RS > 1) s_slots[s] = 0u;
+                if (stamp) a.pieces[4 * j + 2] = global_ns();
+                if (!dead) ring_mark_done(j);
+                if (stamp) a.pieces[4 * j + 3] = global_ns();
+            }
+        }
     }
     return PieceCursor{j, head, dead ? 1u : 0u, best};
 }
@@ -786,8 +798,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
         s_args = args;
         for (uint32_t s = 0; s < kStepSlots; ++s) {
             mbar_init(&s_full[s], 1);
-            s_cnt[s] = 0u;
+            s_slots[s] = 0u;
         }
+        for (uint32_t q = 0; q < kStepSlots * kStepW; ++q) s_cnt[q] = 0u;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         StepRing& r = s_ring;
         r.retired = r.issued = r.head = 0u;
@@ -961,15 +974,16 @@ void Model::build_step() {
     if (const char* e = std::getenv("SMALLM_STEP_PIECE_KB")) cap = std::min(cap, (size_t)std::atoi(e) * 1024);
     else cap = std::min(cap, (size_t)40 * 1024);
     auto geometry = [&](const QMat& m, StepOp& op) {
-        // WS warps cover a row's units (one per lane), RS = 16 / WS row slots
-        // take turns with this CTA's pieces; a piece is rpt rows (even: the
-        // rotary and SwiGLU row pairs stay in one piece), at most `cap` bytes
+        // WS warps cover a row's units (one per lane); RS = 16 / WS row slots
+        // take rpt rows each of every piece (rpt even: rotary and SwiGLU row
+        // pairs stay in one slot), so a piece is R = RS * rpt rows in one
+        // copy, at most `cap` bytes and a third of the ring
         const uint32_t WS = (m.units + 31) / 32;
         const uint32_t RS = kStepW / WS;
-        const uint32_t rpt_max = m.type == SM_T_Q4_0 ? FmtQ4_0::STEP_RPT : FmtQ8_0::STEP_RPT;
-        uint32_t rpt = rpt_max;
-        while (rpt > 2 && (size_t)rpt * m.row_stride > cap) rpt /= 2;
-        if (RS == 0 || rpt < 2 || (size_t)rpt * m.row_stride > ring / 3)
+        uint32_t rpt = m.type == SM_T_Q4_0 ? FmtQ4_0::STEP_RPT : FmtQ8_0::STEP_RPT;
+        while (rpt > 2 && (size_t)RS * rpt * m.row_stride > cap) rpt /= 2;
+        if (RS == 0 || rpt < 2 || RS * rpt * WS > kStepPartRows ||
+            (size_t)RS * rpt * m.row_stride > ring / 3)
             throw Error(1, "persistent step: no piece geometry for a matrix of " + std::to_string(m.cols) + " columns");
         op.w = m.base;
         op.row_stride = m.row_stride;
@@ -980,8 +994,8 @@ void Model::build_step() {
         op.ws = WS;
         op.rs = RS;
         op.rpt = rpt;
-        op.prows = rpt;
-        op.npieces = (m.rows_pad + rpt - 1) / rpt;
+        op.prows = RS * rpt;
+        op.npieces = (m.rows_pad + op.prows - 1) / op.prows;
     };
 
     std::vector<StepOp> ops;
