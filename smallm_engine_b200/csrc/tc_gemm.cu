@@ -27,7 +27,7 @@
 // shared or tensor memory after the CTA has released them.
 //
 // Operands are f16 (11-bit significands, like TF32's): products are exact in
-// the f32 accumulator.  No cluster launch and no multicast.
+// the f32 accumulator.  No cluster launch: every CTA loads its own tiles.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
