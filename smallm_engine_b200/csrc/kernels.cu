@@ -599,8 +599,8 @@ static GemvPlan mgemv_plan(const QMat& m, size_t limit) {
     pl.pair_bytes = pair_bytes;
     pl.piece_bytes = (size_t)nr * cpairs * pair_bytes;
     pl.xbytes = ((size_t)upairs * kXfragPairBytes + (size_t)2 * upairs * kXconstBytes + 127) / 128 * 128;
-    const size_t misc = 8 + kMgemvWarps * 4 + kMgemvWarps * 8;
-    const size_t per_stage = pl.piece_bytes + 24 + kMgemvPartFloats * 4;
+    const size_t misc = 8 + 8 + kMgemvWarps * 4 + kMgemvWarps * 8;  // xready, counter padding, red, best
+    const size_t per_stage = pl.piece_bytes + 16 + 4 + kMgemvPartFloats * 4;  // full, empty, counter, partials
     if (pl.xbytes + misc + 2 * per_stage > limit)
         throw Error(1, "gemv: rows of " + std::to_string(m.cols) + " columns do not fit the shared-memory pipeline");
     uint32_t S = (uint32_t)((limit - pl.xbytes - misc) / per_stage);

@@ -130,21 +130,21 @@ __device__ __forceinline__ void build_xfrag_lane(float4 q, int lane, bool act, u
     const float up = m > 0.f ? __uint_as_float((uint32_t)(B - e + 127) << 23) : 0.f;
     constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: one FMA rounds x * 2^(B-e) to an integer
     constexpr uint32_t kMagicBits = 0x4B400000u;
-    const float v[4] = {q.x, q.y, q.z, q.w};
-    uint32_t p[3] = {0u, 0u, 0u};
-    int sx = 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int X = (int)(__float_as_uint(fmaf(v[k], up, kMagic)) - kMagicBits);
-        const int a0 = (int)(int8_t)(X & 0xFF);
-        const int X1 = (X - a0) >> 8;
-        const int a1 = (int)(int8_t)(X1 & 0xFF);
-        const int a2 = (X1 - a1) >> 8;
-        p[0] |= (uint32_t)(a0 & 0xFF) << (8 * k);
-        p[1] |= (uint32_t)(a1 & 0xFF) << (8 * k);
-        p[2] |= (uint32_t)(a2 & 0xFF) << (8 * k);
-        sx += X;
-    }
+    // X = rint(x * 2^(B-e)) (|X| <= 2^21) from the low mantissa bits; its
+    // balanced signed-byte digits are the bytes of (X + 0x808080) ^ 0x808080
+    // (adding 128 per byte makes every byte's carry explicit; the XOR maps
+    // byte b to the int8 pattern of b - 128).  Four elements' digit words are
+    // then gathered per digit with byte permutes.
+    const uint32_t b0 = __float_as_uint(fmaf(q.x, up, kMagic)), b1 = __float_as_uint(fmaf(q.y, up, kMagic));
+    const uint32_t b2 = __float_as_uint(fmaf(q.z, up, kMagic)), b3 = __float_as_uint(fmaf(q.w, up, kMagic));
+    constexpr uint32_t kBias = 0x808080u;
+    const uint32_t e0 = (b0 - kMagicBits + kBias) ^ kBias, e1 = (b1 - kMagicBits + kBias) ^ kBias;
+    const uint32_t e2 = (b2 - kMagicBits + kBias) ^ kBias, e3 = (b3 - kMagicBits + kBias) ^ kBias;
+    const uint32_t w01 = __byte_perm(e0, e1, 0x5140), w23 = __byte_perm(e2, e3, 0x5140);
+    const uint32_t v01 = __byte_perm(e0, e1, 0x0062), v23 = __byte_perm(e2, e3, 0x0062);
+    const uint32_t p[3] = {__byte_perm(w01, w23, 0x5410), __byte_perm(w01, w23, 0x7632),
+                           __byte_perm(v01, v23, 0x5410)};
+    int sx = (int)((b0 + b1) + (b2 + b3) - 4u * kMagicBits);
     if constexpr (kOffset) {
 #pragma unroll
         for (int o = 1; o < 8; o <<= 1) sx += __shfl_xor_sync(0xffffffffu, sx, o);
@@ -206,9 +206,12 @@ __device__ __forceinline__ float mma_pairs(const uint8_t* pairs, uint32_t pa, ui
 // nr = 1) through an S-stage ring by one producer lane (bulk copies,
 // mbarrier transaction counts).  Warp w takes row group w / (16 / nr) and a
 // 1/(16 / nr) share of each piece's pairs; a lane keeps one row partial
-// across the chunks of a tile.  After a tile's last piece the warps' 16 row
-// partials meet in shared memory and the first warp of each row group sums
-// them and runs the fused epilogue (gemv_epilogue_row).  Every wait is
+// across the chunks of a tile.  Every warp counts itself done with a piece;
+// the LAST one (no warp waits for another) sums the warps' row partials of a
+// tile's last piece, releases the stage to the producer and runs the fused
+// epilogue (gemv_epilogue_row).  (A fixed warp that waited for the others
+// and then ran the epilogue fell one epilogue further behind per piece and
+// held the stages: two copies in flight instead of four.)  Every wait is
 // bounded: on timeout the kernel raises an error bit and skips the math.
 template <class M, int PRO, int EPI>
 __global__ void __launch_bounds__((kMgemvWarps + 1) * 32, 1) smallm_mgemv_kernel(const GemvParams p) {
@@ -220,8 +223,8 @@ __global__ void __launch_bounds__((kMgemvWarps + 1) * 32, 1) smallm_mgemv_kernel
     const uint32_t S = p.stages;
     uint64_t* full = reinterpret_cast<uint64_t*>(stage0 + (size_t)S * p.piece_bytes);
     uint64_t* empty = full + S;
-    uint64_t* done = empty + S;
-    uint64_t* xready = done + S;
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(empty + S);                         // [S] warps done
+    uint64_t* xready = reinterpret_cast<uint64_t*>(cnt + 2 * ((S + 1) / 2));
     float* red = reinterpret_cast<float*>(xready + 1);                              // [W]
     unsigned long long* best_sh = reinterpret_cast<unsigned long long*>(red + W);  // [W]
     float* part = reinterpret_cast<float*>(best_sh + W);                            // [S][W][16]
@@ -236,8 +239,8 @@ __global__ void __launch_bounds__((kMgemvWarps + 1) * 32, 1) smallm_mgemv_kernel
     if (tid == 0) {
         for (uint32_t s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], W);
-            mbar_init(&done[s], W);
+            mbar_init(&empty[s], 1);
+            cnt[s] = 0u;
         }
         mbar_init(xready, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -282,10 +285,9 @@ __global__ void __launch_bounds__((kMgemvWarps + 1) * 32, 1) smallm_mgemv_kernel
     if (tid == 0) mbar_arrive(xready);  // the producer may fill the rest of the ring
 
     unsigned long long best = 0ull;
-    bool dead = false;  // a bounded wait gave up: skip the math, keep the barrier protocol
+    bool dead = false;  // a bounded wait gave up: skip the math, keep the counting protocol
     const uint32_t WK = (uint32_t)W / (p.rt / 16);
     const uint32_t rg = (uint32_t)warp / WK, kp = (uint32_t)warp % WK;
-    uint32_t done_ph = 0u;  // per stage: parity of its next `done` phase
     float acc = 0.f;
     for (uint32_t j = 0; j < npieces; ++j) {
         const uint32_t s = j % S, c = j % NC;
@@ -296,36 +298,38 @@ __global__ void __launch_bounds__((kMgemvWarps + 1) * 32, 1) smallm_mgemv_kernel
         const uint32_t pc = min(p.cpairs, p.upairs - c * p.cpairs);
         const uint8_t* run = stage0 + (size_t)s * p.piece_bytes + (size_t)rg * pc * p.pair_bytes;
         if (!dead) acc = mma_pairs<M>(run, kp * pc / WK, (kp + 1) * pc / WK, c * p.cpairs, xfrag, xconst, lane, acc);
-        __syncwarp();
-        if (c != NC - 1) {  // more chunks of this tile follow: the row partials stay in registers
-            if (lane == 0) mbar_arrive(&empty[s]);
-            continue;
-        }
-        // lanes t and t^2 hold the two blocks of each pair of the same row
-        const float v = acc + __shfl_xor_sync(0xffffffffu, acc, 2);
-        acc = 0.f;
+        const bool lastc = c == NC - 1;
         float* ps = part + (size_t)s * kMgemvPartFloats;
-        if ((lane & 3) < 2) ps[warp * 16 + (lane >> 2) + 8 * (lane & 1)] = v;
+        if (lastc) {
+            // lanes t and t^2 hold the two blocks of each pair of the same row
+            const float v = acc + __shfl_xor_sync(0xffffffffu, acc, 2);
+            acc = 0.f;
+            if ((lane & 3) < 2) ps[warp * 16 + (lane >> 2) + 8 * (lane & 1)] = v;
+        }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&done[s]);
-        if (kp != 0) {  // the row group's first warp finishes the rows
-            if (lane == 0) mbar_arrive(&empty[s]);
-            continue;
+        uint32_t last = 0u;
+        if (lane == 0) {
+            __threadfence_block();
+            last = atomicAdd(&cnt[s], 1u) == (uint32_t)W - 1u ? 1u : 0u;
         }
-        if (!dead && !mbar_wait(&done[s], (done_ph >> s) & 1u)) {
-            dead = true;
-            if (lane == 0) atomicOr(p.err, 4u);
-        }
-        done_ph ^= 1u << s;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
+        __threadfence_block();
+        // the last warp: lane L sums row L of the tile (nr = 2: lanes 16-31 the second row group)
+        const uint32_t rgl = (uint32_t)lane / 16, rl = (uint32_t)lane % 16;
         float r = 0.f;
-        if (lane < 16)
-            for (uint32_t k = 0; k < WK; ++k) r += ps[(rg * WK + k) * 16 + lane];
+        if (lastc && rgl < p.rt / 16)
+            for (uint32_t k = 0; k < WK; ++k) r += ps[(rgl * WK + k) * 16 + rl];
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);  // every reader of the stage is done
-        r *= inv;                               // 1/rms of the fused RMSNorm (1 if plain)
+        if (lane == 0) {
+            cnt[s] = 0u;
+            mbar_arrive(&empty[s]);  // every reader of the stage and its partials is done
+        }
+        if (!lastc) continue;
+        r *= inv;  // 1/rms of the fused RMSNorm (1 if plain)
         const float r_next = __shfl_down_sync(0xffffffffu, r, 1);  // partner row of a pair
-        const uint32_t row = (blockIdx.x + (j / NC) * gridDim.x) * p.rt + rg * 16 + (uint32_t)lane;
-        if (lane < 16 && !dead) gemv_epilogue_row<EPI>(p, row, r, r_next, best);
+        const uint32_t row = (blockIdx.x + (j / NC) * gridDim.x) * p.rt + (uint32_t)lane;
+        if (rgl < p.rt / 16 && !dead) gemv_epilogue_row<EPI>(p, row, r, r_next, best);
     }
 
     if constexpr (EPI == EPI_LOGITS) {
