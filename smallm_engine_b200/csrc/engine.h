@@ -107,15 +107,7 @@ struct GemvArgs {
     // to theirs (it stages cached K/V while the QKV GEMV runs, and the O
     // GEMV prefetches weights while attention runs).
     size_t smem_cap = 0;
-    // split-K scratch of the tensor-core GEMV (Q4_0 / Q8_0 rows longer than
-    // one piece): partials of split_cap floats, tickets of split_tiles words
-    // (zero, and zero again after every launch); null = no split
-    float* split_part = nullptr;
-    unsigned int* split_ticket = nullptr;
-    size_t split_cap = 0, split_tiles = 0;
 };
-// Scratch a GEMV over `m` needs for split K (floats, tickets); zeros when it does not split.
-void gemv_split_need(const QMat& m, size_t& floats, size_t& tiles);
 
 void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_t stream, bool pdl = false);
 

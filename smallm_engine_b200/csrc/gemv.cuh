@@ -71,13 +71,6 @@ struct GemvParams {
     // pieces of at most cpairs block pairs (upairs per row, pair_bytes per 16
     // rows); a stage holds piece_bytes
     uint32_t upairs, nchunk, cpairs, pair_bytes, piece_bytes;
-    // split K (ksplit = 1, nchunk > 1): CTA b takes chunk b % nchunk of tiles
-    // b / nchunk, + gridDim.x / nchunk, ...; each tile's chunk partials meet
-    // in kpart [tiles][nchunk][16] and the last of its CTAs (kticket [tiles],
-    // zero between launches) sums them in chunk order and runs the epilogue
-    uint32_t ksplit;
-    float* kpart;
-    unsigned int* kticket;
     // input vector and fused RMSNorm
     const float* x;
     const float* norm_w;
@@ -446,11 +439,10 @@ __device__ __forceinline__ void gemv_epilogue_row(const P& p, uint32_t row, floa
 // applied to the row results: x is read once.  Loads are issued in batches of
 // kB granules per thread before any is used; the norm weights (constant) are
 // fetched before the wait.  `red` holds W floats.  Ends with a barrier of the
-// consumer warps.  With [glo, ghi) given, only warps whose granules meet it
-// emit (the sum of squares still covers all of x).
+// consumer warps.
 template <int W, int PRO, class Emit>
 __device__ __forceinline__ float gemv_stage_x(const GemvParams& p, int warp, int lane, uint32_t ngr_pad, float* red,
-                                              Emit emit, uint32_t glo = 0u, uint32_t ghi = ~0u) {
+                                              Emit emit) {
     constexpr int kB = PRO == PRO_PLAIN ? 8 : 4;
     constexpr uint32_t kStride = W * 32;
     constexpr bool kRms = PRO != PRO_PLAIN;
@@ -517,10 +509,8 @@ __device__ __forceinline__ float gemv_stage_x(const GemvParams& p, int warp, int
             const uint32_t g = g0 + ctid + k * kStride;
             // a warp whose first granule lies past the end has no block here
             // (warp-uniform, so the shuffles inside stay whole-warp)
-            const uint32_t gw = g0 + (uint32_t)warp * 32 + k * kStride;
-            if (gw >= ngr_pad) continue;
+            if (g0 + (uint32_t)warp * 32 + k * kStride >= ngr_pad) continue;
             const bool act = g < ngr_pad;
-            const bool emit_here = gw + 32 > glo && gw < ghi;  // the warp's granules meet [glo, ghi)
             float4 q = xq[k];
             if constexpr (kRms) {
                 ss += q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w;
@@ -530,7 +520,7 @@ __device__ __forceinline__ float gemv_stage_x(const GemvParams& p, int warp, int
                 q.z *= w.z;
                 q.w *= w.w;
             }
-            if (emit_here) emit(q, lane, act, g);
+            emit(q, lane, act, g);
         }
     }
     if constexpr (kRms) {

@@ -681,33 +681,14 @@ void set_smem_limit_once(const void* fn, int bytes) {
     done.insert({dev, fn, bytes});
 }
 
-void gemv_split_need(const QMat& m, size_t& floats, size_t& tiles) {
-    floats = tiles = 0;
-    if (!mma_format(m.type)) return;
-    const GemvPlan pl = gemv_plan(m, 0);
-    if (pl.nchunk < 2) return;
-    tiles = m.rows_pad / pl.rt;
-    floats = tiles * pl.nchunk * 16;
-}
-
 void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_t stream, bool pdl) {
     const GemvPlan pl = gemv_plan(m, a.smem_cap);
     const void* fn = gemv_kernel_for(m.type, pro, epi, pl.warps);
     unsigned int* err = device_error_flag();
     set_smem_limit_once(fn, (int)kSmemLimit);
     const uint32_t ntiles = m.rows_pad / pl.rt;
-    const uint32_t sms = (uint32_t)device_sm_count();
-    uint32_t grid = sms;
+    uint32_t grid = (uint32_t)device_sm_count();
     if (grid > ntiles) grid = ntiles;
-    // split K when rows span several pieces and the caller gave scratch:
-    // every CTA converts only its chunk of x and the pieces spread evenly
-    // (measured on 4096x14336 Q4_0: 1.73 tiles of 4 pieces per CTA otherwise)
-    bool ksplit = false;
-    if (mma_format(m.type) && pl.nchunk > 1 && a.split_part && a.split_ticket && pl.nchunk <= sms &&
-        (size_t)ntiles * pl.nchunk * 16 <= a.split_cap && ntiles <= a.split_tiles) {
-        ksplit = true;
-        grid = std::min(sms / pl.nchunk, ntiles) * pl.nchunk;
-    }
 
     GemvParams p{};
     p.w = m.base;
@@ -727,20 +708,12 @@ void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_
     p.cpairs = pl.cpairs;
     p.pair_bytes = pl.pair_bytes;
     p.piece_bytes = (uint32_t)pl.piece_bytes;
-    p.ksplit = ksplit ? 1u : 0u;
-    p.kpart = ksplit ? a.split_part : nullptr;
-    p.kticket = ksplit ? a.split_ticket : nullptr;
-    // the tensor-core GEMV streams its first pieces while x is staged
-    // (measured: 1 us less on 28672x4096 than holding them); the CUDA-core
-    // kernel holds the ring fill behind x staging when the rings cannot take
-    // all of a CTA's tiles (measured: -0.9 us on 28672x4096 and 4096x14336
-    // in the decode step, +0.2 us on the 6144 / 4096-row matrices)
-    if (mma_format(m.type)) {
-        p.hold = ~0u;
-    } else {
-        const uint32_t per_cta = (ntiles + grid - 1) / grid;
-        p.hold = per_cta > pl.stages ? 1u : ~0u;
-    }
+    // hold back the ring fill behind x staging only when the rings cannot take
+    // all of a CTA's pieces (measured on the 4-row-tile kernel: -0.9 us on
+    // 28672x4096 and 4096x14336 in the decode step, +0.2 us on the 6144 /
+    // 4096-row matrices)
+    const uint32_t per_cta = (ntiles + grid - 1) / grid * (pl.nchunk ? pl.nchunk : 1u);
+    p.hold = per_cta > pl.stages ? 1u : ~0u;
     p.x = a.x;
     p.norm_w = a.norm_w;
     p.eps = a.eps;

@@ -232,15 +232,8 @@ __global__ void __launch_bounds__((kMgemvWarps + 1) * 32, 1) smallm_mgemv_kernel
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t ntiles = p.rows_pad / p.rt;
     const uint32_t NC = p.nchunk;
-    // this CTA's pieces: all chunks of tiles tb, tb + G2, ... or, split K,
-    // chunk cfix of them
-    const bool ks = p.ksplit != 0u;
-    const uint32_t G2 = ks ? gridDim.x / NC : gridDim.x;
-    const uint32_t tb = ks ? blockIdx.x / NC : blockIdx.x;
-    const uint32_t cfix = ks ? blockIdx.x % NC : 0u;
-    const uint32_t my_tiles = tb < ntiles ? (ntiles - tb + G2 - 1) / G2 : 0u;
-    const uint32_t per_tile = ks ? 1u : NC;
-    const uint32_t npieces = my_tiles * per_tile;
+    const uint32_t my_tiles = blockIdx.x < ntiles ? (ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0u;
+    const uint32_t npieces = my_tiles * NC;
 
     if (tid == 0) trace_mark(p.trace, 0);
     if (tid == 0) {
@@ -274,7 +267,7 @@ __global__ void __launch_bounds__((kMgemvWarps + 1) * 32, 1) smallm_mgemv_kernel
                     atomicOr(p.err, 1u);  // consumers then time out once and skip their work
                     break;
                 }
-                const uint32_t t = tb + (j / per_tile) * G2, c = ks ? cfix : j % NC;
+                const uint32_t t = blockIdx.x + (j / NC) * gridDim.x, c = j % NC;
                 const uint32_t pc = min(p.cpairs, p.upairs - c * p.cpairs);
                 const uint32_t bytes = nr * pc * p.pair_bytes;
                 mbar_arrive_expect_tx(&full[s], bytes);
@@ -285,13 +278,10 @@ __global__ void __launch_bounds__((kMgemvWarps + 1) * 32, 1) smallm_mgemv_kernel
         return;
     }
 
-    // split K: only this CTA's chunk of x is converted
-    const uint32_t glo = ks ? cfix * p.cpairs * 16u : 0u;
-    const uint32_t ghi = ks ? min(p.upairs, (cfix + 1) * p.cpairs) * 16u : ~0u;
-    const float inv = gemv_stage_x<W, PRO>(
-        p, warp, lane, p.upairs * 16u, red,
-        [&](float4 q, int ln, bool act, uint32_t g) { build_xfrag_lane<M::kOffset>(q, ln, act, g >> 3, xfrag, xconst); },
-        glo, ghi);
+    const float inv = gemv_stage_x<W, PRO>(p, warp, lane, p.upairs * 16u, red,
+                                           [&](float4 q, int ln, bool act, uint32_t g) {
+                                               build_xfrag_lane<M::kOffset>(q, ln, act, g >> 3, xfrag, xconst);
+                                           });
     if (tid == 0) mbar_arrive(xready);  // the producer may fill the rest of the ring
 
     unsigned long long best = 0ull;
@@ -300,8 +290,7 @@ __global__ void __launch_bounds__((kMgemvWarps + 1) * 32, 1) smallm_mgemv_kernel
     const uint32_t rg = (uint32_t)warp / WK, kp = (uint32_t)warp % WK;
     float acc = 0.f;
     for (uint32_t j = 0; j < npieces; ++j) {
-        const uint32_t s = j % S, c = ks ? cfix : j % NC;
-        const uint32_t t = tb + (j / per_tile) * G2;
+        const uint32_t s = j % S, c = j % NC;
         if (!dead && !mbar_wait(&full[s], (j / S) & 1u)) {
             dead = true;
             if (lane == 0) atomicOr(p.err, 2u);
@@ -309,7 +298,7 @@ __global__ void __launch_bounds__((kMgemvWarps + 1) * 32, 1) smallm_mgemv_kernel
         const uint32_t pc = min(p.cpairs, p.upairs - c * p.cpairs);
         const uint8_t* run = stage0 + (size_t)s * p.piece_bytes + (size_t)rg * pc * p.pair_bytes;
         if (!dead) acc = mma_pairs<M>(run, kp * pc / WK, (kp + 1) * pc / WK, c * p.cpairs, xfrag, xconst, lane, acc);
-        const bool lastc = ks || c == NC - 1;  // this CTA's last piece of the tile
+        const bool lastc = c == NC - 1;
         float* ps = part + (size_t)s * kMgemvPartFloats;
         if (lastc) {
             // lanes t and t^2 hold the two blocks of each pair of the same row
@@ -337,27 +326,9 @@ __global__ void __launch_bounds__((kMgemvWarps + 1) * 32, 1) smallm_mgemv_kernel
             mbar_arrive(&empty[s]);  // every reader of the stage and its partials is done
         }
         if (!lastc) continue;
-        if (ks) {
-            // the tile's chunk partials meet in global memory; the last of
-            // its CTAs adds them in chunk order (the same sum whichever CTA
-            // is last) and finishes the rows
-            float* kp_t = p.kpart + (size_t)t * NC * 16;
-            if (lane < 16) __stcg(kp_t + (size_t)cfix * 16 + lane, r);
-            __threadfence();
-            __syncwarp();
-            uint32_t win = 0u;
-            if (lane == 0) win = atomicAdd(p.kticket + t, 1u) == NC - 1u ? 1u : 0u;
-            win = __shfl_sync(0xffffffffu, win, 0);
-            if (!win) continue;
-            __threadfence();
-            r = 0.f;
-            if (lane < 16)
-                for (uint32_t k = 0; k < NC; ++k) r += __ldcg(kp_t + (size_t)k * 16 + lane);
-            if (lane == 0) p.kticket[t] = 0u;
-        }
         r *= inv;  // 1/rms of the fused RMSNorm (1 if plain)
         const float r_next = __shfl_down_sync(0xffffffffu, r, 1);  // partner row of a pair
-        const uint32_t row = t * p.rt + (uint32_t)lane;
+        const uint32_t row = (blockIdx.x + (j / NC) * gridDim.x) * p.rt + (uint32_t)lane;
         if (rgl < p.rt / 16 && !dead) gemv_epilogue_row<EPI>(p, row, r, r_next, best);
     }
 

@@ -335,24 +335,6 @@ void Model::load(const std::string& path, const smallm_model_opts& o) {
     st = static_cast<DecodeState*>(dalloc(sizeof(DecodeState)));
     SM_CUDA(cudaMemsetAsync(st, 0, sizeof(DecodeState), stream));
     keys = static_cast<unsigned long long*>(dalloc(8ull * tp_size));
-    {
-        // split-K scratch for the largest GEMV that splits (rows of several pieces)
-        std::vector<const QMat*> mats{&out_m};
-        for (const LayerW& L : layers)
-            for (const QMat* m : {&L.qkv, &L.v, &L.o, &L.gu, &L.down})
-                if (m->base) mats.push_back(m);
-        for (const QMat* m : mats) {
-            size_t f = 0, t = 0;
-            gemv_split_need(*m, f, t);
-            split_cap = std::max(split_cap, f);
-            split_tiles = std::max(split_tiles, t);
-        }
-        if (split_cap) {
-            split_part = static_cast<float*>(dalloc(4 * split_cap));
-            split_ticket = static_cast<unsigned int*>(dalloc(4 * split_tiles));
-            SM_CUDA(cudaMemsetAsync(split_ticket, 0, 4 * split_tiles, stream));
-        }
-    }
     ids_cap = max_ctx;
     ids = static_cast<uint32_t*>(dalloc(4ull * ids_cap));
     SM_CUDA(cudaHostAlloc(&h_st, sizeof(DecodeState), cudaHostAllocDefault));
@@ -480,7 +462,6 @@ void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
         a.trace = slot(TK_QKV);
         a.smem_cap = gemv_cap_attn;
         if (sum_in) gather(a, 2 * i - 1);
-        with_split(a);
         launch_gemv(L.qkv, sum_in ? GEMV_PRO_RMS_SUM : GEMV_PRO_RMS, GEMV_EPI_QKV, a, s, pdl);
         if (!L.fused_v) {
             GemvArgs av = a;
@@ -511,7 +492,6 @@ void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
         ao.trace = slot(TK_O);
         ao.smem_cap = gemv_cap_attn;
         if (tpx) send(ao, 2 * i);
-        with_split(ao);
         launch_gemv(L.o, GEMV_PRO_PLAIN, tpx ? GEMV_EPI_PEER : GEMV_EPI_RESIDUAL, ao, s, pdl);
 
         GemvArgs ag;
@@ -521,7 +501,6 @@ void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
         ag.y = hbuf;
         ag.trace = slot(TK_GATE_UP);
         if (tpx) gather(ag, 2 * i);
-        with_split(ag);
         launch_gemv(L.gu, tpx ? GEMV_PRO_RMS_SUM : GEMV_PRO_RMS, GEMV_EPI_SWIGLU, ag, s, pdl);
 
         GemvArgs ad;
@@ -529,7 +508,6 @@ void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
         ad.y = x;
         ad.trace = slot(TK_DOWN);
         if (tpx) send(ad, 2 * i + 1);
-        with_split(ad);
         launch_gemv(L.down, GEMV_PRO_PLAIN, tpx ? GEMV_EPI_PEER : GEMV_EPI_RESIDUAL, ad, s, pdl);
     }
     GemvArgs al;
@@ -541,7 +519,6 @@ void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
     al.row_offset = v0;
     al.trace = slot(TK_LM_HEAD);
     if (tpx) gather(al, 2 * n_layers - 1);
-    with_split(al);
     launch_gemv(out_m, tpx ? GEMV_PRO_RMS_SUM : GEMV_PRO_RMS, GEMV_EPI_LOGITS, al, s, pdl);
     if (tpx) {
         nccl_check(ncclAllGather(&st->argmax, keys, 1, ncclUint64, comm, s), "ncclAllGather");
@@ -758,7 +735,6 @@ void Model::prefill(const uint32_t* tokens, uint32_t T, uint32_t pos0, float* ou
     al.y = logits_local;
     al.argmax = &st->argmax;
     al.row_offset = v0;
-    with_split(al);
     launch_gemv(out_m, GEMV_PRO_RMS, GEMV_EPI_LOGITS, al, stream);
     if (out_logits) SM_CUDA(cudaMemcpyAsync(out_logits, logits, 4ull * vocab, cudaMemcpyDeviceToHost, stream));
     SM_CUDA(cudaMemcpyAsync(h_st, st, sizeof(DecodeState), cudaMemcpyDeviceToHost, stream));

@@ -45,16 +45,6 @@ struct Model {
     float *logits = nullptr, *logits_local = nullptr;
     uint32_t attn_cluster = 1;  // CTAs per KV head in the cluster attention
     size_t gemv_cap_attn = 0;   // shared-memory cap of the QKV / O GEMVs (room for an attention CTA)
-    // split-K scratch shared by the model's GEMVs (one runs at a time on the stream)
-    float* split_part = nullptr;
-    unsigned int* split_ticket = nullptr;
-    size_t split_cap = 0, split_tiles = 0;
-    void with_split(GemvArgs& a) const {
-        a.split_part = split_part;
-        a.split_ticket = split_ticket;
-        a.split_cap = split_cap;
-        a.split_tiles = split_tiles;
-    }
     // Tensor parallelism (tp_size > 1): the residual is all-reduced through
     // peer memory by the GEMVs themselves (gemv.cuh EPI_PEER / PRO_RMS_SUM).
     // xchg (this rank's, mapped into every peer) holds the receive buffers
