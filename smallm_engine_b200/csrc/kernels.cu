@@ -708,12 +708,17 @@ void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_
     p.cpairs = pl.cpairs;
     p.pair_bytes = pl.pair_bytes;
     p.piece_bytes = (uint32_t)pl.piece_bytes;
-    // hold back the ring fill behind x staging only when the rings cannot take
-    // all of a CTA's pieces (measured on the 4-row-tile kernel: -0.9 us on
-    // 28672x4096 and 4096x14336 in the decode step, +0.2 us on the 6144 /
-    // 4096-row matrices)
-    const uint32_t per_cta = (ntiles + grid - 1) / grid * (pl.nchunk ? pl.nchunk : 1u);
-    p.hold = per_cta > pl.stages ? 1u : ~0u;
+    // the tensor-core GEMV streams its first pieces while x is staged
+    // (measured: 1 us less on 28672x4096 than holding them); the CUDA-core
+    // kernel holds the ring fill behind x staging when the rings cannot take
+    // all of a CTA's tiles (measured: -0.9 us on 28672x4096 and 4096x14336
+    // in the decode step, +0.2 us on the 6144 / 4096-row matrices)
+    if (mma_format(m.type)) {
+        p.hold = ~0u;
+    } else {
+        const uint32_t per_cta = (ntiles + grid - 1) / grid;
+        p.hold = per_cta > pl.stages ? 1u : ~0u;
+    }
     p.x = a.x;
     p.norm_w = a.norm_w;
     p.eps = a.eps;
