@@ -7,30 +7,6 @@
 
 namespace smallm {
 
-// Tiled Q4_0 / Q8_0 storage (mgemv.cuh): rows in tiles of 16, a tile = its
-// block pairs (blocks 2p, 2p+1) of pair_bytes; units pad to even.
-// Byte offsets of storage row r, block u within the matrix:
-__device__ __forceinline__ size_t tiled_pair_base(uint32_t row_stride, uint32_t pair_bytes, uint32_t r, uint32_t u) {
-    return (size_t)(r / 16) * 16 * row_stride + (size_t)(u >> 1) * pair_bytes;
-}
-// Q4_0 nibble byte i (0..15: element i in the low nibble, i + 16 in the high)
-__device__ __forceinline__ size_t tiled_q4_0_byte(uint32_t row_stride, uint32_t r, uint32_t u, uint32_t i) {
-    const uint32_t rr = r % 16, g = rr % 8, hi = rr / 8, h = u & 1u;
-    return tiled_pair_base(row_stride, 576, r, u) + (g * 4 + i / 4) * 16 + (2 * h + hi) * 4 + i % 4;
-}
-// Q8_0 code k (0..31)
-__device__ __forceinline__ size_t tiled_q8_0_byte(uint32_t row_stride, uint32_t r, uint32_t u, uint32_t k) {
-    const uint32_t rr = r % 16, g = rr % 8, hi = rr / 8, h = u & 1u;
-    return tiled_pair_base(row_stride, 1088, r, u) + h * 512 + (g * 4 + (k % 16) / 4) * 16 + (2 * (k / 16) + hi) * 4 +
-           k % 4;
-}
-// f16 scale of (r, u); scale_off 512 (Q4_0) or 1024 (Q8_0)
-__device__ __forceinline__ size_t tiled_scale_byte(uint32_t row_stride, uint32_t pair_bytes, uint32_t scale_off,
-                                                   uint32_t r, uint32_t u) {
-    const uint32_t rr = r % 16, g = rr % 8, hi = rr / 8, h = u & 1u;
-    return tiled_pair_base(row_stride, pair_bytes, r, u) + scale_off + (4 * g + 2 * h + hi) * 2;
-}
-
 // 32 consecutive elements (group g of storage row r) of a repacked matrix,
 // with the reference's exact arithmetic per type (src/core/tensor.cpp:20-111;
 // Q4_K as gguf-py's Q4_K.dequantize_blocks).
@@ -43,20 +19,20 @@ static __device__ __forceinline__ void dequant_group(const QMat m, uint32_t r, u
             break;
         }
         case SM_T_Q4_0: {
-            const uint8_t* s = m.base + tiled_scale_byte(m.row_stride, 576, 512, r, g);
+            const uint8_t* q = row + (size_t)g * 16;
+            const uint8_t* s = row + (size_t)m.units * 16 + (size_t)g * 2;
             const float d = f16_exact(s[0] | (s[1] << 8));
-            for (uint32_t k = 0; k < 16; ++k) {
-                const uint8_t q = m.base[tiled_q4_0_byte(m.row_stride, r, g, k)];
-                out[k] = __fmul_rn(d, (float)((int)(q & 0xF) - 8));
-                out[k + 16] = __fmul_rn(d, (float)((int)(q >> 4) - 8));
+            for (int k = 0; k < 16; ++k) {
+                out[k] = __fmul_rn(d, (float)((int)(q[k] & 0xF) - 8));
+                out[k + 16] = __fmul_rn(d, (float)((int)(q[k] >> 4) - 8));
             }
             break;
         }
         case SM_T_Q8_0: {
-            const uint8_t* s = m.base + tiled_scale_byte(m.row_stride, 1088, 1024, r, g);
+            const int8_t* q = reinterpret_cast<const int8_t*>(row + (size_t)g * 32);
+            const uint8_t* s = row + (size_t)m.units * 32 + (size_t)g * 2;
             const float d = f16_exact(s[0] | (s[1] << 8));
-            for (uint32_t k = 0; k < 32; ++k)
-                out[k] = __fmul_rn(d, (float)(int8_t)m.base[tiled_q8_0_byte(m.row_stride, r, g, k)]);
+            for (int k = 0; k < 32; ++k) out[k] = __fmul_rn(d, (float)q[k]);
             break;
         }
         case SM_T_Q4_K: {

@@ -120,9 +120,6 @@ void set_smem_limit_once(const void* fn, int bytes);
 struct GemvPlan {
     uint32_t rt = 0, stages = 0, ngroups = 0, gsize = 0, kring = 0, warps = 0;
     size_t xbytes = 0, smem = 0;
-    // tensor-core GEMV (Q4_0, Q8_0): pieces of a tile and their sizes
-    uint32_t nchunk = 0, cpairs = 0, upairs = 0, pair_bytes = 0;
-    size_t piece_bytes = 0;
 };
 GemvPlan gemv_plan(const QMat& m, size_t smem_cap = 0);
 

@@ -1,9 +1,5 @@
 // Batch-1 quantized GEMV for sm_100a: y = W . x, W in a repacked GGUF block
-// layout streamed once from HBM.  This file holds what every GEMV shares --
-// parameters, the x fixed point, the x staging and the fused epilogues --
-// and the CUDA-core kernel for the super-block and float formats (Q4_K,
-// Q6_K, F32).  Q4_0 and Q8_0, the formats of the measured workloads, run on
-// the integer tensor cores (mgemv.cuh).
+// layout streamed once from HBM, CUDA cores only.
 //
 // Memory side -- a TMA bulk-copy pipeline.  The device layout stores every
 // row as one contiguous, 16-byte padded record (quants, then scales), so a
@@ -32,8 +28,10 @@
 // order of the f32 rounding of the reference's FMA chain.  A block's integer
 // weight codes q meet x through IDP4A, one exact sum S_d = sum_i q_i D_d,i per
 // digit; the digits are joined in float and the block needs one float scale
-// (weight scale * 2^(e-21)).  The norm's 1/rms is a scalar and is applied to
-// the row results in the epilogue.
+// (weight scale * 2^(e-21)).  4-bit codes are masked in place (the high
+// nibble as 16 q, no shift), so a 32-weight block costs 8 masks and 24 IDP4A.
+// The norm's 1/rms is a scalar and is applied to the row results in the
+// epilogue.
 //
 // Epilogues (fused): plain store, residual add, Q/K/V bias + RoPE + KV-cache
 // append, SwiGLU, logits + greedy argmax.
@@ -47,9 +45,14 @@ enum { PRO_PLAIN = 0, PRO_RMS = 1, PRO_RMS_SUM = 2 };
 enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4, EPI_PEER = 5 };
 constexpr int kMaxTP = 8;
 
-// Consumer warps per CTA of the CUDA-core kernel (one producer warp more; a
-// kernel template parameter, at most Fmt::WIDE for the dot's registers).
-constexpr int kGemvMaxWarps = 16;
+// Consumer warps per CTA (one producer warp more; a kernel template
+// parameter): 16, or 22 for Q4_0 rows of >= 256 units (8192 columns), where
+// the extra warps share the x staging of the long row (measured on the
+// 4096x14336 down projection: 11.86 -> 10.86 us; on 4096-column rows they
+// cost 0.26 us).  22 warps fit 72 registers per thread with room left on the
+// SM for the decode attention's CTAs; the other formats' dots need more
+// registers than 22 warps allow (Fmt::WIDE).
+constexpr int kGemvMaxWarps = 22;
 constexpr int kMaxRT = 32;                                   // storage rows pad to this
 
 struct GemvParams {
@@ -67,10 +70,6 @@ struct GemvParams {
     uint32_t kring;     // stages per ring
     uint32_t xbytes;    // bytes of the staged x region
     uint32_t hold;      // the producer's j-th tile per ring waits for x to be staged (~0u: never)
-    // tensor-core GEMV (mgemv.cuh): a tile of rt = 16 * nr rows is nchunk
-    // pieces of at most cpairs block pairs (upairs per row, pair_bytes per 16
-    // rows); a stage holds piece_bytes
-    uint32_t upairs, nchunk, cpairs, pair_bytes, piece_bytes;
     // input vector and fused RMSNorm
     const float* x;
     const float* norm_w;
@@ -244,11 +243,75 @@ __device__ __forceinline__ float combine(int s0, int s1, int s2) {
 }
 
 // ---------------------------------------------------------------- formats --
-// Device row records (kernels.cu: qmat_alloc / repack; Q4_0 and Q8_0 are
-// stored in the 16-row tiles of the tensor-core GEMV, mgemv.cuh):
+// Device row records (kernels.cu: qmat_alloc / repack):
+//  Q4_0  [units][16 B nibbles] [units][f16 d]          unit = one 32-block
+//  Q8_0  [units][32 B int8]    [units][f16 d]          unit = one 32-block
 //  Q4_K  [nsb][144 B GGUF super-block]                 unit = quarter super-block (64)
 //  Q6_K  [units][48 B codes]   [units][4 x i8 scale] [nsb][f16 d]   unit = 64
 //  F32   [cols][f32]                                   unit = 32 values
+
+// Q4_0: element i of a block is the low nibble of byte i, element i+16 the
+// high nibble (src/core/tensor.cpp:57-63); value (q - 8) * d.  Low nibbles
+// are masked to q, high nibbles masked in place to 16 q (no shift); per digit
+// 16 sum (q - 8) D = 16 L + H - 128 sum D is exact in int32 and below 2^21,
+// and the three digits are joined in float (the record's scale carries 1/16).
+struct FmtQ4_0 {
+    static constexpr int UE = 32, SUBS = 1, WIDE = 22, XK = XK_NIB_SD;
+    static constexpr int STEP_RPT = 4;  // rows per thread and piece in the persistent step
+    static constexpr bool F32X = false;
+    struct Raw { uint4 q; uint32_t s; };
+    __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t units, Raw& r) {
+        r.q = *reinterpret_cast<const uint4*>(row + (size_t)u * 16);
+        r.s = *reinterpret_cast<const uint16_t*>(row + (size_t)units * 16 + (size_t)u * 2);
+    }
+    __device__ __forceinline__ static float dot(const Raw& r, int, const XRec& x, uint32_t) {
+        const uint32_t w[4] = {r.q.x, r.q.y, r.q.z, r.q.w};
+        int l0 = 0, l1 = 0, l2 = 0, h0 = 0, h1 = 0, h2 = 0;  // low nibbles (q) / high nibbles in place (16 q)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t lo = w[j] & 0x0F0F0F0Fu, hi = w[j] & 0xF0F0F0F0u;
+            l0 = dp4a_us(lo, x.d[0][j], l0);
+            l1 = dp4a_us(lo, x.d[1][j], l1);
+            l2 = dp4a_us(lo, x.d[2][j], l2);
+            h0 = dp4a_us(hi, x.d[0][4 + j], h0);
+            h1 = dp4a_us(hi, x.d[1][4 + j], h1);
+            h2 = dp4a_us(hi, x.d[2][4 + j], h2);
+        }
+        const int v0 = 16 * l0 + h0 - 128 * x.s0;
+        const int v1 = 16 * l1 + h1 - 128 * x.s1;
+        const int v2 = 16 * l2 + h2 - 128 * (int)x.s2;
+        return combine(v0, v1, v2) * (h2f(r.s) * x.xs);
+    }
+};
+
+// Q8_0: int8 codes; value q * d.
+struct FmtQ8_0 {
+    static constexpr int UE = 32, SUBS = 1, WIDE = 16, XK = XK_PLAIN;
+    static constexpr int STEP_RPT = 2;  // rows per thread and piece in the persistent step (registers)
+    static constexpr bool F32X = false;
+    struct Raw { uint4 a, b; uint32_t s; };
+    __device__ __forceinline__ static void load(const uint8_t* row, uint32_t u, uint32_t units, Raw& r) {
+        const uint4* q = reinterpret_cast<const uint4*>(row + (size_t)u * 32);
+        // lanes with bit 2 of u set read the upper half first, so the 8 lanes
+        // of each quarter-warp touch distinct banks in both loads
+        const uint32_t f = (u >> 2) & 1u;
+        const uint4 first = q[f], second = q[f ^ 1u];
+        r.a = f ? second : first;
+        r.b = f ? first : second;
+        r.s = *reinterpret_cast<const uint16_t*>(row + (size_t)units * 32 + (size_t)u * 2);
+    }
+    __device__ __forceinline__ static float dot(const Raw& r, int, const XRec& x, uint32_t) {
+        const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
+        int s0 = 0, s1 = 0, s2 = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            s0 = __dp4a((int)w[j], (int)x.d[0][j], s0);
+            s1 = __dp4a((int)w[j], (int)x.d[1][j], s1);
+            s2 = __dp4a((int)w[j], (int)x.d[2][j], s2);
+        }
+        return combine(s0, s1, s2) * (h2f(r.s) * x.xs);
+    }
+};
 
 // Q4_K: GGUF super-blocks {f16 d, f16 dmin, 12 B packed 6-bit scales/mins,
 // 128 B nibbles}; a unit is a quarter super-block: sub-block 2k = low
@@ -424,120 +487,6 @@ __device__ __forceinline__ void gemv_epilogue_row(const P& p, uint32_t row, floa
     }
 }
 
-// ------------------------------------------------------------ x staging --
-
-// Stage x for a GEMV: all W consumer warps of the CTA call it (before they
-// read the weights; it contains the kernel's griddepcontrol.wait).  It reads
-// x -- for PRO_RMS_SUM the residual x_res plus every rank's received partial,
-// in rank order, after the bounded wait for their arrival flags (CTA 0 stores
-// the sum to x_out) -- multiplies it by the RMSNorm weight when the norm is
-// fused, and hands each float4 granule g < ngr_pad to emit(q, lane, act, g):
-// 8 consecutive lanes hold the 8 granules of one 32-element block and every
-// call is warp-uniform (the emitters shuffle); granules at or past cols/4 are
-// zero (padding blocks).  RMSNorm is linear in x given its scalar, so the
-// staged values are x * w and the returned 1/rms (1 without a norm) is
-// applied to the row results: x is read once.  Loads are issued in batches of
-// kB granules per thread before any is used; the norm weights (constant) are
-// fetched before the wait.  `red` holds W floats.  Ends with a barrier of the
-// consumer warps.
-template <int W, int PRO, class Emit>
-__device__ __forceinline__ float gemv_stage_x(const GemvParams& p, int warp, int lane, uint32_t ngr_pad, float* red,
-                                              Emit emit) {
-    constexpr int kB = PRO == PRO_PLAIN ? 8 : 4;
-    constexpr uint32_t kStride = W * 32;
-    constexpr bool kRms = PRO != PRO_PLAIN;
-    const int ctid = warp * 32 + lane;
-    const float4* x4 = reinterpret_cast<const float4*>(p.x);
-    const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
-    const uint32_t ngr = p.cols / 4;  // a multiple of 8: whole blocks are in or out
-    float4 wpre[kB];
-    if constexpr (kRms) {
-#pragma unroll
-        for (int k = 0; k < kB; ++k) {
-            const uint32_t g = ctid + k * kStride;
-            wpre[k] = g < ngr ? w4[g] : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-    }
-    pdl_wait();
-    if (ctid == 0) trace_mark(p.trace, 1);
-    if constexpr (PRO == PRO_RMS_SUM) {
-        // every rank's partial of the previous row-parallel GEMV must have
-        // arrived (bounded wait; on timeout the error flag is raised and the
-        // step's result is not valid)
-        if (ctid == 0) {
-            const unsigned int want = __ldcg(p.epoch) + 1u;
-            const long long t0 = clock64();
-            for (uint32_t r = 0; r < p.tp; ++r) {
-                while (ld_acquire_sys(p.rx_flag + r) != want) {
-                    if (clock64() - t0 > (1ll << 31)) {
-                        atomicOr(p.err, 8u);
-                        break;
-                    }
-                    __nanosleep(32);
-                }
-            }
-        }
-        consumers_sync<W>();
-    }
-    const float4* xr4 = reinterpret_cast<const float4*>(p.rx);
-    float ss = 0.f;
-    for (uint32_t g0 = 0; g0 < ngr_pad; g0 += kB * kStride) {
-        float4 xq[kB];
-#pragma unroll
-        for (int k = 0; k < kB; ++k) {
-            const uint32_t g = g0 + ctid + k * kStride;
-            if constexpr (PRO == PRO_RMS_SUM) {
-                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (g < ngr) {
-                    v = reinterpret_cast<const float4*>(p.x_res)[g];
-                    for (uint32_t r = 0; r < p.tp; ++r) {  // rank order: the same sum on every rank
-                        const float4 d = __ldcg(xr4 + (size_t)r * ngr + g);
-                        v.x += d.x;
-                        v.y += d.y;
-                        v.z += d.z;
-                        v.w += d.w;
-                    }
-                    if (blockIdx.x == 0) reinterpret_cast<float4*>(p.x_out)[g] = v;
-                }
-                xq[k] = v;
-            } else {
-                xq[k] = g < ngr ? x4[g] : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < kB; ++k) {
-            const uint32_t g = g0 + ctid + k * kStride;
-            // a warp whose first granule lies past the end has no block here
-            // (warp-uniform, so the shuffles inside stay whole-warp)
-            if (g0 + (uint32_t)warp * 32 + k * kStride >= ngr_pad) continue;
-            const bool act = g < ngr_pad;
-            float4 q = xq[k];
-            if constexpr (kRms) {
-                ss += q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w;
-                const float4 w = g0 == 0 ? wpre[k] : (g < ngr ? w4[g] : make_float4(0.f, 0.f, 0.f, 0.f));
-                q.x *= w.x;
-                q.y *= w.y;
-                q.z *= w.z;
-                q.w *= w.w;
-            }
-            emit(q, lane, act, g);
-        }
-    }
-    if constexpr (kRms) {
-        ss = warp_sum(ss);
-        if (lane == 0) red[warp] = ss;
-    }
-    consumers_sync<W>();
-    float inv = 1.0f;
-    if constexpr (kRms) {
-        float t = 0.f;
-#pragma unroll
-        for (int k = 0; k < W; ++k) t += red[k];
-        inv = 1.0f / sqrtf(t / (float)p.cols + p.eps);
-    }
-    return inv;
-}
-
 // ------------------------------------------------------------------ kernel --
 
 template <class Fmt, int PRO, int EPI, int W>  // W consumer warps; warp W is the producer
@@ -605,17 +554,109 @@ __global__ void __launch_bounds__((W + 1) * 32, 1) smallm_qgemv_kernel(const Gem
 
     // ---------------- consumers: stage x (after the producer of x finished)
     const int ctid = tid;  // 0 .. 32 * W - 1
-    float inv = 1.0f;
-    if constexpr (Fmt::F32X) {
-        inv = gemv_stage_x<W, PRO>(p, warp, lane, p.cols / 4, red, [&](float4 q, int, bool act, uint32_t g) {
-            if (act) reinterpret_cast<float4*>(xreg)[g] = q;
-        });
-    } else {
-        inv = gemv_stage_x<W, PRO>(p, warp, lane, p.cols / 4, red, [&](float4 q, int ln, bool act, uint32_t g) {
-            build_xrec_lane<Fmt::XK>(q, ln, act, xreg + (size_t)(g >> 3) * kXrecBytes);
-        });
+    // RMSNorm is linear in x given its scalar: the records hold x * w and the
+    // epilogue multiplies each row result by 1/rms, so x is read only once.
+    // 8 consecutive lanes own the 8 float4 granules of one 32-element block;
+    // loads are issued in batches of kB granules per thread before any of them
+    // is used (one batch covers 8192 columns with the norm, 16384 without),
+    // and the norm weights (constant) are fetched before the wait.
+    constexpr int kB = PRO == PRO_PLAIN ? 8 : 4;
+    constexpr uint32_t kStride = W * 32;
+    const float4* x4 = reinterpret_cast<const float4*>(p.x);
+    const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
+    const uint32_t ngr = p.cols / 4;  // a multiple of 8: whole blocks are in or out
+    constexpr bool kRms = PRO != PRO_PLAIN;
+    float4 wpre[kB];
+    if constexpr (kRms) {
+#pragma unroll
+        for (int k = 0; k < kB; ++k) {
+            const uint32_t g = ctid + k * kStride;
+            wpre[k] = g < ngr ? w4[g] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
     }
+    pdl_wait();
+    if (ctid == 0) trace_mark(p.trace, 1);
+    if constexpr (PRO == PRO_RMS_SUM) {
+        // every rank's partial of the previous row-parallel GEMV must have
+        // arrived (bounded wait; on timeout the error flag is raised and the
+        // step's result is not valid)
+        if (ctid == 0) {
+            const unsigned int want = __ldcg(p.epoch) + 1u;
+            const long long t0 = clock64();
+            for (uint32_t r = 0; r < p.tp; ++r) {
+                while (ld_acquire_sys(p.rx_flag + r) != want) {
+                    if (clock64() - t0 > (1ll << 31)) {
+                        atomicOr(p.err, 8u);
+                        break;
+                    }
+                    __nanosleep(32);
+                }
+            }
+        }
+        consumers_sync<W>();
+    }
+    const float4* xr4 = reinterpret_cast<const float4*>(p.rx);
+    float ss = 0.f;
+    for (uint32_t g0 = 0; g0 < ngr; g0 += kB * kStride) {
+        float4 xq[kB];
+#pragma unroll
+        for (int k = 0; k < kB; ++k) {
+            const uint32_t g = g0 + ctid + k * kStride;
+            if constexpr (PRO == PRO_RMS_SUM) {
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (g < ngr) {
+                    v = reinterpret_cast<const float4*>(p.x_res)[g];
+                    for (uint32_t r = 0; r < p.tp; ++r) {  // rank order: the same sum on every rank
+                        const float4 d = __ldcg(xr4 + (size_t)r * ngr + g);
+                        v.x += d.x;
+                        v.y += d.y;
+                        v.z += d.z;
+                        v.w += d.w;
+                    }
+                    if (blockIdx.x == 0) reinterpret_cast<float4*>(p.x_out)[g] = v;
+                }
+                xq[k] = v;
+            } else {
+                xq[k] = g < ngr ? x4[g] : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kB; ++k) {
+            const uint32_t g = g0 + ctid + k * kStride;
+            // a warp whose first granule lies past the end has no block here
+            // (warp-uniform, so the shuffles inside stay whole-warp)
+            if (g0 + (uint32_t)warp * 32 + k * kStride >= ngr) continue;
+            const bool act = g < ngr;
+            float4 q = xq[k];
+            if constexpr (kRms) {
+                ss += q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w;
+                const float4 w = g0 == 0 ? wpre[k] : (act ? w4[g] : make_float4(0.f, 0.f, 0.f, 0.f));
+                q.x *= w.x;
+                q.y *= w.y;
+                q.z *= w.z;
+                q.w *= w.w;
+            }
+            if constexpr (Fmt::F32X) {
+                if (act) reinterpret_cast<float4*>(xreg)[g] = q;
+            } else {
+                // uniform across the warp: all lanes reach the shuffles inside
+                build_xrec_lane<Fmt::XK>(q, lane, act, xreg + (size_t)(g >> 3) * kXrecBytes);
+            }
+        }
+    }
+    float inv = 1.0f;
+    if constexpr (kRms) {
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+    }
+    consumers_sync<W>();
     if (ctid == 0) mbar_arrive(xready);  // the producer may fill the rest of the rings
+    if constexpr (kRms) {
+        float t = 0.f;
+#pragma unroll
+        for (int k = 0; k < W; ++k) t += red[k];
+        inv = 1.0f / sqrtf(t / (float)p.cols + p.eps);
+    }
 
     unsigned long long best = 0ull;
     // A warp whose bounded wait gave up marks itself dead: it skips the math

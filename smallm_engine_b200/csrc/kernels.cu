@@ -10,7 +10,6 @@
 #include "engine.h"
 #include "dequant.cuh"
 #include "gemv.cuh"
-#include "mgemv.cuh"
 
 namespace smallm {
 
@@ -65,9 +64,8 @@ static uint32_t record_stride(uint32_t t, uint32_t cols) {
     const uint32_t units = cols / unit_elems(t);
     switch (t) {
         case SM_T_F32: return cols * 4;
-        // tiles of 16 rows (mgemv.cuh): 16 row records are one tile of even-padded block pairs
-        case SM_T_Q4_0: return (units + (units & 1u)) * 18;
-        case SM_T_Q8_0: return (units + (units & 1u)) * 34;
+        case SM_T_Q4_0: return units * 16 + align16(units * 2);
+        case SM_T_Q8_0: return units * 32 + align16(units * 2);
         case SM_T_Q4_K: return (cols / 256) * 144;
         case SM_T_Q6_K: return align16((uint64_t)units * 52 + (cols / 256) * 2);
         default: return 0;
@@ -98,9 +96,8 @@ void qmat_free(QMat& m) {
 }
 
 // One thread per (storage row, 32-element unit) for Q4_0, Q8_0 and F32:
-// F32 rows as they are; Q4_0 / Q8_0 codes and f16 scales to their places in
-// the 16-row tiles of the tensor-core GEMV (mgemv.cuh).  Source blocks are
-// byte-addressed (18/34-byte GGUF blocks are not aligned).
+// quants to the front of the row record, f16 scales after them.  Source
+// blocks are byte-addressed (18/34-byte GGUF blocks are not aligned).
 __global__ void smallm_repack_blocks_kernel(const uint8_t* src, uint64_t src_row_bytes, uint64_t col_byte0,
                                      const uint32_t* row_map, uint32_t rows, uint32_t rows_pad,
                                      uint32_t nunits, uint32_t stride, uint32_t type, uint8_t* dst) {
@@ -112,19 +109,13 @@ __global__ void smallm_repack_blocks_kernel(const uint8_t* src, uint64_t src_row
     const uint32_t bb = type == SM_T_Q4_0 ? 18 : (type == SM_T_Q8_0 ? 34 : 128);
     const uint32_t qb = type == SM_T_Q4_0 ? 16 : (type == SM_T_Q8_0 ? 32 : 128);
     const uint8_t* b = src + (uint64_t)srow * src_row_bytes + col_byte0 + (uint64_t)u * bb;
+    uint8_t* row = dst + (uint64_t)p * stride;
     if (type == SM_T_F32) {
-        uint8_t* row = dst + (uint64_t)p * stride;
         for (uint32_t i = 0; i < 128; ++i) row[(size_t)u * 128 + i] = b[i];
-    } else if (type == SM_T_Q4_0) {  // 16-row tiles (mgemv.cuh)
-        for (uint32_t i = 0; i < qb; ++i) dst[tiled_q4_0_byte(stride, p, u, i)] = b[2 + i];
-        const size_t so = tiled_scale_byte(stride, 576, 512, p, u);
-        dst[so] = b[0];
-        dst[so + 1] = b[1];
     } else {
-        for (uint32_t i = 0; i < qb; ++i) dst[tiled_q8_0_byte(stride, p, u, i)] = b[2 + i];
-        const size_t so = tiled_scale_byte(stride, 1088, 1024, p, u);
-        dst[so] = b[0];
-        dst[so + 1] = b[1];
+        for (uint32_t i = 0; i < qb; ++i) row[(size_t)u * qb + i] = b[2 + i];
+        row[(size_t)nunits * qb + u * 2] = b[0];
+        row[(size_t)nunits * qb + u * 2 + 1] = b[1];
     }
 }
 
@@ -536,27 +527,11 @@ static const void* pick(int pro, int epi) {
     throw Error(1, "gemv: unsupported prologue/epilogue combination");
 }
 
-template <class M>
-static const void* pick_mma(int pro, int epi) {
-    if (pro == PRO_PLAIN && epi == EPI_STORE) return (const void*)smallm_mgemv_kernel<M, PRO_PLAIN, EPI_STORE>;
-    if (pro == PRO_PLAIN && epi == EPI_RESIDUAL) return (const void*)smallm_mgemv_kernel<M, PRO_PLAIN, EPI_RESIDUAL>;
-    if (pro == PRO_RMS && epi == EPI_STORE) return (const void*)smallm_mgemv_kernel<M, PRO_RMS, EPI_STORE>;
-    if (pro == PRO_RMS && epi == EPI_QKV) return (const void*)smallm_mgemv_kernel<M, PRO_RMS, EPI_QKV>;
-    if (pro == PRO_RMS && epi == EPI_SWIGLU) return (const void*)smallm_mgemv_kernel<M, PRO_RMS, EPI_SWIGLU>;
-    if (pro == PRO_RMS && epi == EPI_LOGITS) return (const void*)smallm_mgemv_kernel<M, PRO_RMS, EPI_LOGITS>;
-    if (pro == PRO_PLAIN && epi == EPI_PEER) return (const void*)smallm_mgemv_kernel<M, PRO_PLAIN, EPI_PEER>;
-    if (pro == PRO_RMS_SUM && epi == EPI_STORE) return (const void*)smallm_mgemv_kernel<M, PRO_RMS_SUM, EPI_STORE>;
-    if (pro == PRO_RMS_SUM && epi == EPI_QKV) return (const void*)smallm_mgemv_kernel<M, PRO_RMS_SUM, EPI_QKV>;
-    if (pro == PRO_RMS_SUM && epi == EPI_SWIGLU) return (const void*)smallm_mgemv_kernel<M, PRO_RMS_SUM, EPI_SWIGLU>;
-    if (pro == PRO_RMS_SUM && epi == EPI_LOGITS) return (const void*)smallm_mgemv_kernel<M, PRO_RMS_SUM, EPI_LOGITS>;
-    throw Error(1, "gemv: unsupported prologue/epilogue combination");
-}
-
-static const void* gemv_kernel_for(uint32_t type, int pro, int epi, uint32_t) {
+static const void* gemv_kernel_for(uint32_t type, int pro, int epi, uint32_t warps) {
     switch (type) {
         case SM_T_F32: return pick<FmtF32, 16>(pro, epi);
-        case SM_T_Q4_0: return pick_mma<MmaQ4_0>(pro, epi);
-        case SM_T_Q8_0: return pick_mma<MmaQ8_0>(pro, epi);
+        case SM_T_Q4_0: return warps == 22 ? pick<FmtQ4_0, 22>(pro, epi) : pick<FmtQ4_0, 16>(pro, epi);
+        case SM_T_Q8_0: return pick<FmtQ8_0, 16>(pro, epi);
         case SM_T_Q4_K: return pick<FmtQ4K, 16>(pro, epi);
         case SM_T_Q6_K: return pick<FmtQ6K, 16>(pro, epi);
         default: throw Error(2, "unsupported tensor type: " + std::to_string(type));
@@ -566,51 +541,9 @@ static const void* gemv_kernel_for(uint32_t type, int pro, int epi, uint32_t) {
 constexpr size_t kSmemLimit = 227 * 1024;
 constexpr uint32_t kMaxStages = 32;
 
-// Consumer warps of the kernel for a matrix (gemv.cuh / mgemv.cuh).
-static uint32_t gemv_warps(const QMat&) { return 16u; }
-
-static bool mma_format(uint32_t type) { return type == SM_T_Q4_0 || type == SM_T_Q8_0; }
-
-// Tensor-core GEMV (mgemv.cuh): pieces of about kMgemvPiece bytes -- the
-// per-SM bulk-copy engine keeps up with HBM only with copies of 16 KB and
-// more (measured: 8 KB copies reach 4.3 TB/s, 16 KB 7.0, 32 KB 7.1 with four
-// in flight per SM).  A tile is 32 rows when a 16-row tile is at most half a
-// piece, else 16 rows in nchunk pieces of cpairs pairs; the ring takes the
-// stages that fit after x (two at least).
-constexpr size_t kMgemvPiece = 40 * 1024;
-static GemvPlan mgemv_plan(const QMat& m, size_t limit) {
-    GemvPlan pl;
-    pl.warps = kMgemvWarps;
-    const uint32_t pair_bytes = m.type == SM_T_Q4_0 ? MmaQ4_0::kPairBytes : MmaQ8_0::kPairBytes;
-    const uint32_t upairs = (m.units + 1) / 2;
-    const size_t tile16 = (size_t)upairs * pair_bytes;
-    uint32_t nr = 1, nchunk = 1, cpairs = upairs;
-    if (2 * tile16 <= kMgemvPiece && m.rows_pad % 32 == 0) {
-        nr = 2;
-    } else if (tile16 > kMgemvPiece) {
-        nchunk = (uint32_t)((tile16 + kMgemvPiece - 1) / kMgemvPiece);
-        cpairs = (upairs + nchunk - 1) / nchunk;
-        nchunk = (upairs + cpairs - 1) / cpairs;
-    }
-    pl.rt = 16 * nr;
-    pl.nchunk = nchunk;
-    pl.cpairs = cpairs;
-    pl.upairs = upairs;
-    pl.pair_bytes = pair_bytes;
-    pl.piece_bytes = (size_t)nr * cpairs * pair_bytes;
-    pl.xbytes = ((size_t)upairs * kXfragPairBytes + (size_t)2 * upairs * kXconstBytes + 127) / 128 * 128;
-    const size_t misc = 8 + 8 + kMgemvWarps * 4 + kMgemvWarps * 8;  // xready, counter padding, red, best
-    const size_t per_stage = pl.piece_bytes + 16 + 4 + kMgemvPartFloats * 4;  // full, empty, counter, partials
-    if (pl.xbytes + misc + 2 * per_stage > limit)
-        throw Error(1, "gemv: rows of " + std::to_string(m.cols) + " columns do not fit the shared-memory pipeline");
-    uint32_t S = (uint32_t)((limit - pl.xbytes - misc) / per_stage);
-    if (S > kMaxStages) S = kMaxStages;
-    pl.stages = S;
-    pl.ngroups = 1;
-    pl.gsize = kMgemvWarps;
-    pl.kring = S;
-    pl.smem = pl.xbytes + (size_t)S * per_stage + misc;
-    return pl;
+// Consumer warps of the kernel for a matrix (gemv.cuh, kGemvMaxWarps).
+static uint32_t gemv_warps(const QMat& m) {
+    return m.type == SM_T_Q4_0 && m.units >= 256 ? 22u : 16u;
 }
 
 // Tiles of 4 rows; as many stages as shared memory (at most smem_cap bytes,
@@ -625,7 +558,6 @@ constexpr uint32_t kGemvMaxGroups = 8;
 GemvPlan gemv_plan(const QMat& m, size_t smem_cap) {
     GemvPlan pl;
     const size_t limit = smem_cap && smem_cap < kSmemLimit ? smem_cap : kSmemLimit;
-    if (mma_format(m.type)) return mgemv_plan(m, limit);
     const uint32_t W = gemv_warps(m);
     pl.warps = W;
     // x records: three digits per 32-element block
@@ -703,22 +635,10 @@ void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_
     p.gsize = pl.gsize;
     p.kring = pl.kring;
     p.xbytes = (uint32_t)pl.xbytes;
-    p.upairs = pl.upairs;
-    p.nchunk = pl.nchunk;
-    p.cpairs = pl.cpairs;
-    p.pair_bytes = pl.pair_bytes;
-    p.piece_bytes = (uint32_t)pl.piece_bytes;
-    // the tensor-core GEMV streams its first pieces while x is staged
-    // (measured: 1 us less on 28672x4096 than holding them); the CUDA-core
-    // kernel holds the ring fill behind x staging when the rings cannot take
-    // all of a CTA's tiles (measured: -0.9 us on 28672x4096 and 4096x14336
-    // in the decode step, +0.2 us on the 6144 / 4096-row matrices)
-    if (mma_format(m.type)) {
-        p.hold = ~0u;
-    } else {
-        const uint32_t per_cta = (ntiles + grid - 1) / grid;
-        p.hold = per_cta > pl.stages ? 1u : ~0u;
-    }
+    // hold back the ring fill behind x staging only when the rings cannot take
+    // all of a CTA's tiles (measured: -0.9 us on 28672x4096 and 4096x14336 in
+    // the decode step, +0.2 us on the 6144 / 4096-row matrices)
+    p.hold = (ntiles + grid - 1) / grid > pl.stages ? 1u : ~0u;
     p.x = a.x;
     p.norm_w = a.norm_w;
     p.eps = a.eps;

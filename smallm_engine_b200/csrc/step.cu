@@ -6,10 +6,10 @@
 // matrices (kernel boundaries, x staging, tails).  Here every SM keeps one
 // resident CTA for the whole step, and the weight pieces of ALL the step's
 // matrices stream, in order, through one shared-memory byte ring that never
-// waits on a data dependency -- only on ring space: a producer warp retires
-// the pieces the 16 consumer warps are done with, in order, and starts the
-// copies of the next pieces that fit (ring_plan).  The consumer warps walk
-// the op list; between dependent ops they meet at a grid-wide
+// waits on a data dependency -- only on ring space: whichever warp frees a
+// piece's space starts the copies of the next pieces that fit (ring_plan),
+// so there is no producer warp and the 16 warps keep 128 registers each.  The
+// warps walk the op list; between dependent ops they meet at a grid-wide
 // barrier (a release counter in global memory), stage the new x and continue
 // on pieces that are often already in shared memory.
 //
@@ -20,13 +20,16 @@
 // barrier count (counter >= signals so far x grid).  The counter is reset by
 // the last CTA of the step, so a captured graph replays the kernel as is.
 //
-// GEMV ops (the tensor-core GEMV of mgemv.cuh with gemv.cuh's fused
-// epilogues): x is staged as the MMA's x fragments; a piece is a 16- or
-// 32-row tile, or a run of a 16-row tile's block pairs (one contiguous range:
-// one bulk copy of ~32 KB, the size the per-SM copy engine needs to keep up
-// with HBM).  Every warp takes a share of each piece's pairs and keeps its
-// row partials across a tile's pieces; the last warp done with a tile's last
-// piece sums the partials and runs the fused epilogue.
+// GEMV ops (same block formats and fused epilogues as gemv.cuh): x is staged
+// as three-digit block fixed point (gemv.cuh, XRec) and every consumer thread
+// keeps the record of ONE 32-element unit of x in registers for the whole
+// op ("x-stationary"): thread (warp w, lane l) owns unit u = (w % WS) * 32 + l
+// of the row slot w / WS (WS = warps per row, ceil(units / 32)), and the RS
+// = 16 / WS row slots of the CTA take RPT rows each of every piece.  A piece
+// is R = RS * RPT consecutive rows (one contiguous range: one bulk copy).
+// Per piece each warp reduces its RPT rows with shuffles, the partials meet
+// in shared memory, and one warp (rotating with the piece) sums them and runs
+// the fused epilogue.
 //
 // ATTN op (qwen2_model.cpp:111-133): split-K over (KV head, position range)
 // items, one item per CTA; 16 warps x 128/hd sub-warps walk the item's
@@ -49,7 +52,6 @@
 #include "dequant.cuh"
 #include "engine.h"
 #include "gemv.cuh"
-#include "mgemv.cuh"
 #include "model.h"
 
 namespace smallm {
@@ -58,8 +60,8 @@ enum { SOP_EMBED = 0, SOP_GEMV = 1, SOP_ATTN = 2 };
 
 constexpr int kStepW = 16;                    // consumer warps (one producer warp more)
 constexpr int kStepThreads = (kStepW + 1) * 32;
-constexpr uint32_t kStepSlots = 8;            // ring pieces in flight at most
-constexpr uint32_t kStepPartFloats = kStepW * 16;  // per slot: every warp's 16 row partials
+constexpr uint32_t kStepSlots = 32;           // ring pieces in flight at most
+constexpr uint32_t kStepPartRows = 64;        // rows of one piece's partials (R <= 64)
 constexpr unsigned int kStepErrBit = 16u;
 constexpr int kStepMaxGroup = 8;           // query heads per KV head
 
@@ -71,7 +73,7 @@ struct StepOp {
     // GEMV: matrix and piece geometry
     const uint8_t* w;
     uint32_t row_stride, rows, rows_pad, cols, units;
-    uint32_t rt, nchunk, cpairs, upairs, pair_bytes;  // tiles of rt rows in nchunk pieces (mgemv.cuh)
+    uint32_t ws, rs, rpt, prows, npieces;
     // GEMV inputs / fused epilogue outputs
     const float* x;
     const float* norm_w;
@@ -185,10 +187,9 @@ struct StepRing {
     uint32_t issued;   // pieces whose copy has been started
     uint32_t freed[kStepSlots];  // j + 1 once piece j (slot j % kStepSlots) is done with
     uint32_t head;     // ring offset just past the newest issued piece
-    uint32_t op, p;    // next piece to issue: op index and this CTA's piece index in the op
+    uint32_t op, p;    // next piece to issue: op index and piece index
     // geometry of op `op` (read from global memory once per op)
-    uint32_t kind, np, nchunk, cpairs, upairs, pair_bytes, nr;
-    size_t tile_bytes;
+    uint32_t kind, np, R, stride, rows_pad;
     const uint8_t* w;
     uint32_t pstart[kStepSlots];  // ring offset of each in-flight piece
 };
@@ -199,8 +200,9 @@ struct StepRing {
 // scoreboard).
 extern __shared__ __align__(128) uint8_t s_dyn[];  // x region (records / attention scratch), then the ring
 __shared__ __align__(8) uint64_t s_full[kStepSlots];  // piece landed in the ring (count 1 + bytes)
-__shared__ uint32_t s_cnt[kStepSlots];                  // warps done with the piece
-__shared__ float s_part[kStepSlots * kStepPartFloats];  // row partials of each piece in flight
+__shared__ uint32_t s_cnt[kStepSlots * kStepW];       // warps of a row slot done with the piece
+__shared__ uint32_t s_slots[kStepSlots];              // row slots done with the piece
+__shared__ float s_part[kStepSlots * kStepPartRows];  // row partials of each piece in flight
 __shared__ StepRing s_ring;
 __shared__ float s_red[32];
 __shared__ unsigned long long s_best[kStepW];
@@ -221,15 +223,10 @@ __device__ __forceinline__ void ring_load_op(const StepArgs& a, StepRing& r) {
     if (r.op >= a.nops) return;
     const StepOp* op = a.ops + r.op;
     r.kind = op->kind;
-    if (r.kind != SOP_GEMV) return;
-    const uint32_t ntiles = op->rows_pad / op->rt;
-    r.nchunk = op->nchunk;
-    r.np = blockIdx.x < ntiles ? (ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x * r.nchunk : 0u;
-    r.cpairs = op->cpairs;
-    r.upairs = op->upairs;
-    r.pair_bytes = op->pair_bytes;
-    r.nr = op->rt / 16;
-    r.tile_bytes = (size_t)op->rt * op->row_stride;
+    r.np = op->npieces;
+    r.R = op->prows;
+    r.stride = op->row_stride;
+    r.rows_pad = op->rows_pad;
     r.w = op->w;
 }
 
@@ -248,13 +245,12 @@ __device__ __forceinline__ uint32_t ring_plan() {
     while (n < 32 && r.issued - r.retired < kStepSlots) {
         while (r.op < a.nops && (r.kind != SOP_GEMV || r.p >= r.np)) {
             ++r.op;
-            r.p = 0u;
+            r.p = blockIdx.x;
             ring_load_op(a, r);
         }
         if (r.op >= a.nops) break;
-        const uint32_t c = r.p % r.nchunk, t = blockIdx.x + (r.p / r.nchunk) * gridDim.x;
-        const uint32_t pc = min(r.cpairs, r.upairs - c * r.cpairs);
-        const uint32_t bytes = r.nr * pc * r.pair_bytes;
+        const uint32_t R = r.R, stride = r.stride;
+        const uint32_t bytes = min(R, r.rows_pad - r.p * R) * stride;
         const uint32_t off = r.head + bytes <= RB ? r.head : 0u;
         if (r.issued != r.retired) {
             const uint32_t tail = r.pstart[r.retired % kStepSlots];
@@ -266,10 +262,10 @@ __device__ __forceinline__ uint32_t ring_plan() {
         r.head = off + bytes;
         s_plan_off[n] = off;
         s_plan_bytes[n] = bytes;
-        s_plan_src[n] = r.w + t * r.tile_bytes + (size_t)c * r.cpairs * r.pair_bytes;
+        s_plan_src[n] = r.w + (size_t)r.p * R * stride;
         ++n;
         ++r.issued;
-        ++r.p;
+        r.p += gridDim.x;
     }
     return n;
 }
@@ -337,24 +333,19 @@ __device__ __forceinline__ void step_producer(int lane) {
     }
 }
 
-// x -> the tensor-core GEMV's x fragments and block constants (mgemv.cuh)
-// in the x region: [upairs][256 B] then [2 upairs][8 B], x times the norm
-// weight when the RMSNorm is fused (its 1/rms is returned and applied per
-// row); the padding block of an odd count is zero.
-template <class M>
+// x -> three-digit records of every 32-element block (times the norm weight
+// when the RMSNorm is fused; its 1/rms is returned and applied per row).
+template <class Fmt>
 __device__ __forceinline__ float step_stage_x(const StepOp& op, int warp, int lane) {
     const int ctid = warp * 32 + lane;
     constexpr uint32_t kStride = kStepW * 32;
     constexpr int kB = 4;
-    const uint32_t ngr = op.cols / 4;        // a multiple of 8: whole blocks
-    const uint32_t ngr_pad = op.upairs * 16;  // with the padding block
-    uint8_t* xfrag = s_dyn;
-    uint8_t* xconst = s_dyn + (size_t)op.upairs * kXfragPairBytes;
+    const uint32_t ngr = op.cols / 4;  // a multiple of 8: whole blocks
     const float4* x4 = reinterpret_cast<const float4*>(op.x);
     const float4* w4 = reinterpret_cast<const float4*>(op.norm_w);
     const bool rms = op.pro == PRO_RMS;
     float ss = 0.f;
-    for (uint32_t g0 = 0; g0 < ngr_pad; g0 += kB * kStride) {
+    for (uint32_t g0 = 0; g0 < ngr; g0 += kB * kStride) {
         float4 xq[kB], wq[kB];
 #pragma unroll
         for (int k = 0; k < kB; ++k) {
@@ -367,7 +358,7 @@ __device__ __forceinline__ float step_stage_x(const StepOp& op, int warp, int la
         for (int k = 0; k < kB; ++k) {
             // a warp whose first granule lies past the end has no block here
             // (warp-uniform, so the shuffles inside stay whole-warp)
-            if (g0 + (uint32_t)warp * 32 + k * kStride >= ngr_pad) continue;
+            if (g0 + (uint32_t)warp * 32 + k * kStride >= ngr) continue;
             const uint32_t g = g0 + ctid + k * kStride;
             float4 q = xq[k];
             ss += q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w;
@@ -375,7 +366,7 @@ __device__ __forceinline__ float step_stage_x(const StepOp& op, int warp, int la
             q.y *= wq[k].y;
             q.z *= wq[k].z;
             q.w *= wq[k].w;
-            build_xfrag_lane<M::kOffset>(q, lane, g < ngr_pad, g >> 3, xfrag, xconst);
+            build_xrec_lane<Fmt::XK>(q, lane, g < ngr, s_dyn + (size_t)(g >> 3) * kXrecBytes);
         }
     }
     if (rms) {
@@ -484,16 +475,12 @@ struct PieceCursor {
     unsigned long long best;
 };
 
-// One GEMV op on the tensor cores (mgemv.cuh): this CTA's tiles t =
-// blockIdx.x, + gridDim.x, ... of rt = 16 nr rows, each as nchunk pieces in
-// ring order.  Warp w takes row group w / (16 / nr) and a share of each
-// piece's block pairs and keeps its lane's row partial across the chunks of a
-// tile; every warp counts itself done with a piece, and the LAST one (no warp
-// waits for another) sums the warps' partials of a tile's last piece, runs
-// the fused epilogue (lane = row of the tile) and hands the piece back to the
-// producer.
-template <class M>
+// One GEMV op (rows per slot op.rpt <= 4: the row loop and the shuffle
+// reduction run for 4 rows, the missing ones as zeros).
+template <class Fmt>
 __device__ __forceinline__ PieceCursor step_gemv(int warp, int lane, PieceCursor cur) {
+    constexpr int RPT = Fmt::STEP_RPT;  // rows per slot at most (register budget)
+    constexpr int LPR = 32 / RPT;
     const StepOp& op = s_op;
     const StepArgs& a = s_args;
     uint8_t* const ring = step_ring();
@@ -502,21 +489,23 @@ __device__ __forceinline__ PieceCursor step_gemv(int warp, int lane, PieceCursor
     uint32_t j = cur.j, head = cur.head;
     bool dead = cur.dead != 0;
     unsigned long long best = cur.best;
-    const float inv = step_stage_x<M>(op, warp, lane);
-    const uint8_t* xfrag = s_dyn;
-    const uint8_t* xconst = s_dyn + (size_t)op.upairs * kXfragPairBytes;
-    const uint32_t nr = op.rt / 16, WK = kStepW / nr, NC = op.nchunk;
-    const uint32_t rg = (uint32_t)warp / WK, kp = (uint32_t)warp % WK;
-    const uint32_t ntiles = op.rows_pad / op.rt;
-    const uint32_t np = blockIdx.x < ntiles ? (ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x * NC : 0u;
+    const float inv = step_stage_x<Fmt>(op, warp, lane);
+    // A piece is R = RS * rpt consecutive rows (one bulk copy of ~32 KB: the
+    // per-SM copy engine needs copies that large to keep up with HBM); row
+    // slot `slot` (WS warps, one unit of x per lane) takes its rpt rows.
+    const uint32_t U = op.units, WS = op.ws, RS = op.rs, R = op.prows, stride = op.row_stride, rpt = op.rpt;
+    const uint32_t slot = (uint32_t)warp / WS, wi = (uint32_t)warp % WS;
+    const bool active = slot < RS;
+    const uint32_t u = wi * 32 + (uint32_t)lane;
+    const uint32_t r0 = slot * rpt;  // this slot's first row in a piece
     const uint32_t pos_op = op.epi == EPI_QKV ? *op.pos : 0u;  // the step's position (RoPE row)
-    float acc = 0.f;
-    for (uint32_t q = 0; q < np; ++q, ++j) {
-        const uint32_t c = q % NC, t = blockIdx.x + (q / NC) * gridDim.x;
-        const uint32_t pc = min(op.cpairs, op.upairs - c * op.cpairs);
-        const uint32_t bytes = nr * pc * op.pair_bytes;
+    const uint32_t npieces = op.npieces, rows_pad = op.rows_pad;
+    for (uint32_t p = blockIdx.x; p < npieces; p += gridDim.x, ++j) {
+        const uint32_t rows_here = min(R, rows_pad - p * R);
+        const uint32_t bytes = rows_here * stride;
         const uint32_t off = head + bytes <= RB ? head : 0u;  // the ring placement, as ring_plan makes it
         head = off + bytes;
+        if (!active) continue;
         const uint32_t s = j % kStepSlots, ph = (j / kStepSlots) & 1u;
         if (!dead && !step_wait(&s_full[s], ph, abort_flag)) {
             dead = true;
@@ -525,45 +514,62 @@ __device__ __forceinline__ PieceCursor step_gemv(int warp, int lane, PieceCursor
         dead = __any_sync(0xffffffffu, dead);  // warp-uniform (the shuffles below)
         const bool stamp = a.pieces && blockIdx.x == 0 && lane == 0 && j < a.piece_cap;
         if (stamp && warp == 0) a.pieces[4 * j + 1] = global_ns();
-        if (!dead)
-            acc = mma_pairs<M>(ring + off + (size_t)rg * pc * op.pair_bytes, kp * pc / WK, (kp + 1) * pc / WK,
-                               c * op.cpairs, xfrag, xconst, lane, acc);
-        const bool lastc = c == NC - 1;
-        if (lastc) {
-            // lanes t and t^2 hold the two blocks of each pair of the same row
-            const float v = acc + __shfl_xor_sync(0xffffffffu, acc, 2);
-            acc = 0.f;
-            if ((lane & 3) < 2) s_part[s * kStepPartFloats + warp * 16 + (lane >> 2) + 8 * (lane & 1)] = v;
+        float acc[RPT];
+#pragma unroll
+        for (int k = 0; k < RPT; ++k) acc[k] = 0.f;
+        if (u < U && r0 < rows_here && !dead) {
+            XRec xr;  // this thread's unit of x (three-digit record)
+            load_xrec(s_dyn, u, xr);
+            const uint8_t* base = ring + off + (size_t)r0 * stride;
+#pragma unroll
+            for (int k = 0; k < RPT; ++k) {
+                if ((uint32_t)k < rpt && r0 + k < rows_here) {
+                    typename Fmt::Raw raw;
+                    Fmt::load(base + (size_t)k * stride, u, U, raw);
+                    acc[k] = Fmt::dot(raw, 0, xr, u);
+                }
+            }
         }
+        // lanes k*LPR .. k*LPR + LPR-1 end with this warp's part of row k
+        const float v = warp_reduce_rows<RPT>(acc, lane);
+        if ((lane % LPR) == 0 && (uint32_t)lane / LPR < rpt)
+            s_part[s * kStepPartRows + (r0 + lane / LPR) * WS + wi] = v;
         __syncwarp();
-        uint32_t last = 0u;
-        if (lane == 0) {
-            __threadfence_block();
-            last = atomicAdd(&s_cnt[s], 1u) == kStepW - 1 ? 1u : 0u;
+        // the slot's last warp to finish closes the slot's rows, and the last
+        // slot to close hands the piece back: no warp waits for another
+        uint32_t last = 1u;
+        if (WS > 1) {
+            if (lane == 0) {
+                __threadfence_block();
+                last = atomicAdd(&s_cnt[s * kStepW + slot], 1u) == WS - 1 ? 1u : 0u;
+            }
+            last = __shfl_sync(0xffffffffu, last, 0);
         }
-        last = __shfl_sync(0xffffffffu, last, 0);
         if (!last) continue;
         __threadfence_block();
-        if (lane == 0) s_cnt[s] = 0u;
-        if (lastc) {
-            // lane L finishes row L of the tile (nr = 2: lanes 16-31 the second row group)
-            const uint32_t rgl = (uint32_t)lane / 16, rl = (uint32_t)lane % 16;
-            float r = 0.f;
-            if (rgl < nr)
-                for (uint32_t k = 0; k < WK; ++k) r += s_part[s * kStepPartFloats + (rgl * WK + k) * 16 + rl];
-            r *= inv;  // 1/rms of the fused RMSNorm (1 if plain)
-            const float r_next = __shfl_down_sync(0xffffffffu, r, 1);  // partner row of a pair
-            const uint32_t row = t * op.rt + (uint32_t)lane;
-            if (rgl < nr && !dead) {
-                const EpiPre e = step_epi_pre(op, row, pos_op);
-                step_epilogue(op, row, r, r_next, e, best);
+        if (lane == 0) s_cnt[s * kStepW + slot] = 0u;
+        {
+            const uint32_t r = r0 + (uint32_t)lane;  // lanes 0..rpt-1: this slot's rows
+            float val = 0.f;
+            if ((uint32_t)lane < rpt)
+                for (uint32_t k = 0; k < WS; ++k) val += s_part[s * kStepPartRows + r * WS + k];
+            val *= inv;  // 1/rms of the fused RMSNorm (1 if plain)
+            const float v_next = __shfl_down_sync(0xffffffffu, val, 1);  // partner row of a pair
+            if ((uint32_t)lane < rpt && r < rows_here && !dead) {
+                const EpiPre e = step_epi_pre(op, p * R + r, pos_op);
+                step_epilogue(op, p * R + r, val, v_next, e, best);
             }
         }
         __syncwarp();
         if (lane == 0) {
-            if (stamp) a.pieces[4 * j + 2] = global_ns();
-            if (!dead) ring_mark_done(j);
-            if (stamp) a.pieces[4 * j + 3] = global_ns();
+            __threadfence_block();
+            const bool piece_done = RS == 1 || atomicAdd(&s_slots[s], 1u) == RS - 1;
+            if (piece_done) {
+                if (RS > 1) s_slots[s] = 0u;
+                if (stamp) a.pieces[4 * j + 2] = global_ns();
+                if (!dead) ring_mark_done(j);
+                if (stamp) a.pieces[4 * j + 3] = global_ns();
+            }
         }
     }
     return PieceCursor{j, head, dead ? 1u : 0u, best};
@@ -792,14 +798,15 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
         s_args = args;
         for (uint32_t s = 0; s < kStepSlots; ++s) {
             mbar_init(&s_full[s], 1);
-            s_cnt[s] = 0u;
+            s_slots[s] = 0u;
         }
+        for (uint32_t q = 0; q < kStepSlots * kStepW; ++q) s_cnt[q] = 0u;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         StepRing& r = s_ring;
         r.retired = r.issued = r.head = 0u;
         for (uint32_t q = 0; q < kStepSlots; ++q) r.freed[q] = 0u;
         r.op = 0u;
-        r.p = 0u;
+        r.p = blockIdx.x;
         ring_load_op(s_args, r);
         s_cta_dead = 0;
     }
@@ -898,10 +905,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) smallm_step_kernel(const Step
 
 template <int HD>
 static const void* step_kernel_hd(uint32_t fa, uint32_t fb) {
-    if (fa == SM_T_Q4_0 && fb == SM_T_Q8_0) return (const void*)smallm_step_kernel<MmaQ4_0, MmaQ8_0, HD>;
-    if (fa == SM_T_Q8_0 && fb == SM_T_Q8_0) return (const void*)smallm_step_kernel<MmaQ8_0, MmaQ8_0, HD>;
-    if (fa == SM_T_Q4_0 && fb == SM_T_Q4_0) return (const void*)smallm_step_kernel<MmaQ4_0, MmaQ4_0, HD>;
-    if (fa == SM_T_Q8_0 && fb == SM_T_Q4_0) return (const void*)smallm_step_kernel<MmaQ8_0, MmaQ4_0, HD>;
+    if (fa == SM_T_Q4_0 && fb == SM_T_Q8_0) return (const void*)smallm_step_kernel<FmtQ4_0, FmtQ8_0, HD>;
+    if (fa == SM_T_Q8_0 && fb == SM_T_Q8_0) return (const void*)smallm_step_kernel<FmtQ8_0, FmtQ8_0, HD>;
+    if (fa == SM_T_Q4_0 && fb == SM_T_Q4_0) return (const void*)smallm_step_kernel<FmtQ4_0, FmtQ4_0, HD>;
+    if (fa == SM_T_Q8_0 && fb == SM_T_Q4_0) return (const void*)smallm_step_kernel<FmtQ8_0, FmtQ4_0, HD>;
     return nullptr;
 }
 
@@ -928,6 +935,8 @@ std::string Model::step_unsupported() const {
         return "embedding format";
     if (hd != 32 && hd != 64 && hd != 128) return "head_dim";
     if (nh_l % nkv_l || nh_l / nkv_l > (uint32_t)kStepMaxGroup) return "head grouping";
+    for (const QMat* m : {&layers[0].qkv, &layers[0].o, &layers[0].gu, &layers[0].down, &out_m})
+        if (m->units > 32u * kStepW) return "rows longer than the step's x registers";
     // opt-in while the per-op kernels are faster on the measured workloads
     const char* want = std::getenv("SMALLM_STEP");
     if (!want || std::strcmp(want, "persistent") != 0) return "per-op kernels (SMALLM_STEP=persistent selects it)";
@@ -946,11 +955,11 @@ void Model::build_step() {
     SM_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
     const size_t dyn_max = (size_t)optin - fa.sharedSizeBytes;
 
-    // x region: the largest op's x fragments, or the attention's per-warp scratch
+    // x region: the largest op's records, or the attention's per-warp scratch
     const uint32_t G = nh_l / nkv_l;
     size_t xbytes = (size_t)kStepW * G * (hd + 4) * 4;
     for (const QMat* m : {&layers[0].qkv, &layers[0].o, &layers[0].gu, &layers[0].down, &out_m})
-        xbytes = std::max(xbytes, (size_t)((m->units + 1) / 2) * (kXfragPairBytes + 2 * kXconstBytes));
+        xbytes = std::max(xbytes, (size_t)m->units * kXrecBytes);
     xbytes = (xbytes + 127) / 128 * 128;
     if (xbytes + 64 * 1024 > dyn_max) {
         step_why = "shared memory";
@@ -958,26 +967,23 @@ void Model::build_step() {
     }
     const size_t ring = (dyn_max - xbytes) / 128 * 128;
 
-    // piece geometry of a matrix (mgemv.cuh): tiles of 16 rows, or 32 when a
-    // 16-row tile is at most half a piece; a tile longer than a piece is cut
-    // into nchunk runs of cpairs block pairs.  A piece is at most `cap` bytes
-    // (40 KB, or SMALLM_STEP_PIECE_KB) and a third of the ring.
+    // piece geometry of a matrix: WS warps per row, RS row slots, RPT rows
+    // per slot (R = RS * RPT rows per piece, even, at most 64, a piece at most
+    // `cap` bytes: 40 KB, or SMALLM_STEP_PIECE_KB, and a third of the ring)
     size_t cap = ring / 3;
     if (const char* e = std::getenv("SMALLM_STEP_PIECE_KB")) cap = std::min(cap, (size_t)std::atoi(e) * 1024);
     else cap = std::min(cap, (size_t)40 * 1024);
     auto geometry = [&](const QMat& m, StepOp& op) {
-        const uint32_t pair_bytes = m.type == SM_T_Q4_0 ? MmaQ4_0::kPairBytes : MmaQ8_0::kPairBytes;
-        const uint32_t upairs = (m.units + 1) / 2;
-        const size_t tile16 = (size_t)upairs * pair_bytes;
-        uint32_t nr = 1, nchunk = 1, cpairs = upairs;
-        if (2 * tile16 <= cap && m.rows_pad % 32 == 0) {
-            nr = 2;
-        } else if (tile16 > cap) {
-            nchunk = (uint32_t)((tile16 + cap - 1) / cap);
-            cpairs = (upairs + nchunk - 1) / nchunk;
-            nchunk = (upairs + cpairs - 1) / cpairs;
-        }
-        if ((size_t)nr * cpairs * pair_bytes > ring / 3)
+        // WS warps cover a row's units (one per lane); RS = 16 / WS row slots
+        // take rpt rows each of every piece (rpt even: rotary and SwiGLU row
+        // pairs stay in one slot), so a piece is R = RS * rpt rows in one
+        // copy, at most `cap` bytes and a third of the ring
+        const uint32_t WS = (m.units + 31) / 32;
+        const uint32_t RS = kStepW / WS;
+        uint32_t rpt = m.type == SM_T_Q4_0 ? FmtQ4_0::STEP_RPT : FmtQ8_0::STEP_RPT;
+        while (rpt > 2 && (size_t)RS * rpt * m.row_stride > cap) rpt /= 2;
+        if (RS == 0 || rpt < 2 || RS * rpt * WS > kStepPartRows ||
+            (size_t)RS * rpt * m.row_stride > ring / 3)
             throw Error(1, "persistent step: no piece geometry for a matrix of " + std::to_string(m.cols) + " columns");
         op.w = m.base;
         op.row_stride = m.row_stride;
@@ -985,11 +991,11 @@ void Model::build_step() {
         op.rows_pad = m.rows_pad;
         op.cols = m.cols;
         op.units = m.units;
-        op.rt = 16 * nr;
-        op.nchunk = nchunk;
-        op.cpairs = cpairs;
-        op.upairs = upairs;
-        op.pair_bytes = pair_bytes;
+        op.ws = WS;
+        op.rs = RS;
+        op.rpt = rpt;
+        op.prows = RS * rpt;
+        op.npieces = (m.rows_pad + op.prows - 1) / op.prows;
     };
 
     std::vector<StepOp> ops;
