@@ -162,23 +162,22 @@ __device__ __forceinline__ void build_xrec_lane(float4 q, int lane, bool act, ui
     uint32_t bits[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) bits[k] = __float_as_uint(fmaf(v[k], up, kMagic));
-    uint32_t p[3] = {0u, 0u, 0u};
-    int ds[3] = {0, 0, 0};  // this lane's digit sums (XK_NIB_SD)
+    // Balanced digits X = D2 2^16 + D1 2^8 + D0 (|X| <= 2^21): they are the
+    // bytes of (X + 0x808080) ^ 0x808080 -- adding 128 per byte makes every
+    // byte's carry explicit and the XOR maps byte b to the int8 pattern of
+    // b - 128 -- gathered per digit across the 4 elements with byte permutes.
+    constexpr uint32_t kBias = 0x808080u;
+    uint32_t el[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {  // balanced digits: X = D2 2^16 + D1 2^8 + D0
-        const int X = (int)(bits[k] - kMagicBits);
-        const int a0 = (int)(int8_t)(X & 0xFF);
-        const int X1 = (X - a0) >> 8;
-        const int a1 = (int)(int8_t)(X1 & 0xFF);
-        const int a2 = (X1 - a1) >> 8;
-        p[0] |= (uint32_t)(a0 & 0xFF) << (8 * k);
-        p[1] |= (uint32_t)(a1 & 0xFF) << (8 * k);
-        p[2] |= (uint32_t)(a2 & 0xFF) << (8 * k);
-        if constexpr (XK == XK_NIB_SD) {
-            ds[0] += a0;
-            ds[1] += a1;
-            ds[2] += a2;
-        }
+    for (int k = 0; k < 4; ++k) el[k] = (bits[k] - kMagicBits + kBias) ^ kBias;
+    const uint32_t w01 = __byte_perm(el[0], el[1], 0x5140), w23 = __byte_perm(el[2], el[3], 0x5140);
+    const uint32_t v01 = __byte_perm(el[0], el[1], 0x0062), v23 = __byte_perm(el[2], el[3], 0x0062);
+    const uint32_t p[3] = {__byte_perm(w01, w23, 0x5410), __byte_perm(w01, w23, 0x7632),
+                           __byte_perm(v01, v23, 0x5410)};
+    int ds[3] = {0, 0, 0};  // this lane's digit sums (XK_NIB_SD)
+    if constexpr (XK == XK_NIB_SD) {
+#pragma unroll
+        for (int d = 0; d < 3; ++d) ds[d] = __dp4a((int)p[d], 0x01010101, 0);
     }
     int t0, t1;
     uint32_t t2;
