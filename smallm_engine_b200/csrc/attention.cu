@@ -277,9 +277,10 @@ void launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {
 constexpr int kCAttnThreads = 128;
 constexpr uint32_t kCAttnChunk = 32;
 constexpr uint32_t kCAttnMaxCluster = 16;
+constexpr uint32_t kCAttnMaxStages = 4;
 
-__host__ __device__ constexpr size_t cattn_smem_floats(uint32_t G, uint32_t hd) {
-    return 2 * (size_t)kCAttnChunk * hd                    // ks, vs
+__host__ __device__ constexpr size_t cattn_smem_floats(uint32_t G, uint32_t hd, uint32_t stages) {
+    return 2 * (size_t)stages * kCAttnChunk * hd           // ks, vs per ring stage
            + (size_t)G * hd                                // qs
            + (size_t)G * kCAttnChunk                       // sc
            + 3 * kAttnMaxGroup                             // corr, pm, pl
@@ -295,7 +296,7 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
     constexpr int DL = HD / 8;                 // head-dim elements per lane in the score pass
     constexpr int DV = DL / 4;                 // ... as float4
     extern __shared__ __align__(128) float sm[];
-    __shared__ __align__(8) uint64_t bar, bar_pre, mrg;
+    __shared__ __align__(8) uint64_t bar[kCAttnMaxStages], bar_pre, mrg;
     __shared__ uint32_t pre_n, pre_rows, early;
     cg::cluster_group cluster = cg::this_cluster();
     const uint32_t C = cluster.num_blocks();
@@ -305,9 +306,11 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int nw = kCAttnThreads / 32;
     const uint32_t S = (G * HD + C - 1) / C;  // outputs merged per CTA
-    float* ks = sm;
-    float* vs = ks + kCAttnChunk * HD;
-    float* qs = vs + kCAttnChunk * HD;
+    const uint32_t NS = a.stages;              // ring of chunk buffers (1..kCAttnMaxStages)
+    // stage st: K rows at sm + st * 2 * kCAttnChunk * HD, V rows right after
+    auto kbuf = [&](uint32_t st) { return sm + (size_t)st * 2 * kCAttnChunk * HD; };
+    auto vbuf = [&](uint32_t st) { return sm + (size_t)st * 2 * kCAttnChunk * HD + kCAttnChunk * HD; };
+    float* qs = sm + (size_t)NS * 2 * kCAttnChunk * HD;
     float* sc = qs + G * HD;
     float* corr = sc + G * kCAttnChunk;
     float* pm = corr + kAttnMaxGroup;
@@ -320,7 +323,7 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
 
     if (tid == 0) {
         trace_mark(a.trace, 0);
-        mbar_init(&bar, 1);
+        for (uint32_t st = 0; st < kCAttnMaxStages; ++st) mbar_init(&bar[st], 1);
         mbar_init(&bar_pre, 1);
         mbar_init(&mrg, 1);
         // the merge barrier completes when every peer's pushed bytes are in:
@@ -342,8 +345,8 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
             const uint32_t bytes = rows * HD * 4;
             const size_t off = ((size_t)g * a.max_ctx + b0) * HD;
             mbar_arrive_expect_tx(&bar_pre, 2 * bytes);
-            bulk_g2s(ks, a.kcache + off, bytes, &bar_pre);
-            bulk_g2s(vs, a.vcache + off, bytes, &bar_pre);
+            bulk_g2s(kbuf(0), a.kcache + off, bytes, &bar_pre);
+            bulk_g2s(vbuf(0), a.vcache + off, bytes, &bar_pre);
         }
         // warm L2 with the rest of the range (longer contexts)
         if (e0 > b0 + kCAttnChunk) {
@@ -368,12 +371,22 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
         if (pre_rows < len1) {
             const uint32_t bytes = (len1 - pre_rows) * HD * 4;
             const size_t off = ((size_t)g * a.max_ctx + b1 + pre_rows) * HD;
-            mbar_arrive_expect_tx(&bar, 2 * bytes);
-            bulk_g2s(ks + pre_rows * HD, a.kcache + off, bytes, &bar);
-            bulk_g2s(vs + pre_rows * HD, a.vcache + off, bytes, &bar);
+            mbar_arrive_expect_tx(&bar[0], 2 * bytes);
+            bulk_g2s(kbuf(0) + pre_rows * HD, a.kcache + off, bytes, &bar[0]);
+            bulk_g2s(vbuf(0) + pre_rows * HD, a.vcache + off, bytes, &bar[0]);
             e = 1;
         }
         early = e;
+        // the next chunks of the range fill the other ring stages at once
+        for (uint32_t k = 1; k < NS; ++k) {
+            const uint32_t c0 = b1 + k * kCAttnChunk;
+            if (c0 >= e1) break;
+            const uint32_t bytes = min(kCAttnChunk, e1 - c0) * HD * 4;
+            const size_t off = ((size_t)g * a.max_ctx + c0) * HD;
+            mbar_arrive_expect_tx(&bar[k], 2 * bytes);
+            bulk_g2s(kbuf(k), a.kcache + off, bytes, &bar[k]);
+            bulk_g2s(vbuf(k), a.vcache + off, bytes, &bar[k]);
+        }
     }
     {
         const float4* q4 = reinterpret_cast<const float4*>(a.q + (size_t)g * G * HD);
@@ -390,37 +403,43 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
     const uint32_t n = pre_n;
     const uint32_t per = (n + C - 1) / C;
     const uint32_t t_begin = min(n, rank * per), t_end = min(n, t_begin + per);
-    uint32_t have = 0;  // rows of the first chunk already in shared memory (or on their way: issued)
-    uint32_t issued = early;
-    if (pre_rows) {
+    if (pre_rows) {  // the first chunk's rows copied before the dependency wait
         if (!mbar_wait(&bar_pre, 0)) {
             ok = false;
             if (tid == 0 && a.err) atomicOr(a.err, 4u);
         }
-        have = pre_rows;
     }
     const float scale = 1.0f / sqrtf((float)HD);
     const int d = tid % HD, part = tid / HD;
     float acc[kAttnMaxGroup];
 #pragma unroll
     for (int h = 0; h < kAttnMaxGroup; ++h) acc[h] = 0.f;
-    uint32_t phase = 0;
-    for (uint32_t c0 = t_begin; c0 < t_end; c0 += kCAttnChunk, have = 0, issued = 0) {
+    // Chunk k lives in ring stage k % NS.  Chunks 0..NS-1 were issued above;
+    // once every thread is past chunk k-1 its stage takes chunk k-1+NS.
+    uint32_t phases = 0;  // per stage: parity of its barrier's next phase
+    uint32_t k = 0;
+    for (uint32_t c0 = t_begin; c0 < t_end; c0 += kCAttnChunk, ++k) {
         const uint32_t len = min(kCAttnChunk, t_end - c0);
+        const uint32_t st = k % NS;
+        const float* ks = kbuf(st);
+        const float* vs = vbuf(st);
         __syncthreads();  // the previous chunk's K/V/scores are no longer read (and q is staged)
-        if (have < len) {
-            if (tid == 0 && !issued) {
-                const uint32_t bytes = (len - have) * HD * 4;
-                const size_t off = ((size_t)g * a.max_ctx + c0 + have) * HD;
-                mbar_arrive_expect_tx(&bar, 2 * bytes);
-                bulk_g2s(ks + have * HD, a.kcache + off, bytes, &bar);
-                bulk_g2s(vs + have * HD, a.vcache + off, bytes, &bar);
+        if (tid == 0 && k >= 1) {
+            const uint32_t kk = k - 1 + NS, cn = t_begin + kk * kCAttnChunk, sn = (k - 1) % NS;
+            if (cn < t_end) {
+                const uint32_t bytes = min(kCAttnChunk, t_end - cn) * HD * 4;
+                const size_t off = ((size_t)g * a.max_ctx + cn) * HD;
+                mbar_arrive_expect_tx(&bar[sn], 2 * bytes);
+                bulk_g2s(kbuf(sn), a.kcache + off, bytes, &bar[sn]);
+                bulk_g2s(vbuf(sn), a.vcache + off, bytes, &bar[sn]);
             }
-            if (!mbar_wait(&bar, phase)) {
+        }
+        if (k >= 1 || early) {  // chunk 0 may have arrived whole before the wait
+            if (!mbar_wait(&bar[st], (phases >> st) & 1u)) {
                 ok = false;
                 if (tid == 0 && a.err) atomicOr(a.err, 4u);
             }
-            phase ^= 1u;
+            phases ^= 1u << st;
         }
         // scores: 8 lanes per position, lane k of the 8 holds elements
         // 4k + 32j .. +3 (conflict-free float4 rows), 16 positions per pass.
@@ -553,8 +572,19 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
     if (tid == 0) trace_mark(a.trace, 2);
 }
 
-size_t attention_cluster_smem(uint32_t n_heads, uint32_t n_kv, uint32_t hd) {
-    return 4 * cattn_smem_floats(n_heads / n_kv, hd);
+size_t attention_cluster_smem(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t stages) {
+    return 4 * cattn_smem_floats(n_heads / n_kv, hd, stages);
+}
+
+// Ring stages of the cluster attention for contexts up to max_ctx over
+// clusters of C: one per 32-position chunk of a CTA's longest range, at most
+// kCAttnMaxStages and 64 KB of K/V rows.
+uint32_t attention_cluster_stages(uint32_t max_ctx, uint32_t C, uint32_t hd) {
+    const uint32_t per = (max_ctx + C - 1) / C;
+    uint32_t ns = (per + kCAttnChunk - 1) / kCAttnChunk;
+    ns = ns < 1 ? 1 : (ns > kCAttnMaxStages ? kCAttnMaxStages : ns);
+    while (ns > 1 && 2ull * ns * kCAttnChunk * hd * 4 > 64 * 1024) --ns;
+    return ns;
 }
 
 static const void* cattn_fn(uint32_t hd) {
@@ -564,9 +594,9 @@ static const void* cattn_fn(uint32_t hd) {
     throw Error(SMALLM_ERR_INVALID, "attention: head_dim must be 32, 64 or 128");
 }
 
-uint32_t attention_cluster_size(uint32_t n_heads, uint32_t n_kv, uint32_t hd) {
+uint32_t attention_cluster_size(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t stages) {
     const void* fn = cattn_fn(hd);
-    const size_t smem = 4 * cattn_smem_floats(n_heads / n_kv, hd);
+    const size_t smem = 4 * cattn_smem_floats(n_heads / n_kv, hd, stages);
     SM_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     SM_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
 #ifndef SMALLM_ATTN_CLUSTER
@@ -600,7 +630,8 @@ void launch_attention_cluster(const AttnArgs& a, uint32_t C, cudaStream_t stream
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.n_kv * C);
     cfg.blockDim = dim3(kCAttnThreads);
-    cfg.dynamicSmemBytes = 4 * cattn_smem_floats(G, a.hd);
+    if (a.stages < 1 || a.stages > kCAttnMaxStages) throw Error(SMALLM_ERR_INVALID, "attention: bad ring depth");
+    cfg.dynamicSmemBytes = 4 * cattn_smem_floats(G, a.hd, a.stages);
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;

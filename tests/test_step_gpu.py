@@ -105,3 +105,27 @@ def test_long_context_persistent_attention(orc, gguf_dir):
             assert float(np.abs(a - b).max()) <= 1e-3 * float(np.abs(b).max()), pos
             assert int(np.argmax(a)) == int(np.argmax(b))
     m.close()
+
+
+@pytest.mark.parametrize("ctx,n_pos", [(768, 700), (2304, 2100)])
+def test_long_context_cluster_attention_ring(orc, gguf_dir, ctx, n_pos):
+    """The per-op step's cluster attention with its ring of chunk buffers
+    sized for max_ctx (2 stages at 768 positions, 4 at 2304 for head_dim 64):
+    each CTA of a 16-CTA cluster walks several 32-position chunks, copies in
+    flight ahead of the one being scored.  Checked against the oracle at the
+    last positions."""
+    spec = synth.tiny_spec("llama-q4_0", ctx=ctx, name=f"tiny-llama-q4_0-{ctx}")
+    path = synth.write_gguf(spec, 24, gguf_dir / f"ring-{ctx}.gguf")
+    m = _load(path, per_op=True)
+    assert m.config().step_launches > 1  # the per-op kernels
+    ref = O.OracleModel(path, orc)
+    rng = np.random.default_rng(6)
+    toks = rng.integers(0, spec.vocab, size=n_pos)
+    for pos, t in enumerate(toks):
+        last = pos >= n_pos - 6
+        a = m.forward(int(t), pos, want_logits=last)
+        b = ref.forward(int(t), pos)
+        if last:
+            assert float(np.abs(a - b).max()) <= 1e-3 * float(np.abs(b).max()), pos
+            assert int(np.argmax(a)) == int(np.argmax(b))
+    m.close()
