@@ -254,10 +254,11 @@ void launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {
 //
 // One thread-block cluster of C CTAs per KV head; CTA c of the cluster owns
 // the c-th of C equal contiguous ranges of positions 0..pos.  It stages its
-// range 32 positions at a time (K and V rows: two bulk copies on one
-// mbarrier), scores the `group` query heads of the KV head against them, and
-// keeps a running (max, sum, unnormalised output) per head across its chunks
-// (online softmax).
+// range in chunks sized for the model's context (32-256 positions, usually
+// the whole range in one; K and V rows: two bulk copies on one mbarrier),
+// scores the `group` query heads of the KV head against them, and keeps a
+// running (max, sum, unnormalised output) per head across its chunks (online
+// softmax).
 //
 // Before the dependency wait.  The position is fixed for the whole step (only
 // the step's last kernel advances it) and rows below it were written by
@@ -275,14 +276,14 @@ void launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {
 // every CTA alive until all of its peers' pushes are done (arrive after the
 // pushes, wait at the end).  No global scratch, no atomics, one launch.
 constexpr int kCAttnThreads = 128;
-constexpr uint32_t kCAttnChunk = 32;
+constexpr uint32_t kCAttnChunkUnit = 32;  // chunks are 1..kCAttnMaxUnits units of positions
+constexpr uint32_t kCAttnMaxUnits = 8;
 constexpr uint32_t kCAttnMaxCluster = 16;
-constexpr uint32_t kCAttnMaxStages = 4;
 
-__host__ __device__ constexpr size_t cattn_smem_floats(uint32_t G, uint32_t hd, uint32_t stages) {
-    return 2 * (size_t)stages * kCAttnChunk * hd           // ks, vs per ring stage
+__host__ __device__ constexpr size_t cattn_smem_floats(uint32_t G, uint32_t hd, uint32_t chunk) {
+    return 2 * (size_t)chunk * hd                          // ks, vs
            + (size_t)G * hd                                // qs
-           + (size_t)G * kCAttnChunk                       // sc
+           + (size_t)G * chunk                             // sc
            + 3 * kAttnMaxGroup                             // corr, pm, pl
            + (size_t)(kCAttnThreads - hd) * kAttnMaxGroup  // V-pass slice partials
            + (size_t)G * hd + kCAttnMaxCluster             // received output slices: C x ceil(G hd / C)
@@ -296,7 +297,7 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
     constexpr int DL = HD / 8;                 // head-dim elements per lane in the score pass
     constexpr int DV = DL / 4;                 // ... as float4
     extern __shared__ __align__(128) float sm[];
-    __shared__ __align__(8) uint64_t bar[kCAttnMaxStages], bar_pre, mrg;
+    __shared__ __align__(8) uint64_t bar, bar_pre, mrg;
     __shared__ uint32_t pre_n, pre_rows, early;
     cg::cluster_group cluster = cg::this_cluster();
     const uint32_t C = cluster.num_blocks();
@@ -306,13 +307,12 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int nw = kCAttnThreads / 32;
     const uint32_t S = (G * HD + C - 1) / C;  // outputs merged per CTA
-    const uint32_t NS = a.stages;              // ring of chunk buffers (1..kCAttnMaxStages)
-    // stage st: K rows at sm + st * 2 * kCAttnChunk * HD, V rows right after
-    auto kbuf = [&](uint32_t st) { return sm + (size_t)st * 2 * kCAttnChunk * HD; };
-    auto vbuf = [&](uint32_t st) { return sm + (size_t)st * 2 * kCAttnChunk * HD + kCAttnChunk * HD; };
-    float* qs = sm + (size_t)NS * 2 * kCAttnChunk * HD;
+    const uint32_t CH = a.chunk;  // positions per chunk (a multiple of kCAttnChunkUnit)
+    float* ks = sm;
+    float* vs = ks + (size_t)CH * HD;
+    float* qs = vs + (size_t)CH * HD;
     float* sc = qs + G * HD;
-    float* corr = sc + G * kCAttnChunk;
+    float* corr = sc + G * CH;
     float* pm = corr + kAttnMaxGroup;
     float* pl = pm + kAttnMaxGroup;
     float* red = pl + kAttnMaxGroup;
@@ -323,7 +323,7 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
 
     if (tid == 0) {
         trace_mark(a.trace, 0);
-        for (uint32_t st = 0; st < kCAttnMaxStages; ++st) mbar_init(&bar[st], 1);
+        mbar_init(&bar, 1);
         mbar_init(&bar_pre, 1);
         mbar_init(&mrg, 1);
         // the merge barrier completes when every peer's pushed bytes are in:
@@ -339,19 +339,19 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
         const uint32_t per0 = (n0 + C - 1) / C;
         const uint32_t b0 = min(n0, rank * per0), e0 = min(n0, b0 + per0);
         // rows below the position are final; the new row comes after the wait
-        const uint32_t fin = min(min(e0, b0 + kCAttnChunk), n0 - 1);
+        const uint32_t fin = min(min(e0, b0 + CH), n0 - 1);
         const uint32_t rows = fin > b0 ? fin - b0 : 0u;
         if (rows) {
             const uint32_t bytes = rows * HD * 4;
             const size_t off = ((size_t)g * a.max_ctx + b0) * HD;
             mbar_arrive_expect_tx(&bar_pre, 2 * bytes);
-            bulk_g2s(kbuf(0), a.kcache + off, bytes, &bar_pre);
-            bulk_g2s(vbuf(0), a.vcache + off, bytes, &bar_pre);
+            bulk_g2s(ks, a.kcache + off, bytes, &bar_pre);
+            bulk_g2s(vs, a.vcache + off, bytes, &bar_pre);
         }
         // warm L2 with the rest of the range (longer contexts)
-        if (e0 > b0 + kCAttnChunk) {
-            const uint32_t bytes = (e0 - b0 - kCAttnChunk) * HD * 4;
-            const size_t off = ((size_t)g * a.max_ctx + b0 + kCAttnChunk) * HD;
+        if (e0 > b0 + CH) {
+            const uint32_t bytes = (e0 - b0 - CH) * HD * 4;
+            const size_t off = ((size_t)g * a.max_ctx + b0 + CH) * HD;
             asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.kcache + off), "r"(bytes) : "memory");
             asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.vcache + off), "r"(bytes) : "memory");
         }
@@ -366,27 +366,17 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
         const uint32_t n1 = pre_n;
         const uint32_t per1 = (n1 + C - 1) / C;
         const uint32_t b1 = min(n1, rank * per1), e1 = min(n1, b1 + per1);
-        const uint32_t len1 = min(kCAttnChunk, e1 - b1);
+        const uint32_t len1 = min(CH, e1 - b1);
         uint32_t e = 0;
         if (pre_rows < len1) {
             const uint32_t bytes = (len1 - pre_rows) * HD * 4;
             const size_t off = ((size_t)g * a.max_ctx + b1 + pre_rows) * HD;
-            mbar_arrive_expect_tx(&bar[0], 2 * bytes);
-            bulk_g2s(kbuf(0) + pre_rows * HD, a.kcache + off, bytes, &bar[0]);
-            bulk_g2s(vbuf(0) + pre_rows * HD, a.vcache + off, bytes, &bar[0]);
+            mbar_arrive_expect_tx(&bar, 2 * bytes);
+            bulk_g2s(ks + pre_rows * HD, a.kcache + off, bytes, &bar);
+            bulk_g2s(vs + pre_rows * HD, a.vcache + off, bytes, &bar);
             e = 1;
         }
         early = e;
-        // the next chunks of the range fill the other ring stages at once
-        for (uint32_t k = 1; k < NS; ++k) {
-            const uint32_t c0 = b1 + k * kCAttnChunk;
-            if (c0 >= e1) break;
-            const uint32_t bytes = min(kCAttnChunk, e1 - c0) * HD * 4;
-            const size_t off = ((size_t)g * a.max_ctx + c0) * HD;
-            mbar_arrive_expect_tx(&bar[k], 2 * bytes);
-            bulk_g2s(kbuf(k), a.kcache + off, bytes, &bar[k]);
-            bulk_g2s(vbuf(k), a.vcache + off, bytes, &bar[k]);
-        }
     }
     {
         const float4* q4 = reinterpret_cast<const float4*>(a.q + (size_t)g * G * HD);
@@ -414,32 +404,27 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
     float acc[kAttnMaxGroup];
 #pragma unroll
     for (int h = 0; h < kAttnMaxGroup; ++h) acc[h] = 0.f;
-    // Chunk k lives in ring stage k % NS.  Chunks 0..NS-1 were issued above;
-    // once every thread is past chunk k-1 its stage takes chunk k-1+NS.
-    uint32_t phases = 0;  // per stage: parity of its barrier's next phase
-    uint32_t k = 0;
-    for (uint32_t c0 = t_begin; c0 < t_end; c0 += kCAttnChunk, ++k) {
-        const uint32_t len = min(kCAttnChunk, t_end - c0);
-        const uint32_t st = k % NS;
-        const float* ks = kbuf(st);
-        const float* vs = vbuf(st);
+    // The chunk is sized for the step's longest range (attention_cluster_chunk),
+    // so at most one chunk after the first remains; the first arrived whole
+    // before the wait but for the new row.
+    uint32_t phase = 0;
+    for (uint32_t c0 = t_begin; c0 < t_end; c0 += CH) {
+        const uint32_t len = min(CH, t_end - c0);
+        const bool first = c0 == t_begin;
         __syncthreads();  // the previous chunk's K/V/scores are no longer read (and q is staged)
-        if (tid == 0 && k >= 1) {
-            const uint32_t kk = k - 1 + NS, cn = t_begin + kk * kCAttnChunk, sn = (k - 1) % NS;
-            if (cn < t_end) {
-                const uint32_t bytes = min(kCAttnChunk, t_end - cn) * HD * 4;
-                const size_t off = ((size_t)g * a.max_ctx + cn) * HD;
-                mbar_arrive_expect_tx(&bar[sn], 2 * bytes);
-                bulk_g2s(kbuf(sn), a.kcache + off, bytes, &bar[sn]);
-                bulk_g2s(vbuf(sn), a.vcache + off, bytes, &bar[sn]);
-            }
+        if (!first && tid == 0) {
+            const uint32_t bytes = len * HD * 4;
+            const size_t off = ((size_t)g * a.max_ctx + c0) * HD;
+            mbar_arrive_expect_tx(&bar, 2 * bytes);
+            bulk_g2s(ks, a.kcache + off, bytes, &bar);
+            bulk_g2s(vs, a.vcache + off, bytes, &bar);
         }
-        if (k >= 1 || early) {  // chunk 0 may have arrived whole before the wait
-            if (!mbar_wait(&bar[st], (phases >> st) & 1u)) {
+        if (!first || early) {
+            if (!mbar_wait(&bar, phase)) {
                 ok = false;
                 if (tid == 0 && a.err) atomicOr(a.err, 4u);
             }
-            phases ^= 1u << st;
+            phase ^= 1u;
         }
         // scores: 8 lanes per position, lane k of the 8 holds elements
         // 4k + 32j .. +3 (conflict-free float4 rows), 16 positions per pass.
@@ -478,18 +463,23 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
             if (l8 == 0 && t < len) {
 #pragma unroll
                 for (int h = 0; h < kAttnMaxGroup; ++h)
-                    if (h < (int)G) sc[h * kCAttnChunk + t] = s[h] * scale;
+                    if (h < (int)G) sc[h * CH + t] = s[h] * scale;
             }
         }
         __syncthreads();
         // online softmax (ops::softmax, ops.cpp:43-57, across chunks)
         for (uint32_t h = warp; h < G; h += nw) {
-            const float s = (uint32_t)lane < len ? sc[h * kCAttnChunk + lane] : -INFINITY;
+            float mx = -INFINITY;
+            for (uint32_t t = lane; t < len; t += 32) mx = fmaxf(mx, sc[h * CH + t]);
             const float m_old = pm[h];
-            const float m_new = fmaxf(m_old, warp_max(s));
-            const float e = (uint32_t)lane < len ? expf(s - m_new) : 0.f;
-            const float l = warp_sum(e);
-            if ((uint32_t)lane < len) sc[h * kCAttnChunk + lane] = e;
+            const float m_new = fmaxf(m_old, warp_max(mx));
+            float l = 0.f;
+            for (uint32_t t = lane; t < len; t += 32) {
+                const float e = expf(sc[h * CH + t] - m_new);
+                sc[h * CH + t] = e;
+                l += e;
+            }
+            l = warp_sum(l);
             if (lane == 0) {
                 const float cf = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
                 corr[h] = cf;
@@ -506,7 +496,7 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
             const float v = ok ? vs[t * HD + d] : 0.f;
 #pragma unroll
             for (int h = 0; h < kAttnMaxGroup; ++h)
-                if (h < (int)G) acc[h] = fmaf(sc[h * kCAttnChunk + t], v, acc[h]);
+                if (h < (int)G) acc[h] = fmaf(sc[h * CH + t], v, acc[h]);
         }
     }
     if constexpr (PARTS > 1) {
@@ -572,19 +562,23 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
     if (tid == 0) trace_mark(a.trace, 2);
 }
 
-size_t attention_cluster_smem(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t stages) {
-    return 4 * cattn_smem_floats(n_heads / n_kv, hd, stages);
+size_t attention_cluster_smem(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t chunk) {
+    return 4 * cattn_smem_floats(n_heads / n_kv, hd, chunk);
 }
 
-// Ring stages of the cluster attention for contexts up to max_ctx over
-// clusters of C: one per 32-position chunk of a CTA's longest range, at most
-// kCAttnMaxStages and 64 KB of K/V rows.
-uint32_t attention_cluster_stages(uint32_t max_ctx, uint32_t C, uint32_t hd) {
+// Positions per chunk of the cluster attention for contexts up to max_ctx
+// over clusters of C: a CTA's longest range rounded up to 32, at most 256
+// positions and 96 KB of K/V rows.  With the whole range in one chunk a CTA
+// copies all its rows but the step's new one before the dependency wait
+// (while the QKV kernel runs) and scores them in one pass (measured on the
+// TinyLlama shape at ~2050 positions: 32-position chunks, one at a time,
+// took ~20 us per layer).
+uint32_t attention_cluster_chunk(uint32_t max_ctx, uint32_t C, uint32_t hd) {
     const uint32_t per = (max_ctx + C - 1) / C;
-    uint32_t ns = (per + kCAttnChunk - 1) / kCAttnChunk;
-    ns = ns < 1 ? 1 : (ns > kCAttnMaxStages ? kCAttnMaxStages : ns);
-    while (ns > 1 && 2ull * ns * kCAttnChunk * hd * 4 > 64 * 1024) --ns;
-    return ns;
+    uint32_t u = (per + kCAttnChunkUnit - 1) / kCAttnChunkUnit;
+    u = u < 1 ? 1 : (u > kCAttnMaxUnits ? kCAttnMaxUnits : u);
+    while (u > 1 && 2ull * u * kCAttnChunkUnit * hd * 4 > 96 * 1024) --u;
+    return u * kCAttnChunkUnit;
 }
 
 static const void* cattn_fn(uint32_t hd) {
@@ -594,9 +588,9 @@ static const void* cattn_fn(uint32_t hd) {
     throw Error(SMALLM_ERR_INVALID, "attention: head_dim must be 32, 64 or 128");
 }
 
-uint32_t attention_cluster_size(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t stages) {
+uint32_t attention_cluster_size(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t chunk) {
     const void* fn = cattn_fn(hd);
-    const size_t smem = 4 * cattn_smem_floats(n_heads / n_kv, hd, stages);
+    const size_t smem = 4 * cattn_smem_floats(n_heads / n_kv, hd, chunk);
     SM_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     SM_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
 #ifndef SMALLM_ATTN_CLUSTER
@@ -630,8 +624,9 @@ void launch_attention_cluster(const AttnArgs& a, uint32_t C, cudaStream_t stream
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.n_kv * C);
     cfg.blockDim = dim3(kCAttnThreads);
-    if (a.stages < 1 || a.stages > kCAttnMaxStages) throw Error(SMALLM_ERR_INVALID, "attention: bad ring depth");
-    cfg.dynamicSmemBytes = 4 * cattn_smem_floats(G, a.hd, a.stages);
+    if (a.chunk < kCAttnChunkUnit || a.chunk > kCAttnChunkUnit * kCAttnMaxUnits || a.chunk % kCAttnChunkUnit)
+        throw Error(SMALLM_ERR_INVALID, "attention: bad chunk size");
+    cfg.dynamicSmemBytes = 4 * cattn_smem_floats(G, a.hd, a.chunk);
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;

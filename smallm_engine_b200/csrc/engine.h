@@ -166,7 +166,7 @@ struct AttnArgs {
     uint32_t n_heads, n_kv, hd, max_ctx, n_split;
     unsigned int* err = nullptr;  // raised if a bounded wait gives up
     TraceSlot* trace = nullptr;   // traced steps only
-    uint32_t stages = 1;          // cluster kernel: chunk buffers in flight (attention_cluster_stages)
+    uint32_t chunk = 32;          // cluster kernel: positions per chunk (attention_cluster_chunk)
 };
 uint32_t attention_splits(uint32_t n_kv, uint32_t max_ctx, int sm_count);
 size_t attention_partial_floats(uint32_t n_heads, uint32_t hd, uint32_t n_split);
@@ -175,12 +175,12 @@ void launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl = false);
 // Cluster attention (the decode step's): one cluster of C CTAs per KV head,
 // partials merged through distributed shared memory.  attention_cluster_size
 // picks the largest C <= 16 the device can schedule (and sets the kernel's
-// attributes on the current device) for a ring of `stages` chunk buffers;
-// attention_cluster_stages sizes that ring for contexts up to max_ctx.
-uint32_t attention_cluster_size(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t stages);
-uint32_t attention_cluster_stages(uint32_t max_ctx, uint32_t C, uint32_t hd);
+// attributes on the current device) for chunks of `chunk` positions;
+// attention_cluster_chunk sizes them for contexts up to max_ctx.
+uint32_t attention_cluster_size(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t chunk);
+uint32_t attention_cluster_chunk(uint32_t max_ctx, uint32_t C, uint32_t hd);
 // Dynamic shared memory of one cluster-attention CTA.
-size_t attention_cluster_smem(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t stages);
+size_t attention_cluster_smem(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t chunk);
 void launch_attention_cluster(const AttnArgs& a, uint32_t C, cudaStream_t stream, bool pdl);
 // The split-K kernel with its scratch in a static array of attention.cu (no
 // allocation; calls that overlap in time race on it).

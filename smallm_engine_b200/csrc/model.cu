@@ -320,13 +320,13 @@ void Model::load(const std::string& path, const smallm_model_opts& o) {
     hbuf = static_cast<float*>(dalloc(4ull * ffn_l));
     logits = static_cast<float*>(dalloc(4ull * vocab_l * tp_size));
     logits_local = tp_size > 1 ? static_cast<float*>(dalloc(4ull * vocab_l)) : logits;
-    // cluster size and ring depth depend on each other (the ring's shared
-    // memory decides which cluster sizes schedule): size the ring for the
-    // largest cluster, then settle on the cluster that fits it
-    attn_cluster = attention_cluster_size(nh_l, nkv_l, hd, 1);
+    // cluster size and chunk depend on each other (the chunk's shared memory
+    // decides which cluster sizes schedule): size the chunk for the largest
+    // cluster, then settle on the cluster that fits it
+    attn_cluster = attention_cluster_size(nh_l, nkv_l, hd, 32);
     for (int it = 0; it < 3; ++it) {
-        attn_stages = attention_cluster_stages(max_ctx, attn_cluster, hd);
-        const uint32_t c = attention_cluster_size(nh_l, nkv_l, hd, attn_stages);
+        attn_chunk = attention_cluster_chunk(max_ctx, attn_cluster, hd);
+        const uint32_t c = attention_cluster_size(nh_l, nkv_l, hd, attn_chunk);
         if (c == attn_cluster) break;
         attn_cluster = c;
     }
@@ -337,7 +337,7 @@ void Model::load(const std::string& path, const smallm_model_opts& o) {
         SM_CUDA(cudaGetDevice(&dev));
         SM_CUDA(cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev));
         SM_CUDA(cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev));
-        const size_t attn = attention_cluster_smem(nh_l, nkv_l, hd, attn_stages) + 256;
+        const size_t attn = attention_cluster_smem(nh_l, nkv_l, hd, attn_chunk) + 256;
         const size_t need = attn + 2 * (size_t)reserved;
         gemv_cap_attn = (size_t)per_sm > need ? (size_t)per_sm - need : 0;
     }
@@ -493,7 +493,7 @@ void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
         at.max_ctx = max_ctx;
         at.err = device_error_flag();
         at.trace = slot(TK_ATTN);
-        at.stages = attn_stages;
+        at.chunk = attn_chunk;
         launch_attention_cluster(at, attn_cluster, s, pdl);
 
         GemvArgs ao;

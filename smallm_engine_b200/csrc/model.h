@@ -44,7 +44,7 @@ struct Model {
     float *x = nullptr, *q = nullptr, *att = nullptr, *hbuf = nullptr;
     float *logits = nullptr, *logits_local = nullptr;
     uint32_t attn_cluster = 1;  // CTAs per KV head in the cluster attention
-    uint32_t attn_stages = 1;   // its ring of chunk buffers (sized for max_ctx)
+    uint32_t attn_chunk = 32;   // its positions per chunk (sized for max_ctx)
     size_t gemv_cap_attn = 0;   // shared-memory cap of the QKV / O GEMVs (room for an attention CTA)
     // Tensor parallelism (tp_size > 1): the residual is all-reduced through
     // peer memory by the GEMVs themselves (gemv.cuh EPI_PEER / PRO_RMS_SUM).

@@ -107,13 +107,14 @@ def test_long_context_persistent_attention(orc, gguf_dir):
     m.close()
 
 
-@pytest.mark.parametrize("ctx,n_pos", [(768, 700), (2304, 2100)])
-def test_long_context_cluster_attention_ring(orc, gguf_dir, ctx, n_pos):
-    """The per-op step's cluster attention with its ring of chunk buffers
-    sized for max_ctx (2 stages at 768 positions, 4 at 2304 for head_dim 64):
-    each CTA of a 16-CTA cluster walks several 32-position chunks, copies in
-    flight ahead of the one being scored.  Checked against the oracle at the
-    last positions."""
+@pytest.mark.parametrize("ctx,n_pos", [(768, 700), (8192, 3300)])
+def test_long_context_cluster_attention_chunks(orc, gguf_dir, ctx, n_pos):
+    """The per-op step's cluster attention with chunks sized for max_ctx
+    (head_dim 64, 16-CTA clusters): 64 positions at 768, where each CTA's
+    range fits one chunk copied before the dependency wait; 192 positions
+    (the 96 KB cap) at 8192, where ~207 positions per CTA take a second
+    chunk after the first.  Checked against the oracle at the last
+    positions."""
     spec = synth.tiny_spec("llama-q4_0", ctx=ctx, name=f"tiny-llama-q4_0-{ctx}")
     path = synth.write_gguf(spec, 24, gguf_dir / f"ring-{ctx}.gguf")
     m = _load(path, per_op=True)
