@@ -36,10 +36,6 @@
 
 namespace smallm {
 
-// Contexts from which the decode step's attention is the split-K kernel
-// (every SM takes a range of positions) instead of one cluster per KV head.
-constexpr uint32_t kAttnSplitFromCtx = 1024;
-
 static void nccl_check(ncclResult_t r, const char* what) {
     if (r != ncclSuccess) throw Error(6, std::string(what) + ": " + ncclGetErrorString(r));
 }
@@ -334,14 +330,6 @@ void Model::load(const std::string& path, const smallm_model_opts& o) {
         if (c == attn_cluster) break;
         attn_cluster = c;
     }
-    if (max_ctx >= kAttnSplitFromCtx) {
-        // long contexts: split-K over (KV head, position range) CTAs on every
-        // SM, partials merged by the last CTA of each head
-        attn_split = attention_splits(nkv_l, max_ctx, device_sm_count());
-        attn_partial = static_cast<float*>(dalloc(4 * attention_partial_floats(nh_l, hd, attn_split)));
-        attn_counter = static_cast<unsigned int*>(dalloc(4ull * nkv_l));
-        SM_CUDA(cudaMemsetAsync(attn_counter, 0, 4ull * nkv_l, stream));
-    }
     {
         // an attention CTA (dynamic + a little static shared memory) next to a
         // GEMV CTA on one SM, each with the per-CTA reservation
@@ -349,8 +337,7 @@ void Model::load(const std::string& path, const smallm_model_opts& o) {
         SM_CUDA(cudaGetDevice(&dev));
         SM_CUDA(cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev));
         SM_CUDA(cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev));
-        const size_t attn = (attn_split ? attention_smem(nh_l, nkv_l, hd, max_ctx, attn_split)
-                                        : attention_cluster_smem(nh_l, nkv_l, hd, attn_chunk)) + 256;
+        const size_t attn = attention_cluster_smem(nh_l, nkv_l, hd, attn_chunk) + 256;
         const size_t need = attn + 2 * (size_t)reserved;
         gemv_cap_attn = (size_t)per_sm > need ? (size_t)per_sm - need : 0;
     }
@@ -507,14 +494,7 @@ void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
         at.err = device_error_flag();
         at.trace = slot(TK_ATTN);
         at.chunk = attn_chunk;
-        if (attn_split) {
-            at.partial = attn_partial;
-            at.counter = attn_counter;
-            at.n_split = attn_split;
-            launch_attention(at, s, pdl);
-        } else {
-            launch_attention_cluster(at, attn_cluster, s, pdl);
-        }
+        launch_attention_cluster(at, attn_cluster, s, pdl);
 
         GemvArgs ao;
         ao.x = att;

@@ -45,10 +45,6 @@ struct Model {
     float *logits = nullptr, *logits_local = nullptr;
     uint32_t attn_cluster = 1;  // CTAs per KV head in the cluster attention
     uint32_t attn_chunk = 32;   // its positions per chunk (sized for max_ctx)
-    // long contexts: the split-K attention (n_kv x attn_split CTAs, ticket merge)
-    uint32_t attn_split = 0;    // 0 = the cluster attention
-    float* attn_partial = nullptr;
-    unsigned int* attn_counter = nullptr;
     size_t gemv_cap_attn = 0;   // shared-memory cap of the QKV / O GEMVs (room for an attention CTA)
     // Tensor parallelism (tp_size > 1): the residual is all-reduced through
     // peer memory by the GEMVs themselves (gemv.cuh EPI_PEER / PRO_RMS_SUM).

@@ -108,13 +108,13 @@ def test_long_context_persistent_attention(orc, gguf_dir):
 
 
 @pytest.mark.parametrize("ctx,n_pos", [(768, 700), (8192, 3300)])
-def test_long_context_decode_attention(orc, gguf_dir, ctx, n_pos):
-    """The per-op step's attention at long positions: at max_ctx 768 the
-    cluster attention (16-CTA clusters, 64-position chunks: each CTA's range
-    copied before the dependency wait); at 8192 the split-K attention that
-    long contexts use (KV head x position-range CTAs on every SM, partials
-    merged by the last CTA of each head).  Checked against the oracle at the
-    last positions."""
+def test_long_context_cluster_attention_chunks(orc, gguf_dir, ctx, n_pos):
+    """The per-op step's cluster attention with chunks sized for max_ctx
+    (head_dim 64, 16-CTA clusters): 64 positions at 768, where each CTA's
+    range fits one chunk copied before the dependency wait; 192 positions
+    (the 96 KB cap) at 8192, where ~207 positions per CTA take a second
+    chunk after the first.  Checked against the oracle at the last
+    positions."""
     spec = synth.tiny_spec("llama-q4_0", ctx=ctx, name=f"tiny-llama-q4_0-{ctx}")
     path = synth.write_gguf(spec, 24, gguf_dir / f"ring-{ctx}.gguf")
     m = _load(path, per_op=True)
