@@ -54,9 +54,10 @@ WORKLOAD = "llama3-8b-q4_0"
 PROMPT = 128
 METRIC = "decode tok/s @B=1 (Llama-3-8B-shaped, Q4_0) + % of HBM BW roofline"
 # dram__bytes_read.sum + dram__bytes_write.sum of one Q4_0 GEMV launch on the
-# 14336x4096 matrix, from one ncu capture of the Q4_0 GEMV kernel:
-# 33.078528 MB read, 0 written (the algorithmic bytes are 33.10 MB).
-GEMV_NCU_TRAFFIC_BYTES = 33078528
+# 14336x4096 matrix, from one ncu capture of the Q4_0 GEMV kernel
+# (profiles/gemv_q4_0_14336x4096.md): 33.091072 MB read, 0 written (the
+# algorithmic bytes are 33.10 MB).
+GEMV_NCU_TRAFFIC_BYTES = 33091072
 
 
 def peaks() -> tuple[float, str]:
