@@ -764,9 +764,12 @@ __global__ void __launch_bounds__((W + 1) * 32, 1) smallm_qgemv_kernel(const Gem
     }
     if constexpr (EPI == EPI_PEER) {
         // every row partial of this CTA is stored (at the peers too); the last
-        // CTA to finish raises this rank's flag at every rank
-        __threadfence_system();
+        // CTA to finish raises this rank's flag at every rank.  One thread
+        // fences after the CTA barrier: the barrier orders the other threads'
+        // peer stores before its system-scope fence, which is cumulative (a
+        // fence in every thread cost each CTA an NVLink round trip per thread)
         consumers_sync<W>();
+        if (ctid == 0) __threadfence_system();
         if (ctid == 0 && atomicAdd(p.done_ctr, 1u) == gridDim.x - 1) {
             *p.done_ctr = 0u;
             __threadfence_system();
