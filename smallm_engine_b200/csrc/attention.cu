@@ -279,6 +279,18 @@ constexpr int kCAttnThreads = 128;
 constexpr uint32_t kCAttnChunkUnit = 32;  // chunks are 1..kCAttnMaxUnits units of positions
 constexpr uint32_t kCAttnMaxUnits = 8;
 constexpr uint32_t kCAttnMaxCluster = 16;
+constexpr uint32_t kCAttnMaxParts = 4;  // clusters per KV head
+
+// Clusters per KV head for contexts up to max_ctx: with few KV heads one
+// cluster of C CTAs per head leaves most SMs idle, so long contexts
+// (>= 1024 positions) split each head's positions over up to 4 clusters
+// while n_kv * parts * C stays within the SMs.
+uint32_t attention_cluster_parts(uint32_t n_kv, uint32_t C, uint32_t max_ctx, int sm_count) {
+    if (max_ctx < 1024) return 1;
+    uint32_t parts = 1;
+    while (parts < kCAttnMaxParts && n_kv * (parts * 2) * C <= (uint32_t)sm_count) parts *= 2;
+    return parts;
+}
 
 __host__ __device__ constexpr size_t cattn_smem_floats(uint32_t G, uint32_t hd, uint32_t chunk) {
     return 2 * (size_t)chunk * hd                          // ks, vs
@@ -289,6 +301,17 @@ __host__ __device__ constexpr size_t cattn_smem_floats(uint32_t G, uint32_t hd, 
            + (size_t)G * hd + kCAttnMaxCluster             // received output slices: C x ceil(G hd / C)
            + 2 * (size_t)kCAttnMaxCluster * kAttnMaxGroup  // received (max, sum) per CTA and head
            + (size_t)kAttnMaxGroup * kCAttnMaxCluster;     // merge weights
+}
+
+// Positions [b, e) of CTA `rank` of the cluster for part kp of a KV head's
+// positions 0..n-1 split into `parts` equal ranges, each over C CTAs.
+__device__ __forceinline__ void cattn_range(uint32_t n, uint32_t parts, uint32_t kp, uint32_t C, uint32_t rank,
+                                            uint32_t& b, uint32_t& e) {
+    const uint32_t pp = (n + parts - 1) / parts;
+    const uint32_t pb = min(n, kp * pp), pe = min(n, pb + pp);
+    const uint32_t per = (pe - pb + C - 1) / C;
+    b = min(pe, pb + rank * per);
+    e = min(pe, b + per);
 }
 
 template <int HD>
@@ -303,7 +326,9 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
     const uint32_t C = cluster.num_blocks();
     const uint32_t rank = cluster.block_rank();
     const uint32_t G = a.n_heads / a.n_kv;
-    const uint32_t g = blockIdx.x / C;  // KV head of this cluster
+    const uint32_t NP = a.parts;               // clusters per KV head
+    const uint32_t g = blockIdx.x / C / NP;    // KV head of this cluster
+    const uint32_t kp = blockIdx.x / C % NP;   // its part of the head's positions
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int nw = kCAttnThreads / 32;
     const uint32_t S = (G * HD + C - 1) / C;  // outputs merged per CTA
@@ -336,8 +361,8 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
     pdl_launch_dependents();
     if (tid == 0) {
         const uint32_t n0 = min(*(volatile const uint32_t*)a.pos + 1, a.max_ctx);
-        const uint32_t per0 = (n0 + C - 1) / C;
-        const uint32_t b0 = min(n0, rank * per0), e0 = min(n0, b0 + per0);
+        uint32_t b0, e0;
+        cattn_range(n0, NP, kp, C, rank, b0, e0);
         // rows below the position are final; the new row comes after the wait
         const uint32_t fin = min(min(e0, b0 + CH), n0 - 1);
         const uint32_t rows = fin > b0 ? fin - b0 : 0u;
@@ -364,8 +389,8 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
         // the rest of the first chunk (from the row the QKV kernel has just
         // written) is copied right away, overlapping the q load
         const uint32_t n1 = pre_n;
-        const uint32_t per1 = (n1 + C - 1) / C;
-        const uint32_t b1 = min(n1, rank * per1), e1 = min(n1, b1 + per1);
+        uint32_t b1, e1;
+        cattn_range(n1, NP, kp, C, rank, b1, e1);
         const uint32_t len1 = min(CH, e1 - b1);
         uint32_t e = 0;
         if (pre_rows < len1) {
@@ -391,8 +416,8 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
     // The position read before the wait is the step's: only the step's last
     // kernel advances it (checked once more at the end).
     const uint32_t n = pre_n;
-    const uint32_t per = (n + C - 1) / C;
-    const uint32_t t_begin = min(n, rank * per), t_end = min(n, t_begin + per);
+    uint32_t t_begin, t_end;
+    cattn_range(n, NP, kp, C, rank, t_begin, t_end);
     if (pre_rows) {  // the first chunk's rows copied before the dependency wait
         if (!mbar_wait(&bar_pre, 0)) {
             ok = false;
@@ -545,7 +570,14 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
         const float M = warp_max(mc);
         const float e = mc == -INFINITY ? 0.f : expf(mc - M);
         const float L = warp_sum(e * lc);
-        if ((uint32_t)lane < C) wts[h * kCAttnMaxCluster + lane] = e / L;
+        // a part of a KV head with no positions yet (parts > 1, short
+        // context) has L = 0: its output is zero and its weight below is zero
+        if ((uint32_t)lane < C) wts[h * kCAttnMaxCluster + lane] = L > 0.f ? e / L : 0.f;
+        if (NP > 1 && rank == 0 && lane == 0) {
+            float* ml = a.part_ml + ((size_t)kp * a.n_heads + (size_t)g * G + h) * 2;
+            ml[0] = M;
+            ml[1] = L;
+        }
     }
     __syncthreads();
     for (uint32_t ol = tid; ol < S; ol += kCAttnThreads) {
@@ -554,7 +586,10 @@ __global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel
         const float* w = wts + (o / HD) * kCAttnMaxCluster;
         float O = 0.f;
         for (uint32_t c = 0; c < C; ++c) O = fmaf(w[c], rpo[c * S + ol], O);
-        a.out[(size_t)g * G * HD + o] = O;
+        // one part: the head's output; several: this part's normalised
+        // output, weighted by (M, L) when the next kernel stages it
+        float* dst = NP > 1 ? a.part_out + (size_t)kp * a.n_heads * HD : a.out;
+        dst[(size_t)g * G * HD + o] = O;
     }
     cluster_wait();
     if (tid == 0 && a.err && min(*(volatile const uint32_t*)a.pos + 1, a.max_ctx) != pre_n)
@@ -573,8 +608,8 @@ size_t attention_cluster_smem(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint
 // (while the QKV kernel runs) and scores them in one pass (measured on the
 // TinyLlama shape at ~2050 positions: 32-position chunks, one at a time,
 // took ~20 us per layer).
-uint32_t attention_cluster_chunk(uint32_t max_ctx, uint32_t C, uint32_t hd) {
-    const uint32_t per = (max_ctx + C - 1) / C;
+uint32_t attention_cluster_chunk(uint32_t max_ctx, uint32_t C, uint32_t hd, uint32_t parts) {
+    const uint32_t per = ((max_ctx + parts - 1) / parts + C - 1) / C;
     uint32_t u = (per + kCAttnChunkUnit - 1) / kCAttnChunkUnit;
     u = u < 1 ? 1 : (u > kCAttnMaxUnits ? kCAttnMaxUnits : u);
     while (u > 1 && 2ull * u * kCAttnChunkUnit * hd * 4 > 96 * 1024) --u;
@@ -622,7 +657,9 @@ void launch_attention_cluster(const AttnArgs& a, uint32_t C, cudaStream_t stream
     if (C < 1 || C > kCAttnMaxCluster) throw Error(SMALLM_ERR_INVALID, "attention: bad cluster size");
     const void* fn = cattn_fn(a.hd);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.n_kv * C);
+    if (a.parts < 1 || a.parts > kCAttnMaxParts || (a.parts > 1 && (!a.part_out || !a.part_ml)))
+        throw Error(SMALLM_ERR_INVALID, "attention: bad part count or missing part buffers");
+    cfg.gridDim = dim3(a.n_kv * a.parts * C);
     cfg.blockDim = dim3(kCAttnThreads);
     if (a.chunk < kCAttnChunkUnit || a.chunk > kCAttnChunkUnit * kCAttnMaxUnits || a.chunk % kCAttnChunkUnit)
         throw Error(SMALLM_ERR_INVALID, "attention: bad chunk size");

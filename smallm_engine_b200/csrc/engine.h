@@ -107,6 +107,10 @@ struct GemvArgs {
     // to theirs (it stages cached K/V while the QKV GEMV runs, and the O
     // GEMV prefetches weights while attention runs).
     size_t smem_cap = 0;
+    // plain prologue only: x is the merge of merge_parts attention partials
+    // (x + k * cols, weighted per head of merge_hd elements by merge_ml)
+    uint32_t merge_parts = 1, merge_hd = 0;
+    const float* merge_ml = nullptr;
 };
 
 void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_t stream, bool pdl = false);
@@ -167,6 +171,13 @@ struct AttnArgs {
     unsigned int* err = nullptr;  // raised if a bounded wait gives up
     TraceSlot* trace = nullptr;   // traced steps only
     uint32_t chunk = 32;          // cluster kernel: positions per chunk (attention_cluster_chunk)
+    // cluster kernel, parts > 1 clusters per KV head (attention_cluster_parts):
+    // part k writes its normalised output to part_out [parts][n_heads * hd]
+    // and its (max, sum) per head to part_ml [parts][n_heads][2]; the next
+    // GEMV merges them while it stages x (GemvArgs::merge_*)
+    uint32_t parts = 1;
+    float* part_out = nullptr;
+    float* part_ml = nullptr;
 };
 uint32_t attention_splits(uint32_t n_kv, uint32_t max_ctx, int sm_count);
 size_t attention_partial_floats(uint32_t n_heads, uint32_t hd, uint32_t n_split);
@@ -178,7 +189,8 @@ void launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl = false);
 // attributes on the current device) for chunks of `chunk` positions;
 // attention_cluster_chunk sizes them for contexts up to max_ctx.
 uint32_t attention_cluster_size(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t chunk);
-uint32_t attention_cluster_chunk(uint32_t max_ctx, uint32_t C, uint32_t hd);
+uint32_t attention_cluster_chunk(uint32_t max_ctx, uint32_t C, uint32_t hd, uint32_t parts);
+uint32_t attention_cluster_parts(uint32_t n_kv, uint32_t C, uint32_t max_ctx, int sm_count);
 // Dynamic shared memory of one cluster-attention CTA.
 size_t attention_cluster_smem(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t chunk);
 void launch_attention_cluster(const AttnArgs& a, uint32_t C, cudaStream_t stream, bool pdl);

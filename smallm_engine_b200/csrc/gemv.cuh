@@ -106,7 +106,36 @@ struct GemvParams {
     unsigned int* done_ctr;         // EPI_PEER: finished CTAs, zero between launches
     const unsigned int* epoch;      // steps completed so far (same on every rank)
     uint32_t tp;
+    // PRO_PLAIN: x is the merge of merge_parts attention partials
+    // ([parts][cols], normalised per part) with per-head (max, sum) weights
+    // merge_ml [parts][cols / merge_hd][2]; 1 = x as is
+    uint32_t merge_parts, merge_hd;
+    const float* merge_ml;
 };
+
+// Granule g (elements 4g..4g+3) of x merged from attention partials: part k
+// of head h weighs exp(M_k - M) L_k over the head's parts (a part with no
+// positions has L_k = 0), the same sum on every CTA.
+__device__ __forceinline__ float4 merge_granule(const GemvParams& p, uint32_t g) {
+    const uint32_t cols = p.cols, h = 4 * g / p.merge_hd, nh = cols / p.merge_hd;
+    float M = -INFINITY;
+    for (uint32_t k = 0; k < p.merge_parts; ++k)
+        if (p.merge_ml[((size_t)k * nh + h) * 2 + 1] > 0.f) M = fmaxf(M, p.merge_ml[((size_t)k * nh + h) * 2]);
+    float wsum = 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (uint32_t k = 0; k < p.merge_parts; ++k) {
+        const float L = p.merge_ml[((size_t)k * nh + h) * 2 + 1];
+        const float w = L > 0.f ? expf(p.merge_ml[((size_t)k * nh + h) * 2] - M) * L : 0.f;
+        const float4 v = reinterpret_cast<const float4*>(p.x + (size_t)k * cols)[g];
+        wsum += w;
+        o.x = fmaf(w, v.x, o.x);
+        o.y = fmaf(w, v.y, o.y);
+        o.z = fmaf(w, v.z, o.z);
+        o.w = fmaf(w, v.w, o.w);
+    }
+    const float r = 1.0f / wsum;
+    return make_float4(o.x * r, o.y * r, o.z * r, o.w * r);
+}
 
 // ------------------------------------------------------- x in fixed point --
 
@@ -615,6 +644,8 @@ __global__ void __launch_bounds__((W + 1) * 32, 1) smallm_qgemv_kernel(const Gem
                     if (blockIdx.x == 0) reinterpret_cast<float4*>(p.x_out)[g] = v;
                 }
                 xq[k] = v;
+            } else if (PRO == PRO_PLAIN && p.merge_parts > 1) {
+                xq[k] = g < ngr ? merge_granule(p, g) : make_float4(0.f, 0.f, 0.f, 0.f);
             } else {
                 xq[k] = g < ngr ? x4[g] : make_float4(0.f, 0.f, 0.f, 0.f);
             }

@@ -668,6 +668,12 @@ void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_
     p.done_ctr = a.done_ctr;
     p.epoch = a.epoch;
     p.tp = a.tp;
+    p.merge_parts = a.merge_parts < 1 ? 1 : a.merge_parts;
+    p.merge_hd = a.merge_hd;
+    p.merge_ml = a.merge_ml;
+    if (p.merge_parts > 1 && (pro != GEMV_PRO_PLAIN || !a.merge_ml || a.merge_hd == 0 || a.merge_hd % 4 ||
+                              m.cols % a.merge_hd))
+        throw Error(1, "gemv: an attention-partial merge needs the plain prologue, (max, sum) and whole heads");
     if ((pro == GEMV_PRO_RMS_SUM || epi == GEMV_EPI_PEER) &&
         (a.tp < 1 || a.tp > (uint32_t)kMaxTPRanks || !a.epoch || (epi == GEMV_EPI_PEER && !a.done_ctr) ||
          (pro == GEMV_PRO_RMS_SUM && (!a.x_res || !a.x_out || !a.rx || !a.rx_flag))))

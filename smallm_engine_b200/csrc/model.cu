@@ -325,10 +325,15 @@ void Model::load(const std::string& path, const smallm_model_opts& o) {
     // cluster, then settle on the cluster that fits it
     attn_cluster = attention_cluster_size(nh_l, nkv_l, hd, 32);
     for (int it = 0; it < 3; ++it) {
-        attn_chunk = attention_cluster_chunk(max_ctx, attn_cluster, hd);
+        attn_parts = attention_cluster_parts(nkv_l, attn_cluster, max_ctx, device_sm_count());
+        attn_chunk = attention_cluster_chunk(max_ctx, attn_cluster, hd, attn_parts);
         const uint32_t c = attention_cluster_size(nh_l, nkv_l, hd, attn_chunk);
         if (c == attn_cluster) break;
         attn_cluster = c;
+    }
+    if (attn_parts > 1) {
+        attn_part_out = static_cast<float*>(dalloc(4ull * attn_parts * nh_l * hd));
+        attn_part_ml = static_cast<float*>(dalloc(8ull * attn_parts * nh_l));
     }
     {
         // an attention CTA (dynamic + a little static shared memory) next to a
@@ -494,10 +499,19 @@ void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
         at.err = device_error_flag();
         at.trace = slot(TK_ATTN);
         at.chunk = attn_chunk;
+        at.parts = attn_parts;
+        at.part_out = attn_part_out;
+        at.part_ml = attn_part_ml;
         launch_attention_cluster(at, attn_cluster, s, pdl);
 
         GemvArgs ao;
         ao.x = att;
+        if (attn_parts > 1) {  // the O GEMV merges the attention's parts as it stages x
+            ao.x = attn_part_out;
+            ao.merge_parts = attn_parts;
+            ao.merge_hd = hd;
+            ao.merge_ml = attn_part_ml;
+        }
         ao.y = x;
         ao.trace = slot(TK_O);
         ao.smem_cap = gemv_cap_attn;

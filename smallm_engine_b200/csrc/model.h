@@ -45,6 +45,9 @@ struct Model {
     float *logits = nullptr, *logits_local = nullptr;
     uint32_t attn_cluster = 1;  // CTAs per KV head in the cluster attention
     uint32_t attn_chunk = 32;   // its positions per chunk (sized for max_ctx)
+    uint32_t attn_parts = 1;    // clusters per KV head (long contexts, few KV heads)
+    float* attn_part_out = nullptr;  // [parts][n_heads * hd] when attn_parts > 1
+    float* attn_part_ml = nullptr;   // [parts][n_heads][2]
     size_t gemv_cap_attn = 0;   // shared-memory cap of the QKV / O GEMVs (room for an attention CTA)
     // Tensor parallelism (tp_size > 1): the residual is all-reduced through
     // peer memory by the GEMVs themselves (gemv.cuh EPI_PEER / PRO_RMS_SUM).
