@@ -71,7 +71,7 @@ void qmat_upload(QMat& m, const uint8_t* host, uint32_t type, uint32_t rows, uin
                  uint64_t src_cols, uint64_t col0, const std::vector<uint32_t>& row_map,
                  cudaStream_t stream);
 
-enum GemvPro { GEMV_PRO_PLAIN = 0, GEMV_PRO_RMS = 1, GEMV_PRO_RMS_SUM = 2 };
+enum GemvPro { GEMV_PRO_PLAIN = 0, GEMV_PRO_RMS = 1, GEMV_PRO_RMS_SUM = 2, GEMV_PRO_MERGE = 3 };
 enum GemvEpi { GEMV_EPI_STORE = 0, GEMV_EPI_RESIDUAL = 1, GEMV_EPI_QKV = 2, GEMV_EPI_SWIGLU = 3,
                GEMV_EPI_LOGITS = 4, GEMV_EPI_PEER = 5 };
 constexpr int kMaxTPRanks = 8;
@@ -107,7 +107,7 @@ struct GemvArgs {
     // to theirs (it stages cached K/V while the QKV GEMV runs, and the O
     // GEMV prefetches weights while attention runs).
     size_t smem_cap = 0;
-    // plain prologue only: x is the merge of merge_parts attention partials
+    // GEMV_PRO_MERGE: x is the merge of merge_parts attention partials
     // (x + k * cols, weighted per head of merge_hd elements by merge_ml)
     uint32_t merge_parts = 1, merge_hd = 0;
     const float* merge_ml = nullptr;

@@ -41,7 +41,7 @@
 
 namespace smallm {
 
-enum { PRO_PLAIN = 0, PRO_RMS = 1, PRO_RMS_SUM = 2 };
+enum { PRO_PLAIN = 0, PRO_RMS = 1, PRO_RMS_SUM = 2, PRO_MERGE = 3 };
 enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4, EPI_PEER = 5 };
 constexpr int kMaxTP = 8;
 
@@ -106,9 +106,9 @@ struct GemvParams {
     unsigned int* done_ctr;         // EPI_PEER: finished CTAs, zero between launches
     const unsigned int* epoch;      // steps completed so far (same on every rank)
     uint32_t tp;
-    // PRO_PLAIN: x is the merge of merge_parts attention partials
+    // PRO_MERGE: x is the merge of merge_parts attention partials
     // ([parts][cols], normalised per part) with per-head (max, sum) weights
-    // merge_ml [parts][cols / merge_hd][2]; 1 = x as is
+    // merge_ml [parts][cols / merge_hd][2]
     uint32_t merge_parts, merge_hd;
     const float* merge_ml;
 };
@@ -593,7 +593,7 @@ __global__ void __launch_bounds__((W + 1) * 32, 1) smallm_qgemv_kernel(const Gem
     const float4* x4 = reinterpret_cast<const float4*>(p.x);
     const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
     const uint32_t ngr = p.cols / 4;  // a multiple of 8: whole blocks are in or out
-    constexpr bool kRms = PRO != PRO_PLAIN;
+    constexpr bool kRms = PRO == PRO_RMS || PRO == PRO_RMS_SUM;
     float4 wpre[kB];
     if constexpr (kRms) {
 #pragma unroll
@@ -644,7 +644,7 @@ __global__ void __launch_bounds__((W + 1) * 32, 1) smallm_qgemv_kernel(const Gem
                     if (blockIdx.x == 0) reinterpret_cast<float4*>(p.x_out)[g] = v;
                 }
                 xq[k] = v;
-            } else if (PRO == PRO_PLAIN && p.merge_parts > 1) {
+            } else if constexpr (PRO == PRO_MERGE) {
                 xq[k] = g < ngr ? merge_granule(p, g) : make_float4(0.f, 0.f, 0.f, 0.f);
             } else {
                 xq[k] = g < ngr ? x4[g] : make_float4(0.f, 0.f, 0.f, 0.f);

@@ -524,6 +524,9 @@ static const void* pick(int pro, int epi) {
     if (pro == PRO_RMS_SUM && epi == EPI_QKV) return (const void*)smallm_qgemv_kernel<Fmt, PRO_RMS_SUM, EPI_QKV, W>;
     if (pro == PRO_RMS_SUM && epi == EPI_SWIGLU) return (const void*)smallm_qgemv_kernel<Fmt, PRO_RMS_SUM, EPI_SWIGLU, W>;
     if (pro == PRO_RMS_SUM && epi == EPI_LOGITS) return (const void*)smallm_qgemv_kernel<Fmt, PRO_RMS_SUM, EPI_LOGITS, W>;
+    // the O projection after a multi-part attention: merge the parts as x is staged
+    if (pro == PRO_MERGE && epi == EPI_RESIDUAL) return (const void*)smallm_qgemv_kernel<Fmt, PRO_MERGE, EPI_RESIDUAL, W>;
+    if (pro == PRO_MERGE && epi == EPI_PEER) return (const void*)smallm_qgemv_kernel<Fmt, PRO_MERGE, EPI_PEER, W>;
     throw Error(1, "gemv: unsupported prologue/epilogue combination");
 }
 
@@ -671,9 +674,9 @@ void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_
     p.merge_parts = a.merge_parts < 1 ? 1 : a.merge_parts;
     p.merge_hd = a.merge_hd;
     p.merge_ml = a.merge_ml;
-    if (p.merge_parts > 1 && (pro != GEMV_PRO_PLAIN || !a.merge_ml || a.merge_hd == 0 || a.merge_hd % 4 ||
-                              m.cols % a.merge_hd))
-        throw Error(1, "gemv: an attention-partial merge needs the plain prologue, (max, sum) and whole heads");
+    if (pro == GEMV_PRO_MERGE && (p.merge_parts < 2 || !a.merge_ml || a.merge_hd == 0 || a.merge_hd % 4 ||
+                                  m.cols % a.merge_hd))
+        throw Error(1, "gemv: an attention-partial merge needs >= 2 parts, their (max, sum) and whole heads");
     if ((pro == GEMV_PRO_RMS_SUM || epi == GEMV_EPI_PEER) &&
         (a.tp < 1 || a.tp > (uint32_t)kMaxTPRanks || !a.epoch || (epi == GEMV_EPI_PEER && !a.done_ctr) ||
          (pro == GEMV_PRO_RMS_SUM && (!a.x_res || !a.x_out || !a.rx || !a.rx_flag))))

@@ -516,7 +516,8 @@ void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
         ao.trace = slot(TK_O);
         ao.smem_cap = gemv_cap_attn;
         if (tpx) send(ao, 2 * i);
-        launch_gemv(L.o, GEMV_PRO_PLAIN, tpx ? GEMV_EPI_PEER : GEMV_EPI_RESIDUAL, ao, s, pdl);
+        launch_gemv(L.o, attn_parts > 1 ? GEMV_PRO_MERGE : GEMV_PRO_PLAIN, tpx ? GEMV_EPI_PEER : GEMV_EPI_RESIDUAL,
+                    ao, s, pdl);
 
         GemvArgs ag;
         ag.x = x;
