@@ -97,9 +97,9 @@ struct GemvArgs {
     float* x_out = nullptr;
     const float* rx = nullptr;
     const unsigned int* rx_flag = nullptr;
-    uint32_t rx_ctas = 1, rx_stride = 1;  // flags per rank (one per producer CTA) and their stride
     float* peer_out[kMaxTPRanks] = {};
-    unsigned int* peer_flag[kMaxTPRanks] = {};  // EPI_PEER: this rank's flags at rank q, one per CTA
+    unsigned int* peer_flag[kMaxTPRanks] = {};
+    unsigned int* done_ctr = nullptr;
     const unsigned int* epoch = nullptr;
     uint32_t tp = 1;
     // Shared memory the launch may use (0: the 227 KB limit).  The decode
@@ -126,8 +126,6 @@ struct GemvPlan {
     size_t xbytes = 0, smem = 0;
 };
 GemvPlan gemv_plan(const QMat& m, size_t smem_cap = 0);
-// CTAs of a GEMV launch over m (the arrival flags an EPI_PEER launch raises per rank).
-uint32_t gemv_grid(const QMat& m);
 
 // Error bits raised by GEMV kernels whose bounded waits gave up (0 = none).
 unsigned int gemv_error_flags(bool clear);

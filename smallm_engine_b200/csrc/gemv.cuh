@@ -92,18 +92,18 @@ struct GemvParams {
     TraceSlot* trace;     // null outside traced steps
     // Tensor-parallel residual, all-reduced through peer memory instead of a
     // separate collective.  EPI_PEER (row-parallel O / down): each finished
-    // row's partial goes straight into every rank's receive buffer, and every
-    // CTA then raises its own arrival flag at every rank (slot blockIdx.x).
+    // row's partial goes straight into every rank's receive buffer, and the
+    // kernel's last CTA raises this rank's arrival flag at every rank.
     // PRO_RMS_SUM (the next GEMV): waits for all ranks' flags, takes
     // x = x_res + sum over ranks of the partials (rank order: identical bits on
     // every rank), CTA 0 stores it to x_out, then the RMSNorm prologue runs.
     const float* x_res;             // PRO_RMS_SUM: residual before the add
     float* x_out;                   // PRO_RMS_SUM: residual after the add
     const float* rx;                // PRO_RMS_SUM: [tp][cols] received partials
-    const unsigned int* rx_flag;    // PRO_RMS_SUM: rank r's flags at rx_flag + r * rx_stride (epoch + 1 when ready)
-    uint32_t rx_ctas, rx_stride;    // PRO_RMS_SUM: flags per rank (the producer's CTAs) and their stride
+    const unsigned int* rx_flag;    // PRO_RMS_SUM: [tp] arrival flags (epoch + 1 when ready)
     float* peer_out[kMaxTP];        // EPI_PEER: rank q's receive slot for this rank's partial
-    unsigned int* peer_flag[kMaxTP];// EPI_PEER: this rank's flags at rank q, one per CTA
+    unsigned int* peer_flag[kMaxTP];// EPI_PEER: this rank's arrival flag at rank q
+    unsigned int* done_ctr;         // EPI_PEER: finished CTAs, zero between launches
     const unsigned int* epoch;      // steps completed so far (same on every rank)
     uint32_t tp;
     // PRO_MERGE: x is the merge of merge_parts attention partials
@@ -608,12 +608,11 @@ __global__ void __launch_bounds__((W + 1) * 32, 1) smallm_qgemv_kernel(const Gem
         // every rank's partial of the previous row-parallel GEMV must have
         // arrived (bounded wait; on timeout the error flag is raised and the
         // step's result is not valid)
-        {  // one flag per (rank, producer CTA); the consumer threads share them
+        if (ctid == 0) {
             const unsigned int want = __ldcg(p.epoch) + 1u;
             const long long t0 = clock64();
-            for (uint32_t i = ctid; i < p.tp * p.rx_ctas; i += kStride) {
-                const unsigned int* f = p.rx_flag + (size_t)(i / p.rx_ctas) * p.rx_stride + i % p.rx_ctas;
-                while (ld_acquire_sys(f) != want) {
+            for (uint32_t r = 0; r < p.tp; ++r) {
+                while (ld_acquire_sys(p.rx_flag + r) != want) {
                     if (clock64() - t0 > (1ll << 31)) {
                         atomicOr(p.err, 8u);
                         break;
@@ -795,17 +794,18 @@ __global__ void __launch_bounds__((W + 1) * 32, 1) smallm_qgemv_kernel(const Gem
         }
     }
     if constexpr (EPI == EPI_PEER) {
-        // every row partial of this CTA is stored (at the peers too): the CTA
-        // raises its own flag at every rank.  One thread fences after the CTA
-        // barrier: the barrier orders the other threads' peer stores before
-        // its system-scope fence, which is cumulative (a fence in every
-        // thread, and a counter with a last-CTA flag raise, cost ~2-4 us per
-        // exchange)
+        // every row partial of this CTA is stored (at the peers too); the last
+        // CTA to finish raises this rank's flag at every rank.  One thread
+        // fences after the CTA barrier: the barrier orders the other threads'
+        // peer stores before its system-scope fence, which is cumulative (a
+        // fence in every thread cost each CTA an NVLink round trip per thread)
         consumers_sync<W>();
-        if (ctid == 0) {
+        if (ctid == 0) __threadfence_system();
+        if (ctid == 0 && atomicAdd(p.done_ctr, 1u) == gridDim.x - 1) {
+            *p.done_ctr = 0u;
             __threadfence_system();
             const unsigned int e = __ldcg(p.epoch) + 1u;
-            for (uint32_t r = 0; r < p.tp; ++r) st_release_sys(p.peer_flag[r] + blockIdx.x, e);
+            for (uint32_t r = 0; r < p.tp; ++r) st_release_sys(p.peer_flag[r], e);
         }
     }
     if (p.trace) {

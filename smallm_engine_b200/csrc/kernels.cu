@@ -616,12 +616,6 @@ void set_smem_limit_once(const void* fn, int bytes) {
     done.insert({dev, fn, bytes});
 }
 
-uint32_t gemv_grid(const QMat& m) {
-    const uint32_t ntiles = m.rows_pad / gemv_plan(m, 0).rt;
-    const uint32_t sms = (uint32_t)device_sm_count();
-    return ntiles < sms ? ntiles : sms;
-}
-
 void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_t stream, bool pdl) {
     const GemvPlan pl = gemv_plan(m, a.smem_cap);
     const void* fn = gemv_kernel_for(m.type, pro, epi, pl.warps);
@@ -674,8 +668,7 @@ void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_
         p.peer_out[r] = a.peer_out[r];
         p.peer_flag[r] = a.peer_flag[r];
     }
-    p.rx_ctas = a.rx_ctas < 1 ? 1 : a.rx_ctas;
-    p.rx_stride = a.rx_stride < 1 ? 1 : a.rx_stride;
+    p.done_ctr = a.done_ctr;
     p.epoch = a.epoch;
     p.tp = a.tp;
     p.merge_parts = a.merge_parts < 1 ? 1 : a.merge_parts;
@@ -685,8 +678,8 @@ void launch_gemv(const QMat& m, int pro, int epi, const GemvArgs& a, cudaStream_
                                   m.cols % a.merge_hd))
         throw Error(1, "gemv: an attention-partial merge needs >= 2 parts, their (max, sum) and whole heads");
     if ((pro == GEMV_PRO_RMS_SUM || epi == GEMV_EPI_PEER) &&
-        (a.tp < 1 || a.tp > (uint32_t)kMaxTPRanks || !a.epoch ||
-         (pro == GEMV_PRO_RMS_SUM && (!a.x_res || !a.x_out || !a.rx || !a.rx_flag || a.rx_ctas > a.rx_stride))))
+        (a.tp < 1 || a.tp > (uint32_t)kMaxTPRanks || !a.epoch || (epi == GEMV_EPI_PEER && !a.done_ctr) ||
+         (pro == GEMV_PRO_RMS_SUM && (!a.x_res || !a.x_out || !a.rx || !a.rx_flag))))
         throw Error(1, "gemv: incomplete tensor-parallel arguments");
     void* args[] = {&p};
     launch_kernel_ex(fn, dim3(grid), dim3((pl.warps + 1) * 32), pl.smem, stream, pdl, args);

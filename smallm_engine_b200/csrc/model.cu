@@ -365,9 +365,7 @@ void Model::load(const std::string& path, const smallm_model_opts& o) {
         // 64-byte handles travel over the communicator)
         const uint32_t ops = 2 * n_layers;
         xchg_rx_bytes = 4ull * ops * tp_size * embd;
-        // arrival flags: per op and sending rank, one per sending CTA
-        xchg_flag_slots = (uint32_t)device_sm_count();
-        const size_t xbytes = xchg_rx_bytes + 4ull * ops * tp_size * xchg_flag_slots;
+        const size_t xbytes = xchg_rx_bytes + 4ull * ops * tp_size;
         xchg = static_cast<uint8_t*>(dalloc(xbytes));
         SM_CUDA(cudaMemset(xchg, 0, xbytes));
         cudaIpcMemHandle_t mine;
@@ -389,6 +387,8 @@ void Model::load(const std::string& path, const smallm_model_opts& o) {
             SM_CUDA(cudaIpcOpenMemHandle(&pm, handles[r], cudaIpcMemLazyEnablePeerAccess));
             peer_xchg[r] = static_cast<uint8_t*>(pm);
         }
+        done = static_cast<unsigned int*>(dalloc(4ull * ops));
+        SM_CUDA(cudaMemset(done, 0, 4ull * ops));
         epoch = static_cast<unsigned int*>(dalloc(4));
         SM_CUDA(cudaMemset(epoch, 0, 4));
         xbuf[0] = x;
@@ -434,11 +434,12 @@ void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
         return reinterpret_cast<float*>(base) + ((size_t)op * tp_size + r) * embd;
     };
     auto flag_at = [&](uint8_t* base, uint32_t op, int r) {
-        return reinterpret_cast<unsigned int*>(base + xchg_rx_bytes) + ((size_t)op * tp_size + r) * xchg_flag_slots;
+        return reinterpret_cast<unsigned int*>(base + xchg_rx_bytes) + (size_t)op * tp_size + r;
     };
     auto send = [&](GemvArgs& a, uint32_t op) {  // this rank's partial of op -> every rank
         a.tp = tp_size;
         a.epoch = epoch;
+        a.done_ctr = done + op;
         for (int r = 0; r < tp_size; ++r) {
             a.peer_out[r] = rx_at(peer_xchg[r], op, tp_rank);
             a.peer_flag[r] = flag_at(peer_xchg[r], op, tp_rank);
@@ -452,9 +453,6 @@ void Model::enqueue_step(cudaStream_t s, TraceSlot* trace) {
         a.x = a.x_res;
         a.rx = rx_at(xchg, op, 0);
         a.rx_flag = flag_at(xchg, op, 0);
-        // op 2i is layer i's O projection, op 2i + 1 its down projection
-        a.rx_ctas = gemv_grid(op % 2 ? layers[op / 2].down : layers[op / 2].o);
-        a.rx_stride = xchg_flag_slots;
     };
     for (uint32_t i = 0; i < n_layers; ++i) {
         LayerW& L = layers[i];

@@ -57,8 +57,8 @@ struct Model {
     float* xbuf[2] = {nullptr, nullptr};  // residual before / after each add (op k reads xbuf[k % 2])
     uint8_t* xchg = nullptr;
     size_t xchg_rx_bytes = 0;
-    uint32_t xchg_flag_slots = 0;     // arrival flags per (op, sending rank): one per sending CTA
     uint8_t* peer_xchg[kMaxTPRanks] = {};  // every rank's xchg as mapped here (own at tp_rank)
+    unsigned int* done = nullptr;          // [op] finished-CTA counters
     unsigned int* epoch = nullptr;         // steps run, identical on every rank
     DecodeState* st = nullptr;
     DecodeState* h_st = nullptr;
