@@ -247,7 +247,7 @@ def reference_arm(args, ws, rank):
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "greedy_ids_head": [int(v) for v in ids[:8]]}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ------------------------------------------------------------------ ours --
@@ -444,12 +444,32 @@ def our_arm(args, ws, rank, local):
         }
         if cpu:
             line["cpu_baseline"] = cpu
-        print(json.dumps(line), flush=True)
+        emit(line)
     barrier(ws)
     m.close()
 
 
+# The result line is the only thing on stdout: libraries loaded on the way
+# (NCCL prints its version there when NCCL_DEBUG is set) write to the
+# process's file descriptor 1, so fd 1 is pointed at stderr for the run and
+# the line goes to the saved original.
+_RESULT_FD = None
+
+
+def emit(line: dict) -> None:
+    data = (json.dumps(line) + "\n").encode()
+    if _RESULT_FD is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_RESULT_FD, data)
+
+
 def main():
+    global _RESULT_FD
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=64)
