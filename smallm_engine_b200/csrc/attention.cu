@@ -275,7 +275,9 @@ void launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {
 // initialisation (arrive at the start, wait before the first push) and keeps
 // every CTA alive until all of its peers' pushes are done (arrive after the
 // pushes, wait at the end).  No global scratch, no atomics, one launch.
-constexpr int kCAttnThreads = 128;
+// 4 warps per CTA, or 8 when a CTA's chunk holds 64 positions or more (long
+// contexts: half the score and V passes; measured on the TinyLlama shape)
+__host__ __device__ constexpr int cattn_threads(uint32_t chunk) { return chunk >= 64 ? 256 : 128; }
 constexpr uint32_t kCAttnChunkUnit = 32;  // chunks are 1..kCAttnMaxUnits units of positions
 constexpr uint32_t kCAttnMaxUnits = 8;
 constexpr uint32_t kCAttnMaxCluster = 16;
@@ -293,11 +295,12 @@ uint32_t attention_cluster_parts(uint32_t n_kv, uint32_t C, uint32_t max_ctx, in
 }
 
 __host__ __device__ constexpr size_t cattn_smem_floats(uint32_t G, uint32_t hd, uint32_t chunk) {
+    // (the V-pass slice partials below are sized for the chunk's thread count)
     return 2 * (size_t)chunk * hd                          // ks, vs
            + (size_t)G * hd                                // qs
            + (size_t)G * chunk                             // sc
            + 3 * kAttnMaxGroup                             // corr, pm, pl
-           + (size_t)(kCAttnThreads - hd) * kAttnMaxGroup  // V-pass slice partials
+           + (size_t)(cattn_threads(chunk) - hd) * kAttnMaxGroup  // V-pass slice partials
            + (size_t)G * hd + kCAttnMaxCluster             // received output slices: C x ceil(G hd / C)
            + 2 * (size_t)kCAttnMaxCluster * kAttnMaxGroup  // received (max, sum) per CTA and head
            + (size_t)kAttnMaxGroup * kCAttnMaxCluster;     // merge weights
@@ -314,8 +317,9 @@ __device__ __forceinline__ void cattn_range(uint32_t n, uint32_t parts, uint32_t
     e = min(pe, b + per);
 }
 
-template <int HD>
-__global__ void __launch_bounds__(kCAttnThreads) smallm_attention_cluster_kernel(const AttnArgs a) {
+template <int HD, int T>
+__global__ void __launch_bounds__(T) smallm_attention_cluster_kernel(const AttnArgs a) {
+    constexpr int kCAttnThreads = T;           // 128 or 256 (cattn_threads of the chunk)
     constexpr int PARTS = kCAttnThreads / HD;  // position slices in the V pass
     constexpr int DL = HD / 8;                 // head-dim elements per lane in the score pass
     constexpr int DV = DL / 4;                 // ... as float4
@@ -616,15 +620,19 @@ uint32_t attention_cluster_chunk(uint32_t max_ctx, uint32_t C, uint32_t hd, uint
     return u * kCAttnChunkUnit;
 }
 
-static const void* cattn_fn(uint32_t hd) {
-    if (hd == 32) return (const void*)smallm_attention_cluster_kernel<32>;
-    if (hd == 64) return (const void*)smallm_attention_cluster_kernel<64>;
-    if (hd == 128) return (const void*)smallm_attention_cluster_kernel<128>;
+static const void* cattn_fn(uint32_t hd, uint32_t chunk) {
+    const bool wide = cattn_threads(chunk) == 256;
+    if (hd == 32) return wide ? (const void*)smallm_attention_cluster_kernel<32, 256>
+                              : (const void*)smallm_attention_cluster_kernel<32, 128>;
+    if (hd == 64) return wide ? (const void*)smallm_attention_cluster_kernel<64, 256>
+                              : (const void*)smallm_attention_cluster_kernel<64, 128>;
+    if (hd == 128) return wide ? (const void*)smallm_attention_cluster_kernel<128, 256>
+                               : (const void*)smallm_attention_cluster_kernel<128, 128>;
     throw Error(SMALLM_ERR_INVALID, "attention: head_dim must be 32, 64 or 128");
 }
 
 uint32_t attention_cluster_size(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t chunk) {
-    const void* fn = cattn_fn(hd);
+    const void* fn = cattn_fn(hd, chunk);
     const size_t smem = 4 * cattn_smem_floats(n_heads / n_kv, hd, chunk);
     SM_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     SM_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -634,7 +642,7 @@ uint32_t attention_cluster_size(uint32_t n_heads, uint32_t n_kv, uint32_t hd, ui
     for (uint32_t C = SMALLM_ATTN_CLUSTER; C > 1; C /= 2) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(n_kv * C);
-        cfg.blockDim = dim3(kCAttnThreads);
+        cfg.blockDim = dim3(cattn_threads(chunk));
         cfg.dynamicSmemBytes = smem;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -655,12 +663,12 @@ void launch_attention_cluster(const AttnArgs& a, uint32_t C, cudaStream_t stream
     if (G > (uint32_t)kAttnMaxGroup || a.n_heads % a.n_kv)
         throw Error(SMALLM_ERR_INVALID, "attention: unsupported head grouping");
     if (C < 1 || C > kCAttnMaxCluster) throw Error(SMALLM_ERR_INVALID, "attention: bad cluster size");
-    const void* fn = cattn_fn(a.hd);
+    const void* fn = cattn_fn(a.hd, a.chunk);
     cudaLaunchConfig_t cfg = {};
     if (a.parts < 1 || a.parts > kCAttnMaxParts || (a.parts > 1 && (!a.part_out || !a.part_ml)))
         throw Error(SMALLM_ERR_INVALID, "attention: bad part count or missing part buffers");
     cfg.gridDim = dim3(a.n_kv * a.parts * C);
-    cfg.blockDim = dim3(kCAttnThreads);
+    cfg.blockDim = dim3(cattn_threads(a.chunk));
     if (a.chunk < kCAttnChunkUnit || a.chunk > kCAttnChunkUnit * kCAttnMaxUnits || a.chunk % kCAttnChunkUnit)
         throw Error(SMALLM_ERR_INVALID, "attention: bad chunk size");
     cfg.dynamicSmemBytes = 4 * cattn_smem_floats(G, a.hd, a.chunk);
